@@ -1,0 +1,400 @@
+/*
+ * base2_oracle.c -- TEST INFRASTRUCTURE ONLY. A plain-C restatement of the reference's CPU machine `base2.py`
+ * (the integer-only GPT-2), used as the parity checker for the CUDA engine and as the timed CPU baseline.
+ * Nothing in the product links or calls this file; only tests/, __graft_entry__.smoke() and bench.py's CPU legs do.
+ *
+ * Every function states the reference lines it follows. Arithmetic is numpy int64 arithmetic exactly as base2.py
+ * gets it:
+ *   - +, -, * wrap modulo 2^64 (numpy int64 array ops do; hazard: power()'s X*EXP2 does wrap at long contexts);
+ *   - np.left_shift by >= 64 gives 0, np.right_shift by >= 64 gives the sign fill (numpy's defined shifts);
+ *   - products (base2.py:29-32) are float64 matmuls asserted below 2^52, hence exact; here they are exact int64
+ *     sums, which give the same integers whenever base2.py's own assert holds.
+ * Signed overflow is undefined in C, so every wrapping operation goes through uint64_t.
+ */
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+typedef int64_t i64;
+typedef uint64_t u64;
+
+static inline i64 wadd(i64 a, i64 b) { return (i64)((u64)a + (u64)b); }
+static inline i64 wsub(i64 a, i64 b) { return (i64)((u64)a - (u64)b); }
+static inline i64 wmul(i64 a, i64 b) { return (i64)((u64)a * (u64)b); }
+static inline i64 np_lsh(i64 x, i64 s) { return (s < 0 || s >= 64) ? 0 : (i64)((u64)x << s); }
+static inline i64 np_rsh(i64 x, i64 s) { return s >= 64 ? (x < 0 ? -1 : 0) : (s < 0 ? 0 : (x >> s)); }
+
+/* base2.py:18-22 rshift: X x 2^-s rounded to nearest (add half, arithmetic shift); s <= 0 shifts left. */
+static inline i64 rshift1(i64 x, i64 s) {
+    i64 up = np_lsh(x, s < 0 ? -s : 0);
+    i64 sp = s > 0 ? s : 0;
+    i64 half = sp > 0 ? np_lsh(1, sp - 1) : 0;
+    return np_rsh(wadd(up, half), sp);
+}
+
+/* Python int.bit_length() of an int64 value (of its magnitude; 64 for INT64_MIN). */
+static inline int bitlen(i64 v) {
+    u64 m = v < 0 ? (u64)0 - (u64)v : (u64)v;
+    return m ? 64 - __builtin_clzll(m) : 0;
+}
+
+/* base2.py:42-48 log2fix: top 1's position t, the next 16 digits m, t*65536 + LOG2[m]. */
+static inline i64 log2fix1(i64 v, const i64 *LOG2) {
+    int t = bitlen(v) - 1;
+    i64 m = t >= 16 ? ((v >> (t - 16)) & 0xFFFF) : (np_lsh(v, 16 - t) & 0xFFFF);
+    return (i64)t * 65536 + LOG2[m];
+}
+
+/* base2.py:50-53 power: X x 2^(F/65536) = rshift(X * EXP2[F & 0xFFFF], 16 - (F >> 16)), the product wrapping. */
+static inline i64 power1(i64 x, i64 F, const i64 *EXP2) {
+    i64 I = F >> 16, f = F & 0xFFFF;
+    return rshift1(wmul(x, EXP2[f]), 16 - I);
+}
+
+/* base2.py:24-27 to16 for one row: sh = max(bit_length(OR |x|) - 15, 0); x16 = rshift(x, sh). Returns sh. */
+static int to16_row(const i64 *x, int n, i64 *x16) {
+    u64 o = 0;
+    for (int i = 0; i < n; i++) o |= (u64)(x[i] < 0 ? wsub(0, x[i]) : x[i]);
+    int top = bitlen((i64)o);
+    int sh = top - 15 > 0 ? top - 15 : 0;
+    for (int i = 0; i < n; i++) x16[i] = rshift1(x[i], sh);
+    return sh;
+}
+
+/* base2.py:78-83 edge: idx = rshift(h, 4) + 32768 picks the share (0 below, 65536 above); rshift(h * share, 16). */
+static inline i64 edge1(i64 h, const i64 *PHI) {
+    i64 idx = wadd(rshift1(h, 16 - 12), 32768);
+    i64 share = idx < 0 ? 0 : (idx > 65535 ? 65536 : PHI[idx]);
+    return rshift1(wmul(h, share), 16);
+}
+
+/* base2.py:34-40 race: the largest value; among equal largest, the lowest index. */
+static i64 race1(const i64 *v, i64 n) {
+    i64 best = 0;
+    for (i64 i = 1; i < n; i++) if (v[i] > v[best]) best = i;
+    return best;
+}
+
+/* ------------------------------------------------------------------------------------------------------------ */
+/* element-wise entry points (the pinning tests call these against base2.py's own outputs)                       */
+/* ------------------------------------------------------------------------------------------------------------ */
+void b2o_rshift(const i64 *x, const i64 *s, i64 n, i64 *y) { for (i64 i = 0; i < n; i++) y[i] = rshift1(x[i], s[i]); }
+void b2o_log2fix(const i64 *v, i64 n, const i64 *LOG2, i64 *y) { for (i64 i = 0; i < n; i++) y[i] = log2fix1(v[i], LOG2); }
+void b2o_power(const i64 *x, const i64 *F, i64 n, const i64 *EXP2, i64 *y) { for (i64 i = 0; i < n; i++) y[i] = power1(x[i], F[i], EXP2); }
+void b2o_edge(const i64 *h, i64 n, const i64 *PHI, i64 *y) { for (i64 i = 0; i < n; i++) y[i] = edge1(h[i], PHI); }
+i64 b2o_race(const i64 *v, i64 n) { return race1(v, n); }
+void b2o_to16(const i64 *X, i64 rows, i64 n, i64 e0, i64 *x16, i64 *ex) {
+    for (i64 r = 0; r < rows; r++) ex[r] = e0 + to16_row(X + r * n, (int)n, x16 + r * n);
+}
+
+/* base2.py:55-60 gauge_log for one row of 768: x16, ex, LS = (log2fix(V) >> 1) - LOG768 + ex*65536,
+ * V = 768*S2 - S1^2 + (EPS40 >> (40 + 2 ex)). n is the row length; the 768 is the reference's constant. */
+static i64 gauge_row(const i64 *x, int n, i64 *x16, i64 *ex_out, const i64 *LOG2, i64 log768, i64 eps40) {
+    i64 ex = -16 + to16_row(x, n, x16);
+    i64 S1 = 0, S2 = 0;
+    for (int i = 0; i < n; i++) { S1 = wadd(S1, x16[i]); S2 = wadd(S2, wmul(x16[i], x16[i])); }
+    i64 V = wsub(wmul(768, S2), wmul(S1, S1));
+    i64 sh = 40 + 2 * ex;
+    V = wadd(V, sh >= 0 ? np_rsh(eps40, sh) : np_lsh(eps40, -sh));
+    *ex_out = ex;
+    return wadd(wsub(log2fix1(V, LOG2) >> 1, log768), wmul(ex, 65536));
+}
+void b2o_gauge_log(const i64 *R, i64 rows, i64 n, const i64 *LOG2, i64 log768, i64 eps40, i64 *x16, i64 *ex, i64 *LS) {
+    for (i64 r = 0; r < rows; r++) LS[r] = gauge_row(R + r * n, (int)n, x16 + r * n, ex + r, LOG2, log768, eps40);
+}
+
+/* ------------------------------------------------------------------------------------------------------------ */
+/* the model                                                                                                     */
+/* ------------------------------------------------------------------------------------------------------------ */
+typedef struct {
+    const int16_t *w;     /* [nin][nout] (reference layout, base2_gpu.py:11) */
+    const i64 *e, *b;     /* [nout] */
+    int nin, nout;
+} bank_t;
+
+typedef struct {
+    int L, d, H, hd, F, V, ctx;
+    bank_t bank[64 * 4 + 1];  /* layer*4 + {qkv, proj, fc, mproj}; head at 4*L */
+    const i64 *wte, *wpe, *PHI, *ARR, *LOG2, *EXP2;
+    i64 alen, log768, eps40;
+} model_t;
+
+void *b2o_create(int L, int d, int H, int F, int V, int ctx) {
+    model_t *m = (model_t *)calloc(1, sizeof(model_t));
+    m->L = L; m->d = d; m->H = H; m->hd = d / H; m->F = F; m->V = V; m->ctx = ctx;
+    return m;
+}
+void b2o_destroy(void *m) { free(m); }
+void b2o_set_bank(void *mv, int idx, const int16_t *w, const i64 *e, const i64 *b, int nin, int nout) {
+    model_t *m = (model_t *)mv;
+    m->bank[idx].w = w; m->bank[idx].e = e; m->bank[idx].b = b; m->bank[idx].nin = nin; m->bank[idx].nout = nout;
+}
+void b2o_set_tables(void *mv, const i64 *wte, const i64 *wpe, const i64 *PHI, const i64 *ARR, i64 alen,
+                    const i64 *LOG2, const i64 *EXP2, i64 log768, i64 eps40) {
+    model_t *m = (model_t *)mv;
+    m->wte = wte; m->wpe = wpe; m->PHI = PHI; m->ARR = ARR; m->alen = alen; m->LOG2 = LOG2; m->EXP2 = EXP2;
+    m->log768 = log768; m->eps40 = eps40;
+}
+
+/* base2.py:29-32 product for one row: pile[j] = sum_i x16[i] * w[i][j], exact. Columns split over threads when
+ * `par` is set (single-stream runs); a multi-stream run parallelises over streams instead. */
+static void product_row(const i64 *x16, const bank_t *bk, i64 *pile, int par) {
+    const int nin = bk->nin, nout = bk->nout;
+    const int CH = 1024;
+    int nch = (nout + CH - 1) / CH;
+#pragma omp parallel for schedule(static) if (par)
+    for (int c = 0; c < nch; c++) {
+        int j0 = c * CH, j1 = j0 + CH < nout ? j0 + CH : nout;
+        i64 acc[1024];
+        for (int j = 0; j < j1 - j0; j++) acc[j] = 0;
+        for (int i = 0; i < nin; i++) {
+            i64 xi = x16[i];
+            if (!xi) continue;
+            const int16_t *wr = bk->w + (size_t)i * nout + j0;
+            for (int j = 0; j < j1 - j0; j++) acc[j] += xi * (i64)wr[j];
+        }
+        for (int j = 0; j < j1 - j0; j++) pile[j0 + j] = acc[j];
+    }
+}
+
+/* base2.py:62-71 gauged_bank (integer gauge) for one row. */
+static void gauged_row(const model_t *m, const bank_t *bk, const i64 *R, i64 *out, i64 *x16, i64 *pile, int par) {
+    i64 ex;
+    i64 LS = gauge_row(R, m->d, x16, &ex, m->LOG2, m->log768, m->eps40);
+    product_row(x16, bk, pile, par);
+    for (int j = 0; j < bk->nout; j++) {
+        i64 F = wsub(wmul(wadd(wadd(bk->e[j], ex), 16), 65536), LS);
+        out[j] = wadd(power1(pile[j], F, m->EXP2), bk->b[j]);
+    }
+}
+
+/* base2.py:73-76 plain_bank for one row, added into R (base2.py:105-106 R = R + plain_bank(...)). */
+static void plain_row_add(const model_t *m, const bank_t *bk, const i64 *X, i64 *R, i64 *x16, i64 *pile, int par) {
+    i64 ex = -16 + to16_row(X, bk->nin, x16);
+    product_row(x16, bk, pile, par);
+    for (int j = 0; j < bk->nout; j++)
+        R[j] = wadd(R[j], wadd(rshift1(pile[j], -wadd(wadd(bk->e[j], ex), 16)), bk->b[j]));
+}
+
+void b2o_gauged_bank(void *mv, int idx, const i64 *R, int rows, i64 *out) {
+    model_t *m = (model_t *)mv; const bank_t *bk = &m->bank[idx];
+    i64 *x16 = (i64 *)malloc(sizeof(i64) * bk->nin), *pile = (i64 *)malloc(sizeof(i64) * bk->nout);
+    for (int r = 0; r < rows; r++) gauged_row(m, bk, R + (size_t)r * bk->nin, out + (size_t)r * bk->nout, x16, pile, 1);
+    free(x16); free(pile);
+}
+void b2o_plain_bank(void *mv, int idx, const i64 *X, int rows, i64 *out) {
+    model_t *m = (model_t *)mv; const bank_t *bk = &m->bank[idx];
+    i64 *x16 = (i64 *)malloc(sizeof(i64) * bk->nin), *pile = (i64 *)malloc(sizeof(i64) * bk->nout);
+    for (int r = 0; r < rows; r++) {
+        i64 *o = out + (size_t)r * bk->nout;
+        memset(o, 0, sizeof(i64) * bk->nout);
+        plain_row_add(m, bk, X + (size_t)r * bk->nin, o, x16, pile, 1);
+    }
+    free(x16); free(pile);
+}
+
+/* the per-stream key/value store: what attention at a later position reads of an earlier one */
+typedef struct {
+    i64 *k16;   /* [L][ctx][d]   to16'd keys per head part */
+    i64 *ek;    /* [L][ctx][H]   their exponents */
+    i64 *v;     /* [L][ctx][d]   values at full width (base2.py:98 reads v[:p+1] unshifted) */
+} cache_t;
+
+static int cache_alloc(const model_t *m, cache_t *c, int ctx) {
+    size_t n = (size_t)m->L * ctx;
+    c->k16 = (i64 *)malloc(sizeof(i64) * n * m->d);
+    c->ek = (i64 *)malloc(sizeof(i64) * n * m->H);
+    c->v = (i64 *)malloc(sizeof(i64) * n * m->d);
+    return c->k16 && c->ek && c->v;
+}
+static void cache_free(cache_t *c) { free(c->k16); free(c->ek); free(c->v); }
+
+/* base2.py:85-100 attention, integer arrival, for the position p of one stream given the keys/values of 0..p.
+ * q: this position's 768 query values (int64). Writes 768 outputs. sc: scratch of >= p+1. */
+static void attend_row(const model_t *m, const cache_t *c, int l, int ctx, int p, const i64 *q, i64 *out, i64 *sc) {
+    const int d = m->d, hd = m->hd;
+    i64 q16[256];
+    for (int h = 0; h < m->H; h++) {
+        i64 eq = -16 + to16_row(q + h * hd, hd, q16);
+        const i64 *K = c->k16 + ((size_t)l * ctx) * d + h * hd;
+        const i64 *EK = c->ek + ((size_t)l * ctx) * m->H + h;
+        const i64 *Vv = c->v + ((size_t)l * ctx) * d + h * hd;
+        for (int s = 0; s <= p; s++) {
+            i64 dot = 0;
+            const i64 *k = K + (size_t)s * d;
+            for (int t = 0; t < hd; t++) dot += q16[t] * k[t];
+            sc[s] = rshift1(dot, -(eq + EK[(size_t)s * m->H] - 3 + 10));
+        }
+        i64 start = sc[race1(sc, p + 1)];
+        i64 Z = 0, num[256];
+        for (int t = 0; t < hd; t++) num[t] = 0;
+        for (int s = 0; s <= p; s++) {
+            i64 dd = wsub(start, sc[s]);
+            i64 a = dd < m->alen ? m->ARR[dd < m->alen - 1 ? dd : m->alen - 1] : 0;
+            if (!a) continue;
+            Z = wadd(Z, a);
+            const i64 *v = Vv + (size_t)s * d;
+            for (int t = 0; t < hd; t++) num[t] = wadd(num[t], wmul(a, v[t]));
+        }
+        i64 F = -log2fix1(Z, m->LOG2);
+        for (int t = 0; t < hd; t++) out[h * hd + t] = power1(num[t], F, m->EXP2);
+    }
+}
+
+typedef struct { i64 *R, *qkv, *att, *hid, *x16, *pile, *sc; } scratch_t;
+
+static int scratch_alloc(const model_t *m, scratch_t *s, int ctx) {
+    int wmax = m->V > m->F ? m->V : m->F;
+    s->R = (i64 *)malloc(sizeof(i64) * m->d);
+    s->qkv = (i64 *)malloc(sizeof(i64) * 3 * m->d);
+    s->att = (i64 *)malloc(sizeof(i64) * m->d);
+    s->hid = (i64 *)malloc(sizeof(i64) * m->F);
+    s->x16 = (i64 *)malloc(sizeof(i64) * (m->F > m->d ? m->F : m->d));
+    s->pile = (i64 *)malloc(sizeof(i64) * wmax);
+    s->sc = (i64 *)malloc(sizeof(i64) * ctx);
+    return s->R && s->qkv && s->att && s->hid && s->x16 && s->pile && s->sc;
+}
+static void scratch_free(scratch_t *s) { free(s->R); free(s->qkv); free(s->att); free(s->hid); free(s->x16); free(s->pile); free(s->sc); }
+
+/* One new position p of one stream through the 12 layers (base2.py:103-106), keys/values appended to the cache;
+ * if `logits` is given, the head's scores for this position (base2.py:107-114). Returns the race's word or -1. */
+static int position(const model_t *m, cache_t *c, scratch_t *s, int ctx, int p, int id, i64 *logits, int par) {
+    const int d = m->d, H = m->H, hd = m->hd;
+    for (int i = 0; i < d; i++) s->R[i] = wadd(m->wte[(size_t)id * d + i], m->wpe[(size_t)p * d + i]);
+    for (int l = 0; l < m->L; l++) {
+        gauged_row(m, &m->bank[4 * l + 0], s->R, s->qkv, s->x16, s->pile, par);
+        for (int h = 0; h < H; h++) {
+            i64 *k16 = c->k16 + ((size_t)l * ctx + p) * d + h * hd;
+            c->ek[((size_t)l * ctx + p) * H + h] = -16 + to16_row(s->qkv + d + h * hd, hd, k16);
+        }
+        memcpy(c->v + ((size_t)l * ctx + p) * d, s->qkv + 2 * d, sizeof(i64) * d);
+        attend_row(m, c, l, ctx, p, s->qkv, s->att, s->sc);
+        plain_row_add(m, &m->bank[4 * l + 1], s->att, s->R, s->x16, s->pile, par);
+        gauged_row(m, &m->bank[4 * l + 2], s->R, s->hid, s->x16, s->pile, par);
+        for (int j = 0; j < m->F; j++) s->hid[j] = edge1(s->hid[j], m->PHI);
+        plain_row_add(m, &m->bank[4 * l + 3], s->hid, s->R, s->x16, s->pile, par);
+    }
+    if (!logits) return -1;
+    gauged_row(m, &m->bank[4 * m->L], s->R, logits, s->x16, s->pile, par);
+    return (int)race1(logits, m->V);
+}
+
+static int nthreads(int want) {
+#ifdef _OPENMP
+    if (want > 0) return want;
+    return omp_get_max_threads();
+#else
+    (void)want; return 1;
+#endif
+}
+
+/* Greedy generation for B independent streams of equal prompt length P (base2.py:122-123: each new word is the
+ * race at the last position, fed back in). tokens: [B][n_new]; logits (optional): [B][n_new][V], the scores each
+ * token was raced on. Streams run in parallel over threads; a single stream splits each bank over threads.
+ * Returns 0, or -1 when memory is short or a position passes the context. */
+int b2o_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+    const model_t *m = (const model_t *)mv;
+    int ctx = P + n_new;
+    if (ctx > m->ctx || P < 1) return -1;
+    int nt = nthreads(threads), err = 0;
+    int par = B == 1;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt) if (B > 1)
+    for (int b = 0; b < B; b++) {
+        cache_t c; scratch_t s;
+        i64 *lg = (i64 *)malloc(sizeof(i64) * m->V);
+        if (!cache_alloc(m, &c, ctx) || !scratch_alloc(m, &s, ctx) || !lg) { err = -1; continue; }
+        for (int p = 0; p < P - 1; p++) position(m, &c, &s, ctx, p, ids[(size_t)b * P + p], NULL, par);
+        int tok = ids[(size_t)b * P + P - 1];
+        for (int t = 0; t < n_new; t++) {
+            tok = position(m, &c, &s, ctx, P - 1 + t, tok, lg, par);
+            tokens[(size_t)b * n_new + t] = tok;
+            if (logits) memcpy(logits + ((size_t)b * n_new + t) * m->V, lg, sizeof(i64) * m->V);
+        }
+        cache_free(&c); scratch_free(&s); free(lg);
+    }
+    return err;
+}
+
+/* Teacher-forced scores (the judge5.py:15-23 pattern): one stream's P ids, the head's scores at positions
+ * [first, last). logits: [(last-first)][V]. */
+int b2o_scores(void *mv, const int32_t *ids, int P, int first, int last, i64 *logits) {
+    const model_t *m = (const model_t *)mv;
+    if (P > m->ctx || first < 0 || last > P || first >= last) return -1;
+    cache_t c; scratch_t s;
+    if (!cache_alloc(m, &c, P) || !scratch_alloc(m, &s, P)) return -1;
+    for (int p = 0; p < P; p++)
+        position(m, &c, &s, P, p, ids[p], (p >= first && p < last) ? logits + (size_t)(p - first) * m->V : NULL, 1);
+    cache_free(&c); scratch_free(&s);
+    return 0;
+}
+
+/* base2.py:122-124 exactly as the reference runs it: every new word recomputes the whole prefix from scratch
+ * (no key/value store kept between words). One stream; used only as the timed CPU baseline. */
+int b2o_greedy_recompute(void *mv, const int32_t *ids, int P, int n_new, int32_t *tokens, int threads) {
+    const model_t *m = (const model_t *)mv;
+    int ctx = P + n_new;
+    if (ctx > m->ctx) return -1;
+    (void)threads;
+    int32_t *seq = (int32_t *)malloc(sizeof(int32_t) * ctx);
+    i64 *lg = (i64 *)malloc(sizeof(i64) * m->V);
+    memcpy(seq, ids, sizeof(int32_t) * P);
+    int n = P;
+    for (int t = 0; t < n_new; t++) {
+        cache_t c; scratch_t s;
+        if (!cache_alloc(m, &c, n) || !scratch_alloc(m, &s, n)) return -1;
+        int tok = -1;
+        for (int p = 0; p < n; p++) tok = position(m, &c, &s, n, p, seq[p], p == n - 1 ? lg : NULL, 1);
+        cache_free(&c); scratch_free(&s);
+        tokens[t] = tok;
+        seq[n++] = tok;
+    }
+    free(seq); free(lg);
+    return 0;
+}
+
+/* b2o_greedy_recompute over B streams of equal prompt length, streams in parallel over threads (each stream as
+ * base2.py runs it: the whole prefix recomputed for every new word). tokens [B][n_new]. */
+int b2o_generate_recompute(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, int threads) {
+    const model_t *m = (const model_t *)mv;
+    if (P + n_new > m->ctx) return -1;
+    int nt = nthreads(threads), err = 0;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt)
+    for (int b = 0; b < B; b++) {
+        int ctx = P + n_new;
+        int32_t *seq = (int32_t *)malloc(sizeof(int32_t) * ctx);
+        i64 *lg = (i64 *)malloc(sizeof(i64) * m->V);
+        memcpy(seq, ids + (size_t)b * P, sizeof(int32_t) * P);
+        int n = P;
+        for (int t = 0; t < n_new && !err; t++) {
+            cache_t c; scratch_t s;
+            if (!cache_alloc(m, &c, n) || !scratch_alloc(m, &s, n)) { err = -1; break; }
+            int tok = -1;
+            for (int p = 0; p < n; p++) tok = position(m, &c, &s, n, p, seq[p], p == n - 1 ? lg : NULL, 0);
+            cache_free(&c); scratch_free(&s);
+            tokens[(size_t)b * n_new + t] = tok;
+            seq[n++] = tok;
+        }
+        free(seq); free(lg);
+    }
+    return err;
+}
+
+/* base2.py:85-100 over a whole sequence's QKV [P][3d] (the reference's own attention() shape): out [P][d]. */
+int b2o_attention(void *mv, const i64 *QKV, int P, i64 *out) {
+    const model_t *m = (const model_t *)mv;
+    const int d = m->d, H = m->H, hd = m->hd;
+    model_t one = *m; one.L = 1;
+    cache_t c; i64 *sc = (i64 *)malloc(sizeof(i64) * P);
+    if (!cache_alloc(&one, &c, P) || !sc) return -1;
+    for (int p = 0; p < P; p++) {
+        for (int h = 0; h < H; h++)
+            c.ek[(size_t)p * H + h] = -16 + to16_row(QKV + (size_t)p * 3 * d + d + h * hd, hd, c.k16 + (size_t)p * d + h * hd);
+        memcpy(c.v + (size_t)p * d, QKV + (size_t)p * 3 * d + 2 * d, sizeof(i64) * d);
+    }
+    for (int p = 0; p < P; p++) attend_row(&one, &c, 0, P, p, QKV + (size_t)p * 3 * d, out + (size_t)p * d, sc);
+    cache_free(&c); free(sc);
+    return 0;
+}

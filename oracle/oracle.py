@@ -1,0 +1,233 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU oracle for the integer GPT-2 machine.
+
+A ctypes front of `base2_oracle.c`, the plain-C restatement of the reference's `base2.py`. Only tests/,
+`__graft_entry__.smoke()` and bench.py's CPU legs import this module; the product never does.
+
+The names mirror base2.py's module namespace (`rshift, to16, power, log2fix, race, edge, gauge_log, gauged_bank,
+plain_bank, attention, forward`, reference `base2.py:18-114`) so a parity test reads like the reference's own
+checks. Arrays follow the converter's keys (`base2_convert.py:31-61`).
+"""
+from __future__ import annotations
+
+import ctypes
+import hashlib
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "_build", "libbase2_oracle.so")
+_SRC = os.path.join(HERE, "base2_oracle.c")
+
+_i64p = np.ctypeslib.ndpointer(np.int64, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_i16p = np.ctypeslib.ndpointer(np.int16, flags="C_CONTIGUOUS")
+_lib = None
+
+
+def _stamp() -> str:
+    with open(_SRC, "rb") as f:
+        return hashlib.sha256(f.read()).hexdigest()
+
+
+def build(force: bool = False) -> str:
+    """Compile base2_oracle.c (make) when the library is missing or older than its source."""
+    stamp = LIB + ".src"
+    fresh = os.path.exists(LIB) and os.path.exists(stamp) and open(stamp).read() == _stamp()
+    if force or not fresh:
+        subprocess.run(["make", "-s", "-B", "-C", HERE], check=True)
+        with open(stamp, "w") as f:
+            f.write(_stamp())
+    return LIB
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(LIB)
+        c_i64, c_int, c_vp = ctypes.c_int64, ctypes.c_int, ctypes.c_void_p
+        L.b2o_rshift.argtypes = [_i64p, _i64p, c_i64, _i64p]
+        L.b2o_log2fix.argtypes = [_i64p, c_i64, _i64p, _i64p]
+        L.b2o_power.argtypes = [_i64p, _i64p, c_i64, _i64p, _i64p]
+        L.b2o_edge.argtypes = [_i64p, c_i64, _i64p, _i64p]
+        L.b2o_race.argtypes = [_i64p, c_i64]
+        L.b2o_race.restype = c_i64
+        L.b2o_to16.argtypes = [_i64p, c_i64, c_i64, c_i64, _i64p, _i64p]
+        L.b2o_gauge_log.argtypes = [_i64p, c_i64, c_i64, _i64p, c_i64, c_i64, _i64p, _i64p, _i64p]
+        L.b2o_create.argtypes = [c_int] * 6
+        L.b2o_create.restype = c_vp
+        L.b2o_destroy.argtypes = [c_vp]
+        L.b2o_set_bank.argtypes = [c_vp, c_int, _i16p, _i64p, _i64p, c_int, c_int]
+        L.b2o_set_tables.argtypes = [c_vp, _i64p, _i64p, _i64p, _i64p, c_i64, _i64p, _i64p, c_i64, c_i64]
+        L.b2o_gauged_bank.argtypes = [c_vp, c_int, _i64p, c_int, _i64p]
+        L.b2o_plain_bank.argtypes = [c_vp, c_int, _i64p, c_int, _i64p]
+        L.b2o_attention.argtypes = [c_vp, _i64p, c_int, _i64p]
+        L.b2o_attention.restype = c_int
+        L.b2o_generate.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, ctypes.c_void_p, c_int]
+        L.b2o_generate.restype = c_int
+        L.b2o_scores.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i64p]
+        L.b2o_scores.restype = c_int
+        L.b2o_greedy_recompute.argtypes = [c_vp, _i32p, c_int, c_int, _i32p, c_int]
+        L.b2o_greedy_recompute.restype = c_int
+        L.b2o_generate_recompute.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, c_int]
+        L.b2o_generate_recompute.restype = c_int
+        _lib = L
+    return _lib
+
+
+def _c64(a):
+    return np.ascontiguousarray(a, dtype=np.int64)
+
+
+# ------------------------------------------------------------------------------------------------------------
+# table-driven element functions (need the tables: pass the converted arrays `M`)
+# ------------------------------------------------------------------------------------------------------------
+def rshift(X, s):
+    """base2.py:18-22"""
+    X, s = np.broadcast_arrays(_c64(X), _c64(s))
+    X, s = _c64(X), _c64(s)
+    y = np.empty_like(X)
+    lib().b2o_rshift(X.ravel(), s.ravel(), X.size, y.ravel())
+    return y
+
+
+def to16(X, e):
+    """base2.py:24-27 (rows of X)"""
+    X = _c64(np.atleast_2d(X))
+    x16, sh = np.empty_like(X), np.empty(X.shape[0], np.int64)
+    lib().b2o_to16(X, X.shape[0], X.shape[1], int(e) if np.ndim(e) == 0 else 0, x16, sh)
+    return x16, (sh if np.ndim(e) == 0 else sh + np.asarray(e, np.int64))
+
+
+def race(v):
+    """base2.py:34-40"""
+    v = _c64(v).ravel()
+    return int(lib().b2o_race(v, v.size))
+
+
+class Oracle:
+    """The machine over one set of converted arrays (keys of base2_gpt2.npz)."""
+
+    def __init__(self, M: dict, n_layer: int = 12, ctx: int = 1024):
+        self.M = {k: np.ascontiguousarray(v) for k, v in M.items()}
+        M = self.M
+        d = M["wte"].shape[1]
+        self.d, self.V, self.L = d, M["head.w"].shape[1], n_layer
+        self.F = M["fc.0.w"].shape[1]
+        self.H = d // 64
+        L = lib()
+        self.h = L.b2o_create(n_layer, d, self.H, self.F, self.V, ctx)
+        self._keep = []
+        for i, name in enumerate([f"{b}.{l}" for l in range(n_layer) for b in ("qkv", "proj", "fc", "mproj")] + ["head"]):
+            w = np.ascontiguousarray(M[name + ".w"], dtype=np.int16)
+            e, b = _c64(M[name + ".e"]), _c64(M[name + ".b"])
+            self._keep += [w, e, b]
+            L.b2o_set_bank(self.h, i, w, e, b, w.shape[0], w.shape[1])
+        self.idx = {name: i for i, name in enumerate([f"{b}.{l}" for l in range(n_layer) for b in ("qkv", "proj", "fc", "mproj")] + ["head"])}
+        t = [_c64(M[k]) for k in ("wte", "wpe", "phi", "arrival", "log2", "exp2")]
+        self._keep += t
+        self.alen = len(t[3])
+        self.log768, self.eps40 = (int(np.asarray(M[k]).reshape(-1)[0]) for k in ("log2_768", "eps40"))
+        L.b2o_set_tables(self.h, t[0], t[1], t[2], t[3], self.alen, t[4], t[5], self.log768, self.eps40)
+        self.PHI, self.LOG2, self.EXP2 = t[2], t[4], t[5]
+
+    def __del__(self):
+        try:
+            lib().b2o_destroy(self.h)
+        except Exception:
+            pass
+
+    # ---- element functions -------------------------------------------------------------------------------------
+    def log2fix(self, V):
+        """base2.py:42-48"""
+        V = _c64(V).ravel()
+        y = np.empty_like(V)
+        lib().b2o_log2fix(V, V.size, self.LOG2, y)
+        return y
+
+    def power(self, X, F):
+        """base2.py:50-53"""
+        X, F = np.broadcast_arrays(_c64(X), _c64(F))
+        X, F = _c64(X), _c64(F)
+        y = np.empty_like(X)
+        lib().b2o_power(X.ravel(), F.ravel(), X.size, self.EXP2, y.ravel())
+        return y
+
+    def edge(self, H):
+        """base2.py:78-83 (integer bend)"""
+        H = _c64(H)
+        y = np.empty_like(H)
+        lib().b2o_edge(H.ravel(), H.size, self.PHI, y.ravel())
+        return y
+
+    def gauge_log(self, R):
+        """base2.py:55-60"""
+        R = _c64(np.atleast_2d(R))
+        x16, ex, LS = np.empty_like(R), np.empty(R.shape[0], np.int64), np.empty(R.shape[0], np.int64)
+        lib().b2o_gauge_log(R, R.shape[0], R.shape[1], self.LOG2, self.log768, self.eps40, x16, ex, LS)
+        return x16, ex, LS
+
+    # ---- banks and attention ----------------------------------------------------------------------------------
+    def gauged_bank(self, R, name):
+        """base2.py:62-71 (integer gauge)"""
+        R = _c64(np.atleast_2d(R))
+        out = np.empty((R.shape[0], self.M[name + ".w"].shape[1]), np.int64)
+        lib().b2o_gauged_bank(self.h, self.idx[name], R, R.shape[0], out)
+        return out
+
+    def plain_bank(self, X, name):
+        """base2.py:73-76"""
+        X = _c64(np.atleast_2d(X))
+        out = np.empty((X.shape[0], self.M[name + ".w"].shape[1]), np.int64)
+        lib().b2o_plain_bank(self.h, self.idx[name], X, X.shape[0], out)
+        return out
+
+    def attention(self, QKV):
+        """base2.py:85-100 (integer arrival) over a whole sequence's QKV [P, 2304]."""
+        QKV = _c64(QKV)
+        out = np.empty((QKV.shape[0], self.d), np.int64)
+        if lib().b2o_attention(self.h, QKV, QKV.shape[0], out):
+            raise MemoryError("oracle attention")
+        return out
+
+    # ---- whole machine ----------------------------------------------------------------------------------------
+    def generate(self, ids, n_new: int, logits: bool = False, threads: int = 0):
+        """Greedy words for each row of ids [B, P] (base2.py:122-123); optionally the scores each was raced on."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), dtype=np.int32)
+        B, P = ids.shape
+        tok = np.empty((B, n_new), np.int32)
+        lg = np.empty((B, n_new, self.V), np.int64) if logits else None
+        rc = lib().b2o_generate(self.h, ids, B, P, n_new, tok, lg.ctypes.data if logits else None, threads)
+        if rc:
+            raise RuntimeError(f"oracle generate failed ({rc})")
+        return (tok, lg) if logits else tok
+
+    def forward(self, ids) -> int:
+        """base2.py:102-114: the word after ids."""
+        return int(self.generate(np.asarray(ids)[None, :], 1)[0, 0])
+
+    def scores(self, ids, first: int, last: int):
+        """Teacher-forced head scores at positions [first, last) (judge5.py:15-23 pattern)."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty((last - first, self.V), np.int64)
+        if lib().b2o_scores(self.h, ids, len(ids), first, last, out):
+            raise RuntimeError("oracle scores failed")
+        return out
+
+    def generate_recompute(self, ids, n_new: int, threads: int = 0):
+        """base2.py's greedy loop (prefix recomputed per word) for each row of ids [B, P], rows in parallel."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), dtype=np.int32)
+        tok = np.empty((ids.shape[0], n_new), np.int32)
+        if lib().b2o_generate_recompute(self.h, ids, ids.shape[0], ids.shape[1], n_new, tok, threads):
+            raise RuntimeError("oracle generate_recompute failed")
+        return tok
+
+    def greedy_recompute(self, ids, n_new: int):
+        """base2.py:122-124 as the reference runs it: the whole prefix recomputed for every new word."""
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        tok = np.empty(n_new, np.int32)
+        if lib().b2o_greedy_recompute(self.h, ids, len(ids), n_new, tok, 0):
+            raise RuntimeError("oracle greedy_recompute failed")
+        return tok

@@ -1,0 +1,621 @@
+// b2_engine.cu -- libbase2cuda.so: the C ABI (include/base2.h) over the machine's sm_100a kernels.
+//
+// One handle = one model on one GPU + a set of stream slots, each with its own key/value store. Work is organised in
+// ROWS: a row is (stream slot, position, token). A prompt pass is many rows per stream (chunked); a decode step is
+// one row per stream. Every kernel reads the row table from device memory, so a decode step is position-agnostic on
+// the host and can be replayed from a CUDA graph.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <string>
+#include <vector>
+
+#include "../../include/base2.h"
+#include "b2_kernels.cuh"
+#include "b2_tc.cuh"
+
+using namespace b2;
+
+namespace {
+
+struct DevBank {
+    int nin = 0, nout = 0;
+    int16_t* w = nullptr;   // [nin][nout] (reference layout, CUDA-core path)
+    int32_t* e = nullptr;
+    int64_t* b = nullptr;
+    TcBank tc;              // tensor-core layout (hi/lo int8 planes), see b2_tc.cuh
+};
+
+}  // namespace
+
+struct b2_handle {
+    b2_config cfg{};
+    int device = 0, flags = 0;
+    std::string err;
+    std::vector<DevBank> banks;   // 4 * L + 1 (head last)
+    int64_t *wte = nullptr, *wpe = nullptr;
+    int32_t *PHI = nullptr, *ARR = nullptr, *LOG2 = nullptr, *EXP2 = nullptr;
+    int alen = 0;
+    int64_t log768 = 0, eps40 = 0;
+    bool have_scalar[2] = {false, false};
+    bool finalized = false;
+    int use_tc = 1;               // tensor-core bank product for row counts >= tc_min_rows
+    int tc_min_rows = 1 << 30;    // (set at finalize when the tensor path is available)
+
+    // stream slots + key/value store
+    int n_slots = 0, max_ctx = 0;
+    KV kv{};
+    int32_t *slot_len = nullptr, *slot_tok = nullptr;
+    bool primed = false;
+
+    // row buffers
+    int max_rows = 0;
+    int32_t *row_slot = nullptr, *row_pos = nullptr, *row_tok = nullptr;
+    int64_t *R = nullptr, *QKV = nullptr, *ATT = nullptr, *HID = nullptr;
+    int32_t *x16 = nullptr, *ex = nullptr, *q16 = nullptr, *qexp = nullptr;
+    int64_t* LS = nullptr;
+    TcRows tcr{};
+    int32_t *head_rows = nullptr, *race_out = nullptr;
+    int64_t* logits = nullptr;   // [n_slots][vocab]
+    uint32_t* d_err = nullptr;
+    std::vector<void*> allocs;
+
+    // launch accounting / per-class event timing (b2_profile)
+    struct Prof {
+        int timing = 0;
+        int64_t launches = 0;
+        int64_t cnt[B2_PROF_N] = {0};
+        std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev[B2_PROF_N];
+        std::vector<cudaEvent_t> pool;
+    } prof;
+};
+
+namespace {
+
+int fail(b2_handle* h, int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    if (h) h->err = buf;
+    return code;
+}
+
+#define CK(call)                                                                                    \
+    do {                                                                                            \
+        cudaError_t e_ = (call);                                                                    \
+        if (e_ != cudaSuccess) return fail(h, B2_ERR_CUDA, "%s: %s", #call, cudaGetErrorString(e_)); \
+    } while (0)
+
+template <class T>
+int dalloc(b2_handle* h, T** p, size_t n) {
+    void* q = nullptr;
+    if (n == 0) n = 1;
+    cudaError_t e = cudaMalloc(&q, n * sizeof(T));
+    if (e != cudaSuccess) return fail(h, B2_ERR_NOMEM, "cudaMalloc(%zu bytes): %s", n * sizeof(T), cudaGetErrorString(e));
+    h->allocs.push_back(q);
+    *p = (T*)q;
+    return B2_OK;
+}
+
+void dfree(b2_handle* h, void* p) {
+    if (!p) return;
+    for (size_t i = 0; i < h->allocs.size(); i++)
+        if (h->allocs[i] == p) { h->allocs.erase(h->allocs.begin() + i); break; }
+    cudaFree(p);
+}
+
+int bank_index(const b2_handle* h, const char* name) {
+    if (!strcmp(name, "head")) return 4 * h->cfg.n_layer;
+    static const char* kinds[4] = {"qkv", "proj", "fc", "mproj"};
+    for (int k = 0; k < 4; k++) {
+        size_t n = strlen(kinds[k]);
+        if (!strncmp(name, kinds[k], n) && name[n] == '.') {
+            int l = atoi(name + n + 1);
+            if (l >= 0 && l < h->cfg.n_layer) return 4 * l + k;
+        }
+    }
+    return -1;
+}
+
+int upload_table32(b2_handle* h, int32_t** dst, const int64_t* src, int64_t n, const char* name) {
+    std::vector<int32_t> t((size_t)n);
+    for (int64_t i = 0; i < n; i++) {
+        if (src[i] < INT32_MIN || src[i] > INT32_MAX) return fail(h, B2_ERR_VALUE, "table %s[%lld] does not fit int32", name, (long long)i);
+        t[i] = (int32_t)src[i];
+    }
+    if (*dst) dfree(h, *dst);
+    int rc = dalloc(h, dst, (size_t)n);
+    if (rc) return rc;
+    CK(cudaMemcpy(*dst, t.data(), sizeof(int32_t) * n, cudaMemcpyHostToDevice));
+    return B2_OK;
+}
+
+int check_launch(b2_handle* h, const char* what) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "launch %s: %s", what, cudaGetErrorString(e));
+    return B2_OK;
+}
+
+// every kernel launch goes through these: a launch count per class and, when timing, a pair of events around it
+cudaEvent_t prof_event(b2_handle* h) {
+    if (!h->prof.pool.empty()) { cudaEvent_t e = h->prof.pool.back(); h->prof.pool.pop_back(); return e; }
+    cudaEvent_t e = nullptr;
+    cudaEventCreate(&e);
+    return e;
+}
+void prof_begin(b2_handle* h, int cls, cudaStream_t st, int n = 1) {
+    h->prof.launches += n;
+    h->prof.cnt[cls] += n;
+    if (h->prof.timing) {
+        cudaEvent_t a = prof_event(h), b = prof_event(h);
+        cudaEventRecord(a, st);
+        h->prof.ev[cls].push_back({a, b});
+    }
+}
+void prof_end(b2_handle* h, int cls, cudaStream_t st) {
+    if (h->prof.timing) cudaEventRecord(h->prof.ev[cls].back().second, st);
+}
+
+// ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
+int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st) {
+    const DevBank& bk = h->banks[bi];
+    if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
+        prof_begin(h, B2_PROF_BANK, st);
+        int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st);
+        prof_end(h, B2_PROF_BANK, st);
+        if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
+        return check_launch(h, "tc_bank");
+    }
+    BankArgs a{h->x16, h->ex, h->LS, bk.w, bk.e, bk.b, bk.nin, bk.nout, rows, out, ldo, out_map, h->EXP2, h->PHI};
+    constexpr int RT = 8;
+    dim3 grid((bk.nout + 255) / 256, (rows + RT - 1) / RT);
+    prof_begin(h, B2_PROF_BANK, st);
+    switch (epi) {
+        case EPI_GAUGED: k_bank_simt<EPI_GAUGED, RT><<<grid, 256, 0, st>>>(a); break;
+        case EPI_GAUGED_EDGE: k_bank_simt<EPI_GAUGED_EDGE, RT><<<grid, 256, 0, st>>>(a); break;
+        case EPI_PLAIN_ADD: k_bank_simt<EPI_PLAIN_ADD, RT><<<grid, 256, 0, st>>>(a); break;
+        default: k_bank_simt<EPI_PLAIN_OUT, RT><<<grid, 256, 0, st>>>(a); break;
+    }
+    prof_end(h, B2_PROF_BANK, st);
+    return check_launch(h, "bank_simt");
+}
+
+int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st) {
+    prof_begin(h, B2_PROF_QUANT, st);
+    if (n > 1024)
+        k_quant<512><<<rows, 512, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40);
+    else
+        k_quant<256><<<rows, 256, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40);
+    prof_end(h, B2_PROF_QUANT, st);
+    int rc = check_launch(h, "quant");
+    if (rc) return rc;
+    if (h->use_tc && rows >= h->tc_min_rows) {
+        prof_begin(h, B2_PROF_QUANT, st);
+        tc_planes(h->tcr, h->x16, n, rows, st);
+        prof_end(h, B2_PROF_QUANT, st);
+        return check_launch(h, "tc_planes");
+    }
+    return B2_OK;
+}
+
+// ---- all layers + head for the rows in the row table --------------------------------------------------------------
+// head rows: rows [0, nhead) of `hrows` (row indices) are scored; their logits go to out rows hmap (slot ids).
+int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
+             int32_t* words_by_slot, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
+    int rc;
+    prof_begin(h, B2_PROF_OTHER, st);
+    k_embed<<<rows, 256, 0, st>>>(h->row_tok, h->row_pos, rows, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, h->d_err);
+    prof_end(h, B2_PROF_OTHER, st);
+    if ((rc = check_launch(h, "embed"))) return rc;
+    for (int l = 0; l < L; l++) {
+        if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 0, EPI_GAUGED, rows, h->QKV, 3 * d, nullptr, st))) return rc;
+        prof_begin(h, B2_PROF_HEADS, st);
+        k_heads<<<dim3(rows, 3 * H), 32, 0, st>>>(h->QKV, rows, h->row_slot, h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err);
+        prof_end(h, B2_PROF_HEADS, st);
+        if ((rc = check_launch(h, "heads"))) return rc;
+        AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT};
+        prof_begin(h, B2_PROF_ATTEND, st);
+        k_attend<4><<<dim3(rows, H), 128, sizeof(int64_t) * h->max_ctx, st>>>(aa);
+        prof_end(h, B2_PROF_ATTEND, st);
+        if ((rc = check_launch(h, "attend"))) return rc;
+        if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
+        if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 2, EPI_GAUGED_EDGE, rows, h->HID, F, nullptr, st))) return rc;
+        if ((rc = run_quant(h, h->HID, F, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
+    }
+    if (nhead <= 0) return B2_OK;
+    if ((rc = run_quant(h, h->R, d, hrows, nhead, 1, st))) return rc;
+    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, nhead, logits, c.vocab, hmap, st))) return rc;
+    prof_begin(h, B2_PROF_RACE, st);
+    k_race<<<nhead, 1024, 0, st>>>(logits, c.vocab, hmap, c.vocab, words_by_slot);
+    prof_end(h, B2_PROF_RACE, st);
+    return check_launch(h, "race");
+}
+
+int ensure_ready(b2_handle* h) {
+    if (!h) return B2_ERR_ARG;
+    if (!h->finalized) return fail(h, B2_ERR_STATE, "b2_finalize has not been called");
+    if (!h->n_slots) return fail(h, B2_ERR_STATE, "b2_alloc_streams has not been called");
+    CK(cudaSetDevice(h->device));
+    return B2_OK;
+}
+
+int read_device_error(b2_handle* h) {
+    uint32_t e = 0;
+    CK(cudaMemcpy(&e, h->d_err, sizeof e, cudaMemcpyDeviceToHost));
+    if (!e) return B2_OK;
+    CK(cudaMemset(h->d_err, 0, sizeof(uint32_t)));
+    if (e & DERR_POS) return fail(h, B2_ERR_CTX, "a position passed the context (device check, bits 0x%x)", e);
+    if (e & DERR_VOVF) return fail(h, B2_ERR_VALUE, "a value-store entry did not fit int32 (device check, bits 0x%x)", e);
+    return fail(h, B2_ERR_DEVICE, "a token id was out of range (device check, bits 0x%x)", e);
+}
+
+}  // namespace
+
+// =====================================================================================================================
+// C ABI
+// =====================================================================================================================
+extern "C" {
+
+int b2_abi_version(void) { return B2_ABI_VERSION; }
+
+const char* b2_last_error(const b2_handle* h) { return h ? h->err.c_str() : "null handle"; }
+
+int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
+    if (!cfg || !out) return B2_ERR_ARG;
+    *out = nullptr;
+    if (cfg->kind != B2_GPT2) return B2_ERR_ARG;
+    if (cfg->n_layer < 1 || cfg->n_layer > 64 || cfg->n_head < 1 || cfg->d_model != cfg->n_head * 64 ||
+        cfg->d_model % 256 || cfg->d_ff % 256 || cfg->vocab < 1 || cfg->n_ctx < 1)
+        return B2_ERR_ARG;
+    if (flags & (B2_GAUGE_FLOAT | B2_EDGE_FLOAT | B2_ARRIVAL_FLOAT)) return B2_ERR_ARG;   // integer stages only
+    b2_handle* h = new b2_handle();
+    h->cfg = *cfg;
+    h->device = device;
+    h->flags = flags;
+    h->banks.resize(4 * cfg->n_layer + 1);
+    if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
+    if (dalloc(h, &h->d_err, 1)) { delete h; return B2_ERR_NOMEM; }
+    cudaMemset(h->d_err, 0, sizeof(uint32_t));
+    *out = h;
+    return B2_OK;
+}
+
+int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t* e, const int64_t* b, int32_t nin, int32_t nout) {
+    if (!h || !name || !w || !e || !b) return fail(h, B2_ERR_ARG, "b2_set_bank: null argument");
+    CK(cudaSetDevice(h->device));
+    int bi = bank_index(h, name);
+    if (bi < 0) return fail(h, B2_ERR_ARG, "b2_set_bank: unknown bank '%s'", name);
+    const b2_config& c = h->cfg;
+    int k = bi == 4 * c.n_layer ? 4 : bi % 4;
+    int want_in[5] = {c.d_model, c.d_model, c.d_model, c.d_ff, c.d_model};
+    int want_out[5] = {3 * c.d_model, c.d_model, c.d_ff, c.d_model, c.vocab};
+    if (nin != want_in[k] || nout != want_out[k])
+        return fail(h, B2_ERR_ARG, "b2_set_bank %s: shape [%d][%d], want [%d][%d]", name, nin, nout, want_in[k], want_out[k]);
+    DevBank& bk = h->banks[bi];
+    if (bk.w) { dfree(h, bk.w); dfree(h, bk.e); dfree(h, bk.b); bk.w = nullptr; }
+    tc_bank_free(bk.tc);
+    bk.nin = nin;
+    bk.nout = nout;
+    int rc;
+    if ((rc = dalloc(h, &bk.w, (size_t)nin * nout))) return rc;
+    if ((rc = dalloc(h, &bk.e, (size_t)nout))) return rc;
+    if ((rc = dalloc(h, &bk.b, (size_t)nout))) return rc;
+    std::vector<int32_t> e32(nout);
+    for (int j = 0; j < nout; j++) {
+        if (e[j] < -200 || e[j] > 200) return fail(h, B2_ERR_VALUE, "bank %s: exponent %lld out of range", name, (long long)e[j]);
+        e32[j] = (int32_t)e[j];
+    }
+    CK(cudaMemcpy(bk.w, w, sizeof(int16_t) * (size_t)nin * nout, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(bk.e, e32.data(), sizeof(int32_t) * nout, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(bk.b, b, sizeof(int64_t) * nout, cudaMemcpyHostToDevice));
+    h->finalized = false;
+    return B2_OK;
+}
+
+int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n) {
+    if (!h || !name || !data || n <= 0) return fail(h, B2_ERR_ARG, "b2_set_array: bad argument");
+    CK(cudaSetDevice(h->device));
+    const b2_config& c = h->cfg;
+    int rc;
+    if (!strcmp(name, "wte") || !strcmp(name, "wpe")) {
+        int64_t want = (int64_t)(name[1] == 't' ? c.vocab : c.n_ctx) * c.d_model;
+        if (n != want) return fail(h, B2_ERR_ARG, "%s: %lld values, want %lld", name, (long long)n, (long long)want);
+        int64_t** dst = name[1] == 't' ? &h->wte : &h->wpe;
+        if (*dst) dfree(h, *dst);
+        if ((rc = dalloc(h, dst, (size_t)n))) return rc;
+        CK(cudaMemcpy(*dst, data, sizeof(int64_t) * n, cudaMemcpyHostToDevice));
+    } else if (!strcmp(name, "phi") || !strcmp(name, "log2") || !strcmp(name, "exp2")) {
+        if (n != 65536) return fail(h, B2_ERR_ARG, "%s: %lld entries, want 65536", name, (long long)n);
+        int32_t** dst = name[0] == 'p' ? &h->PHI : (name[0] == 'l' ? &h->LOG2 : &h->EXP2);
+        if ((rc = upload_table32(h, dst, data, n, name))) return rc;
+    } else if (!strcmp(name, "arrival")) {
+        if (n > (1 << 24)) return fail(h, B2_ERR_ARG, "arrival: too long");
+        if ((rc = upload_table32(h, &h->ARR, data, n, name))) return rc;
+        h->alen = (int)n;
+    } else {
+        return fail(h, B2_ERR_ARG, "b2_set_array: unknown array '%s'", name);
+    }
+    h->finalized = false;
+    return B2_OK;
+}
+
+int b2_set_scalar(b2_handle* h, const char* name, int64_t v) {
+    if (!h || !name) return B2_ERR_ARG;
+    if (!strcmp(name, "log2_768")) { h->log768 = v; h->have_scalar[0] = true; }
+    else if (!strcmp(name, "eps40")) { h->eps40 = v; h->have_scalar[1] = true; }
+    else return fail(h, B2_ERR_ARG, "b2_set_scalar: unknown scalar '%s'", name);
+    return B2_OK;
+}
+
+int b2_finalize(b2_handle* h) {
+    if (!h) return B2_ERR_ARG;
+    CK(cudaSetDevice(h->device));
+    for (size_t i = 0; i < h->banks.size(); i++)
+        if (!h->banks[i].w) return fail(h, B2_ERR_STATE, "bank %zu not set", i);
+    if (!h->wte || !h->wpe || !h->PHI || !h->ARR || !h->LOG2 || !h->EXP2 || !h->have_scalar[0] || !h->have_scalar[1])
+        return fail(h, B2_ERR_STATE, "a table or scalar is missing");
+    // tensor-core layouts of every bank
+    int tc_ok = 1;
+    for (auto& bk : h->banks) {
+        int rc = tc_bank_build(bk.tc, bk.w, bk.nin, bk.nout);
+        if (rc) { tc_ok = 0; break; }
+    }
+    CK(cudaDeviceSynchronize());
+    h->tc_min_rows = tc_ok ? tc_min_rows_default() : (1 << 30);
+    const char* env = getenv("B2_TC_MIN_ROWS");
+    if (env && tc_ok) h->tc_min_rows = atoi(env);
+    h->finalized = true;
+    return B2_OK;
+}
+
+int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
+    if (!h) return B2_ERR_ARG;
+    if (!h->finalized) return fail(h, B2_ERR_STATE, "b2_finalize has not been called");
+    if (n_streams < 1 || max_ctx < 1 || max_ctx > h->cfg.n_ctx)
+        return fail(h, B2_ERR_ARG, "b2_alloc_streams: n_streams %d, max_ctx %d (model n_ctx %d)", n_streams, max_ctx, h->cfg.n_ctx);
+    CK(cudaSetDevice(h->device));
+    const b2_config& c = h->cfg;
+    // drop old stream/row buffers
+    void* old[] = {h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+                   h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
+                   h->race_out, h->logits};
+    for (void* p : old) dfree(h, p);
+    tc_rows_free(h->tcr);
+    h->n_slots = 0;
+    const int L = c.n_layer, H = c.n_head, d = c.d_model, F = c.d_ff;
+    size_t nkv = (size_t)n_streams * L * H * max_ctx;
+    int rc;
+    h->kv.L = L; h->kv.H = H; h->kv.ctx = max_ctx;
+    if ((rc = dalloc(h, &h->kv.k, nkv * 64))) return rc;
+    if ((rc = dalloc(h, &h->kv.kmask, nkv))) return rc;
+    if ((rc = dalloc(h, &h->kv.kexp, nkv))) return rc;
+    if ((rc = dalloc(h, &h->kv.v, nkv * 64))) return rc;
+    if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
+    if ((rc = dalloc(h, &h->slot_tok, n_streams))) return rc;
+    CK(cudaMemset(h->slot_len, 0, sizeof(int32_t) * n_streams));
+    CK(cudaMemset(h->slot_tok, 0, sizeof(int32_t) * n_streams));
+    int mr = n_streams > 2048 ? n_streams : 2048;   // rows per pass (prompt passes are chunked to this)
+    h->max_rows = mr;
+    if ((rc = dalloc(h, &h->row_slot, mr)) || (rc = dalloc(h, &h->row_pos, mr)) || (rc = dalloc(h, &h->row_tok, mr))) return rc;
+    if ((rc = dalloc(h, &h->R, (size_t)mr * d)) || (rc = dalloc(h, &h->QKV, (size_t)mr * 3 * d)) ||
+        (rc = dalloc(h, &h->ATT, (size_t)mr * d)) || (rc = dalloc(h, &h->HID, (size_t)mr * F)))
+        return rc;
+    if ((rc = dalloc(h, &h->x16, (size_t)mr * (F > d ? F : d))) || (rc = dalloc(h, &h->ex, mr)) ||
+        (rc = dalloc(h, &h->LS, mr)) || (rc = dalloc(h, &h->q16, (size_t)mr * d)) || (rc = dalloc(h, &h->qexp, (size_t)mr * H)))
+        return rc;
+    if ((rc = dalloc(h, &h->head_rows, 2 * (size_t)mr)) || (rc = dalloc(h, &h->race_out, n_streams)) ||
+        (rc = dalloc(h, &h->logits, (size_t)n_streams * c.vocab)))
+        return rc;
+    if (h->tc_min_rows < (1 << 30)) {
+        rc = tc_rows_alloc(h->tcr, mr, F > d ? F : d);
+        if (rc) return fail(h, B2_ERR_NOMEM, "tensor-core row buffers: %s", cudaGetErrorString((cudaError_t)rc));
+    }
+    h->n_slots = n_streams;
+    h->max_ctx = max_ctx;
+    h->primed = false;
+    return B2_OK;
+}
+
+int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_streams, int32_t* next_tok,
+               int64_t* logits, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    if (!ids || !lens || !next_tok || n_streams < 1 || n_streams > h->n_slots)
+        return fail(h, B2_ERR_ARG, "b2_prefill: bad argument (n_streams %d of %d slots)", n_streams, h->n_slots);
+    cudaStream_t st = (cudaStream_t)stream;
+    std::vector<int32_t> hl(n_streams);
+    CK(cudaMemcpyAsync(hl.data(), lens, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    size_t total = 0;
+    for (int s = 0; s < n_streams; s++) {
+        if (hl[s] < 1 || hl[s] > h->max_ctx) return fail(h, B2_ERR_CTX, "prompt %d has %d ids (context %d)", s, hl[s], h->max_ctx);
+        total += hl[s];
+    }
+    // row table for all prompt rows (stream-major), then chunks of max_rows
+    std::vector<int32_t> rs(total), rp(total);
+    std::vector<int32_t> last_row(n_streams);
+    size_t o = 0;
+    for (int s = 0; s < n_streams; s++) {
+        for (int p = 0; p < hl[s]; p++) { rs[o] = s; rp[o] = p; o++; }
+        last_row[s] = (int32_t)(o - 1);
+    }
+    int32_t *d_rs = nullptr, *d_rp = nullptr;
+    if ((rc = dalloc(h, &d_rs, total)) || (rc = dalloc(h, &d_rp, total))) return rc;
+    int64_t* lg = logits ? logits : h->logits;
+    rc = B2_OK;
+    do {
+        if (cudaMemcpyAsync(d_rs, rs.data(), sizeof(int32_t) * total, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(d_rp, rp.data(), sizeof(int32_t) * total, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = fail(h, B2_ERR_CUDA, "prefill row table copy");
+            break;
+        }
+        for (size_t r0 = 0; r0 < total && !rc; r0 += h->max_rows) {
+            int rows = (int)(total - r0 < (size_t)h->max_rows ? total - r0 : (size_t)h->max_rows);
+            prof_begin(h, B2_PROF_OTHER, st);
+            k_prefill_rows<<<(rows + 255) / 256, 256, 0, st>>>((int)r0, rows, d_rs, d_rp, ids, h->row_slot, h->row_pos, h->row_tok);
+            prof_end(h, B2_PROF_OTHER, st);
+            // the scored rows in this chunk: each stream's last prompt position
+            std::vector<int32_t> hr, hm;
+            for (int s = 0; s < n_streams; s++)
+                if ((size_t)last_row[s] >= r0 && (size_t)last_row[s] < r0 + rows) { hr.push_back(last_row[s] - (int)r0); hm.push_back(s); }
+            int nh = (int)hr.size();
+            if (nh) {
+                std::vector<int32_t> both(hr);
+                both.insert(both.end(), hm.begin(), hm.end());
+                if (cudaMemcpyAsync(h->head_rows, both.data(), sizeof(int32_t) * both.size(), cudaMemcpyHostToDevice, st) != cudaSuccess) {
+                    rc = fail(h, B2_ERR_CUDA, "prefill head rows copy");
+                    break;
+                }
+                // head rows must stay valid until the chunk's kernels have read them
+            }
+            rc = run_rows(h, rows, h->head_rows, h->head_rows + nh, nh, lg, h->race_out, st);
+            if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = fail(h, B2_ERR_CUDA, "prefill chunk sync");
+        }
+    } while (0);
+    cudaStreamSynchronize(st);
+    dfree(h, d_rs);
+    dfree(h, d_rp);
+    if (rc) return rc;
+    // stream state: length = prompt length, last word = the race's word
+    CK(cudaMemcpyAsync(h->slot_len, lens, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToDevice, st));
+    CK(cudaMemcpyAsync(h->slot_tok, h->race_out, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToDevice, st));
+    CK(cudaMemcpyAsync(next_tok, h->race_out, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToDevice, st));
+    CK(cudaStreamSynchronize(st));
+    h->primed = true;
+    return read_device_error(h);
+}
+
+namespace {
+int step_async(b2_handle* h, const int32_t* tok_in, int n, int32_t* tok_out, int ld_out, int col, int64_t* logits, cudaStream_t st) {
+    prof_begin(h, B2_PROF_OTHER, st);
+    k_decode_rows<<<(n + 127) / 128, 128, 0, st>>>(n, tok_in, h->slot_len, h->slot_tok, h->row_slot, h->row_pos, h->row_tok);
+    prof_end(h, B2_PROF_OTHER, st);
+    int rc = check_launch(h, "decode_rows");
+    if (rc) return rc;
+    // every row is scored; row r = slot r
+    rc = run_rows(h, n, nullptr, nullptr, n, logits ? logits : h->logits, h->race_out, st);
+    if (rc) return rc;
+    prof_begin(h, B2_PROF_OTHER, st);
+    k_decode_commit<<<(n + 127) / 128, 128, 0, st>>>(n, h->race_out, h->slot_len, h->slot_tok, tok_out, ld_out, col);
+    prof_end(h, B2_PROF_OTHER, st);
+    return check_launch(h, "decode_commit");
+}
+}  // namespace
+
+int b2_step(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok_out, int64_t* logits, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    if (n_streams < 1 || n_streams > h->n_slots || !tok_out) return fail(h, B2_ERR_ARG, "b2_step: bad argument");
+    if (!tok_in && !h->primed) return fail(h, B2_ERR_STATE, "b2_step without tok_in before any b2_prefill");
+    return step_async(h, tok_in, n_streams, tok_out, 1, 0, logits, (cudaStream_t)stream);
+}
+
+int b2_generate(b2_handle* h, int32_t n_streams, int32_t n_steps, int32_t* tokens_out, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    if (n_streams < 1 || n_streams > h->n_slots || n_steps < 0 || !tokens_out) return fail(h, B2_ERR_ARG, "b2_generate: bad argument");
+    if (!h->primed) return fail(h, B2_ERR_STATE, "b2_generate before b2_prefill");
+    for (int t = 0; t < n_steps; t++)
+        if ((rc = step_async(h, nullptr, n_streams, tokens_out, n_steps, t, nullptr, (cudaStream_t)stream))) return rc;
+    return B2_OK;
+}
+
+int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok_out) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    if (!tok_in || !tok_out || n_streams < 1 || n_streams > h->n_slots) return fail(h, B2_ERR_ARG, "b2_step_host: bad argument");
+    cudaStream_t st = 0;
+    // the words go in as each stream's last word; the race's answer comes back from race_out
+    CK(cudaMemcpyAsync(h->slot_tok, tok_in, sizeof(int32_t) * n_streams, cudaMemcpyHostToDevice, st));
+    if ((rc = step_async(h, nullptr, n_streams, nullptr, 1, 0, nullptr, st))) return rc;
+    CK(cudaMemcpyAsync(tok_out, h->race_out, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    return read_device_error(h);
+}
+
+int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    int bi = bank_index(h, name);
+    if (bi < 0 || !X || !out || rows < 1 || rows > h->max_rows || mode < 0 || mode > 2)
+        return fail(h, B2_ERR_ARG, "b2_bank: bad argument");
+    cudaStream_t st = (cudaStream_t)stream;
+    const DevBank& bk = h->banks[bi];
+    if ((rc = run_quant(h, X, bk.nin, nullptr, rows, mode < 2, st))) return rc;
+    int epi = mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_OUT);
+    return run_bank(h, bi, epi, rows, out, bk.nout, nullptr, st);
+}
+
+int b2_rewind(b2_handle* h, int32_t n_streams, const int32_t* lens, const int32_t* last_tok, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    if (n_streams < 1 || n_streams > h->n_slots || !lens || !last_tok) return fail(h, B2_ERR_ARG, "b2_rewind: bad argument");
+    cudaStream_t st = (cudaStream_t)stream;
+    prof_begin(h, B2_PROF_OTHER, st);
+    k_rewind<<<(n_streams + 127) / 128, 128, 0, st>>>(n_streams, lens, last_tok, h->cfg.vocab, h->slot_len, h->slot_tok, h->d_err);
+    prof_end(h, B2_PROF_OTHER, st);
+    return check_launch(h, "rewind");
+}
+
+int b2_profile(b2_handle* h, int timing) {
+    if (!h) return B2_ERR_ARG;
+    CK(cudaSetDevice(h->device));
+    CK(cudaDeviceSynchronize());
+    for (int c = 0; c < B2_PROF_N; c++) {
+        for (auto& p : h->prof.ev[c]) { h->prof.pool.push_back(p.first); h->prof.pool.push_back(p.second); }
+        h->prof.ev[c].clear();
+        h->prof.cnt[c] = 0;
+    }
+    h->prof.launches = 0;
+    h->prof.timing = timing;
+    return B2_OK;
+}
+
+int b2_profile_read(b2_handle* h, int64_t* launches, int64_t* counts, double* ms) {
+    if (!h) return B2_ERR_ARG;
+    CK(cudaSetDevice(h->device));
+    CK(cudaDeviceSynchronize());
+    if (launches) *launches = h->prof.launches;
+    for (int c = 0; c < B2_PROF_N; c++) {
+        if (counts) counts[c] = h->prof.cnt[c];
+        double t = 0;
+        for (auto& p : h->prof.ev[c]) {
+            float f = 0;
+            if (cudaEventElapsedTime(&f, p.first, p.second) == cudaSuccess) t += f;
+        }
+        if (ms) ms[c] = t;
+    }
+    return B2_OK;
+}
+
+int b2_sync(b2_handle* h) {
+    if (!h) return B2_ERR_ARG;
+    CK(cudaSetDevice(h->device));
+    CK(cudaDeviceSynchronize());
+    return read_device_error(h);
+}
+
+void b2_destroy(b2_handle* h) {
+    if (!h) return;
+    cudaSetDevice(h->device);
+    cudaDeviceSynchronize();
+    for (auto& bk : h->banks) tc_bank_free(bk.tc);
+    tc_rows_free(h->tcr);
+    for (int c = 0; c < B2_PROF_N; c++)
+        for (auto& p : h->prof.ev[c]) { cudaEventDestroy(p.first); cudaEventDestroy(p.second); }
+    for (auto e : h->prof.pool) cudaEventDestroy(e);
+    for (void* p : h->allocs) cudaFree(p);
+    delete h;
+}
+
+}  // extern "C"

@@ -1,0 +1,404 @@
+// b2_kernels.cuh -- the machine's kernels other than the tensor-core bank product: embedding, to16 + gauge,
+// head split into q16/k16/v with the key/value store append, the arrival (attention), the race, the row bookkeeping,
+// and the CUDA-core bank product used for small row counts and as the on-device cross-check of the tensor path.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "b2_arith.cuh"
+
+namespace b2 {
+
+// sticky device error bits (read back by b2_sync)
+enum : uint32_t {
+    DERR_TOKEN = 1u,     // a token id outside [0, vocab)
+    DERR_POS = 2u,       // a position at or past the store's context (or the position table)
+    DERR_VOVF = 4u,      // a V value outside int32 (the value store holds int32)
+};
+
+B2_DEV void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
+
+// position of (slot, layer, head, pos) in the key/value store: [slot][layer][head][pos]
+B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int ctx) {
+    return (((size_t)slot * L + layer) * H + head) * (size_t)ctx + pos;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// embedding: R = wte[tok] + wpe[pos] (base2.py:103; the Metal engine's nextin, base2_stream.swift:143-146)
+// ---------------------------------------------------------------------------------------------------------------------
+__global__ void k_embed(const int32_t* __restrict__ row_tok, const int32_t* __restrict__ row_pos, int rows,
+                        const int64_t* __restrict__ wte, const int64_t* __restrict__ wpe, int d, int V, int nctx,
+                        int64_t* __restrict__ R, uint32_t* err) {
+    int r = blockIdx.x;
+    if (r >= rows) return;
+    int tok = row_tok[r], pos = row_pos[r];
+    if (tok < 0 || tok >= V) { if (threadIdx.x == 0) set_err(err, DERR_TOKEN); tok = 0; }
+    if (pos < 0 || pos >= nctx) { if (threadIdx.x == 0) set_err(err, DERR_POS); pos = 0; }
+    const int64_t* a = wte + (size_t)tok * d;
+    const int64_t* b = wpe + (size_t)pos * d;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) R[(size_t)r * d + i] = wadd(__ldg(a + i), __ldg(b + i));
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// to16 (base2.py:24-27) + the gauge (base2.py:55-60): one CTA per row. x16 fits int32 (|x16| <= 32768).
+// src_rows (optional) gathers rows (the head reads only the rows it scores).
+// ---------------------------------------------------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int n, const int32_t* __restrict__ src_rows,
+                                              int rows, int32_t* __restrict__ x16, int32_t* __restrict__ ex,
+                                              int64_t* __restrict__ LS, int gauge, const int32_t* __restrict__ LOG2,
+                                              int64_t log768, int64_t eps40) {
+    __shared__ uint64_t s_or[NT / 32];
+    __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
+    int r = blockIdx.x;
+    if (r >= rows) return;
+    int sr = src_rows ? src_rows[r] : r;
+    const int64_t* x = X + (size_t)sr * n;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint64_t o = 0;
+    for (int i = threadIdx.x; i < n; i += NT) o |= mag(x[i]);
+    o = warp_or64(o);
+    if (lane == 0) s_or[wid] = o;
+    __syncthreads();
+    uint64_t all = 0;
+#pragma unroll
+    for (int k = 0; k < NT / 32; k++) all |= s_or[k];
+    int sh = to16_shift(all);
+    int64_t q1 = 0, q2 = 0;
+    for (int i = threadIdx.x; i < n; i += NT) {
+        int64_t v = rshift(x[i], sh);
+        x16[(size_t)r * n + i] = (int32_t)v;
+        q1 += v;
+        q2 += v * v;
+    }
+    if (!gauge) {
+        if (threadIdx.x == 0) ex[r] = -16 + sh;
+        return;
+    }
+    q1 = warp_sum64(q1);
+    q2 = warp_sum64(q2);
+    if (lane == 0) { s_1[wid] = q1; s_2[wid] = q2; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t S1 = 0, S2 = 0;
+        for (int k = 0; k < NT / 32; k++) { S1 = wadd(S1, s_1[k]); S2 = wadd(S2, s_2[k]); }
+        ex[r] = -16 + sh;
+        LS[r] = gauge_LS(S1, S2, -16 + sh, LOG2, log768, eps40);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// bank epilogues (base2.py:62-76, 78-83)
+// ---------------------------------------------------------------------------------------------------------------------
+enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3 };
+
+struct BankArgs {
+    const int32_t* x16;     // [rows][nin]
+    const int32_t* ex;      // [rows]
+    const int64_t* LS;      // [rows] (gauged)
+    const int16_t* w;       // [nin][nout]
+    const int32_t* e;       // [nout]
+    const int64_t* b;       // [nout]
+    int nin, nout, rows;
+    int64_t* out;           // [out row][ldo]
+    int ldo;
+    const int32_t* out_map; // optional row -> out row
+    const int32_t* EXP2;
+    const int32_t* PHI;
+};
+
+template <int EPI>
+B2_DEV void bank_epilogue(const BankArgs& a, int r, int j, int64_t pile) {
+    int orow = a.out_map ? a.out_map[r] : r;
+    int64_t* o = a.out + (size_t)orow * a.ldo + j;
+    int64_t es = wadd(wadd((int64_t)a.e[j], (int64_t)a.ex[r]), 16);
+    if (EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) {
+        int64_t F = wsub(wmul(es, 65536), a.LS[r]);
+        int64_t v = wadd(power(pile, F, a.EXP2), a.b[j]);
+        if (EPI == EPI_GAUGED_EDGE) v = edge(v, a.PHI);
+        *o = v;
+    } else {
+        int64_t v = wadd(rshift(pile, -es), a.b[j]);
+        *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
+    }
+}
+
+// CUDA-core bank product: one thread per output column, RT rows per CTA, the pile exact in int64.
+template <int EPI, int RT>
+__global__ void __launch_bounds__(256) k_bank_simt(BankArgs a) {
+    __shared__ int32_t xs[RT][64];
+    const int j = blockIdx.x * 256 + threadIdx.x;
+    const int r0 = blockIdx.y * RT;
+    int64_t acc[RT];
+#pragma unroll
+    for (int rr = 0; rr < RT; rr++) acc[rr] = 0;
+    for (int k0 = 0; k0 < a.nin; k0 += 64) {
+        for (int t = threadIdx.x; t < RT * 64; t += 256) {
+            int rr = t >> 6, kk = t & 63, r = r0 + rr;
+            xs[rr][kk] = (r < a.rows && k0 + kk < a.nin) ? a.x16[(size_t)r * a.nin + k0 + kk] : 0;
+        }
+        __syncthreads();
+        if (j < a.nout) {
+            const int kmax = a.nin - k0 < 64 ? a.nin - k0 : 64;
+            const int16_t* wp = a.w + (size_t)k0 * a.nout + j;
+            for (int kk = 0; kk < kmax; kk++) {
+                int w = __ldg(wp + (size_t)kk * a.nout);
+#pragma unroll
+                for (int rr = 0; rr < RT; rr++) acc[rr] += (long long)w * (long long)xs[rr][kk];
+            }
+        }
+        __syncthreads();
+    }
+    if (j >= a.nout) return;
+#pragma unroll
+    for (int rr = 0; rr < RT; rr++)
+        if (r0 + rr < a.rows) bank_epilogue<EPI>(a, r0 + rr, j, acc[rr]);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// q/k/v split (the Metal engine's heads16, base2_stream.swift:112-119; base2.py:93 to16 of q and k per head):
+// one warp per (row, part of 3H). q16 -> per-row buffer; k16 + exponent -> key store (int16, with a bit mask of
+// the entries equal to +32768, which int16 cannot hold); v -> value store as int32 (checked).
+// ---------------------------------------------------------------------------------------------------------------------
+struct KV {
+    int16_t* k;        // [slot][L][H][ctx][64]
+    uint64_t* kmask;   // [slot][L][H][ctx]  bit t: k16[t] == +32768
+    int32_t* kexp;     // [slot][L][H][ctx]
+    int32_t* v;        // [slot][L][H][ctx][64]
+    int L, H, ctx;
+};
+
+__global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t* __restrict__ row_slot,
+                        const int32_t* __restrict__ row_pos, int layer, KV kv, int32_t* __restrict__ q16,
+                        int32_t* __restrict__ qexp, uint32_t* err) {
+    const int r = blockIdx.x, part = blockIdx.y, lane = threadIdx.x;
+    const int H = kv.H, d = H * 64;
+    if (r >= rows) return;
+    const int64_t* x = QKV + (size_t)r * 3 * d + (size_t)part * 64;
+    int64_t v0 = x[lane], v1 = x[lane + 32];
+    const int slot = row_slot[r], pos = row_pos[r];
+    if (part < 2 * H) {
+        int sh = to16_shift(warp_or64(mag(v0) | mag(v1)));
+        int64_t a0 = rshift(v0, sh), a1 = rshift(v1, sh);
+        if (part < H) {
+            q16[(size_t)r * d + part * 64 + lane] = (int32_t)a0;
+            q16[(size_t)r * d + part * 64 + lane + 32] = (int32_t)a1;
+            if (lane == 0) qexp[r * H + part] = -16 + sh;
+        } else {
+            if (pos < 0 || pos >= kv.ctx) { if (lane == 0) set_err(err, DERR_POS); return; }
+            size_t idx = kv_index(slot, layer, part - H, pos, kv.L, H, kv.ctx);
+            kv.k[idx * 64 + lane] = (int16_t)(uint16_t)(uint32_t)a0;
+            kv.k[idx * 64 + lane + 32] = (int16_t)(uint16_t)(uint32_t)a1;
+            uint32_t m0 = __ballot_sync(0xffffffffu, a0 == 32768), m1 = __ballot_sync(0xffffffffu, a1 == 32768);
+            if (lane == 0) {
+                kv.kmask[idx] = (uint64_t)m0 | ((uint64_t)m1 << 32);
+                kv.kexp[idx] = -16 + sh;
+            }
+        }
+    } else {
+        if (pos < 0 || pos >= kv.ctx) { if (lane == 0) set_err(err, DERR_POS); return; }
+        size_t idx = kv_index(slot, layer, part - 2 * H, pos, kv.L, H, kv.ctx);
+        bool bad = v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1;
+        if (__any_sync(0xffffffffu, bad) && lane == 0) set_err(err, DERR_VOVF);
+        kv.v[idx * 64 + lane] = (int32_t)v0;
+        kv.v[idx * 64 + lane + 32] = (int32_t)v1;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// the arrival (base2.py:85-100; Metal attend, base2_stream.swift:120-133), one CTA of NW warps per (row, head):
+//   pass 1: scores sc[s] = rshift(q16 . k16[s], -(eq + ek[s] - 3 + 10)) for s <= pos, kept in shared memory;
+//   the clock starts at the largest score; pass 2: a = ARR[start - sc] (0 past the table), Z = sum a,
+//   num = sum a * v; out = power(num, -log2fix(Z)).
+// Shared memory: 8 bytes per key (dynamic).
+// ---------------------------------------------------------------------------------------------------------------------
+struct AttnArgs {
+    const int32_t* row_slot;
+    const int32_t* row_pos;
+    int rows, layer;
+    KV kv;
+    const int32_t* q16;     // [rows][d]
+    const int32_t* qexp;    // [rows][H]
+    const int32_t* ARR;
+    int alen;
+    const int32_t* LOG2;
+    const int32_t* EXP2;
+    int64_t* out;           // [rows][d]
+};
+
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
+    extern __shared__ int64_t sc[];           // [pos + 1]
+    __shared__ int32_t qs[64];
+    __shared__ int64_t red[NW][66];
+    const int r = blockIdx.x, h = blockIdx.y;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    const int H = a.kv.H, d = H * 64;
+    const int slot = a.row_slot[r], p = a.row_pos[r];
+    if (p < 0 || p >= a.kv.ctx) return;      // flagged by k_heads (DERR_POS); never read past the store
+    const int nk = p + 1;
+    if (threadIdx.x < 64) qs[threadIdx.x] = a.q16[(size_t)r * d + h * 64 + threadIdx.x];
+    __syncthreads();
+    const int64_t eq = a.qexp[r * H + h];
+    const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
+    const int16_t* K = a.kv.k + base * 64;
+    const int32_t* Vv = a.kv.v + base * 64;
+    const uint64_t* KM = a.kv.kmask + base;
+    const int32_t* KE = a.kv.kexp + base;
+
+    // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of keys chunk*32 + (lane>>3) + 4i, i = 0..7
+    int qr[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) qr[t] = qs[(lane & 7) * 8 + t];
+    int64_t lmax = INT64_MIN;
+    for (int c = wid; c * 32 < nk; c += NW) {
+        int64_t part[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            int key = c * 32 + (lane >> 3) + 4 * i;
+            part[i] = 0;
+            if (key < nk) {
+                int4 raw = __ldg(reinterpret_cast<const int4*>(K + (size_t)key * 64 + (lane & 7) * 8));
+                const int16_t* kk = reinterpret_cast<const int16_t*>(&raw);
+                int64_t s = 0;
+#pragma unroll
+                for (int t = 0; t < 8; t++) s += (long long)qr[t] * (long long)kk[t];
+                part[i] = s;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            part[i] += __shfl_xor_sync(0xffffffffu, part[i], 1);
+            part[i] += __shfl_xor_sync(0xffffffffu, part[i], 2);
+            part[i] += __shfl_xor_sync(0xffffffffu, part[i], 4);
+        }
+        if ((lane & 7) == 0) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                int key = c * 32 + (lane >> 3) + 4 * i;
+                if (key < nk) {
+                    int64_t dot = part[i];
+                    uint64_t m = __ldg(KM + key);
+                    while (m) { int t = __ffsll((long long)m) - 1; m &= m - 1; dot += 65536LL * qs[t]; }
+                    int64_t s = rshift(dot, -(eq + (int64_t)__ldg(KE + key) - 3 + 10));
+                    sc[key] = s;
+                    lmax = s > lmax ? s : lmax;
+                }
+            }
+        }
+    }
+    lmax = warp_max64(lmax);
+    if (lane == 0) red[wid][0] = lmax;
+    __syncthreads();
+    int64_t start = red[0][0];
+#pragma unroll
+    for (int k = 1; k < NW; k++) start = red[k][0] > start ? red[k][0] : start;
+    __syncthreads();
+
+    // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin, 4 in flight
+    int64_t n0 = 0, n1 = 0, Z = 0;
+    for (int s0 = wid * 4; s0 < nk; s0 += NW * 4) {
+        int64_t av[4];
+        int2 vv[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            int s = s0 + u;
+            av[u] = 0;
+            vv[u] = make_int2(0, 0);
+            if (s < nk) {
+                int64_t dist = wsub(start, sc[s]);
+                av[u] = dist < a.alen ? (int64_t)__ldg(a.ARR + dist) : 0;
+                if (av[u]) vv[u] = __ldg(reinterpret_cast<const int2*>(Vv + (size_t)s * 64) + lane);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            Z = wadd(Z, av[u]);
+            n0 = wadd(n0, wmul(av[u], vv[u].x));
+            n1 = wadd(n1, wmul(av[u], vv[u].y));
+        }
+    }
+    red[wid][2 * lane] = n0;
+    red[wid][2 * lane + 1] = n1;
+    if (lane == 0) red[wid][64] = Z;
+    __syncthreads();
+    if (wid == 0) {
+        int64_t t0 = 0, t1 = 0, zz = 0;
+#pragma unroll
+        for (int k = 0; k < NW; k++) { t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]); }
+        int64_t F = -log2fix(zz, a.LOG2);
+        int64_t* o = a.out + (size_t)r * d + h * 64;
+        o[2 * lane] = power(t0, F, a.EXP2);
+        o[2 * lane + 1] = power(t1, F, a.EXP2);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// the race at the top (base2.py:34-40): argmax with ties to the lowest index; one CTA per scored row
+// ---------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) k_race(const int64_t* __restrict__ logits, int ld, const int32_t* __restrict__ rows_map,
+                                               int V, int32_t* __restrict__ out) {
+    __shared__ int64_t sv[32];
+    __shared__ int si[32];
+    const int r = rows_map ? rows_map[blockIdx.x] : blockIdx.x;
+    const int64_t* x = logits + (size_t)r * ld;
+    int64_t v = INT64_MIN;
+    int i = 0x7fffffff;
+    for (int t = threadIdx.x; t < V; t += 1024) race_merge(v, i, x[t], t);
+    warp_race(v, i);
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = v; si[threadIdx.x >> 5] = i; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = sv[threadIdx.x];
+        i = si[threadIdx.x];
+        warp_race(v, i);
+        if (threadIdx.x == 0) out[r] = i;
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// row bookkeeping for a decode step: one row per stream slot, at the slot's next position
+// ---------------------------------------------------------------------------------------------------------------------
+__global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const int32_t* __restrict__ slot_len,
+                              const int32_t* __restrict__ slot_tok, int32_t* row_slot, int32_t* row_pos, int32_t* row_tok) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    row_slot[s] = s;
+    row_pos[s] = slot_len[s];
+    row_tok[s] = tok_in ? tok_in[s] : slot_tok[s];
+}
+
+// after the race: the word goes straight back in (base2_stream.swift:143-146); stream lengths advance
+__global__ void k_decode_commit(int n, const int32_t* __restrict__ word, int32_t* slot_len, int32_t* slot_tok,
+                                int32_t* tok_out, int ld_out, int col) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    int w = word[s];
+    slot_len[s] += 1;
+    slot_tok[s] = w;
+    if (tok_out) tok_out[(size_t)s * ld_out + col] = w;
+}
+
+// truncate streams back to lens[s] positions (never forward), last_tok[s] fed next
+__global__ void k_rewind(int n, const int32_t* __restrict__ lens, const int32_t* __restrict__ last_tok, int V,
+                         int32_t* slot_len, int32_t* slot_tok, uint32_t* err) {
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s >= n) return;
+    int l = lens[s], t = last_tok[s];
+    if (l < 1 || l > slot_len[s]) { set_err(err, DERR_POS); return; }
+    if (t < 0 || t >= V) { set_err(err, DERR_TOKEN); return; }
+    slot_len[s] = l;
+    slot_tok[s] = t;
+}
+
+// prompt rows for a chunk [r0, r0 + rows) of the concatenated prompts
+__global__ void k_prefill_rows(int r0, int rows, const int32_t* __restrict__ row_slot_all,
+                               const int32_t* __restrict__ row_pos_all, const int32_t* __restrict__ ids,
+                               int32_t* row_slot, int32_t* row_pos, int32_t* row_tok) {
+    int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= rows) return;
+    row_slot[t] = row_slot_all[r0 + t];
+    row_pos[t] = row_pos_all[r0 + t];
+    row_tok[t] = ids[r0 + t];
+}
+
+}  // namespace b2
