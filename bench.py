@@ -209,9 +209,21 @@ def run_ours(args):
     # ---- one full C2 job, untimed: the words (checked below against the reference machine) ----
     first = eng.prefill(ids)
     first_t = torch.as_tensor(first, device="cuda")
+    parity = {}
+    if args.quick:                           # profiling aid: prompt pass + W + K steps, one JSON line, nothing else
+        cur = Cursor()
+        run_steps(args.warmup, first_t, cur)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        run_steps(args.steps, first_t, cur)
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        if rank == 0:
+            print(json.dumps({"quick": True, "steps": args.steps, "ms_per_step": round(1000 * dt / args.steps, 4)}))
+        eng.close()
+        return
     eng.generate_device(B, CYCLE, buf.view(B, CYCLE))
     words = np.concatenate([first[:, None], buf.view(B, CYCLE).cpu().numpy()], 1)
-    parity = {}
     if rank == 0:
         with open(os.path.join(ROOT, "tests", "golden", "gpt2_seed0.json")) as f:
             gold = json.load(f)["c2"]
@@ -310,6 +322,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--quick", action="store_true",
+                    help="profiling aid: prompt pass, --warmup and --steps decode steps, no other pass")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)

@@ -233,7 +233,8 @@ static void attend_row(const model_t *m, const cache_t *c, int l, int ctx, int p
         for (int t = 0; t < hd; t++) num[t] = 0;
         for (int s = 0; s <= p; s++) {
             i64 dd = wsub(start, sc[s]);
-            i64 a = dd < m->alen ? m->ARR[dd < m->alen - 1 ? dd : m->alen - 1] : 0;
+            /* numpy: ARR[min(d, len-1)] where d < len; a negative d indexes from the end (d >= -len) */
+            i64 a = dd >= m->alen ? 0 : (dd >= 0 ? m->ARR[dd] : (dd >= -m->alen ? m->ARR[m->alen + dd] : 0));
             if (!a) continue;
             Z = wadd(Z, a);
             const i64 *v = Vv + (size_t)s * d;

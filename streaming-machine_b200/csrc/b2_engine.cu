@@ -170,7 +170,7 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
     }
-    BankArgs a{h->x16, h->ex, h->LS, bk.w, bk.e, bk.b, bk.nin, bk.nout, rows, out, ldo, out_map, h->EXP2, h->PHI};
+    BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
     constexpr int RT = 8;
     dim3 grid((bk.nout + 255) / 256, (rows + RT - 1) / RT);
     prof_begin(h, B2_PROF_BANK, st);
@@ -185,21 +185,16 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
 }
 
 int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st) {
+    PlaneOut pl{};
+    if (h->use_tc && rows >= h->tc_min_rows)
+        pl = PlaneOut{h->tcr.xh, h->tcr.xl, h->tcr.kmax, h->tcr.rowcorr, h->tcr.nsat, h->tcr.sat};
     prof_begin(h, B2_PROF_QUANT, st);
     if (n > 1024)
-        k_quant<512><<<rows, 512, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40);
+        k_quant<512><<<rows, 512, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40, pl);
     else
-        k_quant<256><<<rows, 256, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40);
+        k_quant<256><<<rows, 256, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40, pl);
     prof_end(h, B2_PROF_QUANT, st);
-    int rc = check_launch(h, "quant");
-    if (rc) return rc;
-    if (h->use_tc && rows >= h->tc_min_rows) {
-        prof_begin(h, B2_PROF_QUANT, st);
-        tc_planes(h->tcr, h->x16, n, rows, st);
-        prof_end(h, B2_PROF_QUANT, st);
-        return check_launch(h, "tc_planes");
-    }
-    return B2_OK;
+    return check_launch(h, "quant");
 }
 
 // ---- all layers + head for the rows in the row table --------------------------------------------------------------
@@ -220,7 +215,7 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
         k_heads<<<dim3(rows, 3 * H), 32, 0, st>>>(h->QKV, rows, h->row_slot, h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err);
         prof_end(h, B2_PROF_HEADS, st);
         if ((rc = check_launch(h, "heads"))) return rc;
-        AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT};
+        AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err};
         prof_begin(h, B2_PROF_ATTEND, st);
         k_attend<4><<<dim3(rows, H), 128, sizeof(int64_t) * h->max_ctx, st>>>(aa);
         prof_end(h, B2_PROF_ATTEND, st);
@@ -256,6 +251,8 @@ int read_device_error(b2_handle* h) {
     CK(cudaMemset(h->d_err, 0, sizeof(uint32_t)));
     if (e & DERR_POS) return fail(h, B2_ERR_CTX, "a position passed the context (device check, bits 0x%x)", e);
     if (e & DERR_VOVF) return fail(h, B2_ERR_VALUE, "a value-store entry did not fit int32 (device check, bits 0x%x)", e);
+    if (e & DERR_INDEX) return fail(h, B2_ERR_VALUE, "an arrival index fell below the table (device check, bits 0x%x)", e);
+    if (e & DERR_TIMEOUT) return fail(h, B2_ERR_DEVICE, "a tensor-core kernel's bounded wait gave up (device check, bits 0x%x)", e);
     return fail(h, B2_ERR_DEVICE, "a token id was out of range (device check, bits 0x%x)", e);
 }
 
@@ -417,7 +414,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
         (rc = dalloc(h, &h->logits, (size_t)n_streams * c.vocab)))
         return rc;
     if (h->tc_min_rows < (1 << 30)) {
-        rc = tc_rows_alloc(h->tcr, mr, F > d ? F : d);
+        rc = tc_rows_alloc(h->tcr, mr, F > d ? F : d, h->d_err);
         if (rc) return fail(h, B2_ERR_NOMEM, "tensor-core row buffers: %s", cudaGetErrorString((cudaError_t)rc));
     }
     h->n_slots = n_streams;

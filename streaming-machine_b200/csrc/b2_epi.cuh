@@ -1,0 +1,51 @@
+// b2_epi.cuh -- pieces shared by every bank-product kernel (CUDA-core and tensor-core): the device error word and
+// what a bank does with a finished pile (base2.py:62-83).
+#pragma once
+#include <stdint.h>
+#include "b2_arith.cuh"
+
+namespace b2 {
+
+// sticky device error bits (read back by b2_sync)
+enum : uint32_t {
+    DERR_TOKEN = 1u,     // a token id outside [0, vocab)
+    DERR_POS = 2u,       // a position at or past the store's context (or the position table)
+    DERR_VOVF = 4u,      // a V value outside int32 (the value store holds int32)
+    DERR_INDEX = 8u,     // an arrival-table index below -len (where base2.py raises IndexError)
+    DERR_TIMEOUT = 16u,  // a bounded wait in a tensor-core kernel gave up (the results of that call are void)
+};
+
+B2_DEV void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
+
+enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3 };
+
+// what a bank does with a finished pile (row r, output column j)
+struct EpiArgs {
+    const int32_t* ex;      // [rows] the input's power of two
+    const int64_t* LS;      // [rows] the gauge (gauged banks)
+    const int32_t* e;       // [nout] the column's power of two
+    const int64_t* b;       // [nout] bias
+    int64_t* out;           // [out row][ldo]
+    int ldo;
+    const int32_t* out_map; // optional row -> out row
+    const int32_t* EXP2;
+    const int32_t* PHI;
+};
+
+template <int EPI>
+B2_DEV void epi_store(const EpiArgs& a, int r, int j, int64_t pile) {
+    int orow = a.out_map ? a.out_map[r] : r;
+    int64_t* o = a.out + (size_t)orow * a.ldo + j;
+    int64_t es = wadd(wadd((int64_t)a.e[j], (int64_t)a.ex[r]), 16);
+    if (EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) {
+        int64_t F = wsub(wmul(es, 65536), a.LS[r]);        // base2.py:70
+        int64_t v = wadd(power(pile, F, a.EXP2), a.b[j]);  // base2.py:71
+        if (EPI == EPI_GAUGED_EDGE) v = edge(v, a.PHI);    // base2.py:106 edge(gauged_bank(...))
+        *o = v;
+    } else {
+        int64_t v = wadd(rshift(pile, -es), a.b[j]);       // base2.py:76
+        *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;       // base2.py:105-106 R = R + ...
+    }
+}
+
+}  // namespace b2

@@ -5,17 +5,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include "b2_arith.cuh"
+#include "b2_epi.cuh"
 
 namespace b2 {
-
-// sticky device error bits (read back by b2_sync)
-enum : uint32_t {
-    DERR_TOKEN = 1u,     // a token id outside [0, vocab)
-    DERR_POS = 2u,       // a position at or past the store's context (or the position table)
-    DERR_VOVF = 4u,      // a V value outside int32 (the value store holds int32)
-};
-
-B2_DEV void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
 
 // position of (slot, layer, head, pos) in the key/value store: [slot][layer][head][pos]
 B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int ctx) {
@@ -42,13 +34,25 @@ __global__ void k_embed(const int32_t* __restrict__ row_tok, const int32_t* __re
 // to16 (base2.py:24-27) + the gauge (base2.py:55-60): one CTA per row. x16 fits int32 (|x16| <= 32768).
 // src_rows (optional) gathers rows (the head reads only the rows it scores).
 // ---------------------------------------------------------------------------------------------------------------------
+// Planes (optional, the tensor-core path): each x16 split into signed bytes xh = min(x >> 8, 127),
+// xl = (x & 255) - 128; the +32768 entries listed in sat/nsat; rowcorr = 128 * sum of the represented values.
+struct PlaneOut {
+    int8_t* xh;
+    int8_t* xl;
+    int ld;             // row stride of xh/xl/sat
+    int64_t* rowcorr;
+    int32_t* nsat;
+    int16_t* sat;
+};
+
 template <int NT>
 __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int n, const int32_t* __restrict__ src_rows,
                                               int rows, int32_t* __restrict__ x16, int32_t* __restrict__ ex,
                                               int64_t* __restrict__ LS, int gauge, const int32_t* __restrict__ LOG2,
-                                              int64_t log768, int64_t eps40) {
+                                              int64_t log768, int64_t eps40, PlaneOut pl) {
     __shared__ uint64_t s_or[NT / 32];
     __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
+    __shared__ int s_nsat;
     int r = blockIdx.x;
     if (r >= rows) return;
     int sr = src_rows ? src_rows[r] : r;
@@ -63,14 +67,22 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
 #pragma unroll
     for (int k = 0; k < NT / 32; k++) all |= s_or[k];
     int sh = to16_shift(all);
+    if (threadIdx.x == 0) s_nsat = 0;
+    __syncthreads();
     int64_t q1 = 0, q2 = 0;
     for (int i = threadIdx.x; i < n; i += NT) {
         int64_t v = rshift(x[i], sh);
-        x16[(size_t)r * n + i] = (int32_t)v;
+        if (x16) x16[(size_t)r * n + i] = (int32_t)v;
         q1 += v;
         q2 += v * v;
+        if (pl.xh) {
+            bool sat = v == 32768;
+            pl.xh[(size_t)r * pl.ld + i] = (int8_t)(sat ? 127 : (v >> 8));
+            pl.xl[(size_t)r * pl.ld + i] = (int8_t)((v & 255) - 128);
+            if (sat) pl.sat[(size_t)r * pl.ld + atomicAdd(&s_nsat, 1)] = (int16_t)i;
+        }
     }
-    if (!gauge) {
+    if (!gauge && !pl.xh) {
         if (threadIdx.x == 0) ex[r] = -16 + sh;
         return;
     }
@@ -82,45 +94,23 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
         int64_t S1 = 0, S2 = 0;
         for (int k = 0; k < NT / 32; k++) { S1 = wadd(S1, s_1[k]); S2 = wadd(S2, s_2[k]); }
         ex[r] = -16 + sh;
-        LS[r] = gauge_LS(S1, S2, -16 + sh, LOG2, log768, eps40);
+        if (gauge) LS[r] = gauge_LS(S1, S2, -16 + sh, LOG2, log768, eps40);
+        if (pl.xh) {
+            pl.nsat[r] = s_nsat;
+            pl.rowcorr[r] = 128 * (S1 - 256 * (int64_t)s_nsat);
+        }
     }
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
 // bank epilogues (base2.py:62-76, 78-83)
 // ---------------------------------------------------------------------------------------------------------------------
-enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3 };
-
 struct BankArgs {
     const int32_t* x16;     // [rows][nin]
-    const int32_t* ex;      // [rows]
-    const int64_t* LS;      // [rows] (gauged)
     const int16_t* w;       // [nin][nout]
-    const int32_t* e;       // [nout]
-    const int64_t* b;       // [nout]
     int nin, nout, rows;
-    int64_t* out;           // [out row][ldo]
-    int ldo;
-    const int32_t* out_map; // optional row -> out row
-    const int32_t* EXP2;
-    const int32_t* PHI;
+    EpiArgs epi;
 };
-
-template <int EPI>
-B2_DEV void bank_epilogue(const BankArgs& a, int r, int j, int64_t pile) {
-    int orow = a.out_map ? a.out_map[r] : r;
-    int64_t* o = a.out + (size_t)orow * a.ldo + j;
-    int64_t es = wadd(wadd((int64_t)a.e[j], (int64_t)a.ex[r]), 16);
-    if (EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) {
-        int64_t F = wsub(wmul(es, 65536), a.LS[r]);
-        int64_t v = wadd(power(pile, F, a.EXP2), a.b[j]);
-        if (EPI == EPI_GAUGED_EDGE) v = edge(v, a.PHI);
-        *o = v;
-    } else {
-        int64_t v = wadd(rshift(pile, -es), a.b[j]);
-        *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
-    }
-}
 
 // CUDA-core bank product: one thread per output column, RT rows per CTA, the pile exact in int64.
 template <int EPI, int RT>
@@ -151,7 +141,7 @@ __global__ void __launch_bounds__(256) k_bank_simt(BankArgs a) {
     if (j >= a.nout) return;
 #pragma unroll
     for (int rr = 0; rr < RT; rr++)
-        if (r0 + rr < a.rows) bank_epilogue<EPI>(a, r0 + rr, j, acc[rr]);
+        if (r0 + rr < a.rows) epi_store<EPI>(a.epi, r0 + rr, j, acc[rr]);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -223,7 +213,18 @@ struct AttnArgs {
     const int32_t* LOG2;
     const int32_t* EXP2;
     int64_t* out;           // [rows][d]
+    uint32_t* err;
 };
+
+// ARR read as base2.py:97 does it: ARR[min(d, len-1)] where d < len, else 0. d is never negative unless a score
+// wrapped; numpy would then index from the table's end (d >= -len) or raise (d < -len, flagged here).
+B2_DEV int64_t arrival(int64_t d, const int32_t* __restrict__ ARR, int alen, uint32_t* err) {
+    if (d >= alen) return 0;
+    if (d >= 0) return (int64_t)__ldg(ARR + d);
+    if (d >= -(int64_t)alen) return (int64_t)__ldg(ARR + (alen + d));
+    set_err(err, DERR_INDEX);
+    return 0;
+}
 
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
@@ -305,8 +306,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
             av[u] = 0;
             vv[u] = make_int2(0, 0);
             if (s < nk) {
-                int64_t dist = wsub(start, sc[s]);
-                av[u] = dist < a.alen ? (int64_t)__ldg(a.ARR + dist) : 0;
+                av[u] = arrival(wsub(start, sc[s]), a.ARR, a.alen, a.err);
                 if (av[u]) vv[u] = __ldg(reinterpret_cast<const int2*>(Vv + (size_t)s * 64) + lane);
             }
         }

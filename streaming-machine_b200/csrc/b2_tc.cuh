@@ -1,40 +1,54 @@
-// b2_tc.cuh -- the bank product on the 5th-generation tensor cores (tcgen05, kind::i8). Interface used by
-// b2_engine.cu; the kernels live in b2_tc.cu.
+// b2_tc.cuh -- the bank product on the 5th-generation tensor cores (tcgen05.mma kind::i8, accumulators in TMEM,
+// operands staged by TMA). Interface used by b2_engine.cu; kernels in b2_tc.cu.
+//
+// Exactness. A weight w (|w| <= 32767) and an activation x16 (-32768..32768) are each split into two signed bytes:
+//     w = 256*wh + wls + 128         wh = w >> 8,            wls = (w & 255) - 128
+//     x = 256*xh + xls + 128 (+256)  xh = min(x >> 8, 127),  xls = (x & 255) - 128   (+256 only for x = +32768)
+// Three int32 accumulators per output, A1 = sum wh*xh, A2 = sum wh*xls + wls*xh, A3 = sum wls*xls, are exact
+// (|A| < 2^27 for 3072 inputs), and the pile (base2.py:29-32) is recovered exactly in int64:
+//     pile = 65536*A1 + 256*A2 + A3 + 128*sum(w) + 128*sum(x_repr) - 16384*nin + 256*sum_{x_i = 32768} w_i
+// where x_repr is x with +32768 read as 32512. The last term runs over a per-row list of the (rare) +32768 entries.
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 namespace b2 {
 
-// A bank in the tensor-core layout: w = 256*wh + (wl + 128) + ... split into two signed int8 planes, K-major.
+struct TcMap { alignas(64) unsigned char bytes[128]; };
+
+// A bank in the tensor-core layout: the two weight planes, K-major ([out][in]), padded to 128 outputs.
 struct TcBank {
     int ready = 0;
     int nin = 0, nout = 0, nout_pad = 0;
-    int8_t* wh = nullptr;       // [nout_pad][nin]  w >> 8
-    int8_t* wl = nullptr;       // [nout_pad][nin]  (w & 255) - 128
-    int64_t* colsum = nullptr;  // [nout]  sum_i w[i][j]
-    alignas(64) unsigned char tmap_wh[128];
-    alignas(64) unsigned char tmap_wl[128];
+    int8_t* wh = nullptr;        // [nout_pad][nin]
+    int8_t* wl = nullptr;        // [nout_pad][nin]
+    int64_t* colcorr = nullptr;  // [nout_pad]  128*sum_i w[i][j] - 16384*nin
+    const int16_t* w16 = nullptr;  // the reference-layout bank [nin][nout] (for the +32768 correction)
+    TcMap map_wh, map_wl;
 };
 
-// Row-side buffers: the activations' planes and their corrections.
+// Row-side buffers: the activations' planes, their corrections, the split-K accumulation.
 struct TcRows {
-    int max_rows = 0, kmax = 0;
-    int8_t* xh = nullptr;       // [max_rows_pad][kmax]
-    int8_t* xl = nullptr;       // [max_rows_pad][kmax]
-    int64_t* rowsum = nullptr;  // [max_rows]  sum_i x_repr[i]
-    int32_t* nsat = nullptr;    // [max_rows]  entries equal to +32768
-    int16_t* sat = nullptr;     // [max_rows][kmax] their indices
-    int64_t* pile = nullptr;    // split-K accumulation [max_rows][max nout]
-    uint32_t* tiles = nullptr;  // split-K arrival counters
+    int rows_cap = 0, kmax = 0;
+    int8_t* xh = nullptr;       // [rows_cap][kmax]
+    int8_t* xl = nullptr;       // [rows_cap][kmax]
+    int64_t* rowcorr = nullptr; // [rows_cap]  128*sum_i x_repr[i]
+    int32_t* nsat = nullptr;    // [rows_cap]  entries equal to +32768
+    int16_t* sat = nullptr;     // [rows_cap][kmax] their indices
+    int64_t* pile = nullptr;    // split-K accumulation [PILE_ROWS][PILE_COLS]
+    uint32_t* counters = nullptr;  // split-K arrival counters
+    uint32_t* err = nullptr;    // device error word (shared with the engine)
+    struct { int k, bn; TcMap h, l; } maps[4];
+    int nmaps = 0;
 };
+
+constexpr int PILE_ROWS = 256, PILE_COLS = 4096, MAX_COUNTERS = 4096;
 
 int tc_min_rows_default();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
 void tc_bank_free(TcBank& t);
-int tc_rows_alloc(TcRows& r, int max_rows, int kmax);
+int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);
-void tc_planes(TcRows& r, const int32_t* x16, int n, int rows, cudaStream_t st);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st);
