@@ -62,6 +62,18 @@ struct b2_handle {
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
 
+    // decode steps: where the words go (device descriptor), programmatic launches, the captured step graph
+    GenDesc* gen_desc = nullptr;
+    int32_t* gen_base = nullptr;
+    int pdl = 1;
+    int use_graph = 1;
+    cudaStream_t cap_stream = nullptr;
+    struct StepGraph {
+        int n = 0;
+        cudaGraphExec_t exec = nullptr;
+        int64_t cnt[B2_PROF_N] = {0};
+    } graph;
+
     // launch accounting / per-class event timing (b2_profile)
     struct Prof {
         int timing = 0;
@@ -106,6 +118,11 @@ void dfree(b2_handle* h, void* p) {
     for (size_t i = 0; i < h->allocs.size(); i++)
         if (h->allocs[i] == p) { h->allocs.erase(h->allocs.begin() + i); break; }
     cudaFree(p);
+}
+
+void drop_graph(b2_handle* h) {
+    if (h->graph.exec) cudaGraphExecDestroy(h->graph.exec);
+    h->graph = b2_handle::StepGraph{};
 }
 
 int bank_index(const b2_handle* h, const char* name) {
@@ -160,12 +177,34 @@ void prof_end(b2_handle* h, int cls, cudaStream_t st) {
     if (h->prof.timing) cudaEventRecord(h->prof.ev[cls].back().second, st);
 }
 
+// every launch: counted per class, bracketed by events when timing, programmatic (PDL) unless timing
+template <typename... KArgs, typename... Args>
+int launch(b2_handle* h, int cls, const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+           cudaStream_t st, Args... args) {
+    prof_begin(h, cls, st);
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = (h->pdl && !h->prof.timing) ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...);
+    prof_end(h, cls, st);
+    if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "launch %s: %s", what, cudaGetErrorString(e));
+    return B2_OK;
+}
+
 // ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
 int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st) {
     const DevBank& bk = h->banks[bi];
     if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
         prof_begin(h, B2_PROF_BANK, st);
-        int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st);
+        int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
+                         h->pdl && !h->prof.timing);
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
@@ -173,28 +212,23 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
     BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
     constexpr int RT = 8;
     dim3 grid((bk.nout + 255) / 256, (rows + RT - 1) / RT);
-    prof_begin(h, B2_PROF_BANK, st);
     switch (epi) {
-        case EPI_GAUGED: k_bank_simt<EPI_GAUGED, RT><<<grid, 256, 0, st>>>(a); break;
-        case EPI_GAUGED_EDGE: k_bank_simt<EPI_GAUGED_EDGE, RT><<<grid, 256, 0, st>>>(a); break;
-        case EPI_PLAIN_ADD: k_bank_simt<EPI_PLAIN_ADD, RT><<<grid, 256, 0, st>>>(a); break;
-        default: k_bank_simt<EPI_PLAIN_OUT, RT><<<grid, 256, 0, st>>>(a); break;
+        case EPI_GAUGED: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_GAUGED, RT>, grid, 256, 0, st, a);
+        case EPI_GAUGED_EDGE: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_GAUGED_EDGE, RT>, grid, 256, 0, st, a);
+        case EPI_PLAIN_ADD: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_PLAIN_ADD, RT>, grid, 256, 0, st, a);
+        default: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_PLAIN_OUT, RT>, grid, 256, 0, st, a);
     }
-    prof_end(h, B2_PROF_BANK, st);
-    return check_launch(h, "bank_simt");
 }
 
 int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st) {
     PlaneOut pl{};
     if (h->use_tc && rows >= h->tc_min_rows)
         pl = PlaneOut{h->tcr.xh, h->tcr.xl, h->tcr.kmax, h->tcr.rowcorr, h->tcr.nsat, h->tcr.sat};
-    prof_begin(h, B2_PROF_QUANT, st);
     if (n > 1024)
-        k_quant<512><<<rows, 512, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40, pl);
-    else
-        k_quant<256><<<rows, 256, 0, st>>>(X, n, src_rows, rows, h->x16, h->ex, h->LS, gauge, h->LOG2, h->log768, h->eps40, pl);
-    prof_end(h, B2_PROF_QUANT, st);
-    return check_launch(h, "quant");
+        return launch(h, B2_PROF_QUANT, "quant", k_quant<512>, rows, 512, 0, st, X, n, src_rows, rows, h->x16, h->ex, h->LS,
+                      gauge, h->LOG2, h->log768, h->eps40, pl);
+    return launch(h, B2_PROF_QUANT, "quant", k_quant<256>, rows, 256, 0, st, X, n, src_rows, rows, h->x16, h->ex, h->LS,
+                  gauge, h->LOG2, h->log768, h->eps40, pl);
 }
 
 // ---- all layers + head for the rows in the row table --------------------------------------------------------------
@@ -204,22 +238,18 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
     int rc;
-    prof_begin(h, B2_PROF_OTHER, st);
-    k_embed<<<rows, 256, 0, st>>>(h->row_tok, h->row_pos, rows, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, h->d_err);
-    prof_end(h, B2_PROF_OTHER, st);
-    if ((rc = check_launch(h, "embed"))) return rc;
+    if ((rc = launch(h, B2_PROF_OTHER, "embed", k_embed, rows, 256, 0, st, h->row_tok, h->row_pos, rows, h->wte, h->wpe, d,
+                     c.vocab, c.n_ctx, h->R, h->d_err)))
+        return rc;
     for (int l = 0; l < L; l++) {
         if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
         if ((rc = run_bank(h, 4 * l + 0, EPI_GAUGED, rows, h->QKV, 3 * d, nullptr, st))) return rc;
-        prof_begin(h, B2_PROF_HEADS, st);
-        k_heads<<<dim3(rows, 3 * H), 32, 0, st>>>(h->QKV, rows, h->row_slot, h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err);
-        prof_end(h, B2_PROF_HEADS, st);
-        if ((rc = check_launch(h, "heads"))) return rc;
+        if ((rc = launch(h, B2_PROF_HEADS, "heads", k_heads, dim3(rows, 3 * H), 32, 0, st, h->QKV, rows, h->row_slot,
+                         h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err)))
+            return rc;
         AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err};
-        prof_begin(h, B2_PROF_ATTEND, st);
-        k_attend<4><<<dim3(rows, H), 128, sizeof(int64_t) * h->max_ctx, st>>>(aa);
-        prof_end(h, B2_PROF_ATTEND, st);
-        if ((rc = check_launch(h, "attend"))) return rc;
+        if ((rc = launch(h, B2_PROF_ATTEND, "attend", k_attend<4>, dim3(rows, H), 128, sizeof(int64_t) * h->max_ctx, st, aa)))
+            return rc;
         if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
         if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
         if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
@@ -230,10 +260,7 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
     if (nhead <= 0) return B2_OK;
     if ((rc = run_quant(h, h->R, d, hrows, nhead, 1, st))) return rc;
     if ((rc = run_bank(h, 4 * L, EPI_GAUGED, nhead, logits, c.vocab, hmap, st))) return rc;
-    prof_begin(h, B2_PROF_RACE, st);
-    k_race<<<nhead, 1024, 0, st>>>(logits, c.vocab, hmap, c.vocab, words_by_slot);
-    prof_end(h, B2_PROF_RACE, st);
-    return check_launch(h, "race");
+    return launch(h, B2_PROF_RACE, "race", k_race, nhead, 1024, 0, st, logits, c.vocab, hmap, c.vocab, words_by_slot);
 }
 
 int ensure_ready(b2_handle* h) {
@@ -280,6 +307,8 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     h->device = device;
     h->flags = flags;
     h->banks.resize(4 * cfg->n_layer + 1);
+    if (const char* v = getenv("B2_PDL")) h->pdl = atoi(v);
+    if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (dalloc(h, &h->d_err, 1)) { delete h; return B2_ERR_NOMEM; }
     cudaMemset(h->d_err, 0, sizeof(uint32_t));
@@ -362,10 +391,10 @@ int b2_finalize(b2_handle* h) {
     if (!h->wte || !h->wpe || !h->PHI || !h->ARR || !h->LOG2 || !h->EXP2 || !h->have_scalar[0] || !h->have_scalar[1])
         return fail(h, B2_ERR_STATE, "a table or scalar is missing");
     // tensor-core layouts of every bank
-    int tc_ok = 1;
+    int tc_ok = tc_init() == 0;
     for (auto& bk : h->banks) {
-        int rc = tc_bank_build(bk.tc, bk.w, bk.nin, bk.nout);
-        if (rc) { tc_ok = 0; break; }
+        if (!tc_ok) break;
+        if (tc_bank_build(bk.tc, bk.w, bk.nin, bk.nout)) tc_ok = 0;
     }
     CK(cudaDeviceSynchronize());
     h->tc_min_rows = tc_ok ? tc_min_rows_default() : (1 << 30);
@@ -388,6 +417,9 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
     tc_rows_free(h->tcr);
+    drop_graph(h);
+    dfree(h, h->gen_desc);
+    dfree(h, h->gen_base);
     h->n_slots = 0;
     const int L = c.n_layer, H = c.n_head, d = c.d_model, F = c.d_ff;
     size_t nkv = (size_t)n_streams * L * H * max_ctx;
@@ -398,6 +430,9 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((rc = dalloc(h, &h->kv.kexp, nkv))) return rc;
     if ((rc = dalloc(h, &h->kv.v, nkv * 64))) return rc;
     if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
+    if ((rc = dalloc(h, &h->gen_base, n_streams))) return rc;
+    if ((rc = dalloc(h, &h->gen_desc, 1))) return rc;
+    CK(cudaMemset(h->gen_desc, 0, sizeof(GenDesc)));
     if ((rc = dalloc(h, &h->slot_tok, n_streams))) return rc;
     CK(cudaMemset(h->slot_len, 0, sizeof(int32_t) * n_streams));
     CK(cudaMemset(h->slot_tok, 0, sizeof(int32_t) * n_streams));
@@ -458,9 +493,9 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
         }
         for (size_t r0 = 0; r0 < total && !rc; r0 += h->max_rows) {
             int rows = (int)(total - r0 < (size_t)h->max_rows ? total - r0 : (size_t)h->max_rows);
-            prof_begin(h, B2_PROF_OTHER, st);
-            k_prefill_rows<<<(rows + 255) / 256, 256, 0, st>>>((int)r0, rows, d_rs, d_rp, ids, h->row_slot, h->row_pos, h->row_tok);
-            prof_end(h, B2_PROF_OTHER, st);
+            if ((rc = launch(h, B2_PROF_OTHER, "prefill_rows", k_prefill_rows, (rows + 255) / 256, 256, 0, st, (int)r0, rows,
+                             d_rs, d_rp, ids, h->row_slot, h->row_pos, h->row_tok)))
+                break;
             // the scored rows in this chunk: each stream's last prompt position
             std::vector<int32_t> hr, hm;
             for (int s = 0; s < n_streams; s++)
@@ -493,19 +528,53 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 }
 
 namespace {
-int step_async(b2_handle* h, const int32_t* tok_in, int n, int32_t* tok_out, int ld_out, int col, int64_t* logits, cudaStream_t st) {
-    prof_begin(h, B2_PROF_OTHER, st);
-    k_decode_rows<<<(n + 127) / 128, 128, 0, st>>>(n, tok_in, h->slot_len, h->slot_tok, h->row_slot, h->row_pos, h->row_tok);
-    prof_end(h, B2_PROF_OTHER, st);
-    int rc = check_launch(h, "decode_rows");
+// one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
+int step_core(b2_handle* h, int n, cudaStream_t st) {
+    int rc = launch(h, B2_PROF_OTHER, "decode_rows", k_decode_rows, (n + 127) / 128, 128, 0, st, n, (const int32_t*)nullptr,
+                    h->slot_len, h->slot_tok, h->row_slot, h->row_pos, h->row_tok);
     if (rc) return rc;
-    // every row is scored; row r = slot r
-    rc = run_rows(h, n, nullptr, nullptr, n, logits ? logits : h->logits, h->race_out, st);
+    if ((rc = run_rows(h, n, nullptr, nullptr, n, h->logits, h->race_out, st))) return rc;
+    return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
+                  h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
+}
+
+// the step captured once per stream count (on an internal stream), then replayed
+int step_graph(b2_handle* h, int n, cudaStream_t st) {
+    if (h->graph.exec && h->graph.n != n) drop_graph(h);
+    if (!h->graph.exec) {
+        if (!h->cap_stream) CK(cudaStreamCreateWithFlags(&h->cap_stream, cudaStreamNonBlocking));
+        CK(cudaStreamSynchronize(st));
+        int64_t before[B2_PROF_N], l0 = h->prof.launches;
+        for (int c = 0; c < B2_PROF_N; c++) before[c] = h->prof.cnt[c];
+        CK(cudaStreamBeginCapture(h->cap_stream, cudaStreamCaptureModeThreadLocal));
+        int rc = step_core(h, n, h->cap_stream);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(h->cap_stream, &g);
+        for (int c = 0; c < B2_PROF_N; c++) { h->graph.cnt[c] = h->prof.cnt[c] - before[c]; h->prof.cnt[c] = before[c]; }
+        h->prof.launches = l0;
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "step capture: %s", cudaGetErrorString(e));
+        e = cudaGraphInstantiate(&h->graph.exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) { h->graph.exec = nullptr; return fail(h, B2_ERR_CUDA, "step graph: %s", cudaGetErrorString(e)); }
+        h->graph.n = n;
+    }
+    CK(cudaGraphLaunch(h->graph.exec, st));
+    for (int c = 0; c < B2_PROF_N; c++) { h->prof.cnt[c] += h->graph.cnt[c]; h->prof.launches += h->graph.cnt[c]; }
+    return B2_OK;
+}
+
+// n_steps decode steps; the words of step t go to out[s * ld + t] (out may be NULL); logits of the last step copied out
+int run_steps(b2_handle* h, int n, int n_steps, int32_t* out, int ld, int64_t* logits, cudaStream_t st) {
+    int rc = launch(h, B2_PROF_OTHER, "gen_begin", k_gen_begin, (n + 127) / 128, 128, 0, st, n, h->slot_len, h->gen_base,
+                    h->gen_desc, out, ld);
     if (rc) return rc;
-    prof_begin(h, B2_PROF_OTHER, st);
-    k_decode_commit<<<(n + 127) / 128, 128, 0, st>>>(n, h->race_out, h->slot_len, h->slot_tok, tok_out, ld_out, col);
-    prof_end(h, B2_PROF_OTHER, st);
-    return check_launch(h, "decode_commit");
+    for (int t = 0; t < n_steps; t++) {
+        rc = (h->use_graph && !h->prof.timing) ? step_graph(h, n, st) : step_core(h, n, st);
+        if (rc) return rc;
+    }
+    if (logits) CK(cudaMemcpyAsync(logits, h->logits, sizeof(int64_t) * n * h->cfg.vocab, cudaMemcpyDeviceToDevice, st));
+    return B2_OK;
 }
 }  // namespace
 
@@ -514,7 +583,9 @@ int b2_step(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok
     if (rc) return rc;
     if (n_streams < 1 || n_streams > h->n_slots || !tok_out) return fail(h, B2_ERR_ARG, "b2_step: bad argument");
     if (!tok_in && !h->primed) return fail(h, B2_ERR_STATE, "b2_step without tok_in before any b2_prefill");
-    return step_async(h, tok_in, n_streams, tok_out, 1, 0, logits, (cudaStream_t)stream);
+    cudaStream_t st = (cudaStream_t)stream;
+    if (tok_in) CK(cudaMemcpyAsync(h->slot_tok, tok_in, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToDevice, st));
+    return run_steps(h, n_streams, 1, tok_out, 1, logits, st);
 }
 
 int b2_generate(b2_handle* h, int32_t n_streams, int32_t n_steps, int32_t* tokens_out, void* stream) {
@@ -522,9 +593,7 @@ int b2_generate(b2_handle* h, int32_t n_streams, int32_t n_steps, int32_t* token
     if (rc) return rc;
     if (n_streams < 1 || n_streams > h->n_slots || n_steps < 0 || !tokens_out) return fail(h, B2_ERR_ARG, "b2_generate: bad argument");
     if (!h->primed) return fail(h, B2_ERR_STATE, "b2_generate before b2_prefill");
-    for (int t = 0; t < n_steps; t++)
-        if ((rc = step_async(h, nullptr, n_streams, tokens_out, n_steps, t, nullptr, (cudaStream_t)stream))) return rc;
-    return B2_OK;
+    return run_steps(h, n_streams, n_steps, tokens_out, n_steps, nullptr, (cudaStream_t)stream);
 }
 
 int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok_out) {
@@ -534,7 +603,7 @@ int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t
     cudaStream_t st = 0;
     // the words go in as each stream's last word; the race's answer comes back from race_out
     CK(cudaMemcpyAsync(h->slot_tok, tok_in, sizeof(int32_t) * n_streams, cudaMemcpyHostToDevice, st));
-    if ((rc = step_async(h, nullptr, n_streams, nullptr, 1, 0, nullptr, st))) return rc;
+    if ((rc = run_steps(h, n_streams, 1, nullptr, 1, nullptr, st))) return rc;
     CK(cudaMemcpyAsync(tok_out, h->race_out, sizeof(int32_t) * n_streams, cudaMemcpyDeviceToHost, st));
     CK(cudaStreamSynchronize(st));
     return read_device_error(h);
@@ -558,10 +627,8 @@ int b2_rewind(b2_handle* h, int32_t n_streams, const int32_t* lens, const int32_
     if (rc) return rc;
     if (n_streams < 1 || n_streams > h->n_slots || !lens || !last_tok) return fail(h, B2_ERR_ARG, "b2_rewind: bad argument");
     cudaStream_t st = (cudaStream_t)stream;
-    prof_begin(h, B2_PROF_OTHER, st);
-    k_rewind<<<(n_streams + 127) / 128, 128, 0, st>>>(n_streams, lens, last_tok, h->cfg.vocab, h->slot_len, h->slot_tok, h->d_err);
-    prof_end(h, B2_PROF_OTHER, st);
-    return check_launch(h, "rewind");
+    return launch(h, B2_PROF_OTHER, "rewind", k_rewind, (n_streams + 127) / 128, 128, 0, st, n_streams, lens, last_tok,
+                  h->cfg.vocab, h->slot_len, h->slot_tok, h->d_err);
 }
 
 int b2_profile(b2_handle* h, int timing) {
@@ -606,6 +673,8 @@ void b2_destroy(b2_handle* h) {
     if (!h) return;
     cudaSetDevice(h->device);
     cudaDeviceSynchronize();
+    drop_graph(h);
+    if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
     tc_rows_free(h->tcr);
     for (int c = 0; c < B2_PROF_N; c++)

@@ -32,6 +32,24 @@ struct EpiArgs {
     const int32_t* PHI;
 };
 
+// the same arithmetic with the row's quantities already at hand: exr = the input's power of two, LSr = the gauge,
+// e2r = EXP2[(-LSr) & 0xFFFF] (power()'s table read depends only on the row, since F = 65536*(e_j + exr + 16) - LSr).
+template <int EPI>
+B2_DEV int64_t epi_value(int64_t pile, int64_t e_j, int64_t b_j, int64_t exr, int64_t LSr, int64_t e2r,
+                         const int32_t* __restrict__ PHI) {
+    int64_t es = wadd(wadd(e_j, exr), 16);
+    if (EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) {
+        int64_t F = wsub(wmul(es, 65536), LSr);
+        int64_t v = wadd(rshift(wmul(pile, e2r), 16 - (F >> 16)), b_j);
+        return EPI == EPI_GAUGED_EDGE ? edge(v, PHI) : v;
+    }
+    return wadd(rshift(pile, -es), b_j);
+}
+
+// PDL: wait for the kernels this one depends on (no-op without programmatic launch), and let the next one start
+B2_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+B2_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 template <int EPI>
 B2_DEV void epi_store(const EpiArgs& a, int r, int j, int64_t pile) {
     int orow = a.out_map ? a.out_map[r] : r;

@@ -20,6 +20,8 @@ B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int
 __global__ void k_embed(const int32_t* __restrict__ row_tok, const int32_t* __restrict__ row_pos, int rows,
                         const int64_t* __restrict__ wte, const int64_t* __restrict__ wpe, int d, int V, int nctx,
                         int64_t* __restrict__ R, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
     int r = blockIdx.x;
     if (r >= rows) return;
     int tok = row_tok[r], pos = row_pos[r];
@@ -50,6 +52,8 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
                                               int rows, int32_t* __restrict__ x16, int32_t* __restrict__ ex,
                                               int64_t* __restrict__ LS, int gauge, const int32_t* __restrict__ LOG2,
                                               int64_t log768, int64_t eps40, PlaneOut pl) {
+    griddep_wait();
+    griddep_launch();
     __shared__ uint64_t s_or[NT / 32];
     __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
     __shared__ int s_nsat;
@@ -115,6 +119,8 @@ struct BankArgs {
 // CUDA-core bank product: one thread per output column, RT rows per CTA, the pile exact in int64.
 template <int EPI, int RT>
 __global__ void __launch_bounds__(256) k_bank_simt(BankArgs a) {
+    griddep_wait();
+    griddep_launch();
     __shared__ int32_t xs[RT][64];
     const int j = blockIdx.x * 256 + threadIdx.x;
     const int r0 = blockIdx.y * RT;
@@ -160,6 +166,8 @@ struct KV {
 __global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t* __restrict__ row_slot,
                         const int32_t* __restrict__ row_pos, int layer, KV kv, int32_t* __restrict__ q16,
                         int32_t* __restrict__ qexp, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
     const int r = blockIdx.x, part = blockIdx.y, lane = threadIdx.x;
     const int H = kv.H, d = H * 64;
     if (r >= rows) return;
@@ -228,6 +236,8 @@ B2_DEV int64_t arrival(int64_t d, const int32_t* __restrict__ ARR, int alen, uin
 
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
+    griddep_wait();
+    griddep_launch();
     extern __shared__ int64_t sc[];           // [pos + 1]
     __shared__ int32_t qs[64];
     __shared__ int64_t red[NW][66];
@@ -337,6 +347,8 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
 // ---------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_race(const int64_t* __restrict__ logits, int ld, const int32_t* __restrict__ rows_map,
                                                int V, int32_t* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
     __shared__ int64_t sv[32];
     __shared__ int si[32];
     const int r = rows_map ? rows_map[blockIdx.x] : blockIdx.x;
@@ -360,6 +372,8 @@ __global__ void __launch_bounds__(1024) k_race(const int64_t* __restrict__ logit
 // ---------------------------------------------------------------------------------------------------------------------
 __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const int32_t* __restrict__ slot_len,
                               const int32_t* __restrict__ slot_tok, int32_t* row_slot, int32_t* row_pos, int32_t* row_tok) {
+    griddep_wait();
+    griddep_launch();
     int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     row_slot[s] = s;
@@ -367,20 +381,41 @@ __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const i
     row_tok[s] = tok_in ? tok_in[s] : slot_tok[s];
 }
 
+// where a decode step's words go: out[s * ld + (slot_len[s] - base[s])], set once per call (k_gen_begin), so one
+// captured step graph serves every call and every position
+struct GenDesc {
+    int32_t* out;
+    int ld;
+};
+
+__global__ void k_gen_begin(int n, const int32_t* __restrict__ slot_len, int32_t* base, GenDesc* desc, int32_t* out, int ld) {
+    griddep_wait();
+    griddep_launch();
+    int s = blockIdx.x * blockDim.x + threadIdx.x;
+    if (s < n) base[s] = slot_len[s];
+    if (s == 0) { desc->out = out; desc->ld = ld; }
+}
+
 // after the race: the word goes straight back in (base2_stream.swift:143-146); stream lengths advance
 __global__ void k_decode_commit(int n, const int32_t* __restrict__ word, int32_t* slot_len, int32_t* slot_tok,
-                                int32_t* tok_out, int ld_out, int col) {
+                                const GenDesc* __restrict__ desc, const int32_t* __restrict__ base) {
+    griddep_wait();
+    griddep_launch();
     int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     int w = word[s];
-    slot_len[s] += 1;
+    int len = slot_len[s];
+    slot_len[s] = len + 1;
     slot_tok[s] = w;
-    if (tok_out) tok_out[(size_t)s * ld_out + col] = w;
+    int32_t* out = desc->out;
+    if (out) out[(size_t)s * desc->ld + (len - base[s])] = w;
 }
 
 // truncate streams back to lens[s] positions (never forward), last_tok[s] fed next
 __global__ void k_rewind(int n, const int32_t* __restrict__ lens, const int32_t* __restrict__ last_tok, int V,
                          int32_t* slot_len, int32_t* slot_tok, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
     int s = blockIdx.x * blockDim.x + threadIdx.x;
     if (s >= n) return;
     int l = lens[s], t = last_tok[s];
@@ -394,6 +429,8 @@ __global__ void k_rewind(int n, const int32_t* __restrict__ lens, const int32_t*
 __global__ void k_prefill_rows(int r0, int rows, const int32_t* __restrict__ row_slot_all,
                                const int32_t* __restrict__ row_pos_all, const int32_t* __restrict__ ids,
                                int32_t* row_slot, int32_t* row_pos, int32_t* row_tok) {
+    griddep_wait();
+    griddep_launch();
     int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= rows) return;
     row_slot[t] = row_slot_all[r0 + t];

@@ -1,12 +1,12 @@
 // b2_tc.cu -- the bank product on tcgen05 tensor cores (kind::i8), exact (see b2_tc.cuh for the identity).
 //
-// One CTA = 128 output columns (the MMA's M, TMEM lanes) x BN rows (the MMA's N, TMEM columns) x a K range.
-// Warp 0 lane 0 streams the four planes of each 128-byte K block into shared memory with TMA (SWIZZLE_128B,
-// K-major), warp 1 lane 0 issues 16 MMAs per K block (4 K steps x {wh.xh, wh.xl, wl.xh, wl.xl}) into three int32
-// accumulators in TMEM, and all four warps read them back (tcgen05.ld) for the epilogue. When the K range is split
-// over CTAs (few tiles, as in a 64-stream decode step), partial piles meet in an int64 buffer by atomic adds (exact
-// in any order) and the last CTA to arrive for a tile finishes it. Every wait is bounded; on a timeout the CTA
-// sets DERR_TIMEOUT, skips its stores, frees its TMEM and returns.
+// A tile = 128 output columns (the MMA's M, TMEM lanes) x 64 rows (the MMA's N, TMEM columns). One thread streams
+// the four planes of each 128-byte K block into shared memory with TMA (SWIZZLE_128B, K-major), one thread issues
+// 16 MMAs per K block (4 K steps x {wh.xh, wh.xl, wl.xh, wl.xl}) into three int32 accumulators in TMEM, and
+// epilogue warps read them back (tcgen05.ld). Two kernels: k_bank_split (decode: few output tiles, the K range split
+// over a thread-block cluster and reduced over DSMEM) and k_bank_tiles (many tiles: persistent, TMEM double-buffered).
+// Every mbarrier wait is bounded; on a timeout the kernel sets DERR_TIMEOUT, stops issuing work, frees its TMEM and
+// returns (the call then reports an error).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -102,159 +102,339 @@ B2_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 B2_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-template <int BN>
-struct Cfg {
-    static constexpr int A = 128 * 128;              // one weight plane of a K block
-    static constexpr int B = BN * 128;               // one row plane of a K block
-    static constexpr int STAGE = 2 * A + 2 * B;
-    static constexpr uint32_t TMEM_COLS = 3 * BN <= 256 ? 256 : 512;
-    // kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, N = BN, M = 128
-    static constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
-};
+// cluster helpers
+B2_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+B2_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+B2_DEV uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+B2_DEV int64_t ld_dsmem(uint32_t addr) {
+    uint64_t v;
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    return (int64_t)v;
+}
+B2_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
+}
+
+constexpr int BN = 64;                               // rows per MMA (the MMA's N)
+constexpr int A_BYTES = 128 * 128;                   // one weight plane of a 128-byte K block
+constexpr int B_BYTES = BN * 128;                    // one row plane of a K block
+constexpr int STAGE = 2 * A_BYTES + 2 * B_BYTES;     // 48 KB
+// kind::i8 instruction descriptor: D s32, A s8, B s8, both K-major, N = 64, M = 128
+constexpr uint32_t IDESC = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
 constexpr int MAX_STAGES = 4;
+constexpr int MAX_SPLIT = 8;      // portable cluster size
+constexpr int MAX_KPS = 3;        // K blocks held by one split CTA
 
 struct TcArgs {
     int nin, nout, rows;
-    int kps;          // K blocks (of 128) per CTA
-    int ksplit;       // CTAs along K per tile
+    int kps;          // K blocks (of 128) per CTA (split) / per tile (tiles)
+    int ksplit;       // CTAs along K per tile (= cluster size)
     int stages;
+    int mtiles, ntiles;
     const int64_t* colcorr;
     const int64_t* rowcorr;
     const int32_t* nsat;
     const int16_t* sat;
     int sat_ld;
     const int16_t* w16;
-    int64_t* pile;
-    uint32_t* counters;
     uint32_t* err;
     EpiArgs epi;
 };
 
-template <int EPI, int BN>
-__global__ void __launch_bounds__(128, 1)
-    k_bank_tc(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
-              const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
-    using C = Cfg<BN>;
+// the 16 MMAs of one K block: 4 K steps x {wh.xh -> A1, wh.xl + wl.xh -> A2, wl.xl -> A3}
+B2_DEV void mma_kblock(uint32_t base, uint32_t tacc, bool first) {
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+        uint64_t ah = sdesc(base + kk * 32), al = sdesc(base + A_BYTES + kk * 32);
+        uint64_t bh = sdesc(base + 2 * A_BYTES + kk * 32), bl = sdesc(base + 2 * A_BYTES + B_BYTES + kk * 32);
+        uint32_t acc = (!first || kk) ? 1u : 0u;
+        mma_i8(tacc + 0 * BN, ah, bh, IDESC, acc);
+        mma_i8(tacc + 1 * BN, ah, bl, IDESC, acc);
+        mma_i8(tacc + 1 * BN, al, bh, IDESC, 1);
+        mma_i8(tacc + 2 * BN, al, bl, IDESC, acc);
+    }
+}
+
+// 65536*A1 + 256*A2 + A3 for 16 rows from TMEM (this warp's lane quadrant, columns n0..n0+15 of each accumulator)
+B2_DEV void tmem_piles16(uint32_t taddr, int64_t (&p)[16]) {
+    uint32_t r1[16], r2[16], r3[16];
+    tmem_ld16(taddr + 0 * BN, r1);
+    tmem_ld16(taddr + 1 * BN, r2);
+    tmem_ld16(taddr + 2 * BN, r3);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 16; q++)
+        p[q] = (int64_t)(int32_t)r1[q] * 65536 + (int64_t)(int32_t)r2[q] * 256 + (int64_t)(int32_t)r3[q];
+}
+
+// everything a finished pile of row n needs besides its column
+struct RowData {
+    int64_t ex, LS, e2, rowc;
+    int32_t nsat, orow;
+};
+template <bool GAUGED>
+B2_DEV RowData load_row(const TcArgs& a, int n) {
+    RowData d{0, 0, 0, 0, 0, n};
+    if (n < a.rows) {
+        d.ex = a.epi.ex[n];
+        if (GAUGED) {
+            d.LS = a.epi.LS[n];
+            d.e2 = __ldg(a.epi.EXP2 + (wsub(0, d.LS) & 0xFFFF));
+        }
+        d.rowc = a.rowcorr[n];
+        d.nsat = a.nsat[n];
+        if (a.epi.out_map) d.orow = a.epi.out_map[n];
+    }
+    return d;
+}
+
+// the finished pile of (row n, column j): corrections, then the bank's epilogue, stored
+template <int EPI>
+B2_DEV void finish(const TcArgs& a, const RowData& r, int n, int j, int64_t pile, int64_t colc, int64_t e_j, int64_t b_j) {
+    pile += colc + r.rowc;
+    for (int u = 0; u < r.nsat; u++) pile += 256 * (int64_t)a.w16[(size_t)a.sat[(size_t)n * a.sat_ld + u] * a.nout + j];
+    int64_t v = epi_value<EPI>(pile, e_j, b_j, r.ex, r.LS, r.e2, a.epi.PHI);
+    int64_t* o = a.epi.out + (size_t)r.orow * a.epi.ldo + j;
+    *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Decode banks (rows <= 64, few output tiles): split-K over a thread-block cluster (1, ksplit, 1). Each CTA holds one
+// or two K blocks (all loaded at once; the weights before the dependency wait), keeps its partial int64 tile in its
+// own shared memory, and after a cluster barrier reduces a 1/ksplit slice of the rows over DSMEM and finishes it.
+// 256 threads: warp 0 lane 0 = TMA, warp 1 lane 0 = MMA, warps 2-7 stage the rows, all 8 warps in the epilogue.
+// ---------------------------------------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(256, 1)
+    k_bank_split(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
+                 const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
     extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], acc_bar;
+    __shared__ uint64_t full_bar[MAX_KPS], acc_bar;
     __shared__ uint32_t tmem_slot;
-    __shared__ int s_abort, s_last;
+    __shared__ int s_dead, s_abort;
+    __shared__ RowData s_row[BN];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    int64_t* P = (int64_t*)smem;   // partial tile [BN][128], over the stage memory once the MMAs are done
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x, ks = blockIdx.y, nt = blockIdx.z;
-    const int S = a.stages;
-    // after any timeout in this or an earlier launch, do nothing (the call is already reported as failed)
-    if (*(volatile uint32_t*)a.err & DERR_TIMEOUT) return;
+    const int mt = blockIdx.x, ks = blockIdx.y;
+    const uint32_t crank = cluster_rank();
 
     if (tid == 0) {
-        for (int s = 0; s < S; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int kb = 0; kb < a.kps; kb++) mbar_init(&full_bar[kb], 1);
         mbar_init(&acc_bar, 1);
         s_abort = 0;
+        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
         fence_mbar_init();
     }
-    if (warp == 0) tmem_alloc(&tmem_slot, C::TMEM_COLS);
+    if (warp == 0) tmem_alloc(&tmem_slot, 256);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
-
-    if (warp == 0 && lane == 0) {
-        // ---- TMA producer ----
+    const bool dead = s_dead != 0;
+    if (tid == 0 && !dead) {          // weights: independent of earlier kernels
         for (int kb = 0; kb < a.kps; kb++) {
-            int s = kb % S;
-            if (kb >= S && !mbar_wait(&empty_bar[s], ((kb / S) - 1) & 1, a.err)) { s_abort = 1; break; }
-            uint8_t* st = smem + s * C::STAGE;
+            uint8_t* st = smem + kb * STAGE;
             int kx = (ks * a.kps + kb) * 128;
-            mbar_expect_tx(&full_bar[s], C::STAGE);
-            tma_load_2d(st, &mwh, &full_bar[s], kx, mt * 128);
-            tma_load_2d(st + C::A, &mwl, &full_bar[s], kx, mt * 128);
-            tma_load_2d(st + 2 * C::A, &mxh, &full_bar[s], kx, nt * BN);
-            tma_load_2d(st + 2 * C::A + C::B, &mxl, &full_bar[s], kx, nt * BN);
+            mbar_expect_tx(&full_bar[kb], STAGE);
+            tma_load_2d(st, &mwh, &full_bar[kb], kx, mt * 128);
+            tma_load_2d(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128);
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---- MMA issuer ----
+    }
+    griddep_wait();
+    griddep_launch();
+    if (tid == 0 && !dead) {
         for (int kb = 0; kb < a.kps; kb++) {
-            int s = kb % S;
-            if (!mbar_wait(&full_bar[s], (kb / S) & 1, a.err)) { s_abort = 1; break; }
+            uint8_t* st = smem + kb * STAGE;
+            int kx = (ks * a.kps + kb) * 128;
+            tma_load_2d(st + 2 * A_BYTES, &mxh, &full_bar[kb], kx, 0);
+            tma_load_2d(st + 2 * A_BYTES + B_BYTES, &mxl, &full_bar[kb], kx, 0);
+        }
+    } else if (warp == 1 && lane == 0 && !dead) {
+        for (int kb = 0; kb < a.kps; kb++) {
+            if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
             tc_fence_after();
-            uint32_t base = saddr(smem + s * C::STAGE);
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                uint64_t ah = sdesc(base + kk * 32), al = sdesc(base + C::A + kk * 32);
-                uint64_t bh = sdesc(base + 2 * C::A + kk * 32), bl = sdesc(base + 2 * C::A + C::B + kk * 32);
-                uint32_t acc = (kb | kk) != 0;
-                mma_i8(tmem + 0 * BN, ah, bh, C::IDESC, acc);   // A1 += wh . xh
-                mma_i8(tmem + 1 * BN, ah, bl, C::IDESC, acc);   // A2 += wh . xl
-                mma_i8(tmem + 1 * BN, al, bh, C::IDESC, 1);     // A2 += wl . xh
-                mma_i8(tmem + 2 * BN, al, bl, C::IDESC, acc);   // A3 += wl . xl
-            }
-            mma_commit(&empty_bar[s]);
+            mma_kblock(saddr(smem + kb * STAGE), tmem, kb == 0);
         }
         mma_commit(&acc_bar);
+    } else if (warp >= 2) {
+        for (int q = tid - 64; q < BN; q += 192) s_row[q] = load_row<GAUGED>(a, q);
     }
     __syncwarp();
-
-    // ---- epilogue: thread = output column m of the tile; TMEM columns = rows ----
-    bool ok = mbar_wait(&acc_bar, 0, a.err);
+    __syncthreads();
+    const bool ok = !dead && mbar_wait(&acc_bar, 0, a.err);
     tc_fence_after();
     __syncthreads();
-    if (!ok || s_abort) goto teardown;
-    {
-        const int m = warp * 32 + lane;
-        const int j = mt * 128 + m;
-        const bool jv = j < a.nout;
-        const int64_t colc = (ks == 0 && jv) ? a.colcorr[j] : 0;
-        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    const bool go = ok && !s_abort;
+    if (go) {
+        // this warp's quadrant (TMEM lanes = output columns) and row half
+        const int m = (warp & 3) * 32 + lane, r0 = (warp >> 2) * 32;
+        const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16);
 #pragma unroll 1
-        for (int n0 = 0; n0 < BN; n0 += 16) {
-            uint32_t r1[16], r2[16], r3[16];
-            tmem_ld16(trow + 0 * BN + n0, r1);
-            tmem_ld16(trow + 1 * BN + n0, r2);
-            tmem_ld16(trow + 2 * BN + n0, r3);
-            tmem_wait_ld();
+        for (int c = 0; c < 2; c++) {
+            int64_t p[16];
+            tmem_piles16(trow + r0 + 16 * c, p);
 #pragma unroll
-            for (int q = 0; q < 16; q++) {
-                const int n = nt * BN + n0 + q;
-                if (n >= a.rows || !jv) continue;
-                int64_t pile = (int64_t)(int32_t)r1[q] * 65536 + (int64_t)(int32_t)r2[q] * 256 + (int64_t)(int32_t)r3[q];
-                if (ks == 0) {
-                    pile += colc + a.rowcorr[n];
-                    const int ns = a.nsat[n];
-                    for (int u = 0; u < ns; u++)
-                        pile += 256 * (int64_t)a.w16[(size_t)a.sat[(size_t)n * a.sat_ld + u] * a.nout + j];
-                }
-                if (a.ksplit == 1)
-                    epi_store<EPI>(a.epi, n, j, pile);
-                else
-                    atomicAdd((unsigned long long*)&a.pile[(size_t)n * PILE_COLS + j], (unsigned long long)pile);
-            }
-        }
-        if (a.ksplit > 1) {
-            __threadfence();
-            __syncthreads();
-            const int tile = nt * gridDim.x + mt;
-            if (tid == 0) s_last = atomicAdd(&a.counters[tile], 1u) == (uint32_t)(a.ksplit - 1);
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                if (jv) {
-                    for (int q = 0; q < BN; q++) {
-                        const int n = nt * BN + q;
-                        if (n >= a.rows) break;
-                        int64_t* p = &a.pile[(size_t)n * PILE_COLS + j];
-                        int64_t v = (int64_t)__ldcg((const long long*)p);
-                        *p = 0;
-                        epi_store<EPI>(a.epi, n, j, v);
-                    }
-                }
-                if (tid == 0) a.counters[tile] = 0;
-            }
+            for (int q = 0; q < 16; q++) P[(r0 + 16 * c + q) * 128 + m] = p[q];
         }
     }
-teardown:
+    tc_fence_before();
+    cluster_sync();                   // every CTA's partial tile is written
+    {
+        const int ksz = a.ksplit;
+        const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
+        const int m = tid & 127;
+        const int j = mt * 128 + m;
+        const bool jv = j < a.nout && go;
+        const int64_t colc = jv ? a.colcorr[j] : 0;
+        const int64_t e_j = jv ? (int64_t)a.epi.e[j] : 0, b_j = jv ? a.epi.b[j] : 0;
+        uint32_t peer[MAX_SPLIT];
+        const uint32_t pbase = saddr(P);
+#pragma unroll
+        for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
+        for (int n = n0 + (tid >> 7); n < n1; n += 2) {
+            if (n >= a.rows || !jv) continue;
+            const uint32_t off = (uint32_t)(n * 128 + m) * 8;
+            int64_t v = 0;
+#pragma unroll
+            for (int p = 0; p < MAX_SPLIT; p++)
+                if (p < ksz) v = wadd(v, ld_dsmem(peer[p] + off));
+            finish<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
+        }
+    }
+    cluster_sync();                   // no CTA leaves while a peer may still read its partial tile
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 256);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Many tiles (the head; prompt passes): a persistent loop over 128-column x 64-row tiles. TMEM holds two accumulator
+// sets (columns 0 and 256) so the epilogue of one tile overlaps the loads and MMAs of the next; a ring of `stages`
+// K blocks feeds the MMAs. 384 threads: warp 0 lane 0 = TMA, warp 1 lane 0 = MMA, warps 4-11 = epilogue
+// (warp w reads TMEM lane quadrant w % 4, rows 32 * ((w - 4) / 4) .. + 32 of the tile).
+// ---------------------------------------------------------------------------------------------------------------------
+template <int EPI>
+__global__ void __launch_bounds__(384, 1)
+    k_bank_tiles(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
+                 const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    constexpr int NEPI = 8;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], tfull[2], tempty[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_dead;
+    __shared__ RowData s_row[NEPI][32];
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int S = a.stages, KB = a.kps;
+    const int total = a.mtiles * a.ntiles;
+    const int G = gridDim.x;
+    const int my_tiles = blockIdx.x < total ? (total - blockIdx.x + G - 1) / G : 0;
+    const int nkb = my_tiles * KB;
+    const int npre = nkb < S ? nkb : S;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) { mbar_init(&full_bar[s], 1); mbar_init(&empty_bar[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NEPI); }
+        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(&tmem_slot, 512);
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, C::TMEM_COLS);
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const bool dead = s_dead != 0;
+    if (tid == 0 && !dead) {          // the first weights: independent of earlier kernels
+        for (int g = 0; g < npre; g++) {
+            const int t = blockIdx.x + (g / KB) * G, kx = (g % KB) * 128;
+            uint8_t* st = smem + g * STAGE;
+            mbar_expect_tx(&full_bar[g], STAGE);
+            tma_load_2d(st, &mwh, &full_bar[g], kx, (t % a.mtiles) * 128);
+            tma_load_2d(st + A_BYTES, &mwl, &full_bar[g], kx, (t % a.mtiles) * 128);
+        }
+    }
+    griddep_wait();
+    griddep_launch();
+    if (dead) {
+        // nothing was issued; fall through to the teardown
+    } else if (warp == 0) {
+        if (lane == 0) {
+            for (int g = 0; g < nkb; g++) {
+                const int s = g % S, t = blockIdx.x + (g / KB) * G, kx = (g % KB) * 128;
+                const int mt = t % a.mtiles, nt = t / a.mtiles;
+                uint8_t* st = smem + s * STAGE;
+                if (g >= npre) {
+                    if (!mbar_wait(&empty_bar[s], ((g / S) - 1) & 1, a.err)) break;
+                    mbar_expect_tx(&full_bar[s], STAGE);
+                    tma_load_2d(st, &mwh, &full_bar[s], kx, mt * 128);
+                    tma_load_2d(st + A_BYTES, &mwl, &full_bar[s], kx, mt * 128);
+                }
+                tma_load_2d(st + 2 * A_BYTES, &mxh, &full_bar[s], kx, nt * BN);
+                tma_load_2d(st + 2 * A_BYTES + B_BYTES, &mxl, &full_bar[s], kx, nt * BN);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; i++) {
+                const int b = i & 1;
+                if (i >= 2 && !mbar_wait(&tempty[b], ((i >> 1) - 1) & 1, a.err)) break;
+                tc_fence_after();
+                for (int kk = 0; kk < KB; kk++) {
+                    const int g = i * KB + kk, s = g % S;
+                    if (!mbar_wait(&full_bar[s], (g / S) & 1, a.err)) { ok = false; break; }
+                    tc_fence_after();
+                    mma_kblock(saddr(smem + s * STAGE), tmem + b * 256, kk == 0);
+                    mma_commit(&empty_bar[s]);
+                }
+                mma_commit(&tfull[b]);
+            }
+        }
+    } else if (warp >= 4) {
+        const int e = warp - 4, quad = warp & 3, r0 = (e >> 2) * 32;
+        const uint32_t tq = (uint32_t)(quad * 32) << 16;
+        for (int i = 0; i < my_tiles; i++) {
+            const int b = i & 1, t = blockIdx.x + i * G;
+            const int mt = t % a.mtiles, nt = t / a.mtiles;
+            // this warp's 32 rows of the tile, staged per warp while the accumulators fill
+            s_row[e][lane] = load_row<GAUGED>(a, nt * BN + r0 + lane);
+            const int j = mt * 128 + quad * 32 + lane;
+            const bool jv = j < a.nout;
+            const int64_t colc = jv ? a.colcorr[j] : 0;
+            const int64_t e_j = jv ? (int64_t)a.epi.e[j] : 0, b_j = jv ? a.epi.b[j] : 0;
+            __syncwarp();
+            if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
+            tc_fence_after();
+#pragma unroll 1
+            for (int c = 0; c < 2; c++) {
+                int64_t p[16];
+                tmem_piles16(tmem + b * 256 + tq + r0 + 16 * c, p);
+#pragma unroll
+                for (int q = 0; q < 16; q++) {
+                    const int rr = 16 * c + q, n = nt * BN + r0 + rr;
+                    if (n < a.rows && jv) finish<EPI>(a, s_row[e][rr], n, j, p[q], colc, e_j, b_j);
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
@@ -312,35 +492,63 @@ int make_map(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld, 
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
 
-template <int EPI, int BN>
-cudaError_t launch(dim3 grid, size_t smem, cudaStream_t st, const TcBank& t, const TcMap& xh, const TcMap& xl, const TcArgs& a) {
-    static bool attr = false;
-    if (!attr) {
-        cudaError_t e = cudaFuncSetAttribute(k_bank_tc<EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (e != cudaSuccess) return e;
-        attr = true;
+template <class K>
+cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y, cudaStream_t st, bool pdl,
+                     const TcBank& t, const TcMap& xh, const TcMap& xl, const TcArgs& a) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
     }
-    k_bank_tc<EPI, BN><<<grid, 128, smem, st>>>(*reinterpret_cast<const CUtensorMap*>(t.map_wh.bytes),
-                                                 *reinterpret_cast<const CUtensorMap*>(t.map_wl.bytes),
-                                                 *reinterpret_cast<const CUtensorMap*>(xh.bytes),
-                                                 *reinterpret_cast<const CUtensorMap*>(xl.bytes), a);
-    return cudaGetLastError();
+    if (cluster_y > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = cluster_y;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kernel, *reinterpret_cast<const CUtensorMap*>(t.map_wh.bytes),
+                              *reinterpret_cast<const CUtensorMap*>(t.map_wl.bytes),
+                              *reinterpret_cast<const CUtensorMap*>(xh.bytes), *reinterpret_cast<const CUtensorMap*>(xl.bytes), a);
 }
 
-template <int BN>
-cudaError_t launch_epi(int epi, dim3 grid, size_t smem, cudaStream_t st, const TcBank& t, const TcMap& xh, const TcMap& xl,
-                       const TcArgs& a) {
-    switch (epi) {
-        case EPI_GAUGED: return launch<EPI_GAUGED, BN>(grid, smem, st, t, xh, xl, a);
-        case EPI_GAUGED_EDGE: return launch<EPI_GAUGED_EDGE, BN>(grid, smem, st, t, xh, xl, a);
-        case EPI_PLAIN_ADD: return launch<EPI_PLAIN_ADD, BN>(grid, smem, st, t, xh, xl, a);
-        default: return launch<EPI_PLAIN_OUT, BN>(grid, smem, st, t, xh, xl, a);
+#define B2_EPI_SWITCH(EPIV, CALL)                                      \
+    switch (EPIV) {                                                    \
+        case EPI_GAUGED: { constexpr int E = EPI_GAUGED; CALL; }           \
+        case EPI_GAUGED_EDGE: { constexpr int E = EPI_GAUGED_EDGE; CALL; } \
+        case EPI_PLAIN_ADD: { constexpr int E = EPI_PLAIN_ADD; CALL; }     \
+        default: { constexpr int E = EPI_PLAIN_OUT; CALL; }                \
     }
-}
 
 }  // namespace
 
 int tc_min_rows_default() { return 1; }
+
+// shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
+int tc_init() {
+    void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
+                     (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>};
+    void* tiles[] = {(void*)k_bank_tiles<EPI_GAUGED>, (void*)k_bank_tiles<EPI_GAUGED_EDGE>,
+                     (void*)k_bank_tiles<EPI_PLAIN_ADD>, (void*)k_bank_tiles<EPI_PLAIN_OUT>};
+    for (void* f : split) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
+        if (e != cudaSuccess) return (int)e;
+    }
+    for (void* f : tiles) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_STAGES * STAGE + 1024);
+        if (e != cudaSuccess) return (int)e;
+    }
+    return 0;
+}
 
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
     tc_bank_free(t);
@@ -384,38 +592,32 @@ int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err) {
     if ((e = cudaMalloc(&r.sat, n * sizeof(int16_t))) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&r.rowcorr, sizeof(int64_t) * r.rows_cap)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&r.nsat, sizeof(int32_t) * r.rows_cap)) != cudaSuccess) return (int)e;
-    if ((e = cudaMalloc(&r.pile, sizeof(int64_t) * PILE_ROWS * PILE_COLS)) != cudaSuccess) return (int)e;
-    if ((e = cudaMalloc(&r.counters, sizeof(uint32_t) * MAX_COUNTERS)) != cudaSuccess) return (int)e;
     cudaMemset(r.xh, 0, n);
     cudaMemset(r.xl, 0, n);
-    cudaMemset(r.pile, 0, sizeof(int64_t) * PILE_ROWS * PILE_COLS);
-    cudaMemset(r.counters, 0, sizeof(uint32_t) * MAX_COUNTERS);
     cudaMemset(r.nsat, 0, sizeof(int32_t) * r.rows_cap);
     r.nmaps = 0;
     return (int)cudaGetLastError();
 }
 
 void tc_rows_free(TcRows& r) {
-    void* ps[] = {r.xh, r.xl, r.sat, r.rowcorr, r.nsat, r.pile, r.counters};
+    void* ps[] = {r.xh, r.xl, r.sat, r.rowcorr, r.nsat};
     for (void* p : ps)
         if (p) cudaFree(p);
     r.xh = r.xl = nullptr;
     r.sat = nullptr;
-    r.rowcorr = r.pile = nullptr;
+    r.rowcorr = nullptr;
     r.nsat = nullptr;
-    r.counters = nullptr;
     r.nmaps = 0;
 }
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st) {
+            cudaStream_t st, bool pdl) {
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
-    const int BN = rows <= 64 ? 64 : 128;
-    // the row planes' tensor maps for (K = nin, box height BN), made once
+    // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
     int mi = -1;
     for (int i = 0; i < r.nmaps; i++)
-        if (r.maps[i].k == t.nin && r.maps[i].bn == BN) mi = i;
+        if (r.maps[i].k == t.nin) mi = i;
     if (mi < 0) {
         if (r.nmaps == 4) return (int)cudaErrorInvalidValue;
         mi = r.nmaps;
@@ -427,35 +629,46 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         r.nmaps++;
     }
     const int mtiles = t.nout_pad / 128, ntiles = (rows + BN - 1) / BN, kb = t.nin / 128;
-    int ksplit = 1;
-    if (rows <= PILE_ROWS && t.nout <= PILE_COLS && mtiles * ntiles < 148 && mtiles * ntiles <= MAX_COUNTERS) {
-        int want = (2 * 148 + mtiles * ntiles - 1) / (mtiles * ntiles);
-        for (int d = 1; d <= kb; d++)
-            if (kb % d == 0 && d <= want) ksplit = d;
-    }
     TcArgs a{};
     a.nin = t.nin;
     a.nout = t.nout;
     a.rows = rows;
-    a.ksplit = ksplit;
-    a.kps = kb / ksplit;
-    a.stages = a.kps < (BN == 64 ? 4 : 3) ? a.kps : (BN == 64 ? 4 : 3);
+    a.mtiles = mtiles;
+    a.ntiles = ntiles;
     a.colcorr = t.colcorr;
     a.rowcorr = r.rowcorr;
     a.nsat = r.nsat;
     a.sat = r.sat;
     a.sat_ld = r.kmax;
     a.w16 = t.w16;
-    a.pile = r.pile;
-    a.counters = r.counters;
     a.err = r.err;
     a.epi = EpiArgs{ex, LS, e, b, out, ldo, out_map, EXP2, PHI};
-    dim3 grid(mtiles, ksplit, ntiles);
+    // split-K over a cluster when there is one row tile and too few output tiles to fill the GPU
+    int ksplit = 1;
+    if (ntiles == 1 && mtiles < 148)
+        for (int d = MAX_SPLIT; d >= 2; d--)
+            if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
     cudaError_t err;
-    if (BN == 64)
-        err = launch_epi<64>(epi, grid, (size_t)a.stages * Cfg<64>::STAGE + 1024, st, t, r.maps[mi].h, r.maps[mi].l, a);
-    else
-        err = launch_epi<128>(epi, grid, (size_t)a.stages * Cfg<128>::STAGE + 1024, st, t, r.maps[mi].h, r.maps[mi].l, a);
+    if (ksplit > 1) {
+        a.ksplit = ksplit;
+        a.kps = kb / ksplit;
+        a.stages = a.kps;
+        size_t smem = (size_t)(a.kps > 2 ? a.kps : 2) * STAGE + 1024;   // >= the 64 KB partial tile
+        dim3 grid(mtiles, ksplit, 1);
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_split<E>, grid, dim3(256), smem, ksplit, st, pdl, t, r.maps[mi].h,
+                                          r.maps[mi].l, a);
+                      break)
+    } else {
+        a.ksplit = 1;
+        a.kps = kb;
+        a.stages = MAX_STAGES;
+        size_t smem = (size_t)MAX_STAGES * STAGE + 1024;
+        int total = mtiles * ntiles;
+        dim3 grid(total < 148 ? total : 148);
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_tiles<E>, grid, dim3(384), smem, 1, st, pdl, t, r.maps[mi].h,
+                                          r.maps[mi].l, a);
+                      break)
+    }
     return (int)err;
 }
 

@@ -27,7 +27,7 @@ struct TcBank {
     TcMap map_wh, map_wl;
 };
 
-// Row-side buffers: the activations' planes, their corrections, the split-K accumulation.
+// Row-side buffers: the activations' planes and their corrections.
 struct TcRows {
     int rows_cap = 0, kmax = 0;
     int8_t* xh = nullptr;       // [rows_cap][kmax]
@@ -35,22 +35,20 @@ struct TcRows {
     int64_t* rowcorr = nullptr; // [rows_cap]  128*sum_i x_repr[i]
     int32_t* nsat = nullptr;    // [rows_cap]  entries equal to +32768
     int16_t* sat = nullptr;     // [rows_cap][kmax] their indices
-    int64_t* pile = nullptr;    // split-K accumulation [PILE_ROWS][PILE_COLS]
-    uint32_t* counters = nullptr;  // split-K arrival counters
     uint32_t* err = nullptr;    // device error word (shared with the engine)
     struct { int k, bn; TcMap h, l; } maps[4];
     int nmaps = 0;
 };
 
-constexpr int PILE_ROWS = 256, PILE_COLS = 4096, MAX_COUNTERS = 4096;
 
 int tc_min_rows_default();
+int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
 void tc_bank_free(TcBank& t);
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st);
+            cudaStream_t st, bool pdl);
 
 }  // namespace b2
