@@ -92,7 +92,8 @@ int b2_generate(b2_handle* h, int32_t n_streams, int32_t n_steps, int32_t* token
 int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok_out);
 
 /* One bank on given rows, for unit parity (base2.py:62-76): mode 0 = gauged_bank, 1 = gauged_bank then edge,
- * 2 = plain_bank. X [rows][nin] int64, out [rows][nout] int64 (device pointers). */
+ * 2 = plain_bank. X [rows][nin] int64, out [rows][nout] int64 (device pointers). mode | 8 runs the decode step's
+ * fused kernel instead (rows <= 64, layer banks only; mode 1 only on fc banks). */
 int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode, void* stream);
 
 /* Truncate streams 0..n_streams-1 back to lens[s] positions with last_tok[s] as the word to feed next (device

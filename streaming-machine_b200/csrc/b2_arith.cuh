@@ -20,6 +20,7 @@ B2_DEV int64_t np_rsh(int64_t x, int64_t s) { return s >= 64 ? (x < 0 ? -1 : 0) 
 
 // base2.py:18-22
 B2_DEV int64_t rshift(int64_t x, int64_t s) {
+    if (s > 0 && s < 64) return (int64_t)((uint64_t)x + (1ull << (s - 1))) >> s;   // the common case, same bits
     int64_t up = np_lsh(x, s < 0 ? -s : 0);
     int64_t sp = s > 0 ? s : 0;
     int64_t half = sp > 0 ? np_lsh(1, sp - 1) : 0;

@@ -58,6 +58,9 @@ struct b2_handle {
     int64_t* LS = nullptr;
     TcRows tcr{};
     int32_t *head_rows = nullptr, *race_out = nullptr;
+    uint64_t* row_or = nullptr;  // decode: per bank input, the OR of |x| over each row ([4L][FUSED_ROWS])
+    int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
+    int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
     int64_t* logits = nullptr;   // [n_slots][vocab]
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
@@ -85,6 +88,9 @@ struct b2_handle {
 };
 
 namespace {
+
+constexpr int FUSED_ROWS = 64;
+constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
 
 int fail(b2_handle* h, int code, const char* fmt, ...) {
     char buf[512];
@@ -231,6 +237,17 @@ int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, in
                   gauge, h->LOG2, h->log768, h->eps40, pl);
 }
 
+// the arrival for `rows` rows at layer l: bulk-copy kernel while a stream's keys fit in shared memory
+int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st) {
+    AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
+                or_out};
+    const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
+    if (h->att_bulk && bulk <= ATT_BULK_MAX)
+        return launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4>, dim3(rows, h->cfg.n_head), 128, bulk, st, aa);
+    return launch(h, B2_PROF_ATTEND, "attend", k_attend<4>, dim3(rows, h->cfg.n_head), 128, sizeof(int64_t) * h->max_ctx,
+                  st, aa);
+}
+
 // ---- all layers + head for the rows in the row table --------------------------------------------------------------
 // head rows: rows [0, nhead) of `hrows` (row indices) are scored; their logits go to out rows hmap (slot ids).
 int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
@@ -247,9 +264,7 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
         if ((rc = launch(h, B2_PROF_HEADS, "heads", k_heads, dim3(rows, 3 * H), 32, 0, st, h->QKV, rows, h->row_slot,
                          h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err)))
             return rc;
-        AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err};
-        if ((rc = launch(h, B2_PROF_ATTEND, "attend", k_attend<4>, dim3(rows, H), 128, sizeof(int64_t) * h->max_ctx, st, aa)))
-            return rc;
+        if ((rc = run_attend(h, rows, l, nullptr, st))) return rc;
         if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
         if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
         if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
@@ -262,6 +277,74 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
     if ((rc = run_bank(h, 4 * L, EPI_GAUGED, nhead, logits, c.vocab, hmap, st))) return rc;
     return launch(h, B2_PROF_RACE, "race", k_race, nhead, 1024, 0, st, logits, c.vocab, hmap, c.vocab, words_by_slot);
 }
+
+// ---- a decode step with the fused banks (n <= FUSED_ROWS streams, row r = slot r) ---------------------------------------
+FusedArgs fused_args(b2_handle* h, const DevBank& bk, const int64_t* X, const uint64_t* xor_in, uint64_t* or_out,
+                     int64_t* out, int ldo, int n) {
+    FusedArgs a{};
+    a.rows = n;
+    a.X = X;
+    a.xor_in = xor_in;
+    a.or_out = or_out;
+    a.e = bk.e;
+    a.b = bk.b;
+    a.out = out;
+    a.ldo = ldo;
+    a.EXP2 = h->EXP2;
+    a.PHI = h->PHI;
+    a.LOG2 = h->LOG2;
+    a.log768 = h->log768;
+    a.eps40 = h->eps40;
+    a.row_slot = h->row_slot;
+    a.row_pos = h->row_pos;
+    a.kv = h->kv;
+    a.err = h->d_err;
+    return a;
+}
+
+int run_fused(b2_handle* h, int bi, int epi, FusedArgs a, cudaStream_t st) {
+    prof_begin(h, B2_PROF_BANK, st);
+    int rc = tc_fused(h->banks[bi].tc, epi, a, st, h->pdl && !h->prof.timing);
+    prof_end(h, B2_PROF_BANK, st);
+    if (rc) return fail(h, B2_ERR_CUDA, "fused bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
+    return B2_OK;
+}
+
+int run_decode(b2_handle* h, int n, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
+    uint64_t* OR = h->row_or;   // slot q of the step: OR[q * FUSED_ROWS + row]
+    int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
+                    h->row_slot, h->row_pos, h->row_tok, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, OR, 4 * L, FUSED_ROWS,
+                    h->d_err);
+    if (rc) return rc;
+    for (int l = 0; l < L; l++) {
+        uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
+        FusedArgs q = fused_args(h, h->banks[4 * l], h->R, o0, nullptr, nullptr, 0, n);
+        q.layer = l;
+        q.q16 = h->q16;
+        q.qexp = h->qexp;
+        if ((rc = run_fused(h, 4 * l, EPI_GAUGED, q, st))) return rc;
+        if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st))) return rc;
+        if ((rc = run_fused(h, 4 * l + 1, EPI_PLAIN_ADD,
+                            fused_args(h, h->banks[4 * l + 1], h->ATT, o0 + FUSED_ROWS, o0 + 2 * FUSED_ROWS, h->R, d, n), st)))
+            return rc;
+        if ((rc = run_fused(h, 4 * l + 2, EPI_GAUGED_EDGE,
+                            fused_args(h, h->banks[4 * l + 2], h->R, o0 + 2 * FUSED_ROWS, o0 + 3 * FUSED_ROWS, h->HID, F, n), st)))
+            return rc;
+        uint64_t* next = l + 1 < L ? o0 + 4 * FUSED_ROWS : nullptr;
+        if ((rc = run_fused(h, 4 * l + 3, EPI_PLAIN_ADD,
+                            fused_args(h, h->banks[4 * l + 3], h->HID, o0 + 3 * FUSED_ROWS, next, h->R, d, n), st)))
+            return rc;
+    }
+    if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
+    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab, (const int32_t*)nullptr,
+                  c.vocab, h->race_out);
+}
+
+bool fused_avail(const b2_handle* h, int n) { return h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS; }
+bool fused_ok(const b2_handle* h, int n) { return h->fused && fused_avail(h, n); }
 
 int ensure_ready(b2_handle* h) {
     if (!h) return B2_ERR_ARG;
@@ -309,7 +392,13 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     h->banks.resize(4 * cfg->n_layer + 1);
     if (const char* v = getenv("B2_PDL")) h->pdl = atoi(v);
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
+    if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
+    if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
+    if (cudaFuncSetAttribute(k_attend_bulk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
+        delete h;
+        return B2_ERR_CUDA;
+    }
     if (dalloc(h, &h->d_err, 1)) { delete h; return B2_ERR_NOMEM; }
     cudaMemset(h->d_err, 0, sizeof(uint32_t));
     *out = h;
@@ -412,7 +501,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+    void* old[] = {h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
@@ -422,13 +511,16 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     dfree(h, h->gen_base);
     h->n_slots = 0;
     const int L = c.n_layer, H = c.n_head, d = c.d_model, F = c.d_ff;
-    size_t nkv = (size_t)n_streams * L * H * max_ctx;
+    const int ctx_stride = (max_ctx + 15) / 16 * 16;
+    size_t nkv = (size_t)n_streams * L * H * ctx_stride;
     int rc;
-    h->kv.L = L; h->kv.H = H; h->kv.ctx = max_ctx;
+    h->kv.L = L; h->kv.H = H; h->kv.ctx = ctx_stride; h->kv.lim = max_ctx;
     if ((rc = dalloc(h, &h->kv.k, nkv * 64))) return rc;
     if ((rc = dalloc(h, &h->kv.kmask, nkv))) return rc;
     if ((rc = dalloc(h, &h->kv.kexp, nkv))) return rc;
     if ((rc = dalloc(h, &h->kv.v, nkv * 64))) return rc;
+    if ((rc = dalloc(h, &h->row_or, (size_t)4 * L * FUSED_ROWS))) return rc;
+    CK(cudaMemset(h->row_or, 0, sizeof(uint64_t) * 4 * L * FUSED_ROWS));
     if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_base, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_desc, 1))) return rc;
@@ -530,6 +622,12 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
 int step_core(b2_handle* h, int n, cudaStream_t st) {
+    if (fused_ok(h, n)) {
+        int rc = run_decode(h, n, st);
+        if (rc) return rc;
+        return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
+                      h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
+    }
     int rc = launch(h, B2_PROF_OTHER, "decode_rows", k_decode_rows, (n + 127) / 128, 128, 0, st, n, (const int32_t*)nullptr,
                     h->slot_len, h->slot_tok, h->row_slot, h->row_pos, h->row_tok);
     if (rc) return rc;
@@ -613,10 +711,22 @@ int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int6
     int rc = ensure_ready(h);
     if (rc) return rc;
     int bi = bank_index(h, name);
+    const int fusedm = mode & 8;
+    mode &= 7;
     if (bi < 0 || !X || !out || rows < 1 || rows > h->max_rows || mode < 0 || mode > 2)
         return fail(h, B2_ERR_ARG, "b2_bank: bad argument");
     cudaStream_t st = (cudaStream_t)stream;
     const DevBank& bk = h->banks[bi];
+    if (fusedm) {
+        // the fused decode kernel on its own: rows <= 64, not the head, q/k/v values returned (no key/value append)
+        if (rows > FUSED_ROWS || bi == 4 * h->cfg.n_layer || !fused_avail(h, rows) || (mode == 1) != (bi % 4 == 2))
+            return fail(h, B2_ERR_ARG, "b2_bank: the fused kernel takes <= %d rows of a layer bank", FUSED_ROWS);
+        uint64_t* xor_in = h->row_or;
+        if ((rc = launch(h, B2_PROF_QUANT, "row_or", k_row_or, rows, 256, 0, st, X, bk.nin, rows, xor_in))) return rc;
+        if (mode == 2) CK(cudaMemsetAsync(out, 0, sizeof(int64_t) * rows * bk.nout, st));
+        FusedArgs a = fused_args(h, bk, X, xor_in, nullptr, out, bk.nout, rows);
+        return run_fused(h, bi, mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_ADD), a, st);
+    }
     if ((rc = run_quant(h, X, bk.nin, nullptr, rows, mode < 2, st))) return rc;
     int epi = mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_OUT);
     return run_bank(h, bi, epi, rows, out, bk.nout, nullptr, st);

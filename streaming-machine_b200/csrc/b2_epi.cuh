@@ -17,6 +17,21 @@ enum : uint32_t {
 
 B2_DEV void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
 
+// the per-stream key/value store (one per engine)
+struct KV {
+    int16_t* k;        // [slot][L][H][ctx][64]
+    uint64_t* kmask;   // [slot][L][H][ctx]  bit t: k16[t] == +32768
+    int32_t* kexp;     // [slot][L][H][ctx]
+    int32_t* v;        // [slot][L][H][ctx][64]
+    int L, H, ctx;     // ctx: the positions' stride (a multiple of 16, so every (slot, layer, head) run is 16-byte aligned)
+    int lim;           // positions actually allocated to a stream (max_ctx); a position at or past it is an error
+};
+
+// position of (slot, layer, head, pos) in the key/value store: [slot][layer][head][pos]
+B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int ctx) {
+    return (((size_t)slot * L + layer) * H + head) * (size_t)ctx + pos;
+}
+
 enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3 };
 
 // what a bank does with a finished pile (row r, output column j)

@@ -6,13 +6,10 @@
 #include <stdint.h>
 #include "b2_arith.cuh"
 #include "b2_epi.cuh"
+#include "b2_ptx.cuh"
 
 namespace b2 {
 
-// position of (slot, layer, head, pos) in the key/value store: [slot][layer][head][pos]
-B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int ctx) {
-    return (((size_t)slot * L + layer) * H + head) * (size_t)ctx + pos;
-}
 
 // ---------------------------------------------------------------------------------------------------------------------
 // embedding: R = wte[tok] + wpe[pos] (base2.py:103; the Metal engine's nextin, base2_stream.swift:143-146)
@@ -155,13 +152,6 @@ __global__ void __launch_bounds__(256) k_bank_simt(BankArgs a) {
 // one warp per (row, part of 3H). q16 -> per-row buffer; k16 + exponent -> key store (int16, with a bit mask of
 // the entries equal to +32768, which int16 cannot hold); v -> value store as int32 (checked).
 // ---------------------------------------------------------------------------------------------------------------------
-struct KV {
-    int16_t* k;        // [slot][L][H][ctx][64]
-    uint64_t* kmask;   // [slot][L][H][ctx]  bit t: k16[t] == +32768
-    int32_t* kexp;     // [slot][L][H][ctx]
-    int32_t* v;        // [slot][L][H][ctx][64]
-    int L, H, ctx;
-};
 
 __global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t* __restrict__ row_slot,
                         const int32_t* __restrict__ row_pos, int layer, KV kv, int32_t* __restrict__ q16,
@@ -182,7 +172,7 @@ __global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t
             q16[(size_t)r * d + part * 64 + lane + 32] = (int32_t)a1;
             if (lane == 0) qexp[r * H + part] = -16 + sh;
         } else {
-            if (pos < 0 || pos >= kv.ctx) { if (lane == 0) set_err(err, DERR_POS); return; }
+            if (pos < 0 || pos >= kv.lim) { if (lane == 0) set_err(err, DERR_POS); return; }
             size_t idx = kv_index(slot, layer, part - H, pos, kv.L, H, kv.ctx);
             kv.k[idx * 64 + lane] = (int16_t)(uint16_t)(uint32_t)a0;
             kv.k[idx * 64 + lane + 32] = (int16_t)(uint16_t)(uint32_t)a1;
@@ -193,7 +183,7 @@ __global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t
             }
         }
     } else {
-        if (pos < 0 || pos >= kv.ctx) { if (lane == 0) set_err(err, DERR_POS); return; }
+        if (pos < 0 || pos >= kv.lim) { if (lane == 0) set_err(err, DERR_POS); return; }
         size_t idx = kv_index(slot, layer, part - 2 * H, pos, kv.L, H, kv.ctx);
         bool bad = v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1;
         if (__any_sync(0xffffffffu, bad) && lane == 0) set_err(err, DERR_VOVF);
@@ -222,6 +212,7 @@ struct AttnArgs {
     const int32_t* EXP2;
     int64_t* out;           // [rows][d]
     uint32_t* err;
+    uint64_t* or_out;       // optional [rows]: OR of |out| per row (the next bank's to16 shift)
 };
 
 // ARR read as base2.py:97 does it: ARR[min(d, len-1)] where d < len, else 0. d is never negative unless a score
@@ -245,7 +236,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     const int H = a.kv.H, d = H * 64;
     const int slot = a.row_slot[r], p = a.row_pos[r];
-    if (p < 0 || p >= a.kv.ctx) return;      // flagged by k_heads (DERR_POS); never read past the store
+    if (p < 0 || p >= a.kv.lim) return;      // flagged by k_heads (DERR_POS); never read past the store
     const int nk = p + 1;
     if (threadIdx.x < 64) qs[threadIdx.x] = a.q16[(size_t)r * d + h * 64 + threadIdx.x];
     __syncthreads();
@@ -337,8 +328,131 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
         for (int k = 0; k < NW; k++) { t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]); }
         int64_t F = -log2fix(zz, a.LOG2);
         int64_t* o = a.out + (size_t)r * d + h * 64;
-        o[2 * lane] = power(t0, F, a.EXP2);
-        o[2 * lane + 1] = power(t1, F, a.EXP2);
+        const int64_t v0 = power(t0, F, a.EXP2), v1 = power(t1, F, a.EXP2);
+        o[2 * lane] = v0;
+        o[2 * lane + 1] = v1;
+        if (a.or_out) {
+            const uint64_t w = warp_or64(mag(v0) | mag(v1));
+            if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)w);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// the arrival with the stream's keys, values and their metadata for this head brought into shared memory by four
+// bulk async copies at once (the whole run of positions 0..pos is contiguous in the store), then:
+//   pass 1  scores (8 lanes per key, 16-byte shared loads), the largest;   pass 1b  a = ARR[start - sc], Z = sum a;
+//   pass 2  num = sum a * v (2 dims per lane, warps split the keys);       out = power(num, -log2fix(Z)).
+// Shared memory: 408 bytes per key (positions rounded up to 4). Used while the context fits; k_attend otherwise.
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int ATT_BYTES_PER_KEY = 128 + 256 + 8 + 4 + 8 + 4;
+
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
+    griddep_wait();
+    griddep_launch();
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ uint64_t bar;
+    __shared__ int32_t qs[64];
+    __shared__ int64_t red[NW][66];
+    const int r = blockIdx.x, h = blockIdx.y;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int H = a.kv.H, d = H * 64;
+    const int slot = a.row_slot[r], p = a.row_pos[r];
+    if (p < 0 || p >= a.kv.lim) return;      // flagged by the qkv bank (DERR_POS); never read past the store
+    const int nk = p + 1, nkr = (nk + 3) & ~3;
+    int16_t* Ks = reinterpret_cast<int16_t*>(sm);
+    int32_t* Vs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 128);
+    uint64_t* KMs = reinterpret_cast<uint64_t*>(sm + (size_t)nkr * 384);
+    int32_t* KEs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 392);
+    int64_t* SCs = reinterpret_cast<int64_t*>(sm + (size_t)nkr * 396);
+    int32_t* AVs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 404);
+    const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0) {
+        mbar_expect_tx(&bar, (uint32_t)nkr * (128 + 256 + 8 + 4));
+        bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)nkr * 128, &bar);
+        bulk_g2s(Vs, a.kv.v + base * 64, (uint32_t)nkr * 256, &bar);
+        bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)nkr * 8, &bar);
+        bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)nkr * 4, &bar);
+    }
+    if (tid < 64) qs[tid] = a.q16[(size_t)r * d + h * 64 + tid];
+    const int64_t eq = a.qexp[r * H + h];
+    __syncthreads();
+    if (!mbar_wait(&bar, 0, a.err)) return;
+
+    // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of key c*4 + (lane>>3)
+    int qr[8];
+#pragma unroll
+    for (int t = 0; t < 8; t++) qr[t] = qs[(lane & 7) * 8 + t];
+    int64_t lmax = INT64_MIN;
+    for (int c = wid; c * 4 < nk; c += NW) {
+        const int key = c * 4 + (lane >> 3);
+        int64_t part = 0;
+        if (key < nk) {
+            const int4 raw = reinterpret_cast<const int4*>(Ks + (size_t)key * 64)[lane & 7];
+            const int16_t* kk = reinterpret_cast<const int16_t*>(&raw);
+#pragma unroll
+            for (int t = 0; t < 8; t++) part += (long long)qr[t] * (long long)kk[t];
+        }
+        part += __shfl_xor_sync(0xffffffffu, part, 1);
+        part += __shfl_xor_sync(0xffffffffu, part, 2);
+        part += __shfl_xor_sync(0xffffffffu, part, 4);
+        if ((lane & 7) == 0 && key < nk) {
+            uint64_t m = KMs[key];
+            while (m) { const int t = __ffsll((long long)m) - 1; m &= m - 1; part += 65536LL * qs[t]; }
+            const int64_t s = rshift(part, -(eq + (int64_t)KEs[key] - 3 + 10));
+            SCs[key] = s;
+            lmax = s > lmax ? s : lmax;
+        }
+    }
+    lmax = warp_max64(lmax);
+    if (lane == 0) red[wid][65] = lmax;
+    __syncthreads();
+    int64_t start = red[0][65];
+#pragma unroll
+    for (int k = 1; k < NW; k++) start = red[k][65] > start ? red[k][65] : start;
+
+    // ---- pass 1b: the arrival weights and their total
+    int64_t z = 0;
+    for (int s = tid; s < nk; s += NW * 32) {
+        const int64_t av = arrival(wsub(start, SCs[s]), a.ARR, a.alen, a.err);
+        AVs[s] = (int32_t)av;
+        z = wadd(z, av);
+    }
+    z = warp_sum64(z);
+    __syncthreads();                 // red[][65] read by everyone; AVs complete
+    if (lane == 0) red[wid][64] = z;
+
+    // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin
+    int64_t n0 = 0, n1 = 0;
+    for (int s = wid; s < nk; s += NW) {
+        const int64_t av = AVs[s];
+        if (!av) continue;
+        const int2 vv = reinterpret_cast<const int2*>(Vs + (size_t)s * 64)[lane];
+        n0 = wadd(n0, wmul(av, vv.x));
+        n1 = wadd(n1, wmul(av, vv.y));
+    }
+    red[wid][2 * lane] = n0;
+    red[wid][2 * lane + 1] = n1;
+    __syncthreads();
+    if (wid == 0) {
+        int64_t t0 = 0, t1 = 0, zz = 0;
+#pragma unroll
+        for (int k = 0; k < NW; k++) { t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]); }
+        const int64_t F = -log2fix(zz, a.LOG2);
+        int64_t* o = a.out + (size_t)r * d + h * 64;
+        const int64_t v0 = power(t0, F, a.EXP2), v1 = power(t1, F, a.EXP2);
+        o[2 * lane] = v0;
+        o[2 * lane + 1] = v1;
+        if (a.or_out) {
+            const uint64_t w = warp_or64(mag(v0) | mag(v1));
+            if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)w);
+        }
     }
 }
 
@@ -379,6 +493,59 @@ __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const i
     row_slot[s] = s;
     row_pos[s] = slot_len[s];
     row_tok[s] = tok_in ? tok_in[s] : slot_tok[s];
+}
+
+// a decode step's first kernel: row s = stream slot s at its next position, R = wte[tok] + wpe[pos], the row's OR
+// of magnitudes (the qkv bank's to16 shift) into or_buf[0], and the step's other OR slots or_buf[1..nor) cleared
+__global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, const int32_t* __restrict__ slot_tok,
+                               int32_t* row_slot, int32_t* row_pos, int32_t* row_tok, const int64_t* __restrict__ wte,
+                               const int64_t* __restrict__ wpe, int d, int V, int nctx, int64_t* __restrict__ R,
+                               uint64_t* or_buf, int nor, int or_ld, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ uint64_t s_or[8];
+    const int s = blockIdx.x;
+    if (s >= n) return;
+    int tok = slot_tok[s], pos = slot_len[s];
+    if (threadIdx.x == 0) { row_slot[s] = s; row_pos[s] = pos; row_tok[s] = tok; }
+    if (tok < 0 || tok >= V) { if (threadIdx.x == 0) set_err(err, DERR_TOKEN); tok = 0; }
+    if (pos < 0 || pos >= nctx) { if (threadIdx.x == 0) set_err(err, DERR_POS); pos = 0; }
+    const int64_t* a = wte + (size_t)tok * d;
+    const int64_t* b = wpe + (size_t)pos * d;
+    uint64_t o = 0;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const int64_t v = wadd(__ldg(a + i), __ldg(b + i));
+        R[(size_t)s * d + i] = v;
+        o |= mag(v);
+    }
+    for (int q = 1 + threadIdx.x; q < nor; q += blockDim.x) or_buf[(size_t)q * or_ld + s] = 0;
+    o = warp_or64(o);
+    if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t all = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) all |= s_or[w];
+        or_buf[s] = all;
+    }
+}
+
+// the OR of |X| over each row (the fused banks' to16 shift when called on their own, b2_bank)
+__global__ void k_row_or(const int64_t* __restrict__ X, int n, int rows, uint64_t* out) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ uint64_t s_or[8];
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    uint64_t o = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) o |= mag(X[(size_t)r * n + i]);
+    o = warp_or64(o);
+    if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        uint64_t all = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) all |= s_or[w];
+        out[r] = all;
+    }
 }
 
 // where a decode step's words go: out[s * ld + (slot_len[s] - base[s])], set once per call (k_gen_begin), so one

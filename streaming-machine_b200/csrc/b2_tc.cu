@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include "b2_epi.cuh"
+#include "b2_ptx.cuh"
 #include "b2_tc.cuh"
 
 namespace b2 {
@@ -18,44 +19,6 @@ namespace b2 {
 namespace {
 
 // ---- PTX wrappers ---------------------------------------------------------------------------------------------------
-B2_DEV uint32_t saddr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-B2_DEV void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(saddr(bar)), "r"(count) : "memory");
-}
-B2_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
-B2_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(saddr(bar)), "r"(bytes) : "memory");
-}
-B2_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(saddr(bar)), "r"(phase)
-        : "memory");
-    return ok != 0;
-}
-// bounded wait: gives up after WAIT_NS of wall time (%globaltimer), sets DERR_TIMEOUT and returns false
-constexpr uint64_t WAIT_NS = 500ull * 1000 * 1000;
-B2_DEV uint64_t gtime() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-    return t;
-}
-B2_DEV bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t* err) {
-    if (mbar_try_wait(bar, phase)) return true;
-    const uint64_t t0 = gtime();
-    for (;;) {
-        for (int i = 0; i < 256; i++)
-            if (mbar_try_wait(bar, phase)) return true;
-        if (gtime() - t0 > WAIT_NS || (*(volatile uint32_t*)err & DERR_TIMEOUT)) break;
-    }
-    atomicOr(err, DERR_TIMEOUT);
-    return false;
-}
 B2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
@@ -118,7 +81,7 @@ B2_DEV uint32_t mapa(uint32_t addr, uint32_t rank) {
 }
 B2_DEV int64_t ld_dsmem(uint32_t addr) {
     uint64_t v;
-    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr));
     return (int64_t)v;
 }
 B2_DEV void mbar_arrive(uint64_t* bar) {
@@ -290,6 +253,8 @@ __global__ void __launch_bounds__(256, 1)
         }
     }
     tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 256);   // TMEM is no longer needed
     cluster_sync();                   // every CTA's partial tile is written
     {
         const int ksz = a.ksplit;
@@ -306,16 +271,16 @@ __global__ void __launch_bounds__(256, 1)
         for (int n = n0 + (tid >> 7); n < n1; n += 2) {
             if (n >= a.rows || !jv) continue;
             const uint32_t off = (uint32_t)(n * 128 + m) * 8;
+            int64_t t[MAX_SPLIT];
+#pragma unroll
+            for (int p = 0; p < MAX_SPLIT; p++) t[p] = p < ksz ? ld_dsmem(peer[p] + off) : 0;
             int64_t v = 0;
 #pragma unroll
-            for (int p = 0; p < MAX_SPLIT; p++)
-                if (p < ksz) v = wadd(v, ld_dsmem(peer[p] + off));
+            for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[p]);
             finish<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
         }
     }
     cluster_sync();                   // no CTA leaves while a peer may still read its partial tile
-    __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 256);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -437,6 +402,355 @@ __global__ void __launch_bounds__(384, 1)
     if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
+// ---------------------------------------------------------------------------------------------------------------------
+// Decode banks, fused (rows <= 64): the previous bank's output arrives as int64 values plus, per row, the OR of their
+// magnitudes (published by its producer with atomicOr). Each CTA of a (1, ksplit, 1) cluster owns 1-3 K blocks:
+//   prologue  weights by TMA (before the dependency wait); the activations of its K range read from global, to16'd with
+//             the row's shift and split into the two signed byte planes straight into SWIZZLE_128B shared memory;
+//             partial S1, S2 (the gauge), the row correction and a bit mask of +32768 entries, per row;
+//   MMA       16 per K block into three TMEM accumulators;
+//   partial   65536*A1 + 256*A2 + A3 + this K range's column and row corrections + 256*w for its +32768 entries
+//             (w read back from its own shared-memory planes), parked in shared memory;
+//   reduce    after a cluster barrier each CTA sums a 1/ksplit slice of the rows over DSMEM (and the row's S1, S2),
+//             finishes them (gauge, power, bias, bend or residual add) and publishes the next bank's row OR; the qkv
+//             bank instead splits its rows into q16 / k16 / v (the Metal engine's heads16) and appends k, v to the
+//             key/value store.
+// ---------------------------------------------------------------------------------------------------------------------
+
+B2_DEV uint32_t sw128(int row, int chunk) { return (uint32_t)((row >> 3) * 1024 + (row & 7) * 128 + ((chunk ^ (row & 7)) << 4)); }
+B2_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+B2_DEV void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+template <int EPI>
+__global__ void __launch_bounds__(256, 2)
+    k_bank_fused(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl, const FusedArgs a) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    constexpr int WSTAGE = 2 * A_BYTES;               // weight planes of one K block
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full_bar[MAX_KPS], acc_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_dead, s_abort;
+    __shared__ int s_sh[BN];
+    __shared__ int64_t s_S1[BN], s_S2[BN], s_rowc[BN];
+    __shared__ uint32_t s_sat[BN][MAX_KPS * 4];       // +32768 entries: bit k of this CTA's K range, per row
+    __shared__ int64_t s_LS[BN], s_e2[BN];
+    __shared__ uint64_t s_hor[8][4];
+    __shared__ unsigned long long s_satrows;       // bit n: row n has a +32768 entry in this CTA's K range
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t* xplanes = smem + a.kps * WSTAGE;         // [kps][2][BN x 128] activation planes
+    int64_t* P = (int64_t*)smem;                      // [BN][128] partial tile, over everything once used
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, ks = blockIdx.y;
+    const uint32_t crank = cluster_rank();
+
+    if (tid == 0) {
+        for (int kb = 0; kb < a.kps; kb++) mbar_init(&full_bar[kb], 1);
+        mbar_init(&acc_bar, 1);
+        s_abort = 0;
+        s_satrows = 0;
+        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
+        fence_mbar_init();
+    }
+    if (tid < BN) {
+        s_S1[tid] = 0;
+        s_S2[tid] = 0;
+        s_rowc[tid] = 0;
+        for (int w = 0; w < MAX_KPS * 4; w++) s_sat[tid][w] = 0;
+    }
+    if (warp == 0) tmem_alloc(&tmem_slot, 256);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const bool dead = s_dead != 0;
+    if (tid == 0 && !dead) {          // weights: independent of earlier kernels
+        for (int kb = 0; kb < a.kps; kb++) {
+            uint8_t* st = smem + kb * WSTAGE;
+            int kx = (ks * a.kps + kb) * 128;
+            mbar_expect_tx(&full_bar[kb], WSTAGE);
+            tma_load_2d(st, &mwh, &full_bar[kb], kx, mt * 128);
+            tma_load_2d(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128);
+        }
+    }
+    griddep_wait();
+    griddep_launch();
+
+    // ---- activations: to16 and the two byte planes, in shared memory ----
+    {
+        const int n = tid >> 2, cg = tid & 3;
+        const bool nv = n < a.rows;
+        const int sh = nv ? to16_shift(a.xor_in[n]) : 0;
+        if (cg == 0) s_sh[n] = sh;
+        int64_t S1 = 0, S2 = 0, rc = 0;
+        for (int kb = 0; kb < a.kps; kb++) {
+            const int k0 = (ks * a.kps + kb) * 128 + cg * 32;
+            uint32_t hw[8], lw[8];
+            uint32_t satw = 0;
+            int64_t s1 = 0;
+            int4 raw[16];
+            const int4* src = reinterpret_cast<const int4*>(a.X + (size_t)n * a.nin + k0);
+#pragma unroll
+            for (int v = 0; v < 16; v++) raw[v] = nv ? src[v] : make_int4(0, 0, 0, 0);
+#pragma unroll
+            for (int v4 = 0; v4 < 8; v4++) {
+                const int4 raw0 = raw[2 * v4], raw1 = raw[2 * v4 + 1];
+                const int64_t xv[4] = {(int64_t)(((uint64_t)(uint32_t)raw0.y << 32) | (uint32_t)raw0.x),
+                                       (int64_t)(((uint64_t)(uint32_t)raw0.w << 32) | (uint32_t)raw0.z),
+                                       (int64_t)(((uint64_t)(uint32_t)raw1.y << 32) | (uint32_t)raw1.x),
+                                       (int64_t)(((uint64_t)(uint32_t)raw1.w << 32) | (uint32_t)raw1.z)};
+                uint32_t h = 0, l = 0;
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int32_t q = (int32_t)rshift(xv[u], sh);
+                    const bool sat = q == 32768;
+                    h |= (uint32_t)(uint8_t)(int8_t)(sat ? 127 : (q >> 8)) << (8 * u);
+                    l |= (uint32_t)(uint8_t)(int8_t)((q & 255) - 128) << (8 * u);
+                    s1 += q;
+                    S2 += (int64_t)q * q;
+                    satw |= (uint32_t)sat << (v4 * 4 + u);
+                }
+                hw[v4] = h;
+                lw[v4] = l;
+            }
+            S1 += s1;
+            rc += 128 * (s1 - 256 * (int64_t)__popc(satw));
+            s_sat[n][kb * 4 + cg] = satw;
+            if (satw) atomicOr(&s_satrows, 1ull << n);
+            const uint32_t bh = saddr(xplanes + kb * 2 * B_BYTES), bl = bh + B_BYTES;
+            st_shared_v4(bh + sw128(n, 2 * cg), hw[0], hw[1], hw[2], hw[3]);
+            st_shared_v4(bh + sw128(n, 2 * cg + 1), hw[4], hw[5], hw[6], hw[7]);
+            st_shared_v4(bl + sw128(n, 2 * cg), lw[0], lw[1], lw[2], lw[3]);
+            st_shared_v4(bl + sw128(n, 2 * cg + 1), lw[4], lw[5], lw[6], lw[7]);
+        }
+        // the row's four threads are adjacent lanes
+#pragma unroll
+        for (int o = 1; o < 4; o <<= 1) {
+            S1 += __shfl_xor_sync(0xffffffffu, S1, o);
+            S2 += __shfl_xor_sync(0xffffffffu, S2, o);
+            rc += __shfl_xor_sync(0xffffffffu, rc, o);
+        }
+        if (cg == 0) { s_S1[n] = S1; s_S2[n] = S2; s_rowc[n] = rc; }
+    }
+    fence_proxy_async();
+    __syncthreads();
+
+    if (warp == 1 && lane == 0 && !dead) {
+        for (int kb = 0; kb < a.kps; kb++) {
+            if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
+        }
+        tc_fence_after();
+        for (int kb = 0; kb < a.kps && !s_abort; kb++) {
+            // A planes at smem + kb * WSTAGE, B planes at xplanes + kb * 2 * B_BYTES
+            const uint32_t abase = saddr(smem + kb * WSTAGE), bbase = saddr(xplanes + kb * 2 * B_BYTES);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+                uint64_t ah = sdesc(abase + kk * 32), al = sdesc(abase + A_BYTES + kk * 32);
+                uint64_t bh = sdesc(bbase + kk * 32), bl = sdesc(bbase + B_BYTES + kk * 32);
+                uint32_t acc = (kb || kk) ? 1u : 0u;
+                mma_i8(tmem + 0 * BN, ah, bh, IDESC, acc);
+                mma_i8(tmem + 1 * BN, ah, bl, IDESC, acc);
+                mma_i8(tmem + 1 * BN, al, bh, IDESC, 1);
+                mma_i8(tmem + 2 * BN, al, bl, IDESC, acc);
+            }
+        }
+        mma_commit(&acc_bar);
+    }
+    __syncwarp();
+    // this CTA's share of the column correction, fetched while the MMAs run
+    int64_t colc = 0;
+    {
+        const int j = mt * 128 + (warp & 3) * 32 + lane;
+        for (int kb = 0; kb < a.kps; kb++) colc += a.colcorr_kb[(size_t)(ks * a.kps + kb) * a.nout_pad + j];
+    }
+    const bool ok = !dead && mbar_wait(&acc_bar, 0, a.err);
+    tc_fence_after();
+    __syncthreads();
+    const bool go = ok && !s_abort;
+
+    // ---- this CTA's corrected partial piles -> P ----
+    {
+        const int m = (warp & 3) * 32 + lane, r0 = (warp >> 2) * 32;
+        int64_t p[32];
+        if (go) {
+            const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + r0;
+            int64_t t16[16];
+            tmem_piles16(trow, t16);
+#pragma unroll
+            for (int q = 0; q < 16; q++) p[q] = t16[q];
+            tmem_piles16(trow + 16, t16);
+#pragma unroll
+            for (int q = 0; q < 16; q++) p[16 + q] = t16[q];
+            const unsigned long long satrows = s_satrows;
+#pragma unroll
+            for (int q = 0; q < 32; q++) p[q] += colc + s_rowc[r0 + q];
+            if ((satrows >> r0) & 0xffffffffull)          // rare: rows of this warp with +32768 entries
+            for (int q = 0; q < 32; q++) {
+                const int n = r0 + q;
+                if (!((satrows >> n) & 1)) continue;
+                int64_t add = 0;
+                for (int kb = 0; kb < a.kps; kb++)
+                    for (int w = 0; w < 4; w++) {
+                        uint32_t bits = s_sat[n][kb * 4 + w];
+                        while (bits) {
+                            const int k = w * 32 + __ffs(bits) - 1;
+                            bits &= bits - 1;
+                            const uint8_t* A = smem + kb * WSTAGE;
+                            const int off = (int)sw128(m, k >> 4) + (k & 15);
+                            const int64_t wv = 256 * (int64_t)(int8_t)A[off] + (int64_t)(int8_t)A[A_BYTES + off] + 128;
+                            add += 256 * wv;
+                        }
+                    }
+                // rare: add into the register file through a fully unrolled select (no dynamic indexing)
+#pragma unroll
+                for (int u = 0; u < 32; u++)
+                    if (u == q) p[u] += add;
+            }
+        }
+        tc_fence_before();
+        __syncthreads();              // every read of the planes and of TMEM is done: P may overwrite them
+        if (warp == 0) tmem_dealloc(tmem, 256);   // free TMEM now: the next kernel's CTAs may allocate early
+        if (go) {
+#pragma unroll
+            for (int q = 0; q < 32; q++) P[(r0 + q) * 128 + m] = p[q];
+        }
+    }
+    tc_fence_before();
+    cluster_sync();                   // every CTA's partial tile and partial row sums are written
+
+    // ---- my slice of rows: sum over the cluster, finish ----
+    const int ksz = a.ksplit;
+    const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
+    uint32_t peer[MAX_SPLIT];
+    {
+        const uint32_t pbase = saddr(P);
+#pragma unroll
+        for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
+    }
+    if (tid < n1 - n0) {
+        const int n = n0 + tid;
+        int64_t LS = 0, e2 = 0;
+        if (GAUGED && n < a.rows) {
+            const uint32_t o1 = saddr(&s_S1[n]), o2 = saddr(&s_S2[n]);
+            int64_t t1[MAX_SPLIT], t2[MAX_SPLIT];
+#pragma unroll
+            for (int p = 0; p < MAX_SPLIT; p++) {
+                t1[p] = p < ksz ? ld_dsmem(mapa(o1, p)) : 0;
+                t2[p] = p < ksz ? ld_dsmem(mapa(o2, p)) : 0;
+            }
+            int64_t S1 = 0, S2 = 0;
+#pragma unroll
+            for (int p = 0; p < MAX_SPLIT; p++) { S1 += t1[p]; S2 += t2[p]; }
+            LS = gauge_LS(S1, S2, -16 + s_sh[n], a.LOG2, a.log768, a.eps40);
+            e2 = __ldg(a.EXP2 + (wsub(0, LS) & 0xFFFF));
+        }
+        s_LS[n] = LS;
+        s_e2[n] = e2;
+    }
+    __syncthreads();
+    {
+        const int m = tid & 127, ro = tid >> 7;
+        const int j = mt * 128 + m;
+        const bool jv = j < a.nout && go;
+        const int64_t e_j = jv ? (int64_t)a.e[j] : 0, b_j = jv ? a.b[j] : 0;
+        const int nit = (n1 - n0 + 1) >> 1;
+        const int H = a.kv.H, dm = H * 64;
+        for (int it0 = 0; it0 < nit; it0 += 4) {
+          int64_t sums[4];
+          {
+            int64_t t[4][MAX_SPLIT];
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int n = n0 + 2 * (it0 + u) + ro;
+                const bool ld = jv && it0 + u < nit && n < n1 && n < a.rows;
+                const uint32_t off = (uint32_t)(n * 128 + m) * 8;
+#pragma unroll
+                for (int p = 0; p < MAX_SPLIT; p++) t[u][p] = (ld && p < ksz) ? ld_dsmem(peer[p] + off) : 0;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                int64_t v = 0;
+#pragma unroll
+                for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[u][p]);
+                sums[u] = v;
+            }
+          }
+          int64_t vals[4];
+          bool valids[4];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int n = n0 + 2 * (it0 + u) + ro;
+            valids[u] = jv && it0 + u < nit && n < n1 && n < a.rows;
+            vals[u] = valids[u] ? epi_value<EPI>(sums[u], e_j, b_j, -16 + s_sh[n], s_LS[n], s_e2[n], a.PHI) : 0;
+          }
+          if (EPI == EPI_GAUGED && a.q16) {
+            // heads16: each 64-column half of the tile is one head part (q, k or v of one head); its rows' OR of
+            // magnitudes over the part's two warps, for the group's four rows at once
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const uint64_t w = warp_or64(valids[u] ? mag(vals[u]) : 0);
+                if (lane == 0) s_hor[warp][u] = w;
+            }
+            __syncthreads();
+            uint64_t por[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++) por[u] = s_hor[warp][u] | s_hor[warp ^ 1][u];
+            __syncthreads();
+            const int part = 2 * mt + (m >> 6), kind = part / H, hh = part % H, dd = m & 63;
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int n = n0 + 2 * (it0 + u) + ro;
+                const bool valid = valids[u];
+                const int64_t val = vals[u];
+                const int sh = to16_shift(por[u]);
+                const int32_t x = (int32_t)rshift(val, sh);
+                if (a.out && valid) a.out[(size_t)n * a.ldo + j] = val;
+                if (kind == 0) {
+                    if (valid) {
+                        a.q16[(size_t)n * dm + hh * 64 + dd] = x;
+                        if (dd == 0) a.qexp[n * H + hh] = -16 + sh;
+                    }
+                } else {
+                    const int pos = valid ? a.row_pos[n] : 0;
+                    const bool pv = valid && pos >= 0 && pos < a.kv.lim;
+                    if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
+                    const size_t idx = pv ? kv_index(a.row_slot[n], a.layer, hh, pos, a.kv.L, H, a.kv.ctx) : 0;
+                    if (kind == 1) {
+                        const uint32_t sat = __ballot_sync(0xffffffffu, pv && x == 32768);
+                        if (pv) {
+                            a.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
+                            if (lane == 0) reinterpret_cast<uint32_t*>(&a.kv.kmask[idx])[dd >> 5] = sat;
+                            if (dd == 0) a.kv.kexp[idx] = -16 + sh;
+                        }
+                    } else if (pv) {
+                        if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
+                        a.kv.v[idx * 64 + dd] = (int32_t)val;
+                    }
+                }
+            }
+          } else {
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                const int n = n0 + 2 * (it0 + u) + ro;
+                const bool valid = valids[u];
+                int64_t o = vals[u];
+                if (valid) {
+                    int64_t* dst = a.out + (size_t)n * a.ldo + j;
+                    if (EPI == EPI_PLAIN_ADD) o = wadd(*dst, o);
+                    *dst = o;
+                }
+                if (EPI != EPI_GAUGED) {
+                    const uint64_t wor = warp_or64(valid ? mag(o) : 0);
+                    if (lane == 0 && a.or_out && valid) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
+                }
+            }
+          }
+        }
+    }
+    cluster_sync();                   // no CTA leaves while a peer may still read its shared memory
+}
+
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
 __global__ void k_weight_planes(const int16_t* __restrict__ w, int nin, int nout, int8_t* __restrict__ wh,
                                 int8_t* __restrict__ wl) {
@@ -464,6 +778,16 @@ __global__ void k_colcorr(const int16_t* __restrict__ w, int nin, int nout, int 
     if (j < nout)
         for (int i = 0; i < nin; i++) s += w[(size_t)i * nout + j];
     cc[j] = j < nout ? 128 * s - 16384 * (int64_t)nin : 0;
+}
+
+// per 128-input block: 128 * sum_{i in block} w[i][j] - 16384 * 128 (the fused decode banks add their blocks' share)
+__global__ void k_colcorr_kb(const int16_t* __restrict__ w, int nin, int nout, int nout_pad, int64_t* __restrict__ cc) {
+    int j = blockIdx.x * blockDim.x + threadIdx.x, kb = blockIdx.y;
+    if (j >= nout_pad) return;
+    int64_t s = 0;
+    if (j < nout)
+        for (int i = kb * 128; i < kb * 128 + 128; i++) s += w[(size_t)i * nout + j];
+    cc[(size_t)kb * nout_pad + j] = j < nout ? 128 * s - 16384 * 128 : 0;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -543,6 +867,12 @@ int tc_init() {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
         if (e != cudaSuccess) return (int)e;
     }
+    void* fused[] = {(void*)k_bank_fused<EPI_GAUGED>, (void*)k_bank_fused<EPI_GAUGED_EDGE>,
+                     (void*)k_bank_fused<EPI_PLAIN_ADD>};
+    for (void* f : fused) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
+        if (e != cudaSuccess) return (int)e;
+    }
     for (void* f : tiles) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_STAGES * STAGE + 1024);
         if (e != cudaSuccess) return (int)e;
@@ -561,8 +891,10 @@ int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
     if ((e = cudaMalloc(&t.wh, (size_t)t.nout_pad * nin)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&t.wl, (size_t)t.nout_pad * nin)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&t.colcorr, sizeof(int64_t) * t.nout_pad)) != cudaSuccess) return (int)e;
+    if ((e = cudaMalloc(&t.colcorr_kb, sizeof(int64_t) * t.nout_pad * (nin / 128))) != cudaSuccess) return (int)e;
     k_weight_planes<<<dim3(t.nout_pad / 32, (nin + 31) / 32), dim3(32, 8)>>>(w, nin, nout, t.wh, t.wl);
     k_colcorr<<<(t.nout_pad + 255) / 256, 256>>>(w, nin, nout, t.nout_pad, t.colcorr);
+    k_colcorr_kb<<<dim3((t.nout_pad + 255) / 256, nin / 128), 256>>>(w, nin, nout, t.nout_pad, t.colcorr_kb);
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
     int rc = make_map(t.map_wh, t.wh, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wl, t.wl, nin, t.nout_pad, nin, 128);
@@ -575,8 +907,9 @@ void tc_bank_free(TcBank& t) {
     if (t.wh) cudaFree(t.wh);
     if (t.wl) cudaFree(t.wl);
     if (t.colcorr) cudaFree(t.colcorr);
+    if (t.colcorr_kb) cudaFree(t.colcorr_kb);
     t.wh = t.wl = nullptr;
-    t.colcorr = nullptr;
+    t.colcorr = t.colcorr_kb = nullptr;
     t.ready = 0;
 }
 
@@ -669,6 +1002,51 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
                                           r.maps[mi].l, a);
                       break)
     }
+    return (int)err;
+}
+
+int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl) {
+    if (!t.ready || a.rows < 1 || a.rows > BN || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD))
+        return (int)cudaErrorInvalidValue;
+    const int mtiles = t.nout_pad / 128, kb = t.nin / 128;
+    int ksplit = 1;
+    for (int d = MAX_SPLIT; d >= 1; d--)
+        if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
+    if (kb / ksplit > MAX_KPS) return (int)cudaErrorInvalidValue;
+    a.nin = t.nin;
+    a.nout = t.nout;
+    a.nout_pad = t.nout_pad;
+    a.kps = kb / ksplit;
+    a.ksplit = ksplit;
+    a.colcorr_kb = t.colcorr_kb;
+    size_t smem = (size_t)(a.kps * STAGE > 64 * 1024 ? a.kps * STAGE : 64 * 1024) + 1024;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(mtiles, ksplit, 1);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (ksplit > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = ksplit;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    const CUtensorMap& mh = *reinterpret_cast<const CUtensorMap*>(t.map_wh.bytes);
+    const CUtensorMap& ml = *reinterpret_cast<const CUtensorMap*>(t.map_wl.bytes);
+    cudaError_t err;
+    if (epi == EPI_GAUGED) err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_GAUGED>, mh, ml, a);
+    else if (epi == EPI_GAUGED_EDGE) err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_GAUGED_EDGE>, mh, ml, a);
+    else err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_PLAIN_ADD>, mh, ml, a);
     return (int)err;
 }
 

@@ -11,6 +11,7 @@
 #pragma once
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include "b2_epi.cuh"
 
 namespace b2 {
 
@@ -23,6 +24,7 @@ struct TcBank {
     int8_t* wh = nullptr;        // [nout_pad][nin]
     int8_t* wl = nullptr;        // [nout_pad][nin]
     int64_t* colcorr = nullptr;  // [nout_pad]  128*sum_i w[i][j] - 16384*nin
+    int64_t* colcorr_kb = nullptr;  // [nin/128][nout_pad] the same per 128-input block
     const int16_t* w16 = nullptr;  // the reference-layout bank [nin][nout] (for the +32768 correction)
     TcMap map_wh, map_wl;
 };
@@ -41,6 +43,31 @@ struct TcRows {
 };
 
 
+// a decode bank with its quantisation fused in (rows <= 64); see k_bank_fused in b2_tc.cu
+struct FusedArgs {
+    int nin, nout, rows, kps, ksplit;
+    const int64_t* X;            // [rows][nin] the bank's input
+    const uint64_t* xor_in;      // [rows] OR of |X| over the row
+    uint64_t* or_out;            // [rows] OR of |output row| for the next bank (EPI_PLAIN_ADD / EPI_GAUGED_EDGE)
+    const int64_t* colcorr_kb;   // [nin / 128][nout_pad]
+    int nout_pad;
+    const int32_t* e;
+    const int64_t* b;
+    int64_t* out;                // R (PLAIN_ADD), H (GAUGED_EDGE), the q/k/v values (GAUGED, optional)
+    int ldo;
+    const int32_t* EXP2;
+    const int32_t* PHI;
+    const int32_t* LOG2;
+    int64_t log768, eps40;
+    const int32_t* row_slot;     // qkv: where each row's key/value goes
+    const int32_t* row_pos;
+    int layer;
+    KV kv;
+    int32_t* q16;
+    int32_t* qexp;
+    uint32_t* err;
+};
+
 int tc_min_rows_default();
 int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
@@ -50,5 +77,6 @@ void tc_rows_free(TcRows& r);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl);
+int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2

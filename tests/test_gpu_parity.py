@@ -164,5 +164,5 @@ def test_launch_count_and_profile(gpu_engine):
     e.generate_device(4, 2)
     n, by = e.profile_read()
     e.profile(False)
-    assert n == sum(c for c, _ in by.values()) and n >= 2 * 120
+    assert n == sum(c for c, _ in by.values()) and n >= 2 * 60
     assert by["bank"][0] == 2 * 49 and by["bank"][1] > 0
