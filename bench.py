@@ -281,11 +281,12 @@ def run_ours(args):
     keys = sum(P + 1 + t for t in range(CYCLE))                    # keys attended per stream over the cycle
     att_bytes = B * KV_BYTES_PER_KEY * keys
     att_gbs = att_bytes / (att_ms / 1000.0) / 1e9
-    traffic = None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
+    traffic = None       # DRAM bytes per bank launch from the committed ncu summary of the same kernel
+    tp = os.path.join(ROOT, "profiles", "bank_split_decode_c2.md")
     if os.path.exists(tp):
-        with open(tp) as f:
-            traffic = json.load(f).get("bank_bytes_per_launch")
+        import re
+        mt = re.search(r"bank_dram_bytes_per_launch_avg:\s*(\d+)", open(tp).read())
+        traffic = int(mt.group(1)) if mt else None
     roofline = {"bound": "hbm", "achieved": round(bank_gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(bank_gbs / peak, 4), "traffic": traffic,
                 "kernel": "bank product (49 launches per step: 48 banks + head)",
