@@ -49,7 +49,8 @@ def peaks():
 
 
 def env_rank():
-    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+    from streaming_machine_b200.shard import rank_env
+    return rank_env()
 
 
 # ---------------------------------------------------------------------------------------------------------------------
@@ -167,11 +168,8 @@ def run_ours(args):
             dist.barrier(device_ids=[local_rank])
 
     def max_over_ranks(x: float) -> float:
-        if not dist:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        from streaming_machine_b200.shard import max_over_ranks as mor
+        return mor(x, dist, device="cuda")
 
     from streaming_machine_b200 import convert, engine
     if rank == 0:
@@ -181,7 +179,8 @@ def run_ours(args):
         barrier()
         M = convert.load_gpt2(0)
     eng = engine.Engine(M, device=local_rank, n_streams=B, max_ctx=P + CYCLE + 1)
-    ids = np.random.default_rng(SEED).integers(0, V, (B * world, P))[rank * B:(rank + 1) * B]
+    from streaming_machine_b200.shard import stream_ids
+    ids = stream_ids(SEED, B, P, rank, world, V)
     lens = torch.full((B,), P, dtype=torch.int32, device="cuda")
     buf = torch.empty(B * CYCLE, dtype=torch.int32, device="cuda")
 
