@@ -399,3 +399,283 @@ int b2o_attention(void *mv, const i64 *QKV, int P, i64 *out) {
     cache_free(&c); free(sc);
     return 0;
 }
+
+/* ============================================================================================================ */
+/* Pythia-160M: the reference's foundation0/pythia_base2.py (size=160m, plates=finished, order=plain)           */
+/* ============================================================================================================ */
+typedef __int128 i128;
+
+/* pythia_base2.py:87-90 power for one element, exactly (Python big ints): X*EXP2[f] then the rounded shift by
+ * 16 - I. Returns -1 when the result leaves int64 (where the reference's .astype(np.int64) raises). */
+static int power_exact1(i64 x, i64 F, const i64 *EXP2, i64 *out) {
+    i64 I = F >> 16, f = F & 0xFFFF, s = 16 - I;
+    i128 p = (i128)x * (i128)EXP2[f], r;
+    if (s <= 0) {
+        if (p == 0) r = 0;
+        else if (-s >= 64) return -1;
+        else {
+            r = p << (-s);
+            if ((r >> (-s)) != p) return -1;
+        }
+    } else if (s >= 100) {
+        r = 0;                                /* |p| < 2^81: (p + 2^(s-1)) >> s is 0 */
+    } else {
+        r = (p + ((i128)1 << (s - 1))) >> s;  /* floor shift, as Python's >> */
+    }
+    if (r > (i128)INT64_MAX || r < (i128)INT64_MIN) return -1;
+    *out = (i64)r;
+    return 0;
+}
+
+/* pythia_base2.py:87-90 over an array: the int64 path when every |X| < 2^45, else the exact path. Returns -1 on an
+ * exact result outside int64. */
+int b2p_power(const i64 *x, const i64 *F, i64 n, const i64 *EXP2, i64 *y) {
+    int big = 0;
+    for (i64 i = 0; i < n; i++) if ((x[i] < 0 ? (u64)0 - (u64)x[i] : (u64)x[i]) >= ((u64)1 << 45)) big = 1;
+    for (i64 i = 0; i < n; i++) {
+        if (!big) y[i] = power1(x[i], F[i], EXP2);
+        else if (power_exact1(x[i], F[i], EXP2, &y[i])) return -1;
+    }
+    return 0;
+}
+
+typedef struct {
+    int L, d, H, hd, F, V, ctx, rot;
+    bank_t bank[64 * 4 + 1];                   /* layer*4 + {qkv, proj, fc, mproj}; head at 4*L (bias zeros) */
+    const i64 *ng[64 * 2 + 1], *nb[64 * 2 + 1]; /* ln1.l = 2l, ln2.l = 2l+1, lnf = 2L: gains (16-bit) and offsets */
+    i64 nge[64 * 2 + 1];
+    const int16_t *emb; const i64 *embe;       /* embed_in [V][d] and its per-word power of two */
+    const i64 *PHI, *ARR, *LOG2, *EXP2, *COS, *SIN;
+    i64 alen, eps40, half;
+} pmodel_t;
+
+void *b2p_create(int L, int d, int H, int F, int V, int ctx, int rot) {
+    pmodel_t *m = (pmodel_t *)calloc(1, sizeof(pmodel_t));
+    m->L = L; m->d = d; m->H = H; m->hd = d / H; m->F = F; m->V = V; m->ctx = ctx; m->rot = rot;
+    return m;
+}
+void b2p_set_bank(void *mv, int idx, const int16_t *w, const i64 *e, const i64 *b, int nin, int nout) {
+    pmodel_t *m = (pmodel_t *)mv;
+    m->bank[idx].w = w; m->bank[idx].e = e; m->bank[idx].b = b; m->bank[idx].nin = nin; m->bank[idx].nout = nout;
+}
+void b2p_set_norm(void *mv, int idx, const i64 *g, i64 ge, const i64 *b) {
+    pmodel_t *m = (pmodel_t *)mv;
+    m->ng[idx] = g; m->nge[idx] = ge; m->nb[idx] = b;
+}
+void b2p_set_tables(void *mv, const int16_t *emb, const i64 *embe, const i64 *PHI, const i64 *ARR, i64 alen,
+                    const i64 *LOG2, const i64 *EXP2, const i64 *COS, const i64 *SIN, i64 eps40, i64 half) {
+    pmodel_t *m = (pmodel_t *)mv;
+    m->emb = emb; m->embe = embe; m->PHI = PHI; m->ARR = ARR; m->alen = alen; m->LOG2 = LOG2; m->EXP2 = EXP2;
+    m->COS = COS; m->SIN = SIN; m->eps40 = eps40; m->half = half;
+}
+
+/* pythia_base2.py:100-110 gauge for one row: c = d*x16 - S1, V = d*S2 - S1^2 + (EPS40 >> (40 + 2 ex)),
+ * LS = log2fix(V) >> 1, out = power(c*g, (ge + 16)*65536 - LS) + b (exact power). */
+static int gauge_ln_row(const pmodel_t *m, int idx, const i64 *R, i64 *out, i64 *x16) {
+    const int d = m->d;
+    i64 ex = -16 + to16_row(R, d, x16);
+    i64 S1 = 0, S2 = 0;
+    for (int i = 0; i < d; i++) { S1 = wadd(S1, x16[i]); S2 = wadd(S2, wmul(x16[i], x16[i])); }
+    i64 V = wadd(wsub(wmul(d, S2), wmul(S1, S1)), np_rsh(m->eps40, 40 + 2 * ex));
+    i64 LS = log2fix1(V, m->LOG2) >> 1;
+    i64 F = wsub(wmul(wadd(m->nge[idx], 16), 65536), LS);
+    for (int i = 0; i < d; i++) {
+        i64 c = wsub(wmul(d, x16[i]), S1);
+        if (power_exact1(wmul(c, m->ng[idx][i]), F, m->EXP2, &out[i])) return -1;
+        out[i] = wadd(out[i], m->nb[idx][i]);
+    }
+    return 0;
+}
+
+/* pythia_base2.py:112-114 plain for one row into out (bias b may be NULL: the head) */
+static void plain_row(const pmodel_t *m, const bank_t *bk, const i64 *X, i64 *out, i64 *x16, i64 *pile, int par) {
+    i64 ex = -16 + to16_row(X, bk->nin, x16);
+    product_row(x16, bk, pile, par);
+    for (int j = 0; j < bk->nout; j++)
+        out[j] = wadd(rshift1(pile[j], -wadd(wadd(bk->e[j], ex), 16)), bk->b ? bk->b[j] : 0);
+}
+
+/* pythia_base2.py:116-123 turn for one head part of one position: pairs (i, i + rot/2), cos/sin at 2^-30 */
+static int turn_row(const pmodel_t *m, const i64 *x, int pos, i64 *y) {
+    const int r = m->rot / 2;
+    for (int t = 0; t < m->hd; t++) y[t] = x[t];
+    for (int t = 0; t < m->rot; t++) if ((x[t] < 0 ? -x[t] : x[t]) >= ((i64)1 << 31)) return -1;
+    for (int t = 0; t < r; t++) {
+        i64 c = m->COS[(size_t)pos * r + t], s = m->SIN[(size_t)pos * r + t], a = x[t], b = x[t + r];
+        y[t] = rshift1(wsub(wmul(a, c), wmul(b, s)), 30);
+        y[t + r] = rshift1(wadd(wmul(b, c), wmul(a, s)), 30);
+    }
+    return 0;
+}
+
+/* the per-stream store for Pythia: k16, its exponent, v (full width) per layer */
+static int pcache_alloc(const pmodel_t *m, cache_t *c, int ctx) {
+    size_t n = (size_t)m->L * ctx;
+    c->k16 = (i64 *)malloc(sizeof(i64) * n * m->d);
+    c->ek = (i64 *)malloc(sizeof(i64) * n * m->H);
+    c->v = (i64 *)malloc(sizeof(i64) * n * m->d);
+    return c->k16 && c->ek && c->v;
+}
+
+/* pythia_base2.py:125-141 attention at position p of one stream, given qkv (this position's [3d], per head q, k, v
+ * in Pythia's order) and the store (k16 turned and to16'd, v raw) for 0..p already filled by the caller. */
+static int pattend_row(const pmodel_t *m, const cache_t *c, int l, int ctx, int p, const i64 *qkv, i64 *out, i64 *sc) {
+    const int d = m->d, hd = m->hd;
+    i64 qt[256], q16[256];
+    for (int h = 0; h < m->H; h++) {
+        if (turn_row(m, qkv + h * 3 * hd, p, qt)) return -1;
+        i64 eq = -16 + to16_row(qt, hd, q16);
+        const i64 *K = c->k16 + ((size_t)l * ctx) * d + h * hd;
+        const i64 *EK = c->ek + ((size_t)l * ctx) * m->H + h;
+        const i64 *Vv = c->v + ((size_t)l * ctx) * d + h * hd;
+        i64 lev = INT64_MIN;
+        for (int s = 0; s <= p; s++) {
+            i64 dot = 0;
+            const i64 *k = K + (size_t)s * d;
+            for (int t = 0; t < hd; t++) dot += q16[t] * k[t];
+            i64 F = wsub(wmul(eq + EK[(size_t)s * m->H] + 10, 65536), m->half);
+            if (power_exact1(dot, F, m->EXP2, &sc[s])) return -1;
+            if (sc[s] > lev) lev = sc[s];
+        }
+        i64 Z = 0, num[256];
+        for (int t = 0; t < hd; t++) num[t] = 0;
+        for (int s = 0; s <= p; s++) {
+            i64 dd = wsub(lev, sc[s]);
+            i64 a = dd < m->alen ? m->ARR[dd < 0 ? 0 : dd] : 0;
+            if (!a) continue;
+            Z = wadd(Z, a);
+            const i64 *v = Vv + (size_t)s * d;
+            for (int t = 0; t < hd; t++) num[t] = wadd(num[t], wmul(a, v[t]));
+        }
+        i64 F = -log2fix1(Z, m->LOG2);
+        for (int t = 0; t < hd; t++) if (power_exact1(num[t], F, m->EXP2, &out[h * hd + t])) return -1;
+    }
+    return 0;
+}
+
+typedef struct { i64 *R, *G, *qkv, *att, *hid, *x16, *pile, *sc, *At, *Mo; } pscratch_t;
+
+static int pscratch_alloc(const pmodel_t *m, pscratch_t *s, int ctx) {
+    int wmax = m->V > m->F ? m->V : m->F;
+    s->R = (i64 *)malloc(sizeof(i64) * m->d); s->G = (i64 *)malloc(sizeof(i64) * m->d);
+    s->qkv = (i64 *)malloc(sizeof(i64) * 3 * m->d); s->att = (i64 *)malloc(sizeof(i64) * m->d);
+    s->hid = (i64 *)malloc(sizeof(i64) * m->F); s->x16 = (i64 *)malloc(sizeof(i64) * (m->F > m->d ? m->F : m->d));
+    s->pile = (i64 *)malloc(sizeof(i64) * wmax); s->sc = (i64 *)malloc(sizeof(i64) * ctx);
+    s->At = (i64 *)malloc(sizeof(i64) * m->d); s->Mo = (i64 *)malloc(sizeof(i64) * m->d);
+    return s->R && s->G && s->qkv && s->att && s->hid && s->x16 && s->pile && s->sc && s->At && s->Mo;
+}
+static void pscratch_free(pscratch_t *s) {
+    free(s->R); free(s->G); free(s->qkv); free(s->att); free(s->hid); free(s->x16); free(s->pile); free(s->sc);
+    free(s->At); free(s->Mo);
+}
+
+/* One new position of one stream (pythia_base2.py:151-160): returns the race's word (logits given) or -1 (none),
+ * -2 on a value the reference would reject (an exact power outside int64, a turn input past 2^31). */
+static int pposition(const pmodel_t *m, cache_t *c, pscratch_t *s, int ctx, int p, int id, i64 *logits, int par) {
+    const int d = m->d, H = m->H, hd = m->hd;
+    for (int i = 0; i < d; i++) s->R[i] = rshift1((i64)m->emb[(size_t)id * d + i], -(m->embe[id] + 16));
+    for (int l = 0; l < m->L; l++) {
+        /* attention branch */
+        if (gauge_ln_row(m, 2 * l, s->R, s->G, s->x16)) return -2;
+        plain_row(m, &m->bank[4 * l + 0], s->G, s->qkv, s->x16, s->pile, par);
+        for (int h = 0; h < H; h++) {
+            i64 kt[256];
+            if (turn_row(m, s->qkv + h * 3 * hd + hd, p, kt)) return -2;
+            c->ek[((size_t)l * ctx + p) * H + h] = -16 + to16_row(kt, hd, c->k16 + ((size_t)l * ctx + p) * d + h * hd);
+            memcpy(c->v + ((size_t)l * ctx + p) * d + h * hd, s->qkv + h * 3 * hd + 2 * hd, sizeof(i64) * hd);
+        }
+        if (pattend_row(m, c, l, ctx, p, s->qkv, s->att, s->sc)) return -2;
+        plain_row(m, &m->bank[4 * l + 1], s->att, s->At, s->x16, s->pile, par);
+        /* MLP branch, from the same R */
+        if (gauge_ln_row(m, 2 * l + 1, s->R, s->G, s->x16)) return -2;
+        plain_row(m, &m->bank[4 * l + 2], s->G, s->hid, s->x16, s->pile, par);
+        for (int j = 0; j < m->F; j++) s->hid[j] = edge1(s->hid[j], m->PHI);
+        plain_row(m, &m->bank[4 * l + 3], s->hid, s->Mo, s->x16, s->pile, par);
+        for (int i = 0; i < d; i++) s->R[i] = wadd(wadd(s->R[i], s->At[i]), s->Mo[i]);
+    }
+    if (!logits) return -1;
+    if (gauge_ln_row(m, 2 * m->L, s->R, s->G, s->x16)) return -2;
+    plain_row(m, &m->bank[4 * m->L], s->G, logits, s->x16, s->pile, par);
+    return (int)race1(logits, m->V);
+}
+
+/* greedy words for B streams of equal prompt length (the loop of pythia_base2.py:175), logits optional */
+int b2p_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    int ctx = P + n_new;
+    if (ctx > m->ctx || P < 1) return -1;
+    int nt = nthreads(threads), err = 0, par = B == 1;
+#pragma omp parallel for schedule(dynamic, 1) num_threads(nt) if (B > 1)
+    for (int b = 0; b < B; b++) {
+        cache_t c; pscratch_t s;
+        i64 *lg = (i64 *)malloc(sizeof(i64) * m->V);
+        if (!pcache_alloc(m, &c, ctx) || !pscratch_alloc(m, &s, ctx) || !lg) { err = -1; continue; }
+        for (int p = 0; p < P - 1 && !err; p++)
+            if (pposition(m, &c, &s, ctx, p, ids[(size_t)b * P + p], NULL, par) == -2) err = -2;
+        int tok = ids[(size_t)b * P + P - 1];
+        for (int t = 0; t < n_new && !err; t++) {
+            tok = pposition(m, &c, &s, ctx, P - 1 + t, tok, lg, par);
+            if (tok == -2) { err = -2; break; }
+            tokens[(size_t)b * n_new + t] = tok;
+            if (logits) memcpy(logits + ((size_t)b * n_new + t) * m->V, lg, sizeof(i64) * m->V);
+        }
+        cache_free(&c); pscratch_free(&s); free(lg);
+    }
+    return err;
+}
+
+/* teacher-forced scores at positions [first, last) of one stream (pythia_base2.py:151-160 with last) */
+int b2p_scores(void *mv, const int32_t *ids, int P, int first, int last, i64 *logits) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    if (P > m->ctx || first < 0 || last > P || first >= last) return -1;
+    cache_t c; pscratch_t s;
+    if (!pcache_alloc(m, &c, P) || !pscratch_alloc(m, &s, P)) return -1;
+    int rc = 0;
+    for (int p = 0; p < P && !rc; p++)
+        if (pposition(m, &c, &s, P, p, ids[p], (p >= first && p < last) ? logits + (size_t)(p - first) * m->V : NULL, 1) == -2)
+            rc = -2;
+    cache_free(&c); pscratch_free(&s);
+    return rc;
+}
+
+/* element entry points for the pinning tests */
+int b2p_gauge(void *mv, int idx, const i64 *R, int rows, i64 *out) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    i64 *x16 = (i64 *)malloc(sizeof(i64) * m->d);
+    int rc = 0;
+    for (int r = 0; r < rows && !rc; r++) rc = gauge_ln_row(m, idx, R + (size_t)r * m->d, out + (size_t)r * m->d, x16);
+    free(x16);
+    return rc;
+}
+int b2p_turn(void *mv, const i64 *X, const i64 *pos, int rows, i64 *Y) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    for (int r = 0; r < rows; r++) if (turn_row(m, X + (size_t)r * m->hd, (int)pos[r], Y + (size_t)r * m->hd)) return -1;
+    return 0;
+}
+int b2p_plain(void *mv, int idx, const i64 *X, int rows, i64 *out) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    const bank_t *bk = &m->bank[idx];
+    i64 *x16 = (i64 *)malloc(sizeof(i64) * bk->nin), *pile = (i64 *)malloc(sizeof(i64) * bk->nout);
+    for (int r = 0; r < rows; r++) plain_row(m, bk, X + (size_t)r * bk->nin, out + (size_t)r * bk->nout, x16, pile, 1);
+    free(x16); free(pile);
+    return 0;
+}
+/* pythia_base2.py:125-141 over a whole sequence's QKV [P][3d] */
+int b2p_attention(void *mv, const i64 *QKV, int P, i64 *out) {
+    const pmodel_t *m = (const pmodel_t *)mv;
+    const int d = m->d, H = m->H, hd = m->hd;
+    pmodel_t one = *m; one.L = 1;
+    cache_t c; i64 *sc = (i64 *)malloc(sizeof(i64) * P);
+    if (!pcache_alloc(&one, &c, P) || !sc) return -1;
+    for (int p = 0; p < P; p++)
+        for (int h = 0; h < H; h++) {
+            i64 kt[256];
+            if (turn_row(m, QKV + (size_t)p * 3 * d + h * 3 * hd + hd, p, kt)) return -2;
+            c.ek[(size_t)p * H + h] = -16 + to16_row(kt, hd, c.k16 + (size_t)p * d + h * hd);
+            memcpy(c.v + (size_t)p * d + h * hd, QKV + (size_t)p * 3 * d + h * 3 * hd + 2 * hd, sizeof(i64) * hd);
+        }
+    int rc = 0;
+    for (int p = 0; p < P && !rc; p++) rc = pattend_row(&one, &c, 0, P, p, QKV + (size_t)p * 3 * d, out + (size_t)p * d, sc);
+    cache_free(&c); free(sc);
+    return rc;
+}

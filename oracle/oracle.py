@@ -73,6 +73,22 @@ def lib():
         L.b2o_greedy_recompute.restype = c_int
         L.b2o_generate_recompute.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, c_int]
         L.b2o_generate_recompute.restype = c_int
+        # Pythia (foundation0/pythia_base2.py)
+        L.b2p_power.argtypes = [_i64p, _i64p, c_i64, _i64p, _i64p]
+        L.b2p_power.restype = c_int
+        L.b2p_create.argtypes = [c_int] * 7
+        L.b2p_create.restype = c_vp
+        L.b2p_set_bank.argtypes = [c_vp, c_int, _i16p, _i64p, ctypes.c_void_p, c_int, c_int]
+        L.b2p_set_norm.argtypes = [c_vp, c_int, _i64p, c_i64, _i64p]
+        L.b2p_set_tables.argtypes = [c_vp, _i16p, _i64p, _i64p, _i64p, c_i64, _i64p, _i64p, _i64p, _i64p, c_i64, c_i64]
+        for f in ("b2p_generate", "b2p_scores", "b2p_gauge", "b2p_turn", "b2p_plain", "b2p_attention"):
+            getattr(L, f).restype = c_int
+        L.b2p_generate.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, ctypes.c_void_p, c_int]
+        L.b2p_scores.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i64p]
+        L.b2p_gauge.argtypes = [c_vp, c_int, _i64p, c_int, _i64p]
+        L.b2p_turn.argtypes = [c_vp, _i64p, _i64p, c_int, _i64p]
+        L.b2p_plain.argtypes = [c_vp, c_int, _i64p, c_int, _i64p]
+        L.b2p_attention.argtypes = [c_vp, _i64p, c_int, _i64p]
         _lib = L
     return _lib
 
@@ -231,3 +247,91 @@ class Oracle:
         if lib().b2o_greedy_recompute(self.h, ids, len(ids), n_new, tok, 0):
             raise RuntimeError("oracle greedy_recompute failed")
         return tok
+
+
+class PythiaOracle:
+    """The Pythia-160M machine (reference foundation0/pythia_base2.py) over converted arrays (keys of
+    base2_pythia-160m.npz; `plates=finished`, `order=plain`)."""
+
+    def __init__(self, M: dict):
+        self.M = {k: np.ascontiguousarray(v) for k, v in M.items()}
+        M = self.M
+        self.L, self.d, self.H, self.hd = (int(np.asarray(M[k]).reshape(-1)[0]) for k in ("L", "d", "heads", "hs"))
+        self.rot, self.V = int(np.asarray(M["rot"]).reshape(-1)[0]), int(np.asarray(M["vocab"]).reshape(-1)[0])
+        self.F = M["fc.0.w"].shape[1]
+        L = lib()
+        self.h = L.b2p_create(self.L, self.d, self.H, self.F, self.V, M["cos"].shape[0], self.rot)
+        self._keep = []
+        self.idx = {}
+        names = [f"{b}.{l}" for l in range(self.L) for b in ("qkv", "proj", "fc", "mproj")] + ["head"]
+        for i, name in enumerate(names):
+            w = np.ascontiguousarray(M[name + ".w"], dtype=np.int16)
+            e = _c64(M[name + ".e"])
+            b = _c64(M[name + ".b"]) if name + ".b" in M else None
+            self._keep += [w, e, b]
+            L.b2p_set_bank(self.h, i, w, e, b.ctypes.data if b is not None else None, w.shape[0], w.shape[1])
+            self.idx[name] = i
+        for i, name in enumerate([f"ln{k}.{l}" for l in range(self.L) for k in (1, 2)] + ["lnf"]):
+            g, b = _c64(M[name + ".g"]), _c64(M[name + ".b"])
+            self._keep += [g, b]
+            L.b2p_set_norm(self.h, i, g, int(np.asarray(M[name + ".ge"]).reshape(-1)[0]), b)
+            self.idx[name] = i
+        emb, embe = np.ascontiguousarray(M["embed.w"], dtype=np.int16), _c64(M["embed.e"])
+        t = [_c64(M[k]) for k in ("phi", "arrival", "log2", "exp2", "cos", "sin")]
+        self._keep += [emb, embe] + t
+        self.EXP2 = t[3]
+        L.b2p_set_tables(self.h, emb, embe, t[0], t[1], len(t[1]), t[2], t[3], t[4], t[5],
+                         int(np.asarray(M["eps40"]).reshape(-1)[0]), int(np.asarray(M["half_log2_hs"]).reshape(-1)[0]))
+
+    def power(self, X, F):
+        """pythia_base2.py:87-90 over one array (int64 below 2^45, exact above)."""
+        X, F = np.broadcast_arrays(_c64(X), _c64(F))
+        X, F = _c64(X), _c64(F)
+        y = np.empty_like(X)
+        if lib().b2p_power(X.ravel(), F.ravel(), X.size, self.EXP2, y.ravel()):
+            raise OverflowError("power: result outside int64")
+        return y
+
+    def gauge(self, R, name):
+        R = _c64(np.atleast_2d(R))
+        out = np.empty_like(R)
+        if lib().b2p_gauge(self.h, self.idx[name], R, R.shape[0], out):
+            raise OverflowError("gauge")
+        return out
+
+    def turn(self, X, pos):
+        X = _c64(np.atleast_2d(X))
+        out = np.empty_like(X)
+        if lib().b2p_turn(self.h, X, _c64(pos), X.shape[0], out):
+            raise AssertionError("turn: input past 2^31")
+        return out
+
+    def plain(self, X, name):
+        X = _c64(np.atleast_2d(X))
+        out = np.empty((X.shape[0], self.M[name + ".w"].shape[1]), np.int64)
+        lib().b2p_plain(self.h, self.idx[name], X, X.shape[0], out)
+        return out
+
+    def attention(self, QKV):
+        QKV = _c64(QKV)
+        out = np.empty((QKV.shape[0], self.d), np.int64)
+        if lib().b2p_attention(self.h, QKV, QKV.shape[0], out):
+            raise RuntimeError("attention")
+        return out
+
+    def generate(self, ids, n_new: int, logits: bool = False, threads: int = 0):
+        ids = np.ascontiguousarray(np.atleast_2d(ids), dtype=np.int32)
+        B, P = ids.shape
+        tok = np.empty((B, n_new), np.int32)
+        lg = np.empty((B, n_new, self.V), np.int64) if logits else None
+        rc = lib().b2p_generate(self.h, ids, B, P, n_new, tok, lg.ctypes.data if logits else None, threads)
+        if rc:
+            raise RuntimeError(f"pythia oracle generate failed ({rc})")
+        return (tok, lg) if logits else tok
+
+    def scores(self, ids, first: int, last: int):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        out = np.empty((last - first, self.V), np.int64)
+        if lib().b2p_scores(self.h, ids, len(ids), first, last, out):
+            raise RuntimeError("pythia oracle scores failed")
+        return out

@@ -169,3 +169,119 @@ def load_gpt2(seed: int = 0, cache: bool = True) -> dict:
         np.savez(tmp, **out)
         os.replace(tmp, path)
     return out
+
+
+# ================================================================================================================
+# Pythia-160M (reference foundation0/pythia_convert.py, foundation0/pythia_base2.py)
+# ================================================================================================================
+PYTHIA160M = dict(n_layer=12, d=768, n_head=12, d_head=64, d_ff=3072, vocab=50304, n_ctx=2048, rotary_pct=0.25,
+                  rotary_base=10000, eps=1e-5)
+
+
+def pythia_seeded_state(seed: int = 0, cfg: dict = PYTHIA160M) -> dict:
+    """Safetensors-named fp32 state of a seeded random-init Pythia-160M: embed_in, embed_out, then per layer
+    query_key_value, dense, dense_h_to_4h, dense_4h_to_h (torch Linear [out, in]), each
+    float32(standard_normal) * float32(0.02) from numpy default_rng(seed) in that order; layer-norm gains 1,
+    offsets and biases 0. The same state serves as the reference's "start" and "finished" checkpoints."""
+    rng = np.random.default_rng(seed)
+    d, F, V = cfg["d"], cfg["d_ff"], cfg["vocab"]
+    s = np.float32(0.02)
+
+    def normal(shape):
+        return rng.standard_normal(shape, dtype=np.float32) * s
+
+    sd = {"gpt_neox.embed_in.weight": normal((V, d)), "embed_out.weight": normal((V, d))}
+    for l in range(cfg["n_layer"]):
+        p = f"gpt_neox.layers.{l}."
+        sd[p + "attention.query_key_value.weight"] = normal((3 * d, d))
+        sd[p + "attention.dense.weight"] = normal((d, d))
+        sd[p + "mlp.dense_h_to_4h.weight"] = normal((F, d))
+        sd[p + "mlp.dense_4h_to_h.weight"] = normal((d, F))
+        sd[p + "attention.query_key_value.bias"] = np.zeros(3 * d, np.float32)
+        sd[p + "attention.dense.bias"] = np.zeros(d, np.float32)
+        sd[p + "mlp.dense_h_to_4h.bias"] = np.zeros(F, np.float32)
+        sd[p + "mlp.dense_4h_to_h.bias"] = np.zeros(d, np.float32)
+        for ln in ("input_layernorm", "post_attention_layernorm"):
+            sd[p + ln + ".weight"] = np.ones(d, np.float32)
+            sd[p + ln + ".bias"] = np.zeros(d, np.float32)
+    sd["gpt_neox.final_layer_norm.weight"] = np.ones(d, np.float32)
+    sd["gpt_neox.final_layer_norm.bias"] = np.zeros(d, np.float32)
+    return sd
+
+
+def shared16(Wf: np.ndarray, Ws: np.ndarray, axis: int):
+    """16-bit whole numbers with one power of two per neuron along `axis`, shared by the finished and start weights
+    (reference pythia_convert.py:50-60)."""
+    mf, ms = np.abs(Wf).max(axis), np.abs(Ws).max(axis)
+    e = np.ceil(np.log2(np.maximum(np.maximum(mf, ms), 1e-30) / 32767)).astype(np.int64)
+    sh = np.expand_dims(e, axis)
+    qf, qs = np.round(Wf / 2.0 ** sh).astype(np.int64), np.round(Ws / 2.0 ** sh).astype(np.int64)
+    if np.abs(qf).max() > 32767 or np.abs(qs).max() > 32767:
+        raise ValueError("shared16: a weight does not fit 16 bits")
+    return qf.astype(np.int16), qs.astype(np.int16), e
+
+
+def convert_pythia(finished: dict, start: dict | None = None, cfg: dict = PYTHIA160M) -> dict:
+    """Pythia state(s) -> the base-2 machine's arrays, keyed like base2_pythia-160m.npz (pythia_convert.py:64-110)."""
+    start = finished if start is None else start
+
+    def get(sd, k):
+        return np.asarray(sd[("gpt_neox." + k) if not k.startswith("embed_out") else k], dtype=np.float64)
+
+    out = {}
+
+    def plate(name, key, bias=True):
+        Wf, Ws = get(finished, key + ".weight").T, get(start, key + ".weight").T
+        out[name + ".w"], out[name + ".s"], out[name + ".e"] = shared16(Wf, Ws, 0)
+        if bias:
+            out[name + ".b"], out[name + ".bs"] = stream(get(finished, key + ".bias")), stream(get(start, key + ".bias"))
+
+    def norm(name, key):
+        gf, gs = get(finished, key + ".weight"), get(start, key + ".weight")
+        ge = int(np.ceil(np.log2(max(np.abs(gf).max(), np.abs(gs).max()) / 32767)))
+        out[name + ".g"] = np.round(gf / 2.0 ** ge).astype(np.int64)
+        out[name + ".gs"] = np.round(gs / 2.0 ** ge).astype(np.int64)
+        out[name + ".ge"] = np.array(ge)
+        out[name + ".b"], out[name + ".bs"] = stream(get(finished, key + ".bias")), stream(get(start, key + ".bias"))
+
+    L, d, NH = cfg["n_layer"], cfg["d"], cfg["n_head"]
+    HS = d // NH
+    ROT = int(HS * cfg["rotary_pct"])
+    for l in range(L):
+        p = f"layers.{l}."
+        norm(f"ln1.{l}", p + "input_layernorm")
+        norm(f"ln2.{l}", p + "post_attention_layernorm")
+        plate(f"qkv.{l}", p + "attention.query_key_value")
+        plate(f"proj.{l}", p + "attention.dense")
+        plate(f"fc.{l}", p + "mlp.dense_h_to_4h")
+        plate(f"mproj.{l}", p + "mlp.dense_4h_to_h")
+    norm("lnf", "final_layer_norm")
+    plate("head", "embed_out", bias=False)
+    out["embed.w"], out["embed.s"], out["embed.e"] = shared16(get(finished, "embed_in.weight"),
+                                                              get(start, "embed_in.weight"), 1)
+    t = tables()
+    for k in ("phi", "arrival", "log2", "exp2"):
+        out[k] = t[k]
+    inv = float(cfg["rotary_base"]) ** (-np.arange(0, ROT, 2) / ROT)
+    ang = np.arange(cfg["n_ctx"])[:, None] * inv[None, :]
+    out["cos"] = np.array([[round(math.cos(x) * 2 ** 30) for x in row] for row in ang], dtype=np.int64)
+    out["sin"] = np.array([[round(math.sin(x) * 2 ** 30) for x in row] for row in ang], dtype=np.int64)
+    out["eps40"] = np.array(round(cfg["eps"] * d * d * 2 ** 40))
+    out["half_log2_hs"] = np.array(round(math.log2(HS) / 2 * 65536))
+    for k, v in dict(d=d, L=L, heads=NH, hs=HS, rot=ROT, vocab=cfg["vocab"]).items():
+        out[k] = np.array(v)
+    return out
+
+
+def load_pythia(seed: int = 0, cache: bool = True) -> dict:
+    """The converted seeded Pythia-160M machine, cached as an .npz."""
+    path = os.path.join(cache_dir(), f"base2_pythia160m_seed{seed}.npz")
+    if cache and os.path.exists(path):
+        with np.load(path) as z:
+            return {k: z[k] for k in z.files}
+    out = convert_pythia(pythia_seeded_state(seed))
+    if cache:
+        tmp = path + f".tmp{os.getpid()}.npz"
+        np.savez(tmp, **out)
+        os.replace(tmp, path)
+    return out
