@@ -1,5 +1,6 @@
 /*
- * base2.h -- C ABI of libbase2cuda.so, the B200 (sm_100a) engine for streaming-machine's integer-only GPT-2.
+ * base2.h -- C ABI of libbase2cuda.so, the B200 (sm_100a) engine for streaming-machine's integer-only GPT-2 and
+ * its Pythia variant (foundation0/pythia_base2.py).
  *
  * The reference has no FFI: its "API" is base2.py's module namespace (forward, gauged_bank, plain_bank, attention,
  * edge, race, ...; base2.py:18-114), the converter's npz keys (base2_convert.py:31-61) and the Metal engine's prompt
@@ -46,23 +47,27 @@ typedef struct {
     int32_t d_model;    /* 768 */
     int32_t n_head;     /* 12 (head size d_model / n_head = 64) */
     int32_t d_ff;       /* 3072 */
-    int32_t vocab;      /* 50257 (GPT-2) */
-    int32_t n_ctx;      /* 1024: rows of the position table */
+    int32_t vocab;      /* 50257 (GPT-2), 50304 (Pythia-160M) */
+    int32_t n_ctx;      /* 1024: rows of the position table (GPT-2); 2048: rows of the turn tables (Pythia) */
 } b2_config;
 
 /* Create a handle on `device` (replaces base2.py's module import, base2.py:10-16). flags: B2_*_FLOAT bits. */
 int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out);
 
 /* One weight bank in the converter's layout (base2_convert.py:40-45, base2_gpu.py:9-14): name "qkv.L", "proj.L",
- * "fc.L", "mproj.L" or "head"; w [nin][nout] int16, e [nout] per-column power of two, b [nout] bias (stream scale). */
+ * "fc.L", "mproj.L" or "head"; w [nin][nout] int16, e [nout] per-column power of two, b [nout] bias (stream scale;
+ * NULL = no bias, Pythia's head, pythia_base2.py:56). Pythia's qkv columns are per head q, k, v (pythia_base2.py:126). */
 int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t* e, const int64_t* b,
                 int32_t nin, int32_t nout);
 
 /* A table or embedding by its npz key (base2_convert.py:46-59): "wte" [vocab][d], "wpe" [n_ctx][d], "phi" [65536],
- * "arrival" [n], "log2" [65536], "exp2" [65536]. */
+ * "arrival" [n], "log2" [65536], "exp2" [65536]. Pythia (pythia_convert.py's keys, `plates=finished`): "embed.w"
+ * [vocab][d] and "embed.e" [vocab] (each word's row and its power of two), "cos"/"sin" [n_ctx][rot/2] at 2^-30, and
+ * each norm's gain and offset "ln1.<l>.g", "ln1.<l>.b", "ln2.<l>.g", "ln2.<l>.b", "lnf.g", "lnf.b" [d]. */
 int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n);
 
-/* A scalar by its npz key: "log2_768", "eps40" (base2_convert.py:60-61). */
+/* A scalar by its npz key: "log2_768", "eps40" (base2_convert.py:60-61); Pythia: "eps40", "half_log2_hs", "rot"
+ * (16) and each norm's gain exponent "ln1.<l>.ge", "ln2.<l>.ge", "lnf.ge". */
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v);
 
 /* All arrays given: build the device layouts. */
@@ -92,9 +97,14 @@ int b2_generate(b2_handle* h, int32_t n_streams, int32_t n_steps, int32_t* token
 int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t* tok_out);
 
 /* One bank on given rows, for unit parity (base2.py:62-76): mode 0 = gauged_bank, 1 = gauged_bank then edge,
- * 2 = plain_bank. X [rows][nin] int64, out [rows][nout] int64 (device pointers). mode | 8 runs the decode step's
- * fused kernel instead (rows <= 64, layer banks only; mode 1 only on fc banks). */
+ * 2 = plain_bank, 3 = plain_bank then edge (Pythia's fc, pythia_base2.py:166; Pythia takes modes 2 and 3 only).
+ * X [rows][nin] int64, out [rows][nout] int64 (device pointers). mode | 8 runs the decode step's fused kernel instead
+ * (GPT-2, rows <= 64, layer banks only; mode 1 only on fc banks). */
 int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode, void* stream);
+
+/* Pythia's layer norm on given rows (pythia_base2.py:100-110, gauge(R, name)): name "ln1.<l>", "ln2.<l>" or "lnf";
+ * X, out [rows][d] int64 (device pointers). */
+int b2_gauge(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, void* stream);
 
 /* Truncate streams 0..n_streams-1 back to lens[s] positions with last_tok[s] as the word to feed next (device
  * pointers). Keys/values below lens[s] are kept. A truncation past a stream's current length is a device-checked

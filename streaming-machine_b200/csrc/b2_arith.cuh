@@ -57,6 +57,27 @@ B2_DEV int64_t power(int64_t x, int64_t F, const int32_t* __restrict__ EXP2) {
     return rshift(wmul(x, (int64_t)__ldg(EXP2 + f)), 16 - I);
 }
 
+// pythia_base2.py:87-90: power with Python's whole numbers (the reference leaves int64 past |X| >= 2^45): the
+// product in 128 bits, the rounded shift, the result back in int64. *bad is set when it does not fit (where the
+// reference's astype(np.int64) raises). Equals power() whenever power() does not wrap.
+B2_DEV int64_t power_exact(int64_t x, int64_t F, const int32_t* __restrict__ EXP2, bool* bad) {
+    const int64_t I = F >> 16, f = F & 0xFFFF, s = 16 - I;
+    const __int128 p = (__int128)x * (__int128)__ldg(EXP2 + f);
+    __int128 r;
+    if (s <= 0) {
+        if (p == 0) return 0;
+        if (-s >= 64) { *bad = true; return 0; }
+        r = p << (-s);
+        if ((r >> (-s)) != p) { *bad = true; return 0; }
+    } else if (s >= 100) {
+        r = 0;                                    // |p| < 2^81
+    } else {
+        r = (p + ((__int128)1 << (s - 1))) >> s;  // floor, as Python's >>
+    }
+    if (r > (__int128)INT64_MAX || r < (__int128)INT64_MIN) { *bad = true; return 0; }
+    return (int64_t)r;
+}
+
 // base2.py:78-83 (integer bend)
 B2_DEV int64_t edge(int64_t h, const int32_t* __restrict__ PHI) {
     int64_t idx = wadd(rshift(h, 16 - 12), 32768);
@@ -86,6 +107,11 @@ B2_DEV int64_t warp_sum64(int64_t v) {
 B2_DEV int64_t warp_max64(int64_t v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) { int64_t u = __shfl_xor_sync(0xffffffffu, v, o); v = u > v ? u : v; }
+    return v;
+}
+B2_DEV uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) { uint64_t u = __shfl_xor_sync(0xffffffffu, v, o); v = u > v ? u : v; }
     return v;
 }
 // (value, index) keep-larger with ties to the lower index: the race (base2.py:34-40)

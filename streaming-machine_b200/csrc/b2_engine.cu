@@ -40,6 +40,20 @@ struct b2_handle {
     int alen = 0;
     int64_t log768 = 0, eps40 = 0;
     bool have_scalar[2] = {false, false};
+
+    // Pythia (kind B2_PYTHIA, pythia_base2.py): the layer norms kept whole (gain g at 2^ge, offset b), ln1.l at 2l,
+    // ln2.l at 2l + 1, lnf at 2L; the turn tables [n_ctx][rot/2] at 2^-30; the score's half power; the word rows
+    // (embed.w, one power of two per word in embed.e) held on the host until b2_finalize puts them on the 2^-16 scale
+    struct Norm {
+        int64_t *g = nullptr, *b = nullptr;
+        int64_t ge = 0;
+        bool have_ge = false;
+    };
+    std::vector<Norm> norms;
+    int32_t *COS = nullptr, *SIN = nullptr;
+    int64_t cs_len = 0, half = 0, rot = 0;
+    bool have_half = false, have_rot = false;
+    std::vector<int64_t> emb_w, emb_e;
     bool finalized = false;
     int use_tc = 1;               // tensor-core bank product for row counts >= tc_min_rows
     int tc_min_rows = 1 << 30;    // (set at finalize when the tensor path is available)
@@ -144,6 +158,18 @@ int bank_index(const b2_handle* h, const char* name) {
     return -1;
 }
 
+// Pythia norm names: "ln1.<l>.<part>", "ln2.<l>.<part>", "lnf.<part>" -> index (2l, 2l + 1, 2L) and the part
+int norm_index(const b2_handle* h, const char* name, const char** part) {
+    if (h->cfg.kind != B2_PYTHIA) return -1;
+    if (!strncmp(name, "lnf.", 4)) { *part = name + 4; return 2 * h->cfg.n_layer; }
+    if (strncmp(name, "ln", 2) || (name[2] != '1' && name[2] != '2') || name[3] != '.') return -1;
+    char* end = nullptr;
+    long l = strtol(name + 4, &end, 10);
+    if (end == name + 4 || *end != '.' || l < 0 || l >= h->cfg.n_layer) return -1;
+    *part = end + 1;
+    return 2 * (int)l + (name[2] - '1');
+}
+
 int upload_table32(b2_handle* h, int32_t** dst, const int64_t* src, int64_t n, const char* name) {
     std::vector<int32_t> t((size_t)n);
     for (int64_t i = 0; i < n; i++) {
@@ -222,6 +248,7 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         case EPI_GAUGED: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_GAUGED, RT>, grid, 256, 0, st, a);
         case EPI_GAUGED_EDGE: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_GAUGED_EDGE, RT>, grid, 256, 0, st, a);
         case EPI_PLAIN_ADD: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_PLAIN_ADD, RT>, grid, 256, 0, st, a);
+        case EPI_PLAIN_EDGE: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_PLAIN_EDGE, RT>, grid, 256, 0, st, a);
         default: return launch(h, B2_PROF_BANK, "bank_simt", k_bank_simt<EPI_PLAIN_OUT, RT>, grid, 256, 0, st, a);
     }
 }
@@ -240,18 +267,66 @@ int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, in
 // the arrival for `rows` rows at layer l: bulk-copy kernel while a stream's keys fit in shared memory
 int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st) {
     AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
-                or_out};
+                or_out, h->half};
+    const bool py = h->cfg.kind == B2_PYTHIA;
+    const dim3 grid(rows, h->cfg.n_head);
     const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
     if (h->att_bulk && bulk <= ATT_BULK_MAX)
-        return launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4>, dim3(rows, h->cfg.n_head), 128, bulk, st, aa);
-    return launch(h, B2_PROF_ATTEND, "attend", k_attend<4>, dim3(rows, h->cfg.n_head), 128, sizeof(int64_t) * h->max_ctx,
-                  st, aa);
+        return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, true>, grid, 128, bulk, st, aa)
+                  : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, false>, grid, 128, bulk, st, aa);
+    const size_t sm = sizeof(int64_t) * h->max_ctx;
+    return py ? launch(h, B2_PROF_ATTEND, "attend", k_attend<4, true>, grid, 128, sm, st, aa)
+              : launch(h, B2_PROF_ATTEND, "attend", k_attend<4, false>, grid, 128, sm, st, aa);
+}
+
+// Pythia's layer norm (pythia_base2.py:100-110) of rows of X (gathered by src_rows when given) into out [rows][d]
+int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows, int ni, int64_t* out, cudaStream_t st) {
+    const b2_handle::Norm& nm = h->norms[ni];
+    return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, rows, 256, 0, st, X, h->cfg.d_model, src_rows, rows,
+                  (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2, (const int32_t*)h->EXP2,
+                  h->eps40, h->d_err);
+}
+
+// Pythia's layers + head (pythia_base2.py:161-169): the parallel residual R <- R + A(g1 R) + M(g2 R). Both norms read R
+// before either branch adds into it; the branch sums go into R in the order mproj, proj (wrapping int64 adds, so the
+// order does not change R). Buffers: g1 R in ATT until the qkv bank has read it, g2 R in HID until the fc bank has.
+int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
+                    int32_t* words_by_slot, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
+    int rc;
+    if ((rc = launch(h, B2_PROF_OTHER, "embed", k_embed, rows, 256, 0, st, h->row_tok, h->row_pos, rows, h->wte,
+                     (const int64_t*)nullptr, d, c.vocab, c.n_ctx, h->R, h->d_err)))
+        return rc;
+    for (int l = 0; l < L; l++) {
+        if ((rc = run_gauge(h, h->R, nullptr, rows, 2 * l, h->ATT, st))) return rc;
+        if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, rows, h->QKV, 3 * d, nullptr, st))) return rc;
+        if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(rows, 3 * H), 32, 0, st,
+                         (const int64_t*)h->QKV, rows, (const int32_t*)h->row_slot, (const int32_t*)h->row_pos, l, h->kv,
+                         (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err)))
+            return rc;
+        if ((rc = run_attend(h, rows, l, nullptr, st))) return rc;
+        if ((rc = run_gauge(h, h->R, nullptr, rows, 2 * l + 1, h->HID, st))) return rc;
+        if ((rc = run_quant(h, h->HID, d, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 2, EPI_PLAIN_EDGE, rows, h->HID, F, nullptr, st))) return rc;
+        if ((rc = run_quant(h, h->HID, F, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
+        if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
+        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
+    }
+    if (nhead <= 0) return B2_OK;
+    if ((rc = run_gauge(h, h->R, hrows, nhead, 2 * L, h->ATT, st))) return rc;
+    if ((rc = run_quant(h, h->ATT, d, nullptr, nhead, 0, st))) return rc;
+    if ((rc = run_bank(h, 4 * L, EPI_PLAIN_OUT, nhead, logits, c.vocab, hmap, st))) return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race, nhead, 1024, 0, st, logits, c.vocab, hmap, c.vocab, words_by_slot);
 }
 
 // ---- all layers + head for the rows in the row table --------------------------------------------------------------
 // head rows: rows [0, nhead) of `hrows` (row indices) are scored; their logits go to out rows hmap (slot ids).
 int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
              int32_t* words_by_slot, cudaStream_t st) {
+    if (h->cfg.kind == B2_PYTHIA) return run_rows_pythia(h, rows, hrows, hmap, nhead, logits, words_by_slot, st);
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
     int rc;
@@ -343,7 +418,9 @@ int run_decode(b2_handle* h, int n, cudaStream_t st) {
                   c.vocab, h->race_out);
 }
 
-bool fused_avail(const b2_handle* h, int n) { return h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS; }
+bool fused_avail(const b2_handle* h, int n) {
+    return h->cfg.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS;
+}
 bool fused_ok(const b2_handle* h, int n) { return h->fused && fused_avail(h, n); }
 
 int ensure_ready(b2_handle* h) {
@@ -363,6 +440,9 @@ int read_device_error(b2_handle* h) {
     if (e & DERR_VOVF) return fail(h, B2_ERR_VALUE, "a value-store entry did not fit int32 (device check, bits 0x%x)", e);
     if (e & DERR_INDEX) return fail(h, B2_ERR_VALUE, "an arrival index fell below the table (device check, bits 0x%x)", e);
     if (e & DERR_TIMEOUT) return fail(h, B2_ERR_DEVICE, "a tensor-core kernel's bounded wait gave up (device check, bits 0x%x)", e);
+    if (e & DERR_RANGE)
+        return fail(h, B2_ERR_VALUE, "a value passed the range the reference asserts (turn input >= 2^31, a power or the "
+                    "arrival's sum past int64; device check, bits 0x%x)", e);
     return fail(h, B2_ERR_DEVICE, "a token id was out of range (device check, bits 0x%x)", e);
 }
 
@@ -380,7 +460,7 @@ const char* b2_last_error(const b2_handle* h) { return h ? h->err.c_str() : "nul
 int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (!cfg || !out) return B2_ERR_ARG;
     *out = nullptr;
-    if (cfg->kind != B2_GPT2) return B2_ERR_ARG;
+    if (cfg->kind != B2_GPT2 && cfg->kind != B2_PYTHIA) return B2_ERR_ARG;
     if (cfg->n_layer < 1 || cfg->n_layer > 64 || cfg->n_head < 1 || cfg->d_model != cfg->n_head * 64 ||
         cfg->d_model % 256 || cfg->d_ff % 256 || cfg->vocab < 1 || cfg->n_ctx < 1)
         return B2_ERR_ARG;
@@ -390,12 +470,14 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     h->device = device;
     h->flags = flags;
     h->banks.resize(4 * cfg->n_layer + 1);
+    if (cfg->kind == B2_PYTHIA) h->norms.resize(2 * cfg->n_layer + 1);
     if (const char* v = getenv("B2_PDL")) h->pdl = atoi(v);
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
     if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
-    if (cudaFuncSetAttribute(k_attend_bulk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
+    if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
         delete h;
         return B2_ERR_CUDA;
     }
@@ -406,7 +488,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
 }
 
 int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t* e, const int64_t* b, int32_t nin, int32_t nout) {
-    if (!h || !name || !w || !e || !b) return fail(h, B2_ERR_ARG, "b2_set_bank: null argument");
+    if (!h || !name || !w || !e) return fail(h, B2_ERR_ARG, "b2_set_bank: null argument");
     CK(cudaSetDevice(h->device));
     int bi = bank_index(h, name);
     if (bi < 0) return fail(h, B2_ERR_ARG, "b2_set_bank: unknown bank '%s'", name);
@@ -432,7 +514,8 @@ int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t*
     }
     CK(cudaMemcpy(bk.w, w, sizeof(int16_t) * (size_t)nin * nout, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(bk.e, e32.data(), sizeof(int32_t) * nout, cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(bk.b, b, sizeof(int64_t) * nout, cudaMemcpyHostToDevice));
+    if (b) CK(cudaMemcpy(bk.b, b, sizeof(int64_t) * nout, cudaMemcpyHostToDevice));
+    else CK(cudaMemset(bk.b, 0, sizeof(int64_t) * nout));   // no bias (Pythia's head, pythia_base2.py:56)
     h->finalized = false;
     return B2_OK;
 }
@@ -457,6 +540,22 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
         if (n > (1 << 24)) return fail(h, B2_ERR_ARG, "arrival: too long");
         if ((rc = upload_table32(h, &h->ARR, data, n, name))) return rc;
         h->alen = (int)n;
+    } else if (c.kind == B2_PYTHIA && (!strcmp(name, "cos") || !strcmp(name, "sin"))) {
+        if (n % c.n_ctx) return fail(h, B2_ERR_ARG, "%s: %lld values, want n_ctx (%d) x rot/2", name, (long long)n, c.n_ctx);
+        if ((rc = upload_table32(h, name[0] == 'c' ? &h->COS : &h->SIN, data, n, name))) return rc;
+        h->cs_len = n;
+    } else if (c.kind == B2_PYTHIA && (!strcmp(name, "embed.w") || !strcmp(name, "embed.e"))) {
+        const bool rows = name[6] == 'w';
+        const int64_t want = rows ? (int64_t)c.vocab * c.d_model : c.vocab;
+        if (n != want) return fail(h, B2_ERR_ARG, "%s: %lld values, want %lld", name, (long long)n, (long long)want);
+        (rows ? h->emb_w : h->emb_e).assign(data, data + n);
+    } else if (const char* part = nullptr; norm_index(h, name, &part) >= 0 && (!strcmp(part, "g") || !strcmp(part, "b"))) {
+        if (n != c.d_model) return fail(h, B2_ERR_ARG, "%s: %lld values, want %d", name, (long long)n, c.d_model);
+        b2_handle::Norm& nm = h->norms[norm_index(h, name, &part)];
+        int64_t** dst = part[0] == 'g' ? &nm.g : &nm.b;
+        if (*dst) dfree(h, *dst);
+        if ((rc = dalloc(h, dst, (size_t)n))) return rc;
+        CK(cudaMemcpy(*dst, data, sizeof(int64_t) * n, cudaMemcpyHostToDevice));
     } else {
         return fail(h, B2_ERR_ARG, "b2_set_array: unknown array '%s'", name);
     }
@@ -466,18 +565,79 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
 
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v) {
     if (!h || !name) return B2_ERR_ARG;
+    const char* part = nullptr;
+    const int ni = norm_index(h, name, &part);
     if (!strcmp(name, "log2_768")) { h->log768 = v; h->have_scalar[0] = true; }
     else if (!strcmp(name, "eps40")) { h->eps40 = v; h->have_scalar[1] = true; }
-    else return fail(h, B2_ERR_ARG, "b2_set_scalar: unknown scalar '%s'", name);
+    else if (h->cfg.kind == B2_PYTHIA && !strcmp(name, "half_log2_hs")) { h->half = v; h->have_half = true; }
+    else if (h->cfg.kind == B2_PYTHIA && !strcmp(name, "rot")) { h->rot = v; h->have_rot = true; }
+    else if (ni >= 0 && !strcmp(part, "ge")) {
+        if (v < -64 || v > 64) return fail(h, B2_ERR_VALUE, "%s = %lld out of range", name, (long long)v);
+        h->norms[ni].ge = v;
+        h->norms[ni].have_ge = true;
+    } else return fail(h, B2_ERR_ARG, "b2_set_scalar: unknown scalar '%s'", name);
+    h->finalized = false;
     return B2_OK;
 }
+
+namespace {
+// Pythia's own arrays checked, and the word rows put on the stream's scale once: R0 = rshift(embed.w, -(embed.e + 16))
+// (pythia_base2.py:163), kept as the [vocab][d] int64 table the embedding kernel reads
+int finalize_pythia(b2_handle* h) {
+    const b2_config& c = h->cfg;
+    for (size_t i = 0; i < h->norms.size(); i++)
+        if (!h->norms[i].g || !h->norms[i].b || !h->norms[i].have_ge) return fail(h, B2_ERR_STATE, "norm %zu not set", i);
+    if (!h->have_rot || h->rot != 16)
+        return fail(h, B2_ERR_ARG, "rot = %lld: the turn kernel takes 16 turned dims per head", (long long)h->rot);
+    if (!h->have_half) return fail(h, B2_ERR_STATE, "half_log2_hs not set");
+    if (!h->COS || !h->SIN || h->cs_len != (int64_t)c.n_ctx * (h->rot / 2))
+        return fail(h, B2_ERR_STATE, "cos/sin missing or not [n_ctx][rot/2]");
+    if (h->emb_w.empty() || h->emb_e.empty()) {
+        if (h->wte) return B2_OK;    // already built by an earlier finalize
+        return fail(h, B2_ERR_STATE, "embed.w / embed.e not set");
+    }
+    const int d = c.d_model;
+    std::vector<int64_t> t((size_t)c.vocab * d);
+    for (int v = 0; v < c.vocab; v++) {
+        const int64_t s = h->emb_e[v] + 16;   // a left shift by s (the reference's rshift by -s)
+        for (int i = 0; i < d; i++) {
+            const int64_t x = h->emb_w[(size_t)v * d + i];
+            int64_t y;
+            if (s >= 0) {
+                const uint64_t m = x < 0 ? (uint64_t)0 - (uint64_t)x : (uint64_t)x;
+                if (s > 61 || (m >> (62 - s)) != 0)
+                    return fail(h, B2_ERR_VALUE, "embed row %d: a value past 2^62 on the stream's scale", v);
+                y = (int64_t)((uint64_t)x << s);
+            } else {
+                const int64_t r = -s;                 // rounded: add half, shift (|x| < 2^15, r <= 62 keeps it exact)
+                if (r > 62) return fail(h, B2_ERR_VALUE, "embed row %d: exponent %lld out of range", v, (long long)h->emb_e[v]);
+                y = (x + ((int64_t)1 << (r - 1))) >> r;
+            }
+            t[(size_t)v * d + i] = y;
+        }
+    }
+    if (h->wte) dfree(h, h->wte);
+    int rc = dalloc(h, &h->wte, t.size());
+    if (rc) return rc;
+    CK(cudaMemcpy(h->wte, t.data(), sizeof(int64_t) * t.size(), cudaMemcpyHostToDevice));
+    std::vector<int64_t>().swap(h->emb_w);
+    std::vector<int64_t>().swap(h->emb_e);
+    return B2_OK;
+}
+}  // namespace
 
 int b2_finalize(b2_handle* h) {
     if (!h) return B2_ERR_ARG;
     CK(cudaSetDevice(h->device));
     for (size_t i = 0; i < h->banks.size(); i++)
         if (!h->banks[i].w) return fail(h, B2_ERR_STATE, "bank %zu not set", i);
-    if (!h->wte || !h->wpe || !h->PHI || !h->ARR || !h->LOG2 || !h->EXP2 || !h->have_scalar[0] || !h->have_scalar[1])
+    if (h->cfg.kind == B2_PYTHIA) {
+        int rc = finalize_pythia(h);
+        if (rc) return rc;
+    } else if (!h->wte || !h->wpe || !h->have_scalar[0]) {
+        return fail(h, B2_ERR_STATE, "a table or scalar is missing");
+    }
+    if (!h->PHI || !h->ARR || !h->LOG2 || !h->EXP2 || !h->have_scalar[1])
         return fail(h, B2_ERR_STATE, "a table or scalar is missing");
     // tensor-core layouts of every bank
     int tc_ok = tc_init() == 0;
@@ -713,13 +873,15 @@ int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int6
     int bi = bank_index(h, name);
     const int fusedm = mode & 8;
     mode &= 7;
-    if (bi < 0 || !X || !out || rows < 1 || rows > h->max_rows || mode < 0 || mode > 2)
+    if (bi < 0 || !X || !out || rows < 1 || rows > h->max_rows || mode < 0 || mode > 3)
         return fail(h, B2_ERR_ARG, "b2_bank: bad argument");
+    if (h->cfg.kind == B2_PYTHIA && (mode < 2 || fusedm))
+        return fail(h, B2_ERR_ARG, "b2_bank: Pythia's banks are plain (modes 2 and 3); its norm is b2_gauge");
     cudaStream_t st = (cudaStream_t)stream;
     const DevBank& bk = h->banks[bi];
     if (fusedm) {
         // the fused decode kernel on its own: rows <= 64, not the head, q/k/v values returned (no key/value append)
-        if (rows > FUSED_ROWS || bi == 4 * h->cfg.n_layer || !fused_avail(h, rows) || (mode == 1) != (bi % 4 == 2))
+        if (rows > FUSED_ROWS || bi == 4 * h->cfg.n_layer || !fused_avail(h, rows) || mode == 3 || (mode == 1) != (bi % 4 == 2))
             return fail(h, B2_ERR_ARG, "b2_bank: the fused kernel takes <= %d rows of a layer bank", FUSED_ROWS);
         uint64_t* xor_in = h->row_or;
         if ((rc = launch(h, B2_PROF_QUANT, "row_or", k_row_or, rows, 256, 0, st, X, bk.nin, rows, xor_in))) return rc;
@@ -728,8 +890,20 @@ int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int6
         return run_fused(h, bi, mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_ADD), a, st);
     }
     if ((rc = run_quant(h, X, bk.nin, nullptr, rows, mode < 2, st))) return rc;
-    int epi = mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_OUT);
-    return run_bank(h, bi, epi, rows, out, bk.nout, nullptr, st);
+    const int epi[4] = {EPI_GAUGED, EPI_GAUGED_EDGE, EPI_PLAIN_OUT, EPI_PLAIN_EDGE};
+    return run_bank(h, bi, epi[mode], rows, out, bk.nout, nullptr, st);
+}
+
+int b2_gauge(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, void* stream) {
+    int rc = ensure_ready(h);
+    if (rc) return rc;
+    const char* part = nullptr;
+    char full[64];
+    snprintf(full, sizeof full, "%s.g", name ? name : "");
+    const int ni = name ? norm_index(h, full, &part) : -1;
+    if (ni < 0 || !X || !out || rows < 1 || rows > h->max_rows)
+        return fail(h, B2_ERR_ARG, "b2_gauge: bad argument (a Pythia norm name: ln1.<l>, ln2.<l> or lnf)");
+    return run_gauge(h, X, nullptr, rows, ni, out, (cudaStream_t)stream);
 }
 
 int b2_rewind(b2_handle* h, int32_t n_streams, const int32_t* lens, const int32_t* last_tok, void* stream) {

@@ -13,6 +13,7 @@ enum : uint32_t {
     DERR_VOVF = 4u,      // a V value outside int32 (the value store holds int32)
     DERR_INDEX = 8u,     // an arrival-table index below -len (where base2.py raises IndexError)
     DERR_TIMEOUT = 16u,  // a bounded wait in a tensor-core kernel gave up (the results of that call are void)
+    DERR_RANGE = 32u,    // a value where the reference raises: an exact power outside int64, a turn input past 2^31
 };
 
 B2_DEV void set_err(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
@@ -32,7 +33,7 @@ B2_DEV size_t kv_index(int slot, int layer, int head, int pos, int L, int H, int
     return (((size_t)slot * L + layer) * H + head) * (size_t)ctx + pos;
 }
 
-enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3 };
+enum { EPI_GAUGED = 0, EPI_GAUGED_EDGE = 1, EPI_PLAIN_ADD = 2, EPI_PLAIN_OUT = 3, EPI_PLAIN_EDGE = 4 };
 
 // what a bank does with a finished pile (row r, output column j)
 struct EpiArgs {
@@ -58,7 +59,8 @@ B2_DEV int64_t epi_value(int64_t pile, int64_t e_j, int64_t b_j, int64_t exr, in
         int64_t v = wadd(rshift(wmul(pile, e2r), 16 - (F >> 16)), b_j);
         return EPI == EPI_GAUGED_EDGE ? edge(v, PHI) : v;
     }
-    return wadd(rshift(pile, -es), b_j);
+    const int64_t v = wadd(rshift(pile, -es), b_j);
+    return EPI == EPI_PLAIN_EDGE ? edge(v, PHI) : v;     // pythia_base2.py:156 edge(plain(..., fc))
 }
 
 // PDL: wait for the kernels this one depends on (no-op without programmatic launch), and let the next one start
@@ -77,6 +79,7 @@ B2_DEV void epi_store(const EpiArgs& a, int r, int j, int64_t pile) {
         *o = v;
     } else {
         int64_t v = wadd(rshift(pile, -es), a.b[j]);       // base2.py:76
+        if (EPI == EPI_PLAIN_EDGE) v = edge(v, a.PHI);
         *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;       // base2.py:105-106 R = R + ...
     }
 }

@@ -25,8 +25,8 @@ __global__ void k_embed(const int32_t* __restrict__ row_tok, const int32_t* __re
     if (tok < 0 || tok >= V) { if (threadIdx.x == 0) set_err(err, DERR_TOKEN); tok = 0; }
     if (pos < 0 || pos >= nctx) { if (threadIdx.x == 0) set_err(err, DERR_POS); pos = 0; }
     const int64_t* a = wte + (size_t)tok * d;
-    const int64_t* b = wpe + (size_t)pos * d;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) R[(size_t)r * d + i] = wadd(__ldg(a + i), __ldg(b + i));
+    const int64_t* b = wpe ? wpe + (size_t)pos * d : nullptr;   // Pythia has no position table (rotary instead)
+    for (int i = threadIdx.x; i < d; i += blockDim.x) R[(size_t)r * d + i] = b ? wadd(__ldg(a + i), __ldg(b + i)) : __ldg(a + i);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -100,6 +100,118 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
             pl.nsat[r] = s_nsat;
             pl.rowcorr[r] = 128 * (S1 - 256 * (int64_t)s_nsat);
         }
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Pythia's gauge (pythia_base2.py:100-110), the layer norm kept whole: to16 of the row, S1, S2,
+// V = d*S2 - S1^2 + (EPS40 >> (40 + 2 ex)), LS = log2fix(V) >> 1, and for each lane
+// out = power(c * g, (ge + 16) * 65536 - LS) + b with c = d * x16 - S1 (power exactly, as the reference's big ints).
+// One CTA per row; src_rows (optional) gathers rows. Output int64 [rows][d] (the plain bank after it to16s it).
+// ---------------------------------------------------------------------------------------------------------------------
+template <int NT>
+__global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, int d, const int32_t* __restrict__ src_rows,
+                                                 int rows, const int64_t* __restrict__ g, int64_t ge,
+                                                 const int64_t* __restrict__ b, int64_t* __restrict__ out,
+                                                 const int32_t* __restrict__ LOG2, const int32_t* __restrict__ EXP2,
+                                                 int64_t eps40, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ uint64_t s_or[NT / 32];
+    __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
+    __shared__ int64_t s_F, s_S1;
+    const int r = blockIdx.x;
+    if (r >= rows) return;
+    const int sr = src_rows ? src_rows[r] : r;
+    const int64_t* x = R + (size_t)sr * d;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    uint64_t o = 0;
+    for (int i = threadIdx.x; i < d; i += NT) o |= mag(x[i]);
+    o = warp_or64(o);
+    if (lane == 0) s_or[wid] = o;
+    __syncthreads();
+    uint64_t all = 0;
+#pragma unroll
+    for (int k = 0; k < NT / 32; k++) all |= s_or[k];
+    const int sh = to16_shift(all);
+    int64_t q1 = 0, q2 = 0;
+    for (int i = threadIdx.x; i < d; i += NT) {
+        const int64_t v = rshift(x[i], sh);
+        q1 += v;
+        q2 += v * v;
+    }
+    q1 = warp_sum64(q1);
+    q2 = warp_sum64(q2);
+    if (lane == 0) { s_1[wid] = q1; s_2[wid] = q2; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int64_t S1 = 0, S2 = 0;
+        for (int k = 0; k < NT / 32; k++) { S1 = wadd(S1, s_1[k]); S2 = wadd(S2, s_2[k]); }
+        const int64_t ex = -16 + sh;
+        const int64_t V = wadd(wsub(wmul(d, S2), wmul(S1, S1)), np_rsh(eps40, 40 + 2 * ex));
+        const int64_t LS = log2fix(V, LOG2) >> 1;
+        s_F = wsub(wmul(wadd(ge, 16), 65536), LS);
+        s_S1 = S1;
+    }
+    __syncthreads();
+    const int64_t F = s_F, S1 = s_S1;
+    bool bad = false;
+    for (int i = threadIdx.x; i < d; i += NT) {
+        const int64_t c = wsub(wmul(d, rshift(x[i], sh)), S1);
+        out[(size_t)r * d + i] = wadd(power_exact(wmul(c, g[i]), F, EXP2, &bad), b[i]);
+    }
+    if (bad) set_err(err, DERR_RANGE);
+}
+
+// Pythia's q/k/v split (pythia_base2.py:116-134): one warp per (row, part of 3H), parts ordered per head q, k, v.
+// q and k: the first `rot` dims turned by the position (pairs (i, i + rot/2), cos/sin at 2^-30; inputs past 2^31
+// are where the reference asserts), then to16 over the head; v to the value store as it is.
+__global__ void k_heads_pythia(const int64_t* __restrict__ QKV, int rows, const int32_t* __restrict__ row_slot,
+                               const int32_t* __restrict__ row_pos, int layer, KV kv, int rot,
+                               const int32_t* __restrict__ COS, const int32_t* __restrict__ SIN, int32_t* __restrict__ q16,
+                               int32_t* __restrict__ qexp, uint32_t* err) {
+    griddep_wait();
+    griddep_launch();
+    const int r = blockIdx.x, part = blockIdx.y, lane = threadIdx.x;
+    const int H = kv.H, d = H * 64, h = part / 3, kind = part % 3;
+    if (r >= rows) return;
+    const int64_t* x = QKV + (size_t)r * 3 * d + (size_t)part * 64;
+    int64_t v0 = x[lane], v1 = x[lane + 32];
+    const int slot = row_slot[r], pos = row_pos[r];
+    if (pos < 0 || pos >= kv.lim) { if (lane == 0) set_err(err, DERR_POS); return; }   // never index past the tables
+    if (kind < 2) {
+        const int half = rot >> 1;                                       // rot == 16: pairs (t, t + 8) in lanes 0..15
+        const bool big = lane < rot && mag(v0) >= (1ull << 31);
+        if (__any_sync(0xffffffffu, big) && lane == 0) set_err(err, DERR_RANGE);
+        const int64_t other = __shfl_xor_sync(0xffffffffu, v0, half);   // lane t < half holds a, lane t + half holds b
+        if (lane < rot) {
+            const int t = lane < half ? lane : lane - half;
+            const int64_t c = COS[(size_t)pos * half + t], s = SIN[(size_t)pos * half + t];
+            if (lane < half) v0 = rshift(wsub(wmul(v0, c), wmul(other, s)), 30);          // a*c - b*s
+            else v0 = rshift(wadd(wmul(v0, c), wmul(other, s)), 30);                       // b*c + a*s
+        }
+        const int sh = to16_shift(warp_or64(mag(v0) | mag(v1)));
+        const int64_t a0 = rshift(v0, sh), a1 = rshift(v1, sh);
+        if (kind == 0) {
+            q16[(size_t)r * d + h * 64 + lane] = (int32_t)a0;
+            q16[(size_t)r * d + h * 64 + lane + 32] = (int32_t)a1;
+            if (lane == 0) qexp[r * H + h] = -16 + sh;
+        } else {
+            const size_t idx = kv_index(slot, layer, h, pos, kv.L, H, kv.ctx);
+            kv.k[idx * 64 + lane] = (int16_t)(uint16_t)(uint32_t)a0;
+            kv.k[idx * 64 + lane + 32] = (int16_t)(uint16_t)(uint32_t)a1;
+            const uint32_t m0 = __ballot_sync(0xffffffffu, a0 == 32768), m1 = __ballot_sync(0xffffffffu, a1 == 32768);
+            if (lane == 0) {
+                kv.kmask[idx] = (uint64_t)m0 | ((uint64_t)m1 << 32);
+                kv.kexp[idx] = -16 + sh;
+            }
+        }
+    } else {
+        const size_t idx = kv_index(slot, layer, h, pos, kv.L, H, kv.ctx);
+        const bool bad = v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1;
+        if (__any_sync(0xffffffffu, bad) && lane == 0) set_err(err, DERR_VOVF);
+        kv.v[idx * 64 + lane] = (int32_t)v0;
+        kv.v[idx * 64 + lane + 32] = (int32_t)v1;
     }
 }
 
@@ -213,7 +325,22 @@ struct AttnArgs {
     int64_t* out;           // [rows][d]
     uint32_t* err;
     uint64_t* or_out;       // optional [rows]: OR of |out| per row (the next bank's to16 shift)
+    int64_t half;           // Pythia: log2(head size) / 2 at 2^-16 (the score's 1/sqrt(64) as a power)
 };
+
+// the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
+// - HALF) (pythia_base2.py:135; |q.k| <= 64 * 2^30 < 2^45, the int64 power, whose left shift the reference bounds by
+// 2^62: DERR_RANGE past it)
+template <bool PY>
+B2_DEV int64_t score(int64_t dot, int64_t eq, int64_t ek, const AttnArgs& a) {
+    if (PY) {
+        const int64_t F = (eq + ek + 10) * 65536 - a.half, s = 16 - (F >> 16);
+        const int64_t p = dot * (int64_t)__ldg(a.EXP2 + (F & 0xFFFF));
+        if (s < 0 && (s <= -62 || mag(p) >= (1ull << (62 + s)))) set_err(a.err, DERR_RANGE);
+        return rshift(p, s);
+    }
+    return rshift(dot, -(eq + ek - 3 + 10));
+}
 
 // ARR read as base2.py:97 does it: ARR[min(d, len-1)] where d < len, else 0. d is never negative unless a score
 // wrapped; numpy would then index from the table's end (d >= -len) or raise (d < -len, flagged here).
@@ -225,7 +352,7 @@ B2_DEV int64_t arrival(int64_t d, const int32_t* __restrict__ ARR, int alen, uin
     return 0;
 }
 
-template <int NW>
+template <int NW, bool PY>
 __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
     griddep_wait();
     griddep_launch();
@@ -281,7 +408,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
                     int64_t dot = part[i];
                     uint64_t m = __ldg(KM + key);
                     while (m) { int t = __ffsll((long long)m) - 1; m &= m - 1; dot += 65536LL * qs[t]; }
-                    int64_t s = rshift(dot, -(eq + (int64_t)__ldg(KE + key) - 3 + 10));
+                    int64_t s = score<PY>(dot, eq, (int64_t)__ldg(KE + key), a);
                     sc[key] = s;
                     lmax = s > lmax ? s : lmax;
                 }
@@ -298,6 +425,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
 
     // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin, 4 in flight
     int64_t n0 = 0, n1 = 0, Z = 0;
+    uint64_t vmax = 0;      // Pythia: the largest |v| met (pythia_base2.py:139 asserts max|v| * Z < 2^62)
     for (int s0 = wid * 4; s0 < nk; s0 += NW * 4) {
         int64_t av[4];
         int2 vv[4];
@@ -316,19 +444,28 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
             Z = wadd(Z, av[u]);
             n0 = wadd(n0, wmul(av[u], vv[u].x));
             n1 = wadd(n1, wmul(av[u], vv[u].y));
+            if (PY && av[u]) vmax = max(vmax, max(mag(vv[u].x), mag(vv[u].y)));
         }
     }
     red[wid][2 * lane] = n0;
     red[wid][2 * lane + 1] = n1;
     if (lane == 0) red[wid][64] = Z;
+    if (PY) { vmax = warp_max_u64(vmax); if (lane == 0) red[wid][65] = (int64_t)vmax; }
     __syncthreads();
     if (wid == 0) {
         int64_t t0 = 0, t1 = 0, zz = 0;
+        uint64_t vm = 0;
 #pragma unroll
-        for (int k = 0; k < NW; k++) { t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]); }
+        for (int k = 0; k < NW; k++) {
+            t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]);
+            if (PY) vm = max(vm, (uint64_t)red[k][65]);
+        }
         int64_t F = -log2fix(zz, a.LOG2);
         int64_t* o = a.out + (size_t)r * d + h * 64;
-        const int64_t v0 = power(t0, F, a.EXP2), v1 = power(t1, F, a.EXP2);
+        bool bad = PY && (unsigned __int128)vm * (unsigned __int128)(uint64_t)zz >= ((unsigned __int128)1 << 62);
+        const int64_t v0 = PY ? power_exact(t0, F, a.EXP2, &bad) : power(t0, F, a.EXP2);
+        const int64_t v1 = PY ? power_exact(t1, F, a.EXP2, &bad) : power(t1, F, a.EXP2);
+        if (PY && bad) set_err(a.err, DERR_RANGE);
         o[2 * lane] = v0;
         o[2 * lane + 1] = v1;
         if (a.or_out) {
@@ -347,7 +484,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
 // ---------------------------------------------------------------------------------------------------------------------
 constexpr int ATT_BYTES_PER_KEY = 128 + 256 + 8 + 4 + 8 + 4;
 
-template <int NW>
+template <int NW, bool PY>
 __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     griddep_wait();
     griddep_launch();
@@ -405,7 +542,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         if ((lane & 7) == 0 && key < nk) {
             uint64_t m = KMs[key];
             while (m) { const int t = __ffsll((long long)m) - 1; m &= m - 1; part += 65536LL * qs[t]; }
-            const int64_t s = rshift(part, -(eq + (int64_t)KEs[key] - 3 + 10));
+            const int64_t s = score<PY>(part, eq, (int64_t)KEs[key], a);
             SCs[key] = s;
             lmax = s > lmax ? s : lmax;
         }
@@ -430,23 +567,33 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
 
     // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin
     int64_t n0 = 0, n1 = 0;
+    uint64_t vmax = 0;
     for (int s = wid; s < nk; s += NW) {
         const int64_t av = AVs[s];
         if (!av) continue;
         const int2 vv = reinterpret_cast<const int2*>(Vs + (size_t)s * 64)[lane];
         n0 = wadd(n0, wmul(av, vv.x));
         n1 = wadd(n1, wmul(av, vv.y));
+        if (PY) vmax = max(vmax, max(mag(vv.x), mag(vv.y)));
     }
     red[wid][2 * lane] = n0;
     red[wid][2 * lane + 1] = n1;
+    if (PY) { vmax = warp_max_u64(vmax); if (lane == 0) red[wid][65] = (int64_t)vmax; }
     __syncthreads();
     if (wid == 0) {
         int64_t t0 = 0, t1 = 0, zz = 0;
+        uint64_t vm = 0;
 #pragma unroll
-        for (int k = 0; k < NW; k++) { t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]); }
+        for (int k = 0; k < NW; k++) {
+            t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]);
+            if (PY) vm = max(vm, (uint64_t)red[k][65]);
+        }
         const int64_t F = -log2fix(zz, a.LOG2);
         int64_t* o = a.out + (size_t)r * d + h * 64;
-        const int64_t v0 = power(t0, F, a.EXP2), v1 = power(t1, F, a.EXP2);
+        bool bad = PY && (unsigned __int128)vm * (unsigned __int128)(uint64_t)zz >= ((unsigned __int128)1 << 62);
+        const int64_t v0 = PY ? power_exact(t0, F, a.EXP2, &bad) : power(t0, F, a.EXP2);
+        const int64_t v1 = PY ? power_exact(t1, F, a.EXP2, &bad) : power(t1, F, a.EXP2);
+        if (PY && bad) set_err(a.err, DERR_RANGE);
         o[2 * lane] = v0;
         o[2 * lane + 1] = v1;
         if (a.or_out) {

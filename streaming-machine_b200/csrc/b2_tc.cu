@@ -850,6 +850,7 @@ cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y
         case EPI_GAUGED: { constexpr int E = EPI_GAUGED; CALL; }           \
         case EPI_GAUGED_EDGE: { constexpr int E = EPI_GAUGED_EDGE; CALL; } \
         case EPI_PLAIN_ADD: { constexpr int E = EPI_PLAIN_ADD; CALL; }     \
+        case EPI_PLAIN_EDGE: { constexpr int E = EPI_PLAIN_EDGE; CALL; }   \
         default: { constexpr int E = EPI_PLAIN_OUT; CALL; }                \
     }
 
@@ -860,9 +861,11 @@ int tc_min_rows_default() { return 1; }
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
 int tc_init() {
     void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
-                     (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>};
+                     (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>,
+                     (void*)k_bank_split<EPI_PLAIN_EDGE>};
     void* tiles[] = {(void*)k_bank_tiles<EPI_GAUGED>, (void*)k_bank_tiles<EPI_GAUGED_EDGE>,
-                     (void*)k_bank_tiles<EPI_PLAIN_ADD>, (void*)k_bank_tiles<EPI_PLAIN_OUT>};
+                     (void*)k_bank_tiles<EPI_PLAIN_ADD>, (void*)k_bank_tiles<EPI_PLAIN_OUT>,
+                     (void*)k_bank_tiles<EPI_PLAIN_EDGE>};
     for (void* f : split) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
         if (e != cudaSuccess) return (int)e;

@@ -1,7 +1,7 @@
 """Host side of the CUDA engine: the reference machine's interface (base2.py) over the C ABI of libbase2cuda.so.
 
     from streaming_machine_b200 import convert, engine
-    M = convert.load_gpt2(seed=0)                     # arrays keyed like base2_gpt2.npz
+    M = convert.load_gpt2(seed=0)                     # arrays keyed like base2_gpt2.npz (or base2_pythia-160m.npz)
     eng = engine.Engine(M, n_streams=64, max_ctx=160)
     first = eng.prefill(prompts)                      # the race's word after each prompt  (base2_stream.swift:274-275)
     nxt = eng.step()                                  # one new position per stream        (base2_stream.swift:276-280)
@@ -18,13 +18,14 @@ import numpy as np
 
 from . import build as _build
 
+B2_GPT2, B2_PYTHIA = 0, 1
 B2_GAUGE_FLOAT, B2_EDGE_FLOAT, B2_ARRIVAL_FLOAT = 1, 2, 4
 STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_CTX", 5: "ERR_VALUE", 6: "ERR_STATE",
           7: "ERR_DEVICE"}
 
 # every symbol include/base2.h declares
 EXPORTS = ("b2_create", "b2_set_bank", "b2_set_array", "b2_set_scalar", "b2_finalize", "b2_alloc_streams",
-           "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_rewind", "b2_profile",
+           "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_gauge", "b2_rewind", "b2_profile",
            "b2_profile_read", "b2_sync", "b2_last_error", "b2_destroy", "b2_abi_version")
 PROF_CLASSES = ("bank", "attend", "quant", "heads", "race", "other")
 
@@ -59,6 +60,7 @@ def lib():
         L.b2_generate.argtypes = [vp, i32, i32, vp, vp]
         L.b2_step_host.argtypes = [vp, vp, i32, vp]
         L.b2_bank.argtypes = [vp, cp, vp, i32, vp, i32, vp]
+        L.b2_gauge.argtypes = [vp, cp, vp, i32, vp, vp]
         L.b2_rewind.argtypes = [vp, i32, vp, vp, vp]
         L.b2_profile.argtypes = [vp, ctypes.c_int]
         L.b2_profile_read.argtypes = [vp, vp, vp, vp]
@@ -81,8 +83,13 @@ def _torch():
     return torch
 
 
+def _scalar(M, k) -> int:
+    return int(np.asarray(M[k]).reshape(-1)[0])
+
+
 class Engine:
-    """The integer GPT-2 machine on one GPU, with `n_streams` independent streams of up to `max_ctx` positions."""
+    """The integer GPT-2 machine (base2.py) or its Pythia variant (foundation0/pythia_base2.py, chosen when M holds
+    Pythia's "embed.w") on one GPU, with `n_streams` independent streams of up to `max_ctx` positions."""
 
     def __init__(self, M: dict, device: int = 0, n_streams: int = 1, max_ctx: int = 1024,
                  gauge: str = "int", edge: str = "int", arrival: str = "int"):
@@ -91,10 +98,18 @@ class Engine:
         self.device = torch.device("cuda", device)
         flags = (B2_GAUGE_FLOAT if gauge == "float" else 0) | (B2_EDGE_FLOAT if edge == "float" else 0) | \
                 (B2_ARRIVAL_FLOAT if arrival == "float" else 0)
-        d = int(M["wte"].shape[1])
+        self.pythia = "embed.w" in M
         n_layer = sum(1 for k in M if k.startswith("qkv.") and k.endswith(".w"))
-        self.cfg = Config(0, n_layer, d, d // 64, int(M["fc.0.w"].shape[1]), int(M["head.w"].shape[1]),
-                          int(M["wpe"].shape[0]))
+        if self.pythia:
+            d = int(M["embed.w"].shape[1])
+            if _scalar(M, "hs") != 64 or _scalar(M, "heads") * 64 != d:
+                raise ValueError("the engine takes heads of 64 dims")
+            self.cfg = Config(B2_PYTHIA, n_layer, d, d // 64, int(M["fc.0.w"].shape[1]), int(M["head.w"].shape[1]),
+                              int(M["cos"].shape[0]))
+        else:
+            d = int(M["wte"].shape[1])
+            self.cfg = Config(B2_GPT2, n_layer, d, d // 64, int(M["fc.0.w"].shape[1]), int(M["head.w"].shape[1]),
+                              int(M["wpe"].shape[0]))
         self.V = self.cfg.vocab
         L = lib()
         h = ctypes.c_void_p()
@@ -103,14 +118,22 @@ class Engine:
         for name in [f"{b}.{l}" for l in range(n_layer) for b in ("qkv", "proj", "fc", "mproj")] + ["head"]:
             w = np.ascontiguousarray(M[name + ".w"], dtype=np.int16)
             e = np.ascontiguousarray(M[name + ".e"], dtype=np.int64)
-            b = np.ascontiguousarray(M[name + ".b"], dtype=np.int64)
-            self._call("b2_set_bank", h, name.encode(), w.ctypes.data, e.ctypes.data, b.ctypes.data,
-                       w.shape[0], w.shape[1])
-        for k in ("wte", "wpe", "phi", "arrival", "log2", "exp2"):
+            b = np.ascontiguousarray(M[name + ".b"], dtype=np.int64) if name + ".b" in M else None   # Pythia's head
+            self._call("b2_set_bank", h, name.encode(), w.ctypes.data, e.ctypes.data,
+                       b.ctypes.data if b is not None else None, w.shape[0], w.shape[1])
+        if self.pythia:
+            norms = [f"ln{i}.{l}" for l in range(n_layer) for i in (1, 2)] + ["lnf"]
+            arrays = ["embed.w", "embed.e", "cos", "sin", "phi", "arrival", "log2", "exp2"] + \
+                     [f"{n}.{p}" for n in norms for p in ("g", "b")]
+            scalars = ["eps40", "half_log2_hs", "rot"] + [f"{n}.ge" for n in norms]
+        else:
+            arrays = ["wte", "wpe", "phi", "arrival", "log2", "exp2"]
+            scalars = ["log2_768", "eps40"]
+        for k in arrays:
             a = np.ascontiguousarray(M[k], dtype=np.int64)
             self._call("b2_set_array", h, k.encode(), a.ctypes.data, a.size)
-        for k in ("log2_768", "eps40"):
-            self._call("b2_set_scalar", h, k.encode(), int(np.asarray(M[k]).reshape(-1)[0]))
+        for k in scalars:
+            self._call("b2_set_scalar", h, k.encode(), _scalar(M, k))
         self._call("b2_finalize", h)
         self.n_streams, self.max_ctx = 0, 0
         self.alloc_streams(n_streams, max_ctx)
@@ -198,12 +221,21 @@ class Engine:
         return int(self.prefill([ids])[0])
 
     def bank(self, name: str, X, mode: int = 0):
-        """One bank on rows X (base2.py:62-76): mode 0 gauged, 1 gauged + edge, 2 plain."""
+        """One bank on rows X (base2.py:62-76): mode 0 gauged, 1 gauged + edge, 2 plain, 3 plain + edge
+        (Pythia's fc, pythia_base2.py:166)."""
         X = self.torch.as_tensor(np.ascontiguousarray(X, dtype=np.int64)).to(self.device)
         nout = {"qkv": 3, "proj": 1, "fc": 4, "mproj": 1}.get(name.split(".")[0], None)
         nout = self.V if name == "head" else nout * self.cfg.d_model
         out = self.torch.empty((X.shape[0], nout), dtype=self.torch.int64, device=self.device)
         self._call("b2_bank", self.h, name.encode(), X.data_ptr(), X.shape[0], out.data_ptr(), mode, self._stream())
+        self._call("b2_sync", self.h)
+        return out.cpu().numpy()
+
+    def gauge(self, name: str, X):
+        """Pythia's layer norm on rows X (pythia_base2.py:100-110): name "ln1.<l>", "ln2.<l>" or "lnf"."""
+        X = self.torch.as_tensor(np.ascontiguousarray(X, dtype=np.int64)).to(self.device)
+        out = self.torch.empty_like(X)
+        self._call("b2_gauge", self.h, name.encode(), X.data_ptr(), X.shape[0], out.data_ptr(), self._stream())
         self._call("b2_sync", self.h)
         return out.cpu().numpy()
 

@@ -40,10 +40,38 @@ def gload(name):
 
 
 @pytest.fixture(scope="session")
+def PM():
+    """The seeded Pythia-160M machine (keys of the reference converter's base2_pythia-160m.npz)."""
+    from streaming_machine_b200 import convert
+    return convert.load_pythia(0)
+
+
+@pytest.fixture(scope="session")
+def porc(PM):
+    from oracle.oracle import PythiaOracle
+    return PythiaOracle(PM)
+
+
+@pytest.fixture(scope="session")
+def pgold():
+    import json
+    with open(os.path.join(GOLDEN, "pythia_seed0.json")) as f:
+        return json.load(f)
+
+
+@pytest.fixture(scope="session")
 def gpu_engine(M):
     """One engine per session (uploading the weights and building their layouts is the costly part)."""
     from streaming_machine_b200 import engine
     e = engine.Engine(M, n_streams=1, max_ctx=64)
+    yield e
+    e.close()
+
+
+@pytest.fixture(scope="session")
+def pythia_engine(PM):
+    from streaming_machine_b200 import engine
+    e = engine.Engine(PM, n_streams=1, max_ctx=128)
     yield e
     e.close()
 

@@ -1,37 +1,17 @@
 """Pin the Pythia-160M oracle to the reference's own foundation0/pythia_base2.py (vectors from
 tests/golden/make_golden_pythia.py) and our converter to the reference's pythia_convert.py."""
 import hashlib
-import json
-import os
 
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, gload
+from conftest import gload
 
 V = 50304
 
 
 def sha(a):
     return hashlib.sha256(np.ascontiguousarray(np.asarray(a, dtype=np.int64)).tobytes()).hexdigest()
-
-
-@pytest.fixture(scope="session")
-def PM():
-    from streaming_machine_b200 import convert
-    return convert.load_pythia(0)
-
-
-@pytest.fixture(scope="session")
-def porc(PM):
-    from oracle.oracle import PythiaOracle
-    return PythiaOracle(PM)
-
-
-@pytest.fixture(scope="session")
-def pgold():
-    with open(os.path.join(GOLDEN, "pythia_seed0.json")) as f:
-        return json.load(f)
 
 
 def test_pythia_converter_matches_reference(PM, pgold):
