@@ -106,6 +106,19 @@ int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int6
  * X, out [rows][d] int64 (device pointers). */
 int b2_gauge(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, void* stream);
 
+/* b2_bank (modes 0-3, same results) for callers that cannot let the library allocate device memory: a host whose
+ * own allocator owns the GPU's memory, or code that must not pay cudaMalloc/cudaFree's implicit device-wide
+ * synchronisation. This call allocates nothing and needs only b2_finalize (not b2_alloc_streams). The quantised rows
+ * go to a fixed scratch area of B2_NOALLOC_SCRATCH_BYTES inside the library's device image, one per device:
+ * rows x (4 nin + 12) bytes plus alignment must fit (about 1,360 rows of a 768-input bank, 340 of a 3,072-input
+ * bank); larger calls return B2_ERR_ARG and should use b2_bank. The area is shared by every handle on the device, so
+ * calls on one device must not overlap: two calls in flight at once (other threads or other streams) race on it and
+ * give wrong results. Nothing in it needs to start at zero. X, out device pointers; work queued on `stream` (the
+ * CUDA-core bank kernel). No reference counterpart (the reference allocates per call, base2.py:62-76). */
+#define B2_NOALLOC_SCRATCH_BYTES (4u << 20)
+int b2_bank_noalloc(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode,
+                    void* stream);
+
 /* Truncate streams 0..n_streams-1 back to lens[s] positions with last_tok[s] as the word to feed next (device
  * pointers). Keys/values below lens[s] are kept. A truncation past a stream's current length is a device-checked
  * error (B2_ERR_CTX). The reference has no counterpart: its machine recomputes every prefix (base2.py:123). */

@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -904,6 +905,83 @@ int b2_gauge(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int
     if (ni < 0 || !X || !out || rows < 1 || rows > h->max_rows)
         return fail(h, B2_ERR_ARG, "b2_gauge: bad argument (a Pythia norm name: ln1.<l>, ln2.<l> or lnf)");
     return run_gauge(h, X, nullptr, rows, ni, out, (cudaStream_t)stream);
+}
+
+// ---- b2_bank_noalloc: b2_bank for callers that cannot let the library allocate device memory ----------------------
+// The quantised rows (x16, ex, LS) that b2_bank keeps in buffers from b2_alloc_streams go instead to this fixed area
+// of the library's own device image, one per device, shared by every handle on that device. Its address is looked up
+// once per device (first call, device current) and cached.
+}  // extern "C"
+
+namespace {
+constexpr size_t NOALLOC_BYTES = 4u << 20;   // B2_NOALLOC_SCRATCH_BYTES in base2.h
+constexpr int NOALLOC_MAX_DEVICES = 64;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_BYTES];
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[NOALLOC_MAX_DEVICES] = {};
+
+size_t align256(size_t n) { return (n + 255) & ~(size_t)255; }
+}  // namespace
+
+extern "C" {
+
+int b2_bank_noalloc(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode,
+                    void* stream) {
+    if (!h) return B2_ERR_ARG;
+    if (!h->finalized) return fail(h, B2_ERR_STATE, "b2_bank_noalloc: b2_finalize has not been called");
+    const int bi = name ? bank_index(h, name) : -1;
+    if (bi < 0 || !X || !out || rows < 1 || mode < 0 || mode > 3)
+        return fail(h, B2_ERR_ARG, "b2_bank_noalloc: bad argument");
+    if (h->cfg.kind == B2_PYTHIA && mode < 2)
+        return fail(h, B2_ERR_ARG, "b2_bank_noalloc: Pythia's banks are plain (modes 2 and 3)");
+    if (h->device < 0 || h->device >= NOALLOC_MAX_DEVICES)
+        return fail(h, B2_ERR_ARG, "b2_bank_noalloc: device %d past the %d this entry point serves", h->device,
+                    NOALLOC_MAX_DEVICES);
+    const DevBank& bk = h->banks[bi];
+    // x16 [rows][nin] int32, ex [rows] int32, LS [rows] int64, each at a 256-byte boundary
+    const size_t o_ex = align256((size_t)rows * bk.nin * sizeof(int32_t));
+    const size_t o_ls = o_ex + align256((size_t)rows * sizeof(int32_t));
+    const size_t need = o_ls + (size_t)rows * sizeof(int64_t);
+    if (need > NOALLOC_BYTES)
+        return fail(h, B2_ERR_ARG, "b2_bank_noalloc: %d rows of %d inputs need %zu bytes of scratch, the fixed area holds "
+                    "%zu (use b2_bank for larger calls)", rows, bk.nin, need, NOALLOC_BYTES);
+    CK(cudaSetDevice(h->device));
+    unsigned char* base = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_ptr[h->device]) {
+            void* p = nullptr;
+            cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+            if (e != cudaSuccess || !p)
+                return fail(h, B2_ERR_CUDA, "b2_bank_noalloc: scratch address on device %d: %s", h->device,
+                            cudaGetErrorString(e));
+            g_noalloc_ptr[h->device] = p;
+        }
+        base = (unsigned char*)g_noalloc_ptr[h->device];
+    }
+    // nothing here has to start at zero: every scratch entry a kernel reads was written earlier in the same call
+    int32_t* x16 = (int32_t*)base;
+    int32_t* ex = (int32_t*)(base + o_ex);
+    int64_t* LS = (int64_t*)(base + o_ls);
+    cudaStream_t st = (cudaStream_t)stream;
+    const int gauge = mode < 2;
+    if (bk.nin > 1024)
+        k_quant<512><<<rows, 512, 0, st>>>(X, bk.nin, nullptr, rows, x16, ex, LS, gauge, h->LOG2, h->log768, h->eps40,
+                                           PlaneOut{});
+    else
+        k_quant<256><<<rows, 256, 0, st>>>(X, bk.nin, nullptr, rows, x16, ex, LS, gauge, h->LOG2, h->log768, h->eps40,
+                                           PlaneOut{});
+    if (int rc = check_launch(h, "b2_bank_noalloc quant")) return rc;
+    BankArgs a{x16, bk.w, bk.nin, bk.nout, rows, {ex, LS, bk.e, bk.b, out, bk.nout, nullptr, h->EXP2, h->PHI}};
+    constexpr int RT = 8;
+    const dim3 grid((bk.nout + 255) / 256, (rows + RT - 1) / RT);
+    switch (mode) {
+        case 0: k_bank_simt<EPI_GAUGED, RT><<<grid, 256, 0, st>>>(a); break;
+        case 1: k_bank_simt<EPI_GAUGED_EDGE, RT><<<grid, 256, 0, st>>>(a); break;
+        case 2: k_bank_simt<EPI_PLAIN_OUT, RT><<<grid, 256, 0, st>>>(a); break;
+        default: k_bank_simt<EPI_PLAIN_EDGE, RT><<<grid, 256, 0, st>>>(a); break;
+    }
+    return check_launch(h, "b2_bank_noalloc bank");
 }
 
 int b2_rewind(b2_handle* h, int32_t n_streams, const int32_t* lens, const int32_t* last_tok, void* stream) {

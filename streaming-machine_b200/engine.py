@@ -25,8 +25,8 @@ STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_CTX", 5:
 
 # every symbol include/base2.h declares
 EXPORTS = ("b2_create", "b2_set_bank", "b2_set_array", "b2_set_scalar", "b2_finalize", "b2_alloc_streams",
-           "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_gauge", "b2_rewind", "b2_profile",
-           "b2_profile_read", "b2_sync", "b2_last_error", "b2_destroy", "b2_abi_version")
+           "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_gauge", "b2_bank_noalloc",
+           "b2_rewind", "b2_profile", "b2_profile_read", "b2_sync", "b2_last_error", "b2_destroy", "b2_abi_version")
 PROF_CLASSES = ("bank", "attend", "quant", "heads", "race", "other")
 
 
@@ -61,6 +61,7 @@ def lib():
         L.b2_step_host.argtypes = [vp, vp, i32, vp]
         L.b2_bank.argtypes = [vp, cp, vp, i32, vp, i32, vp]
         L.b2_gauge.argtypes = [vp, cp, vp, i32, vp, vp]
+        L.b2_bank_noalloc.argtypes = [vp, cp, vp, i32, vp, i32, vp]
         L.b2_rewind.argtypes = [vp, i32, vp, vp, vp]
         L.b2_profile.argtypes = [vp, ctypes.c_int]
         L.b2_profile_read.argtypes = [vp, vp, vp, vp]
