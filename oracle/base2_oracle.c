@@ -10,7 +10,10 @@
  *   - products (base2.py:29-32) are float64 matmuls asserted below 2^52, hence exact; here they are exact int64
  *     sums, which give the same integers whenever base2.py's own assert holds.
  * Signed overflow is undefined in C, so every wrapping operation goes through uint64_t.
+ * The float stage switches (gauge=/edge=/arrival=/turn= float) are float64 in the reference's own operation order,
+ * each multiply and add rounded on its own (built with -ffp-contract=off), means and sums in numpy's pairwise order.
  */
+#include <math.h>
 #include <stdint.h>
 #include <stdlib.h>
 #include <string.h>
@@ -107,6 +110,99 @@ void b2o_gauge_log(const i64 *R, i64 rows, i64 n, const i64 *LOG2, i64 log768, i
 }
 
 /* ------------------------------------------------------------------------------------------------------------ */
+/* float stage switches: shared pieces                                                                            */
+/* ------------------------------------------------------------------------------------------------------------ */
+enum { F_GAUGE = 1, F_EDGE = 2, F_ARRIVAL = 4, F_TURN = 8 };
+typedef __int128 i128;
+
+/* numpy's pairwise sum, the order np.add.reduce / np.mean use along a contiguous axis (numpy's pairwise_sum):
+ * fewer than 8 terms in order; up to 128 in eight interleaved partial sums folded ((0+1)+(2+3))+((4+5)+(6+7)) and
+ * then the remainder in order; more: split at half the count rounded down to a multiple of 8. */
+double b2f_pairwise(const double *a, i64 n) {
+    if (n < 8) {
+        double r = 0.0;
+        for (i64 i = 0; i < n; i++) r += a[i];
+        return r;
+    }
+    if (n <= 128) {
+        double r[8];
+        for (int j = 0; j < 8; j++) r[j] = a[j];
+        i64 i = 8;
+        for (; i < n - (n % 8); i += 8)
+            for (int j = 0; j < 8; j++) r[j] += a[i + j];
+        double res = ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
+        for (; i < n; i++) res += a[i];
+        return res;
+    }
+    i64 n2 = n / 2;
+    n2 -= n2 % 8;
+    return b2f_pairwise(a, n2) + b2f_pairwise(a + n2, n - n2);
+}
+
+/* the row at 2^-16, its mean and sqrt(mean((x - mean)^2) + 1e-5) (base2.py:67, pythia_base2.py:103). x, t: n
+ * doubles of scratch; on return x holds x - mean. */
+static double row_sigma(const i64 *R, int n, double *x, double *t) {
+    for (int i = 0; i < n; i++) x[i] = (double)R[i] / 65536.0;
+    const double mu = b2f_pairwise(x, n) / (double)n;
+    for (int i = 0; i < n; i++) { x[i] = x[i] - mu; t[i] = x[i] * x[i]; }
+    return sqrt(b2f_pairwise(t, n) / (double)n + 1e-5);
+}
+
+/* an exact 128-bit dot product as the nearest double (ties to even) */
+double b2f_i128_to_double(i128 x) {
+    if (x >= (i128)INT64_MIN && x <= (i128)INT64_MAX) return (double)(i64)x;
+    const int neg = x < 0;
+    unsigned __int128 u = neg ? (unsigned __int128)0 - (unsigned __int128)x : (unsigned __int128)x;
+    int top = 127;
+    while (!((u >> top) & 1)) top--;
+    const int sh = top - 62;                                 /* keep 63 bits */
+    u64 keep = (u64)(u >> sh);
+    const int sticky = (u & (((unsigned __int128)1 << sh) - 1)) != 0;
+    u64 mant = keep >> 10, rem = keep & 1023;                /* 53 bits + 10 to round away */
+    if (rem > 512 || (rem == 512 && (sticky || (mant & 1)))) mant++;
+    const double r = ldexp((double)mant, sh + 10);
+    return neg ? -r : r;
+}
+
+/* base2.py:79-80, edge=float: 0.5 h (1 + tanh(0.7978845608028654 (h + 0.044715 h^3))) at 2^-16, rounded */
+static i64 edge_tanh1(i64 H) {
+    const double h = (double)H / 65536.0;
+    const double t = 0.7978845608028654 * (h + 0.044715 * pow(h, 3.0));
+    return (i64)rint(0.5 * h * (1.0 + tanh(t)) * 65536.0);
+}
+/* pythia_base2.py:144-146, edge=float: h 0.5 (1 + erf(h / sqrt 2)) at 2^-16, rounded */
+static i64 edge_erf1(i64 H) {
+    const double h = (double)H / 65536.0;
+    return (i64)rint(h * 0.5 * (1.0 + erf(h / 1.4142135623730951)) * 65536.0);
+}
+void b2f_edge(const i64 *h, i64 n, int erf_form, i64 *y) {
+    for (i64 i = 0; i < n; i++) y[i] = erf_form ? edge_erf1(h[i]) : edge_tanh1(h[i]);
+}
+
+/* base2.py:89-92 / pythia_base2.py:130-133, arrival=float, for the last row of a causal run over positions 0..p:
+ * s = (q / 2^16).(k / 2^16) / 8 (the dot exact, then rounded once), a = exp(s - max s) / (its pairwise sum),
+ * out = round(sum_s a_s (v_s / 2^16) * 2^16) with the sum over s in order. q, K rows (stride ldk), V rows (stride
+ * ldv) at full width; e: p+1 doubles of scratch. */
+static void arrival_float_row(const i64 *q, const i64 *K, size_t ldk, const i64 *V, size_t ldv, int p, int hd,
+                              i64 *out, double *e) {
+    double mx = -INFINITY;
+    for (int s = 0; s <= p; s++) {
+        i128 dot = 0;
+        for (int t = 0; t < hd; t++) dot += (i128)q[t] * (i128)K[(size_t)s * ldk + t];
+        e[s] = ldexp(b2f_i128_to_double(dot), -32) / 8.0;
+        if (e[s] > mx) mx = e[s];
+    }
+    for (int s = 0; s <= p; s++) e[s] = exp(e[s] - mx);
+    const double Z = b2f_pairwise(e, p + 1);
+    for (int s = 0; s <= p; s++) e[s] = e[s] / Z;
+    for (int t = 0; t < hd; t++) {
+        double acc = 0.0;
+        for (int s = 0; s <= p; s++) acc = acc + e[s] * ((double)V[(size_t)s * ldv + t] / 65536.0);
+        out[t] = (i64)rint(acc * 65536.0);
+    }
+}
+
+/* ------------------------------------------------------------------------------------------------------------ */
 /* the model                                                                                                     */
 /* ------------------------------------------------------------------------------------------------------------ */
 typedef struct {
@@ -120,6 +216,7 @@ typedef struct {
     bank_t bank[64 * 4 + 1];  /* layer*4 + {qkv, proj, fc, mproj}; head at 4*L */
     const i64 *wte, *wpe, *PHI, *ARR, *LOG2, *EXP2;
     i64 alen, log768, eps40;
+    int flags;                /* F_GAUGE | F_EDGE | F_ARRIVAL: stages back to float64 (base2.py:10-11) */
 } model_t;
 
 void *b2o_create(int L, int d, int H, int F, int V, int ctx) {
@@ -128,6 +225,7 @@ void *b2o_create(int L, int d, int H, int F, int V, int ctx) {
     return m;
 }
 void b2o_destroy(void *m) { free(m); }
+void b2o_set_flags(void *mv, int flags) { ((model_t *)mv)->flags = flags; }
 void b2o_set_bank(void *mv, int idx, const int16_t *w, const i64 *e, const i64 *b, int nin, int nout) {
     model_t *m = (model_t *)mv;
     m->bank[idx].w = w; m->bank[idx].e = e; m->bank[idx].b = b; m->bank[idx].nin = nin; m->bank[idx].nout = nout;
@@ -160,15 +258,31 @@ static void product_row(const i64 *x16, const bank_t *bk, i64 *pile, int par) {
     }
 }
 
-/* base2.py:62-71 gauged_bank (integer gauge) for one row. */
-static void gauged_row(const model_t *m, const bank_t *bk, const i64 *R, i64 *out, i64 *x16, i64 *pile, int par) {
+/* base2.py:62-71 gauged_bank for one row; with gauge=float base2.py:66-69 (layer banks) or :110-113 (head: the
+ * bias at 2^-16 added before the rounding). */
+static void gauged_row_h(const model_t *m, const bank_t *bk, const i64 *R, i64 *out, i64 *x16, i64 *pile, int par,
+                         int head) {
     i64 ex;
     i64 LS = gauge_row(R, m->d, x16, &ex, m->LOG2, m->log768, m->eps40);
     product_row(x16, bk, pile, par);
+    if (m->flags & F_GAUGE) {
+        double *x = (double *)malloc(sizeof(double) * 2 * m->d);
+        const double sig = row_sigma(R, m->d, x, x + m->d);
+        free(x);
+        for (int j = 0; j < bk->nout; j++) {
+            const double val = (double)pile[j] * ldexp(1.0, (int)(bk->e[j] + ex)) / sig;
+            out[j] = head ? (i64)rint((val + (double)bk->b[j] / 65536.0) * 65536.0)
+                          : wadd((i64)rint(val * 65536.0), bk->b[j]);
+        }
+        return;
+    }
     for (int j = 0; j < bk->nout; j++) {
         i64 F = wsub(wmul(wadd(wadd(bk->e[j], ex), 16), 65536), LS);
         out[j] = wadd(power1(pile[j], F, m->EXP2), bk->b[j]);
     }
+}
+static void gauged_row(const model_t *m, const bank_t *bk, const i64 *R, i64 *out, i64 *x16, i64 *pile, int par) {
+    gauged_row_h(m, bk, R, out, x16, pile, par, 0);
 }
 
 /* base2.py:73-76 plain_bank for one row, added into R (base2.py:105-106 R = R + plain_bank(...)). */
@@ -201,6 +315,7 @@ typedef struct {
     i64 *k16;   /* [L][ctx][d]   to16'd keys per head part */
     i64 *ek;    /* [L][ctx][H]   their exponents */
     i64 *v;     /* [L][ctx][d]   values at full width (base2.py:98 reads v[:p+1] unshifted) */
+    i64 *kraw;  /* [L][ctx][d]   keys at full width (arrival=float only; NULL otherwise) */
 } cache_t;
 
 static int cache_alloc(const model_t *m, cache_t *c, int ctx) {
@@ -208,14 +323,22 @@ static int cache_alloc(const model_t *m, cache_t *c, int ctx) {
     c->k16 = (i64 *)malloc(sizeof(i64) * n * m->d);
     c->ek = (i64 *)malloc(sizeof(i64) * n * m->H);
     c->v = (i64 *)malloc(sizeof(i64) * n * m->d);
-    return c->k16 && c->ek && c->v;
+    c->kraw = (m->flags & F_ARRIVAL) ? (i64 *)malloc(sizeof(i64) * n * m->d) : NULL;
+    return c->k16 && c->ek && c->v && (c->kraw || !(m->flags & F_ARRIVAL));
 }
-static void cache_free(cache_t *c) { free(c->k16); free(c->ek); free(c->v); }
+static void cache_free(cache_t *c) { free(c->k16); free(c->ek); free(c->v); free(c->kraw); }
 
 /* base2.py:85-100 attention, integer arrival, for the position p of one stream given the keys/values of 0..p.
  * q: this position's 768 query values (int64). Writes 768 outputs. sc: scratch of >= p+1. */
 static void attend_row(const model_t *m, const cache_t *c, int l, int ctx, int p, const i64 *q, i64 *out, i64 *sc) {
     const int d = m->d, hd = m->hd;
+    if (m->flags & F_ARRIVAL) {      /* base2.py:89-92 */
+        double *e = (double *)sc;    /* sc holds >= p+1 i64, the same size */
+        for (int h = 0; h < m->H; h++)
+            arrival_float_row(q + h * hd, c->kraw + ((size_t)l * ctx) * d + h * hd, d,
+                              c->v + ((size_t)l * ctx) * d + h * hd, d, p, hd, out + h * hd, e);
+        return;
+    }
     i64 q16[256];
     for (int h = 0; h < m->H; h++) {
         i64 eq = -16 + to16_row(q + h * hd, hd, q16);
@@ -272,14 +395,15 @@ static int position(const model_t *m, cache_t *c, scratch_t *s, int ctx, int p, 
             c->ek[((size_t)l * ctx + p) * H + h] = -16 + to16_row(s->qkv + d + h * hd, hd, k16);
         }
         memcpy(c->v + ((size_t)l * ctx + p) * d, s->qkv + 2 * d, sizeof(i64) * d);
+        if (c->kraw) memcpy(c->kraw + ((size_t)l * ctx + p) * d, s->qkv + d, sizeof(i64) * d);
         attend_row(m, c, l, ctx, p, s->qkv, s->att, s->sc);
         plain_row_add(m, &m->bank[4 * l + 1], s->att, s->R, s->x16, s->pile, par);
         gauged_row(m, &m->bank[4 * l + 2], s->R, s->hid, s->x16, s->pile, par);
-        for (int j = 0; j < m->F; j++) s->hid[j] = edge1(s->hid[j], m->PHI);
+        for (int j = 0; j < m->F; j++) s->hid[j] = (m->flags & F_EDGE) ? edge_tanh1(s->hid[j]) : edge1(s->hid[j], m->PHI);
         plain_row_add(m, &m->bank[4 * l + 3], s->hid, s->R, s->x16, s->pile, par);
     }
     if (!logits) return -1;
-    gauged_row(m, &m->bank[4 * m->L], s->R, logits, s->x16, s->pile, par);
+    gauged_row_h(m, &m->bank[4 * m->L], s->R, logits, s->x16, s->pile, par, 1);
     return (int)race1(logits, m->V);
 }
 
@@ -394,6 +518,7 @@ int b2o_attention(void *mv, const i64 *QKV, int P, i64 *out) {
         for (int h = 0; h < H; h++)
             c.ek[(size_t)p * H + h] = -16 + to16_row(QKV + (size_t)p * 3 * d + d + h * hd, hd, c.k16 + (size_t)p * d + h * hd);
         memcpy(c.v + (size_t)p * d, QKV + (size_t)p * 3 * d + 2 * d, sizeof(i64) * d);
+        if (c.kraw) memcpy(c.kraw + (size_t)p * d, QKV + (size_t)p * 3 * d + d, sizeof(i64) * d);
     }
     for (int p = 0; p < P; p++) attend_row(&one, &c, 0, P, p, QKV + (size_t)p * 3 * d, out + (size_t)p * d, sc);
     cache_free(&c); free(sc);
@@ -403,7 +528,6 @@ int b2o_attention(void *mv, const i64 *QKV, int P, i64 *out) {
 /* ============================================================================================================ */
 /* Pythia-160M: the reference's foundation0/pythia_base2.py (size=160m, plates=finished, order=plain)           */
 /* ============================================================================================================ */
-typedef __int128 i128;
 
 /* pythia_base2.py:87-90 power for one element, exactly (Python big ints): X*EXP2[f] then the rounded shift by
  * 16 - I. Returns -1 when the result leaves int64 (where the reference's .astype(np.int64) raises). */
@@ -447,12 +571,37 @@ typedef struct {
     const int16_t *emb; const i64 *embe;       /* embed_in [V][d] and its per-word power of two */
     const i64 *PHI, *ARR, *LOG2, *EXP2, *COS, *SIN;
     i64 alen, eps40, half;
+    int flags;                                 /* F_GAUGE | F_TURN | F_EDGE | F_ARRIVAL (pythia_base2.py:20) */
+    double *cosf, *sinf;                       /* turn=float: cos/sin of pos * 10000^(-2i/rot), [ctx][rot/2] */
 } pmodel_t;
 
 void *b2p_create(int L, int d, int H, int F, int V, int ctx, int rot) {
     pmodel_t *m = (pmodel_t *)calloc(1, sizeof(pmodel_t));
     m->L = L; m->d = d; m->H = H; m->hd = d / H; m->F = F; m->V = V; m->ctx = ctx; m->rot = rot;
     return m;
+}
+/* pythia_base2.py:118-120: ang = pos * 10000^(-(0, 2, .., rot-2) / rot), its cos and sin (the C library's, which
+ * are numpy's float64 cos/sin) */
+void b2p_set_flags(void *mv, int flags) {
+    pmodel_t *m = (pmodel_t *)mv;
+    m->flags = flags;
+    free(m->cosf); free(m->sinf); m->cosf = m->sinf = NULL;
+    if (!(flags & F_TURN)) return;
+    const int r = m->rot / 2;
+    m->cosf = (double *)malloc(sizeof(double) * (size_t)m->ctx * r);
+    m->sinf = (double *)malloc(sizeof(double) * (size_t)m->ctx * r);
+    for (int t = 0; t < r; t++) {
+        const double inv = pow(10000.0, (double)(-2 * t) / (double)m->rot);
+        for (int p = 0; p < m->ctx; p++) {
+            const double ang = (double)p * inv;
+            m->cosf[(size_t)p * r + t] = cos(ang);
+            m->sinf[(size_t)p * r + t] = sin(ang);
+        }
+    }
+}
+void b2p_destroy(void *mv) {
+    pmodel_t *m = (pmodel_t *)mv;
+    free(m->cosf); free(m->sinf); free(m);
 }
 void b2p_set_bank(void *mv, int idx, const int16_t *w, const i64 *e, const i64 *b, int nin, int nout) {
     pmodel_t *m = (pmodel_t *)mv;
@@ -473,6 +622,14 @@ void b2p_set_tables(void *mv, const int16_t *emb, const i64 *embe, const i64 *PH
  * LS = log2fix(V) >> 1, out = power(c*g, (ge + 16)*65536 - LS) + b (exact power). */
 static int gauge_ln_row(const pmodel_t *m, int idx, const i64 *R, i64 *out, i64 *x16) {
     const int d = m->d;
+    if (m->flags & F_GAUGE) {          /* pythia_base2.py:102-104 */
+        double *x = (double *)malloc(sizeof(double) * 2 * d);
+        const double sg = row_sigma(R, d, x, x + d), sc = ldexp(1.0, (int)m->nge[idx]);
+        for (int i = 0; i < d; i++)
+            out[i] = wadd((i64)rint(x[i] / sg * (double)m->ng[idx][i] * sc * 65536.0), m->nb[idx][i]);
+        free(x);
+        return 0;
+    }
     i64 ex = -16 + to16_row(R, d, x16);
     i64 S1 = 0, S2 = 0;
     for (int i = 0; i < d; i++) { S1 = wadd(S1, x16[i]); S2 = wadd(S2, wmul(x16[i], x16[i])); }
@@ -499,6 +656,15 @@ static void plain_row(const pmodel_t *m, const bank_t *bk, const i64 *X, i64 *ou
 static int turn_row(const pmodel_t *m, const i64 *x, int pos, i64 *y) {
     const int r = m->rot / 2;
     for (int t = 0; t < m->hd; t++) y[t] = x[t];
+    if (m->flags & F_TURN) {           /* pythia_base2.py:118-120 */
+        for (int t = 0; t < r; t++) {
+            const double c = m->cosf[(size_t)pos * r + t], s = m->sinf[(size_t)pos * r + t];
+            const double a = (double)x[t], b = (double)x[t + r];
+            y[t] = (i64)rint(a * c - b * s);
+            y[t + r] = (i64)rint(b * c + a * s);
+        }
+        return 0;
+    }
     for (int t = 0; t < m->rot; t++) if ((x[t] < 0 ? -x[t] : x[t]) >= ((i64)1 << 31)) return -1;
     for (int t = 0; t < r; t++) {
         i64 c = m->COS[(size_t)pos * r + t], s = m->SIN[(size_t)pos * r + t], a = x[t], b = x[t + r];
@@ -514,7 +680,8 @@ static int pcache_alloc(const pmodel_t *m, cache_t *c, int ctx) {
     c->k16 = (i64 *)malloc(sizeof(i64) * n * m->d);
     c->ek = (i64 *)malloc(sizeof(i64) * n * m->H);
     c->v = (i64 *)malloc(sizeof(i64) * n * m->d);
-    return c->k16 && c->ek && c->v;
+    c->kraw = (m->flags & F_ARRIVAL) ? (i64 *)malloc(sizeof(i64) * n * m->d) : NULL;   /* turned keys, full width */
+    return c->k16 && c->ek && c->v && (c->kraw || !(m->flags & F_ARRIVAL));
 }
 
 /* pythia_base2.py:125-141 attention at position p of one stream, given qkv (this position's [3d], per head q, k, v
@@ -522,6 +689,15 @@ static int pcache_alloc(const pmodel_t *m, cache_t *c, int ctx) {
 static int pattend_row(const pmodel_t *m, const cache_t *c, int l, int ctx, int p, const i64 *qkv, i64 *out, i64 *sc) {
     const int d = m->d, hd = m->hd;
     i64 qt[256], q16[256];
+    if (m->flags & F_ARRIVAL) {        /* pythia_base2.py:130-133 */
+        double *e = (double *)sc;
+        for (int h = 0; h < m->H; h++) {
+            if (turn_row(m, qkv + h * 3 * hd, p, qt)) return -1;
+            arrival_float_row(qt, c->kraw + ((size_t)l * ctx) * d + h * hd, d, c->v + ((size_t)l * ctx) * d + h * hd, d,
+                              p, hd, out + h * hd, e);
+        }
+        return 0;
+    }
     for (int h = 0; h < m->H; h++) {
         if (turn_row(m, qkv + h * 3 * hd, p, qt)) return -1;
         i64 eq = -16 + to16_row(qt, hd, q16);
@@ -582,6 +758,7 @@ static int pposition(const pmodel_t *m, cache_t *c, pscratch_t *s, int ctx, int 
             i64 kt[256];
             if (turn_row(m, s->qkv + h * 3 * hd + hd, p, kt)) return -2;
             c->ek[((size_t)l * ctx + p) * H + h] = -16 + to16_row(kt, hd, c->k16 + ((size_t)l * ctx + p) * d + h * hd);
+            if (c->kraw) memcpy(c->kraw + ((size_t)l * ctx + p) * d + h * hd, kt, sizeof(i64) * hd);
             memcpy(c->v + ((size_t)l * ctx + p) * d + h * hd, s->qkv + h * 3 * hd + 2 * hd, sizeof(i64) * hd);
         }
         if (pattend_row(m, c, l, ctx, p, s->qkv, s->att, s->sc)) return -2;
@@ -589,7 +766,7 @@ static int pposition(const pmodel_t *m, cache_t *c, pscratch_t *s, int ctx, int 
         /* MLP branch, from the same R */
         if (gauge_ln_row(m, 2 * l + 1, s->R, s->G, s->x16)) return -2;
         plain_row(m, &m->bank[4 * l + 2], s->G, s->hid, s->x16, s->pile, par);
-        for (int j = 0; j < m->F; j++) s->hid[j] = edge1(s->hid[j], m->PHI);
+        for (int j = 0; j < m->F; j++) s->hid[j] = (m->flags & F_EDGE) ? edge_erf1(s->hid[j]) : edge1(s->hid[j], m->PHI);
         plain_row(m, &m->bank[4 * l + 3], s->hid, s->Mo, s->x16, s->pile, par);
         for (int i = 0; i < d; i++) s->R[i] = wadd(wadd(s->R[i], s->At[i]), s->Mo[i]);
     }
@@ -672,6 +849,7 @@ int b2p_attention(void *mv, const i64 *QKV, int P, i64 *out) {
             i64 kt[256];
             if (turn_row(m, QKV + (size_t)p * 3 * d + h * 3 * hd + hd, p, kt)) return -2;
             c.ek[(size_t)p * H + h] = -16 + to16_row(kt, hd, c.k16 + (size_t)p * d + h * hd);
+            if (c.kraw) memcpy(c.kraw + (size_t)p * d + h * hd, kt, sizeof(i64) * hd);
             memcpy(c.v + (size_t)p * d + h * hd, QKV + (size_t)p * 3 * d + h * 3 * hd + 2 * hd, sizeof(i64) * hd);
         }
     int rc = 0;

@@ -56,6 +56,12 @@ def lib():
         L.b2o_race.restype = c_i64
         L.b2o_to16.argtypes = [_i64p, c_i64, c_i64, c_i64, _i64p, _i64p]
         L.b2o_gauge_log.argtypes = [_i64p, c_i64, c_i64, _i64p, c_i64, c_i64, _i64p, _i64p, _i64p]
+        L.b2o_set_flags.argtypes = [c_vp, c_int]
+        L.b2p_set_flags.argtypes = [c_vp, c_int]
+        L.b2p_destroy.argtypes = [c_vp]
+        L.b2f_pairwise.argtypes = [np.ctypeslib.ndpointer(np.float64, flags="C_CONTIGUOUS"), c_i64]
+        L.b2f_pairwise.restype = ctypes.c_double
+        L.b2f_edge.argtypes = [_i64p, c_i64, c_int, _i64p]
         L.b2o_create.argtypes = [c_int] * 6
         L.b2o_create.restype = c_vp
         L.b2o_destroy.argtypes = [c_vp]
@@ -123,10 +129,28 @@ def race(v):
     return int(lib().b2o_race(v, v.size))
 
 
+# the float stage switches (base2.py:10-11, pythia_base2.py:20): bits as in include/base2.h
+GAUGE_FLOAT, EDGE_FLOAT, ARRIVAL_FLOAT, TURN_FLOAT = 1, 2, 4, 8
+
+
+def pairwise_sum(a) -> float:
+    """numpy's float64 pairwise summation order (what np.sum / np.mean give along a contiguous axis)"""
+    a = np.ascontiguousarray(a, dtype=np.float64).ravel()
+    return float(lib().b2f_pairwise(a, a.size))
+
+
+def edge_float(H, erf_form: bool = False):
+    """edge=float: GPT-2's tanh form (base2.py:79-80) or Pythia's erf form (pythia_base2.py:144-146)"""
+    H = _c64(H)
+    y = np.empty_like(H)
+    lib().b2f_edge(H.ravel(), H.size, int(erf_form), y.ravel())
+    return y
+
+
 class Oracle:
     """The machine over one set of converted arrays (keys of base2_gpt2.npz)."""
 
-    def __init__(self, M: dict, n_layer: int = 12, ctx: int = 1024):
+    def __init__(self, M: dict, n_layer: int = 12, ctx: int = 1024, flags: int = 0):
         self.M = {k: np.ascontiguousarray(v) for k, v in M.items()}
         M = self.M
         d = M["wte"].shape[1]
@@ -148,6 +172,12 @@ class Oracle:
         self.log768, self.eps40 = (int(np.asarray(M[k]).reshape(-1)[0]) for k in ("log2_768", "eps40"))
         L.b2o_set_tables(self.h, t[0], t[1], t[2], t[3], self.alen, t[4], t[5], self.log768, self.eps40)
         self.PHI, self.LOG2, self.EXP2 = t[2], t[4], t[5]
+        self.set_flags(flags)
+
+    def set_flags(self, flags: int):
+        """GAUGE_FLOAT | EDGE_FLOAT | ARRIVAL_FLOAT: those stages back to float64 (base2.py:10-11)"""
+        self.flags = flags
+        lib().b2o_set_flags(self.h, flags)
 
     def __del__(self):
         try:
@@ -253,7 +283,7 @@ class PythiaOracle:
     """The Pythia-160M machine (reference foundation0/pythia_base2.py) over converted arrays (keys of
     base2_pythia-160m.npz; `plates=finished`, `order=plain`)."""
 
-    def __init__(self, M: dict):
+    def __init__(self, M: dict, flags: int = 0):
         self.M = {k: np.ascontiguousarray(v) for k, v in M.items()}
         M = self.M
         self.L, self.d, self.H, self.hd = (int(np.asarray(M[k]).reshape(-1)[0]) for k in ("L", "d", "heads", "hs"))
@@ -282,6 +312,12 @@ class PythiaOracle:
         self.EXP2 = t[3]
         L.b2p_set_tables(self.h, emb, embe, t[0], t[1], len(t[1]), t[2], t[3], t[4], t[5],
                          int(np.asarray(M["eps40"]).reshape(-1)[0]), int(np.asarray(M["half_log2_hs"]).reshape(-1)[0]))
+        self.set_flags(flags)
+
+    def set_flags(self, flags: int):
+        """GAUGE_FLOAT | EDGE_FLOAT | ARRIVAL_FLOAT | TURN_FLOAT (pythia_base2.py:20)"""
+        self.flags = flags
+        lib().b2p_set_flags(self.h, flags)
 
     def power(self, X, F):
         """pythia_base2.py:87-90 over one array (int64 below 2^45, exact above)."""

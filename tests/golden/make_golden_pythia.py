@@ -34,7 +34,7 @@ def sha(a) -> str:
     return hashlib.sha256(np.ascontiguousarray(np.asarray(a, dtype=np.int64)).tobytes()).hexdigest()
 
 
-def load_reference(ref, sd, work):
+def load_reference(ref, sd, work, argv=()):
     import safetensors
 
     class _File:
@@ -55,7 +55,7 @@ def load_reference(ref, sd, work):
             sys.argv = ["pythia_convert.py", "size=160m"]
             exec(compile(open(os.path.join(src0, "pythia_convert.py")).read(), "pythia_convert.py", "exec"),
                  {"__name__": "pythia_convert", "__file__": os.path.join(work, "pythia_convert.py")})
-        sys.argv = ["pythia_base2.py", "size=160m"]
+        sys.argv = ["pythia_base2.py", "size=160m", *argv]
         ns = {"__name__": "pythia_base2", "__file__": os.path.join(work, "pythia_base2.py")}
         exec(compile(open(os.path.join(src0, "pythia_base2.py")).read(), "pythia_base2.py", "exec"), ns)
         return ns
