@@ -38,8 +38,12 @@ typedef enum {
 
 typedef enum { B2_GPT2 = 0, B2_PYTHIA = 1 } b2_kind;
 
-/* stage switches (base2.py:10-11 gauge=/edge=/arrival=): a set bit puts that stage back to float64 */
-enum { B2_GAUGE_FLOAT = 1, B2_EDGE_FLOAT = 2, B2_ARRIVAL_FLOAT = 4 };
+/* stage switches (base2.py:10-11 gauge=/edge=/arrival=; pythia_base2.py:20 adds turn=): a set bit puts that stage
+ * back to float64, in the reference's order of operations (base2.py:66-69, 79-80, 89-92, 110-113; pythia_base2.py:
+ * 102-104, 118-120, 130-133, 144-146). The gauge and the turn give the reference's integers exactly; the bends and
+ * the arrival use the device's tanh/pow/erf/exp, which can differ from the C library's in the last place and so,
+ * rarely, move an integer by one. A handle with any switch set runs the CUDA-core bank kernel. */
+enum { B2_GAUGE_FLOAT = 1, B2_EDGE_FLOAT = 2, B2_ARRIVAL_FLOAT = 4, B2_TURN_FLOAT = 8 /* Pythia only */ };
 
 typedef struct {
     int32_t kind;       /* b2_kind */

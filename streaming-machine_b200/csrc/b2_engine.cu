@@ -9,6 +9,7 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <cmath>
 #include <mutex>
 #include <string>
 #include <vector>
@@ -52,6 +53,9 @@ struct b2_handle {
     };
     std::vector<Norm> norms;
     int32_t *COS = nullptr, *SIN = nullptr;
+    double *cosf = nullptr, *sinf = nullptr;   // turn=float: float64 cos/sin of pos * 10000^(-2i/rot), [n_ctx][rot/2]
+    double* sigf = nullptr;                    // gauge=float (GPT-2): per row sqrt(var + 1e-5) [max_rows]
+    int64_t* qraw = nullptr;                   // arrival=float (Pythia): turned queries at full width [max_rows][d]
     int64_t cs_len = 0, half = 0, rot = 0;
     bool have_half = false, have_rot = false;
     std::vector<int64_t> emb_w, emb_e;
@@ -231,6 +235,18 @@ int launch(b2_handle* h, int cls, const char* what, void (*kernel)(KArgs...), di
     return B2_OK;
 }
 
+// the float stages (B2_*_FLOAT) that bank bi's epilogue takes: GPT-2's gauged banks and head (gauge), its fc (tanh
+// bend); Pythia's fc (erf bend; Pythia's float gauge is its own norm kernel)
+int bank_float_stages(const b2_handle* h, int bi) {
+    const int f = h->flags, head = bi == 4 * h->cfg.n_layer, kind = bi % 4;
+    if (!f) return 0;
+    if (h->cfg.kind == B2_PYTHIA) return (!head && kind == 2 && (f & B2_EDGE_FLOAT)) ? FE_EDGE_ERF : 0;
+    int r = 0;
+    if (f & B2_GAUGE_FLOAT) r |= head ? FE_GAUGE_HEAD : (kind == 0 || kind == 2) ? FE_GAUGE : 0;
+    if ((f & B2_EDGE_FLOAT) && !head && kind == 2) r |= FE_EDGE_TANH;
+    return r;
+}
+
 // ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
 int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st) {
     const DevBank& bk = h->banks[bi];
@@ -243,6 +259,8 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         return check_launch(h, "tc_bank");
     }
     BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
+    a.flt = bank_float_stages(h, bi);
+    a.sig = h->sigf;
     constexpr int RT = 8;
     dim3 grid((bk.nout + 255) / 256, (rows + RT - 1) / RT);
     switch (epi) {
@@ -254,7 +272,16 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
     }
 }
 
+int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st);
+
+// to16 (+ the gauge) of rows; with gauge=float (GPT-2) the rows' sigma as well (base2.py:67)
 int run_quant(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st) {
+    int rc = run_quant_int(h, X, n, src_rows, rows, gauge, st);
+    if (rc || !gauge || !(h->flags & B2_GAUGE_FLOAT) || h->cfg.kind != B2_GPT2) return rc;
+    return launch(h, B2_PROF_QUANT, "sigma", k_sigma<256>, rows, 256, 0, st, X, n, src_rows, rows, h->sigf);
+}
+
+int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows, int rows, int gauge, cudaStream_t st) {
     PlaneOut pl{};
     if (h->use_tc && rows >= h->tc_min_rows)
         pl = PlaneOut{h->tcr.xh, h->tcr.xl, h->tcr.kmax, h->tcr.rowcorr, h->tcr.nsat, h->tcr.sat};
@@ -271,6 +298,11 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st)
                 or_out, h->half};
     const bool py = h->cfg.kind == B2_PYTHIA;
     const dim3 grid(rows, h->cfg.n_head);
+    if (h->flags & B2_ARRIVAL_FLOAT) {
+        aa.qf = py ? h->qraw : h->QKV;                    // GPT-2: q is the first third of the qkv row
+        aa.ldq = py ? h->cfg.d_model : 3 * h->cfg.d_model;
+        return launch(h, B2_PROF_ATTEND, "attend_float", k_attend_float, grid, 64, sizeof(double) * h->max_ctx, st, aa);
+    }
     const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
     if (h->att_bulk && bulk <= ATT_BULK_MAX)
         return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, true>, grid, 128, bulk, st, aa)
@@ -283,6 +315,9 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st)
 // Pythia's layer norm (pythia_base2.py:100-110) of rows of X (gathered by src_rows when given) into out [rows][d]
 int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows, int ni, int64_t* out, cudaStream_t st) {
     const b2_handle::Norm& nm = h->norms[ni];
+    if (h->flags & B2_GAUGE_FLOAT)
+        return launch(h, B2_PROF_QUANT, "gauge_ln_float", k_gauge_ln_float<256>, rows, 256, 0, st, X, h->cfg.d_model,
+                      src_rows, rows, (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out);
     return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, rows, 256, 0, st, X, h->cfg.d_model, src_rows, rows,
                   (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2, (const int32_t*)h->EXP2,
                   h->eps40, h->d_err);
@@ -305,7 +340,8 @@ int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t*
         if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, rows, h->QKV, 3 * d, nullptr, st))) return rc;
         if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(rows, 3 * H), 32, 0, st,
                          (const int64_t*)h->QKV, rows, (const int32_t*)h->row_slot, (const int32_t*)h->row_pos, l, h->kv,
-                         (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err)))
+                         (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err,
+                         (const double*)h->cosf, (const double*)h->sinf, h->qraw)))
             return rc;
         if ((rc = run_attend(h, rows, l, nullptr, st))) return rc;
         if ((rc = run_gauge(h, h->R, nullptr, rows, 2 * l + 1, h->HID, st))) return rc;
@@ -465,7 +501,9 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (cfg->n_layer < 1 || cfg->n_layer > 64 || cfg->n_head < 1 || cfg->d_model != cfg->n_head * 64 ||
         cfg->d_model % 256 || cfg->d_ff % 256 || cfg->vocab < 1 || cfg->n_ctx < 1)
         return B2_ERR_ARG;
-    if (flags & (B2_GAUGE_FLOAT | B2_EDGE_FLOAT | B2_ARRIVAL_FLOAT)) return B2_ERR_ARG;   // integer stages only
+    const int allowed = B2_GAUGE_FLOAT | B2_EDGE_FLOAT | B2_ARRIVAL_FLOAT | (cfg->kind == B2_PYTHIA ? B2_TURN_FLOAT : 0);
+    if (flags & ~allowed) return B2_ERR_ARG;
+    if (flags && cfg->d_model > FLT_MAXD) return B2_ERR_ARG;
     b2_handle* h = new b2_handle();
     h->cfg = *cfg;
     h->device = device;
@@ -640,8 +678,25 @@ int b2_finalize(b2_handle* h) {
     }
     if (!h->PHI || !h->ARR || !h->LOG2 || !h->EXP2 || !h->have_scalar[1])
         return fail(h, B2_ERR_STATE, "a table or scalar is missing");
-    // tensor-core layouts of every bank
-    int tc_ok = tc_init() == 0;
+    if ((h->flags & B2_TURN_FLOAT) && !h->cosf) {
+        // pythia_base2.py:118-120: ang = pos * 10000^(-(0, 2, ..) / rot), cos and sin by the C library (numpy's values)
+        const int r = (int)h->rot / 2, n = h->cfg.n_ctx;
+        std::vector<double> c((size_t)n * r), s((size_t)n * r);
+        for (int t = 0; t < r; t++) {
+            const double inv = std::pow(10000.0, (double)(-2 * t) / (double)h->rot);
+            for (int p = 0; p < n; p++) {
+                const double ang = (double)p * inv;
+                c[(size_t)p * r + t] = std::cos(ang);
+                s[(size_t)p * r + t] = std::sin(ang);
+            }
+        }
+        int rc;
+        if ((rc = dalloc(h, &h->cosf, c.size())) || (rc = dalloc(h, &h->sinf, s.size()))) return rc;
+        CK(cudaMemcpy(h->cosf, c.data(), sizeof(double) * c.size(), cudaMemcpyHostToDevice));
+        CK(cudaMemcpy(h->sinf, s.data(), sizeof(double) * s.size(), cudaMemcpyHostToDevice));
+    }
+    // tensor-core layouts of every bank (the float stages run on the CUDA-core bank kernel only)
+    int tc_ok = !h->flags && tc_init() == 0;
     for (auto& bk : h->banks) {
         if (!tc_ok) break;
         if (tc_bank_build(bk.tc, bk.w, bk.nin, bk.nout)) tc_ok = 0;
@@ -662,7 +717,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+    void* old[] = {h->sigf, h->qraw, h->kv.kraw, h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
@@ -671,6 +726,9 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     dfree(h, h->gen_desc);
     dfree(h, h->gen_base);
     h->n_slots = 0;
+    h->sigf = nullptr;
+    h->qraw = nullptr;
+    h->kv.kraw = nullptr;
     const int L = c.n_layer, H = c.n_head, d = c.d_model, F = c.d_ff;
     const int ctx_stride = (max_ctx + 15) / 16 * 16;
     size_t nkv = (size_t)n_streams * L * H * ctx_stride;
@@ -680,6 +738,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((rc = dalloc(h, &h->kv.kmask, nkv))) return rc;
     if ((rc = dalloc(h, &h->kv.kexp, nkv))) return rc;
     if ((rc = dalloc(h, &h->kv.v, nkv * 64))) return rc;
+    if ((h->flags & B2_ARRIVAL_FLOAT) && (rc = dalloc(h, &h->kv.kraw, nkv * 64))) return rc;
     if ((rc = dalloc(h, &h->row_or, (size_t)4 * L * FUSED_ROWS))) return rc;
     CK(cudaMemset(h->row_or, 0, sizeof(uint64_t) * 4 * L * FUSED_ROWS));
     if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
@@ -698,6 +757,8 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((rc = dalloc(h, &h->x16, (size_t)mr * (F > d ? F : d))) || (rc = dalloc(h, &h->ex, mr)) ||
         (rc = dalloc(h, &h->LS, mr)) || (rc = dalloc(h, &h->q16, (size_t)mr * d)) || (rc = dalloc(h, &h->qexp, (size_t)mr * H)))
         return rc;
+    if ((h->flags & B2_GAUGE_FLOAT) && (rc = dalloc(h, &h->sigf, mr))) return rc;
+    if ((h->flags & B2_ARRIVAL_FLOAT) && (rc = dalloc(h, &h->qraw, (size_t)mr * d))) return rc;
     if ((rc = dalloc(h, &h->head_rows, 2 * (size_t)mr)) || (rc = dalloc(h, &h->race_out, n_streams)) ||
         (rc = dalloc(h, &h->logits, (size_t)n_streams * c.vocab)))
         return rc;
@@ -934,6 +995,7 @@ int b2_bank_noalloc(b2_handle* h, const char* name, const int64_t* X, int32_t ro
         return fail(h, B2_ERR_ARG, "b2_bank_noalloc: bad argument");
     if (h->cfg.kind == B2_PYTHIA && mode < 2)
         return fail(h, B2_ERR_ARG, "b2_bank_noalloc: Pythia's banks are plain (modes 2 and 3)");
+    if (h->flags) return fail(h, B2_ERR_ARG, "b2_bank_noalloc: integer stages only (the handle has float switches)");
     if (h->device < 0 || h->device >= NOALLOC_MAX_DEVICES)
         return fail(h, B2_ERR_ARG, "b2_bank_noalloc: device %d past the %d this entry point serves", h->device,
                     NOALLOC_MAX_DEVICES);

@@ -26,6 +26,7 @@ struct KV {
     int32_t* v;        // [slot][L][H][ctx][64]
     int L, H, ctx;     // ctx: the positions' stride (a multiple of 16, so every (slot, layer, head) run is 16-byte aligned)
     int lim;           // positions actually allocated to a stream (max_ctx); a position at or past it is an error
+    int64_t* kraw = nullptr;   // arrival=float only: the keys at full width, [slot][L][H][ctx][64]
 };
 
 // position of (slot, layer, head, pos) in the key/value store: [slot][layer][head][pos]

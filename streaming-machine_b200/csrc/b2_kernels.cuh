@@ -6,6 +6,7 @@
 #include <stdint.h>
 #include "b2_arith.cuh"
 #include "b2_epi.cuh"
+#include "b2_float.cuh"
 #include "b2_ptx.cuh"
 
 namespace b2 {
@@ -166,10 +167,14 @@ __global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, 
 // Pythia's q/k/v split (pythia_base2.py:116-134): one warp per (row, part of 3H), parts ordered per head q, k, v.
 // q and k: the first `rot` dims turned by the position (pairs (i, i + rot/2), cos/sin at 2^-30; inputs past 2^31
 // are where the reference asserts), then to16 over the head; v to the value store as it is.
+// turn=float (pythia_base2.py:118-120): cosf/sinf, float64 cos and sin of the angles made on the host, replace the
+// integer turn: round(a c - b s), round(b c + a s). arrival=float: the turned q (qraw [rows][d]) and k (kv.kraw) at
+// full width as well.
 __global__ void k_heads_pythia(const int64_t* __restrict__ QKV, int rows, const int32_t* __restrict__ row_slot,
                                const int32_t* __restrict__ row_pos, int layer, KV kv, int rot,
                                const int32_t* __restrict__ COS, const int32_t* __restrict__ SIN, int32_t* __restrict__ q16,
-                               int32_t* __restrict__ qexp, uint32_t* err) {
+                               int32_t* __restrict__ qexp, uint32_t* err, const double* __restrict__ cosf,
+                               const double* __restrict__ sinf, int64_t* __restrict__ qraw) {
     griddep_wait();
     griddep_launch();
     const int r = blockIdx.x, part = blockIdx.y, lane = threadIdx.x;
@@ -181,10 +186,18 @@ __global__ void k_heads_pythia(const int64_t* __restrict__ QKV, int rows, const 
     if (pos < 0 || pos >= kv.lim) { if (lane == 0) set_err(err, DERR_POS); return; }   // never index past the tables
     if (kind < 2) {
         const int half = rot >> 1;                                       // rot == 16: pairs (t, t + 8) in lanes 0..15
-        const bool big = lane < rot && mag(v0) >= (1ull << 31);
+        const bool big = !cosf && lane < rot && mag(v0) >= (1ull << 31);
         if (__any_sync(0xffffffffu, big) && lane == 0) set_err(err, DERR_RANGE);
         const int64_t other = __shfl_xor_sync(0xffffffffu, v0, half);   // lane t < half holds a, lane t + half holds b
-        if (lane < rot) {
+        if (cosf) {
+            if (lane < rot) {
+                const int t = lane < half ? lane : lane - half;
+                const double c = cosf[(size_t)pos * half + t], s = sinf[(size_t)pos * half + t];
+                const double me = i2d(v0), ot = i2d(other);
+                v0 = lane < half ? rint64(__dsub_rn(__dmul_rn(me, c), __dmul_rn(ot, s)))      // a c - b s
+                                 : rint64(__dadd_rn(__dmul_rn(me, c), __dmul_rn(ot, s)));     // b c + a s
+            }
+        } else if (lane < rot) {
             const int t = lane < half ? lane : lane - half;
             const int64_t c = COS[(size_t)pos * half + t], s = SIN[(size_t)pos * half + t];
             if (lane < half) v0 = rshift(wsub(wmul(v0, c), wmul(other, s)), 30);          // a*c - b*s
@@ -192,6 +205,12 @@ __global__ void k_heads_pythia(const int64_t* __restrict__ QKV, int rows, const 
         }
         const int sh = to16_shift(warp_or64(mag(v0) | mag(v1)));
         const int64_t a0 = rshift(v0, sh), a1 = rshift(v1, sh);
+        if (kind == 0 && qraw) { qraw[(size_t)r * d + h * 64 + lane] = v0; qraw[(size_t)r * d + h * 64 + lane + 32] = v1; }
+        if (kind == 1 && kv.kraw) {
+            const size_t idx = kv_index(slot, layer, h, pos, kv.L, H, kv.ctx);
+            kv.kraw[idx * 64 + lane] = v0;
+            kv.kraw[idx * 64 + lane + 32] = v1;
+        }
         if (kind == 0) {
             q16[(size_t)r * d + h * 64 + lane] = (int32_t)a0;
             q16[(size_t)r * d + h * 64 + lane + 32] = (int32_t)a1;
@@ -223,7 +242,32 @@ struct BankArgs {
     const int16_t* w;       // [nin][nout]
     int nin, nout, rows;
     EpiArgs epi;
+    int flt = 0;                    // float stage switches of this bank's epilogue (FE_* bits), 0: integer
+    const double* sig = nullptr;    // gauge=float: per row sqrt(var + 1e-5) of the stream at 2^-16
 };
+
+// the bank epilogue with float stages (base2.py:66-69 gauged bank, :110-113 head, :79-80 bend; pythia_base2.py:144-146
+// bend): pile * 2^(we + ex) / sig at 2^-16 rounded, the bias after (layer banks) or before the rounding (head)
+template <int EPI>
+B2_DEV void epi_store_float(const BankArgs& a, int r, int j, int64_t pile) {
+    const EpiArgs& e = a.epi;
+    const int orow = e.out_map ? e.out_map[r] : r;
+    int64_t* o = e.out + (size_t)orow * e.ldo + j;
+    const int64_t es = wadd(wadd((int64_t)e.e[j], (int64_t)e.ex[r]), 16);
+    int64_t v;
+    if ((EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) && (a.flt & (FE_GAUGE | FE_GAUGE_HEAD))) {
+        const double val = __ddiv_rn(__dmul_rn(i2d(pile), scalbn(1.0, (int)(es - 16))), a.sig[r]);
+        v = (a.flt & FE_GAUGE_HEAD) ? rint64(__dmul_rn(__dadd_rn(val, __ddiv_rn(i2d(e.b[j]), 65536.0)), 65536.0))
+                                    : wadd(rint64(__dmul_rn(val, 65536.0)), e.b[j]);
+    } else if (EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE) {
+        v = wadd(power(pile, wsub(wmul(es, 65536), e.LS[r]), e.EXP2), e.b[j]);
+    } else {
+        v = wadd(rshift(pile, -es), e.b[j]);
+    }
+    if (EPI == EPI_GAUGED_EDGE || EPI == EPI_PLAIN_EDGE)
+        v = (a.flt & FE_EDGE_TANH) ? edge_tanh(v) : (a.flt & FE_EDGE_ERF) ? edge_erf(v) : edge(v, e.PHI);
+    *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
+}
 
 // CUDA-core bank product: one thread per output column, RT rows per CTA, the pile exact in int64.
 template <int EPI, int RT>
@@ -254,6 +298,11 @@ __global__ void __launch_bounds__(256) k_bank_simt(BankArgs a) {
         __syncthreads();
     }
     if (j >= a.nout) return;
+    if (a.flt) {
+        for (int rr = 0; rr < RT; rr++)
+            if (r0 + rr < a.rows) epi_store_float<EPI>(a, r0 + rr, j, acc[rr]);
+        return;
+    }
 #pragma unroll
     for (int rr = 0; rr < RT; rr++)
         if (r0 + rr < a.rows) epi_store<EPI>(a.epi, r0 + rr, j, acc[rr]);
@@ -288,6 +337,7 @@ __global__ void k_heads(const int64_t* __restrict__ QKV, int rows, const int32_t
             size_t idx = kv_index(slot, layer, part - H, pos, kv.L, H, kv.ctx);
             kv.k[idx * 64 + lane] = (int16_t)(uint16_t)(uint32_t)a0;
             kv.k[idx * 64 + lane + 32] = (int16_t)(uint16_t)(uint32_t)a1;
+            if (kv.kraw) { kv.kraw[idx * 64 + lane] = v0; kv.kraw[idx * 64 + lane + 32] = v1; }   // arrival=float
             uint32_t m0 = __ballot_sync(0xffffffffu, a0 == 32768), m1 = __ballot_sync(0xffffffffu, a1 == 32768);
             if (lane == 0) {
                 kv.kmask[idx] = (uint64_t)m0 | ((uint64_t)m1 << 32);
@@ -326,6 +376,8 @@ struct AttnArgs {
     uint32_t* err;
     uint64_t* or_out;       // optional [rows]: OR of |out| per row (the next bank's to16 shift)
     int64_t half;           // Pythia: log2(head size) / 2 at 2^-16 (the score's 1/sqrt(64) as a power)
+    const int64_t* qf;      // arrival=float: the queries at full width, row r's head h at qf[r * ldq + h * 64]
+    int ldq;
 };
 
 // the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
@@ -723,6 +775,103 @@ __global__ void k_decode_commit(int n, const int32_t* __restrict__ word, int32_t
     slot_tok[s] = w;
     int32_t* out = desc->out;
     if (out) out[(size_t)s * desc->ld + (len - base[s])] = w;
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// float stage switches (see b2_float.cuh): the gauge's sigma, Pythia's float norm, the float arrival. One CTA per
+// row (per row and head for the arrival); the pairwise sums run in one thread, in numpy's order.
+// ---------------------------------------------------------------------------------------------------------------------
+// the row at 2^-16 into x[], x - mean into x[], (x - mean)^2 into t[]; returns sqrt(mean t + 1e-5)
+// (base2.py:67, pythia_base2.py:103). Block-wide; d <= the shared arrays' length.
+template <int NT>
+__device__ double row_sigma(const int64_t* __restrict__ R, int d, double* x, double* t) {
+    __shared__ double s_mu, s_sg;
+    for (int i = threadIdx.x; i < d; i += NT) x[i] = __ddiv_rn(i2d(R[i]), 65536.0);
+    __syncthreads();
+    if (threadIdx.x == 0) s_mu = __ddiv_rn(pairwise_sum(x, d), (double)d);
+    __syncthreads();
+    const double mu = s_mu;
+    for (int i = threadIdx.x; i < d; i += NT) { const double c = __dsub_rn(x[i], mu); x[i] = c; t[i] = __dmul_rn(c, c); }
+    __syncthreads();
+    if (threadIdx.x == 0) s_sg = __dsqrt_rn(__dadd_rn(__ddiv_rn(pairwise_sum(t, d), (double)d), 1e-5));
+    __syncthreads();
+    return s_sg;
+}
+
+constexpr int FLT_MAXD = 1024;   // the float norms take rows of up to 1,024 (d = 768 here)
+
+// GPT-2 gauge=float: sig[r] of row src_rows[r] (or r) of R (base2.py:67 and :111)
+template <int NT>
+__global__ void __launch_bounds__(NT) k_sigma(const int64_t* __restrict__ R, int d, const int32_t* __restrict__ src_rows,
+                                             int rows, double* __restrict__ sig) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ double x[FLT_MAXD], t[FLT_MAXD];
+    const int r = blockIdx.x;
+    if (r >= rows || d > FLT_MAXD) return;
+    const double s = row_sigma<NT>(R + (size_t)(src_rows ? src_rows[r] : r) * d, d, x, t);
+    if (threadIdx.x == 0) sig[r] = s;
+}
+
+// Pythia gauge=float (pythia_base2.py:102-104): round((x - mu) / sg * g * 2^ge * 2^16) + b
+template <int NT>
+__global__ void __launch_bounds__(NT) k_gauge_ln_float(const int64_t* __restrict__ R, int d,
+                                                      const int32_t* __restrict__ src_rows, int rows,
+                                                      const int64_t* __restrict__ g, int64_t ge,
+                                                      const int64_t* __restrict__ b, int64_t* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ double x[FLT_MAXD], t[FLT_MAXD];
+    const int r = blockIdx.x;
+    if (r >= rows || d > FLT_MAXD) return;
+    const double sg = row_sigma<NT>(R + (size_t)(src_rows ? src_rows[r] : r) * d, d, x, t);
+    const double sc = scalbn(1.0, (int)ge);
+    for (int i = threadIdx.x; i < d; i += NT)
+        out[(size_t)r * d + i] =
+            wadd(rint64(__dmul_rn(__dmul_rn(__dmul_rn(__ddiv_rn(x[i], sg), i2d(g[i])), sc), 65536.0)), b[i]);
+}
+
+// arrival=float (base2.py:89-92, pythia_base2.py:130-133) for row r at position p, head h: s = (q/2^16).(k/2^16)/8
+// (the dot exact in 128 bits, rounded once), a = exp(s - max s) / (pairwise sum), out = round(sum_s a v / 2^16 * 2^16)
+// with the sum over s in order. 64 threads (one per output dim); dynamic shared memory: 8 bytes per key.
+__global__ void __launch_bounds__(64) k_attend_float(AttnArgs a) {
+    griddep_wait();
+    griddep_launch();
+    extern __shared__ double e[];
+    __shared__ int64_t qs[64];
+    __shared__ double red[2], s_Z;
+    const int r = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int H = a.kv.H, d = H * 64;
+    const int slot = a.row_slot[r], p = a.row_pos[r];
+    if (p < 0 || p >= a.kv.lim) return;      // flagged by the heads kernel (DERR_POS)
+    const int nk = p + 1;
+    qs[tid] = a.qf[(size_t)r * a.ldq + h * 64 + tid];
+    __syncthreads();
+    const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
+    double mx = -INFINITY;
+    for (int s = tid; s < nk; s += 64) {
+        const int64_t* k = a.kv.kraw + (base + s) * 64;
+        __int128 dot = 0;
+        for (int t = 0; t < 64; t++) dot += (__int128)qs[t] * (__int128)k[t];
+        const double v = __ddiv_rn(scalbn(i128_to_double(dot), -32), 8.0);
+        e[s] = v;
+        mx = fmax(mx, v);
+    }
+    for (int o = 16; o > 0; o >>= 1) mx = fmax(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if ((tid & 31) == 0) red[tid >> 5] = mx;
+    __syncthreads();
+    mx = fmax(red[0], red[1]);
+    for (int s = tid; s < nk; s += 64) e[s] = exp(__dsub_rn(e[s], mx));
+    __syncthreads();
+    if (tid == 0) s_Z = pairwise_sum(e, nk);
+    __syncthreads();
+    const double Z = s_Z;
+    for (int s = tid; s < nk; s += 64) e[s] = __ddiv_rn(e[s], Z);
+    __syncthreads();
+    const int32_t* V = a.kv.v + base * 64 + tid;
+    double acc = 0.0;
+    for (int s = 0; s < nk; s++) acc = __dadd_rn(acc, __dmul_rn(e[s], __ddiv_rn((double)V[(size_t)s * 64], 65536.0)));
+    a.out[(size_t)r * d + h * 64 + tid] = rint64(__dmul_rn(acc, 65536.0));
 }
 
 // truncate streams back to lens[s] positions (never forward), last_tok[s] fed next

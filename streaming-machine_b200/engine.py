@@ -19,7 +19,7 @@ import numpy as np
 from . import build as _build
 
 B2_GPT2, B2_PYTHIA = 0, 1
-B2_GAUGE_FLOAT, B2_EDGE_FLOAT, B2_ARRIVAL_FLOAT = 1, 2, 4
+B2_GAUGE_FLOAT, B2_EDGE_FLOAT, B2_ARRIVAL_FLOAT, B2_TURN_FLOAT = 1, 2, 4, 8
 STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_CTX", 5: "ERR_VALUE", 6: "ERR_STATE",
           7: "ERR_DEVICE"}
 
@@ -93,12 +93,15 @@ class Engine:
     Pythia's "embed.w") on one GPU, with `n_streams` independent streams of up to `max_ctx` positions."""
 
     def __init__(self, M: dict, device: int = 0, n_streams: int = 1, max_ctx: int = 1024,
-                 gauge: str = "int", edge: str = "int", arrival: str = "int"):
+                 gauge: str = "int", edge: str = "int", arrival: str = "int", turn: str = "int"):
+        """gauge=/edge=/arrival= "float" (and Pythia's turn=) put that stage back to float64, as the reference's
+        switches do (base2.py:10-11, pythia_base2.py:20)."""
         torch = _torch()
         self.torch = torch
         self.device = torch.device("cuda", device)
         flags = (B2_GAUGE_FLOAT if gauge == "float" else 0) | (B2_EDGE_FLOAT if edge == "float" else 0) | \
-                (B2_ARRIVAL_FLOAT if arrival == "float" else 0)
+                (B2_ARRIVAL_FLOAT if arrival == "float" else 0) | (B2_TURN_FLOAT if turn == "float" else 0)
+        self.flags = flags
         self.pythia = "embed.w" in M
         n_layer = sum(1 for k in M if k.startswith("qkv.") and k.endswith(".w"))
         if self.pythia:

@@ -72,4 +72,6 @@ def test_create_rejects_bad_config():
     h = ctypes.c_void_p()
     assert L.b2_create(ctypes.byref(cfg), 0, 0, ctypes.byref(h)) == 1 and not h.value
     cfg = engine.Config(0, 12, 768, 12, 3072, 50257, 1024)
-    assert L.b2_create(ctypes.byref(cfg), 0, 7, ctypes.byref(h)) == 1   # float stage switches are not built
+    assert L.b2_create(ctypes.byref(cfg), 0, 8, ctypes.byref(h)) == 1   # turn=float is Pythia's switch only
+    cfg = engine.Config(2, 12, 768, 12, 3072, 50257, 1024)
+    assert L.b2_create(ctypes.byref(cfg), 0, 0, ctypes.byref(h)) == 1   # unknown model kind
