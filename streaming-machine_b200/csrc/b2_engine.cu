@@ -16,6 +16,7 @@
 
 #include "../../include/base2.h"
 #include "b2_kernels.cuh"
+#include "b2_mega.cuh"
 #include "b2_tc.cuh"
 
 using namespace b2;
@@ -80,6 +81,8 @@ struct b2_handle {
     uint64_t* row_or = nullptr;  // decode: per bank input, the OR of |x| over each row ([4L][FUSED_ROWS])
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
+    int use_mega = 0;            // decode steps of <= 64 streams as one persistent kernel (B2_MEGA=1)
+    MegaPlan mega;
     int64_t* logits = nullptr;   // [n_slots][vocab]
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
@@ -455,6 +458,54 @@ int run_decode(b2_handle* h, int n, cudaStream_t st) {
                   c.vocab, h->race_out);
 }
 
+bool mega_ok(const b2_handle* h, int n) {
+    return h->use_mega && h->mega.ready && h->cfg.kind == B2_GPT2 && !h->flags && n <= 64 && h->tc_min_rows <= 1 &&
+           mega_att_slot_bytes(h->max_ctx) > 0;
+}
+
+// the decode step for n <= 64 streams (row r = slot r) as one persistent kernel, then the head and the race
+int run_mega(b2_handle* h, int n, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    MegaArgs a{};
+    a.L = c.n_layer;
+    a.H = c.n_head;
+    a.d = c.d_model;
+    a.F = c.d_ff;
+    a.rows = n;
+    a.slot_len = h->slot_len;
+    a.slot_tok = h->slot_tok;
+    a.row_slot = h->row_slot;
+    a.row_pos = h->row_pos;
+    a.row_tok = h->row_tok;
+    a.wte = h->wte;
+    a.wpe = h->wpe;
+    a.vocab = c.vocab;
+    a.nctx = c.n_ctx;
+    a.R = h->R;
+    a.ATT = h->ATT;
+    a.HID = h->HID;
+    a.OR = h->row_or;
+    a.q16 = h->q16;
+    a.qexp = h->qexp;
+    a.kv = h->kv;
+    a.EXP2 = h->EXP2;
+    a.PHI = h->PHI;
+    a.LOG2 = h->LOG2;
+    a.ARR = h->ARR;
+    a.alen = h->alen;
+    a.log768 = h->log768;
+    a.eps40 = h->eps40;
+    a.err = h->d_err;
+    prof_begin(h, B2_PROF_BANK, st);
+    int rc = mega_launch(h->mega, a, st);
+    prof_end(h, B2_PROF_BANK, st);
+    if (rc) return fail(h, B2_ERR_CUDA, "decode-step kernel: %s", cudaGetErrorString((cudaError_t)rc));
+    if ((rc = run_quant(h, h->R, c.d_model, nullptr, n, 1, st))) return rc;
+    if ((rc = run_bank(h, 4 * c.n_layer, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab,
+                  (const int32_t*)nullptr, c.vocab, h->race_out);
+}
+
 bool fused_avail(const b2_handle* h, int n) {
     return h->cfg.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS;
 }
@@ -514,6 +565,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
     if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
+    if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
@@ -703,6 +755,20 @@ int b2_finalize(b2_handle* h) {
     }
     CK(cudaDeviceSynchronize());
     h->tc_min_rows = tc_ok ? tc_min_rows_default() : (1 << 30);
+    mega_free(h->mega);
+    if (tc_ok && h->cfg.kind == B2_GPT2 && !h->flags) {
+        // the one-kernel decode step; without it (a plan that does not fit) decode runs as separate launches
+        std::vector<TcBank> tcs;
+        std::vector<const int32_t*> es;
+        std::vector<const int64_t*> bs;
+        for (int i = 0; i < 4 * h->cfg.n_layer; i++) {
+            tcs.push_back(h->banks[i].tc);
+            es.push_back(h->banks[i].e);
+            bs.push_back(h->banks[i].b);
+        }
+        if (mega_plan(h->mega, tcs.data(), es.data(), bs.data(), h->cfg.n_layer)) mega_free(h->mega);
+        cudaGetLastError();
+    }
     const char* env = getenv("B2_TC_MIN_ROWS");
     if (env && tc_ok) h->tc_min_rows = atoi(env);
     h->finalized = true;
@@ -844,6 +910,12 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
 int step_core(b2_handle* h, int n, cudaStream_t st) {
+    if (mega_ok(h, n)) {
+        int rc = run_mega(h, n, st);
+        if (rc) return rc;
+        return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
+                      h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
+    }
     if (fused_ok(h, n)) {
         int rc = run_decode(h, n, st);
         if (rc) return rc;
@@ -1100,6 +1172,7 @@ void b2_destroy(b2_handle* h) {
     drop_graph(h);
     if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
+    mega_free(h->mega);
     tc_rows_free(h->tcr);
     for (int c = 0; c < B2_PROF_N; c++)
         for (auto& p : h->prof.ev[c]) { cudaEventDestroy(p.first); cudaEventDestroy(p.second); }

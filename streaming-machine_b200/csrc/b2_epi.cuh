@@ -85,4 +85,14 @@ B2_DEV void epi_store(const EpiArgs& a, int r, int j, int64_t pile) {
     }
 }
 
+// ARR read as base2.py:97 does it: ARR[min(d, len-1)] where d < len, else 0. d is never negative unless a score
+// wrapped; numpy would then index from the table's end (d >= -len) or raise (d < -len, flagged here).
+B2_DEV int64_t arrival(int64_t d, const int32_t* __restrict__ ARR, int alen, uint32_t* err) {
+    if (d >= alen) return 0;
+    if (d >= 0) return (int64_t)__ldg(ARR + d);
+    if (d >= -(int64_t)alen) return (int64_t)__ldg(ARR + (alen + d));
+    set_err(err, DERR_INDEX);
+    return 0;
+}
+
 }  // namespace b2
