@@ -83,6 +83,8 @@ struct b2_handle {
     int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
     int use_mega = 0;            // decode steps of <= 64 streams as one persistent kernel (B2_MEGA=1)
     MegaPlan mega;
+    uint64_t* mega_trace = nullptr;   // B2_MEGA_TRACE=<file>: the last step's phase timestamps, written at b2_destroy
+    std::string mega_trace_path;
     int64_t* logits = nullptr;   // [n_slots][vocab]
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
@@ -496,6 +498,7 @@ int run_mega(b2_handle* h, int n, cudaStream_t st) {
     a.log768 = h->log768;
     a.eps40 = h->eps40;
     a.err = h->d_err;
+    a.trace = h->mega_trace;
     prof_begin(h, B2_PROF_BANK, st);
     int rc = mega_launch(h->mega, a, st);
     prof_end(h, B2_PROF_BANK, st);
@@ -566,6 +569,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
+    if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
@@ -768,6 +772,11 @@ int b2_finalize(b2_handle* h) {
         }
         if (mega_plan(h->mega, tcs.data(), es.data(), bs.data(), h->cfg.n_layer)) mega_free(h->mega);
         cudaGetLastError();
+        if (h->mega.ready && !h->mega_trace_path.empty() && !h->mega_trace) {
+            const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
+            if (cudaMalloc(&h->mega_trace, n * sizeof(uint64_t)) != cudaSuccess) h->mega_trace = nullptr;
+            else cudaMemset(h->mega_trace, 0, n * sizeof(uint64_t));
+        }
     }
     const char* env = getenv("B2_TC_MIN_ROWS");
     if (env && tc_ok) h->tc_min_rows = atoi(env);
@@ -1171,6 +1180,17 @@ void b2_destroy(b2_handle* h) {
     cudaDeviceSynchronize();
     drop_graph(h);
     if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
+    if (h->mega_trace) {
+        const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
+        std::vector<uint64_t> t(n);
+        if (cudaMemcpy(t.data(), h->mega_trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost) == cudaSuccess) {
+            if (FILE* f = fopen(h->mega_trace_path.c_str(), "wb")) {
+                fwrite(t.data(), sizeof(uint64_t), n, f);
+                fclose(f);
+            }
+        }
+        cudaFree(h->mega_trace);
+    }
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
     mega_free(h->mega);
     tc_rows_free(h->tcr);

@@ -39,7 +39,7 @@ namespace b2 {
 
 namespace {
 
-constexpr int NT = 256;                              // threads per CTA (8 warps)
+constexpr int NT = 512;                              // threads per CTA (16 warps: latency-bound code needs them)
 constexpr int WST = 2 * A_BYTES;                     // weight planes of one 128-input K block: 32 KB
 constexpr int XST = 2 * B_BYTES;                     // activation planes of one K block: 16 KB
 constexpr int MAXKPS = 4;                            // K blocks per CTA (mproj: 24 blocks over 6 CTAs)
@@ -64,6 +64,14 @@ B2_DEV void fence_async_global() { asm volatile("fence.proxy.async.global;" ::: 
 B2_DEV int64_t ldcg(const int64_t* p) { return (int64_t)__ldcg((const long long*)p); }
 B2_DEV uint64_t ldcgu(const uint64_t* p) { return (uint64_t)__ldcg((const unsigned long long*)p); }
 B2_DEV int32_t ldcg_i32(const int32_t* p) { return __ldcg(p); }
+
+// profiling aid: thread 0 stamps the time of step k of phase ph
+B2_DEV void stamp(const MegaArgs& a, int ph, int k) {
+    if (a.trace && threadIdx.x == 0 && ph < MEGA_MAX_PHASES) {
+        a.trace[((size_t)blockIdx.x * MEGA_MAX_PHASES + ph) * MEGA_STAMPS + k] = gtime();
+        if (k == 0) a.trace[((size_t)blockIdx.x * MEGA_MAX_PHASES + ph) * MEGA_STAMPS + 7] = clock64();
+    }
+}
 
 // bounded wait ignoring the error word: the final drain of our own copies and MMAs
 B2_DEV void mbar_drain(uint64_t* bar, uint32_t parity) {
@@ -91,15 +99,17 @@ B2_DEV void grid_sync(uint32_t* bar, uint32_t target, uint32_t* err) {
 }
 
 struct Sh {
-    uint64_t wbar[MAXKPS], accbar, abar[MAX_SLOTS];
+    uint64_t wbar[MAXKPS], accbar, abar[MAX_SLOTS], rbar;
     uint32_t tmem;
     int sh[BN];
-    int64_t S1[BN], S2[BN], rowc[BN], LS[BN], e2[BN];
+    int32_t pos[BN], slot[BN];       // the rows' positions and stream slots (fixed for the whole step)
+    alignas(16) int64_t S12[BN][2];  // partial S1, S2 per row (sent to the peers as 16-byte rows)
+    int64_t rowc[BN], LS[BN], e2[BN];
     uint32_t sat[BN][MAXKPS * 4];
     unsigned long long satrows;
-    uint64_t hor[8][4];
+    uint64_t hor[16][2];
     int32_t qs[MAX_SLOTS][64];
-    int64_t red[8][66];
+    int64_t red[2][8][66];           // the arrival: per warp group, per warp
     int nslots, slot_bytes;
 };
 
@@ -110,6 +120,7 @@ struct Track {
     uint32_t acc;              // all threads: completed accbar phases
     uint32_t aarm[MAX_SLOTS];  // tid 0: times abar[s] was armed
     uint32_t await_;           // all threads: parity bits of the next abar waits
+    uint32_t rpar;             // all threads: completed rbar phases (the reduction's incoming slices)
 };
 
 struct Unit {
@@ -148,88 +159,163 @@ B2_DEV void issue_weights(const MegaArgs& a, int bi, const MegaBank& bk, const U
 // one bank round (see the header). X: the bank's input [rows][nin]; xor_in: its rows' OR; out: R (PLAIN_ADD) or HID
 // (GAUGED_EDGE); or_out: the next bank's OR slot (may be null); HEADS: the qkv bank's heads16 + key/value append.
 // `prefetched`: the weights were issued already. All CTAs of a cluster call this the same number of times.
+//
+// Shared memory: weights [0, kps*32K), activation planes after them; once the MMAs are done, the partial tile P
+// [64 rows][128] int64 at [0, 64K), and the receive buffers RB (one slice of rows per sub-group peer) and R12 (their
+// partial S1, S2) above it. The K-split reduction is pushed, not pulled: after a cluster barrier each CTA sends every
+// peer the peer's slice of rows of P (one bulk copy shared::cta -> shared::cluster each, completing on the peer's
+// mbarrier), then sums its own slice locally.
 // ---------------------------------------------------------------------------------------------------------------------
-template <int EPI, bool HEADS>
-B2_DEV void bank_round(const MegaArgs& a, int bi, const MegaBank& bk, const Unit u, bool prefetched, const int64_t* X,
-                       const uint64_t* xor_in, uint64_t* or_out, int64_t* out, int ldo, int layer, uint8_t* smem, Sh& s,
-                       Track& t) {
-    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+constexpr int RB_BASE = 64 * 1024;
+B2_DEV int slice_rows(int ks) { return (BN + ks - 1) / ks; }
+B2_DEV int r12_base(int ks) { return RB_BASE + ks * slice_rows(ks) * 1024; }
+B2_DEV void bulk_s2c(uint32_t dst_cluster, const void* src, uint32_t bytes, uint32_t bar_cluster) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_cluster),
+                 "r"(saddr(src)), "r"(bytes), "r"(bar_cluster)
+                 : "memory");
+}
+// to16 of one int64 (given as its two 32-bit halves) by the row's shift (0..49, base2.py:24-27): add half, shift
+B2_DEV int32_t to16v(int lo, int hi, int sh) {
+    const uint64_t x = ((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo;
+    return sh ? (int32_t)((int64_t)(x + (1ull << (sh - 1))) >> sh) : (int32_t)(int64_t)x;
+}
+B2_DEV uint32_t hbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)(x == 32768 ? 127 : (x >> 8)); }
+B2_DEV uint32_t lbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)((x & 255) - 128); }
+B2_DEV uint32_t redux_add(uint32_t v) { return __reduce_add_sync(0xffffffffu, v); }
+// named barrier `id` (1..15) over `count` threads, and its AND-reduction form
+B2_DEV void group_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+B2_DEV bool group_and(int id, int count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+B2_DEV void st_shared_u16(uint32_t addr, uint32_t v) { asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((uint16_t)v) : "memory"); }
+
+// the bank epilogue with the mode chosen at run time (one copy of the code for every bank keeps it in the
+// instruction cache): base2.py:70-71 gauged (+ the bend, :106) or :76 plain added into the residual
+B2_DEV int64_t epi_rt(int epi, int64_t pile, int64_t e_j, int64_t b_j, int64_t exr, int64_t LSr, int64_t e2r,
+                      const int32_t* __restrict__ PHI) {
+    const int64_t es = wadd(wadd(e_j, exr), 16);
+    if (epi == EPI_PLAIN_ADD) return wadd(rshift(pile, -es), b_j);
+    const int64_t F = wsub(wmul(es, 65536), LSr);
+    const int64_t v = wadd(rshift(wmul(pile, e2r), 16 - (F >> 16)), b_j);
+    return epi == EPI_GAUGED_EDGE ? edge(v, PHI) : v;
+}
+
+struct BankIO {
+    int bi, epi;
+    bool heads;                  // the qkv bank: heads16 and the key/value append instead of stores
+    const int64_t* X;            // the bank's input [rows][nin]
+    const uint64_t* xor_in;      // its rows' OR of magnitudes
+    uint64_t* or_out;            // the next bank's OR slot (null: none)
+    int64_t* out;                // R (PLAIN_ADD) or HID (GAUGED_EDGE)
+    int ldo;
+};
+
+__device__ __noinline__ void bank_round(const MegaArgs& a, const BankIO& io, const Unit u, bool prefetched, int layer,
+                                        uint8_t* smem, Sh& s, Track& t, int ph) {
+    const MegaBank& bk = a.banks[io.bi];
+    const int EPI = io.epi;
+    const bool HEADS = io.heads;
+    const bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    const int64_t* X = io.X;
+    const uint64_t* xor_in = io.xor_in;
+    uint64_t* or_out = io.or_out;
+    int64_t* out = io.out;
+    const int ldo = io.ldo, bi = io.bi;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const uint32_t tmem = s.tmem;
     uint8_t* xplanes = smem + bk.kps * WST;
-    int64_t* P = (int64_t*)smem;                     // [BN][128] partial tile, over the planes once read
+    int64_t* P = (int64_t*)smem;
     const int kps = bk.kps, ks = bk.ks;
+    const int SR = slice_rows(ks);
+    const int n0 = u.kk * BN / ks, n1 = (u.kk + 1) * BN / ks;   // my slice of rows in the reduction
+    const int g0 = u.g * ks;                                     // my sub-group's first cluster rank
+    int64_t* RB = (int64_t*)(smem + RB_BASE);                    // [ks][SR][128]
+    int64_t* R12 = (int64_t*)(smem + r12_base(ks));              // [ks][BN][2]
+    // epilogue mapping: column m, rows n0 + ro, n0 + ro + 4, ...
+    const int m = tid & 127, ro = tid >> 7;
+    const int j = u.mt * 128 + m;
 
     if (u.on) {
         if (tid == 0 && !prefetched) issue_weights(a, bi, bk, u, smem, s, t);
+        uint64_t xo = 0;
+        if (tid < BN && tid < a.rows) xo = ldcgu(xor_in + tid);
         if (tid < BN) {
-            s.S1[tid] = 0;
-            s.S2[tid] = 0;
+            s.S12[tid][0] = 0;
+            s.S12[tid][1] = 0;
             s.rowc[tid] = 0;
+            #pragma unroll 1
             for (int w = 0; w < MAXKPS * 4; w++) s.sat[tid][w] = 0;
         }
         if (tid == 0) s.satrows = 0;
+        if (tid < BN) s.sh[tid] = to16_shift(xo);
         __syncthreads();
-        // ---- activations: to16 with the row's shift, the two byte planes, partial S1 / S2 / row correction ----
-        {
-            const int n = tid >> 2, cg = tid & 3;
-            const bool nv = n < a.rows;
-            const int sh = nv ? to16_shift(ldcgu(xor_in + n)) : 0;
-            if (cg == 0) s.sh[n] = sh;
-            int64_t S1 = 0, S2 = 0, rc = 0;
-            for (int kb = 0; kb < kps; kb++) {
-                const int k0 = (u.kk * kps + kb) * 128 + cg * 32;
-                uint32_t hw[8], lw[8];
-                uint32_t satw = 0;
-                int64_t s1 = 0;
-                int4 raw[16];
-                const int4* src = reinterpret_cast<const int4*>(X + (size_t)n * bk.nin + k0);
+        stamp(a, ph, 8);
+        // ---- activations: warp w takes rows w, w+16, w+32, w+48; lane l values 2l, 2l+1, 64+2l, 65+2l of each K
+        //      block, a row's 1 KB loaded coalesced by the whole warp; row sums by warp reduction (redux) ----
+#pragma unroll 1
+        for (int kb = 0; kb < kps; kb++) {
+            const int kx = (u.kk * kps + kb) * 128;
+            const uint32_t bh = saddr(xplanes + kb * XST), bl = bh + B_BYTES;
+            int4 ra[4], rb[4];
 #pragma unroll
-                for (int v = 0; v < 16; v++) raw[v] = nv ? __ldcg(src + v) : make_int4(0, 0, 0, 0);
+            for (int i = 0; i < 4; i++) {
+                const int n = warp + 16 * i;
+                const bool nv = n < a.rows;
+                const int4* src = reinterpret_cast<const int4*>(X + (size_t)n * bk.nin + kx);
+                ra[i] = nv ? __ldcg(src + lane) : make_int4(0, 0, 0, 0);
+                rb[i] = nv ? __ldcg(src + 32 + lane) : make_int4(0, 0, 0, 0);
+            }
 #pragma unroll
-                for (int v4 = 0; v4 < 8; v4++) {
-                    const int4 r0 = raw[2 * v4], r1 = raw[2 * v4 + 1];
-                    const int64_t xv[4] = {(int64_t)(((uint64_t)(uint32_t)r0.y << 32) | (uint32_t)r0.x),
-                                           (int64_t)(((uint64_t)(uint32_t)r0.w << 32) | (uint32_t)r0.z),
-                                           (int64_t)(((uint64_t)(uint32_t)r1.y << 32) | (uint32_t)r1.x),
-                                           (int64_t)(((uint64_t)(uint32_t)r1.w << 32) | (uint32_t)r1.z)};
-                    uint32_t h = 0, l = 0;
-#pragma unroll
-                    for (int q = 0; q < 4; q++) {
-                        const int32_t x = (int32_t)rshift(xv[q], sh);
-                        const bool sat = x == 32768;
-                        h |= (uint32_t)(uint8_t)(int8_t)(sat ? 127 : (x >> 8)) << (8 * q);
-                        l |= (uint32_t)(uint8_t)(int8_t)((x & 255) - 128) << (8 * q);
-                        s1 += x;
-                        S2 += (int64_t)x * x;
-                        satw |= (uint32_t)sat << (v4 * 4 + q);
-                    }
-                    hw[v4] = h;
-                    lw[v4] = l;
+            for (int i = 0; i < 4; i++) {
+                const int n = warp + 16 * i;
+                const int sh = s.sh[n];
+                const int32_t x0 = to16v(ra[i].x, ra[i].y, sh), x1 = to16v(ra[i].z, ra[i].w, sh);
+                const int32_t x2 = to16v(rb[i].x, rb[i].y, sh), x3 = to16v(rb[i].z, rb[i].w, sh);
+                const uint32_t o = (uint32_t)((2 * lane) & 15);
+                st_shared_u16(bh + sw128(n, lane >> 3) + o, hbyte(x0) | (hbyte(x1) << 8));
+                st_shared_u16(bh + sw128(n, 4 + (lane >> 3)) + o, hbyte(x2) | (hbyte(x3) << 8));
+                st_shared_u16(bl + sw128(n, lane >> 3) + o, lbyte(x0) | (lbyte(x1) << 8));
+                st_shared_u16(bl + sw128(n, 4 + (lane >> 3)) + o, lbyte(x2) | (lbyte(x3) << 8));
+                const int sat = (x0 == 32768) + (x1 == 32768) + (x2 == 32768) + (x3 == 32768);
+                if (sat) {                                         // rare: the +32768 list
+                    const int32_t xs[4] = {x0, x1, x2, x3};
+#pragma unroll 1
+                    for (int q = 0; q < 4; q++)
+                        if (xs[q] == 32768) {
+                            const int kk = q < 2 ? 2 * lane + q : 64 + 2 * lane + (q - 2);
+                            atomicOr(&s.sat[n][kb * 4 + (kk >> 5)], 1u << (kk & 31));
+                            atomicOr(&s.satrows, 1ull << n);
+                        }
                 }
-                S1 += s1;
-                rc += 128 * (s1 - 256 * (int64_t)__popc(satw));
-                s.sat[n][kb * 4 + cg] = satw;
-                if (satw) atomicOr(&s.satrows, 1ull << n);
-                const uint32_t bh = saddr(xplanes + kb * XST), bl = bh + B_BYTES;
-                st_shared_v4(bh + sw128(n, 2 * cg), hw[0], hw[1], hw[2], hw[3]);
-                st_shared_v4(bh + sw128(n, 2 * cg + 1), hw[4], hw[5], hw[6], hw[7]);
-                st_shared_v4(bl + sw128(n, 2 * cg), lw[0], lw[1], lw[2], lw[3]);
-                st_shared_v4(bl + sw128(n, 2 * cg + 1), lw[4], lw[5], lw[6], lw[7]);
+                // S1 (|sum| < 2^17 per lane), S2 as 16-bit halves (each lane's sum of 4 squares <= 2^32), +32768 count
+                const uint64_t sq = (uint64_t)((int64_t)x0 * x0) + (uint64_t)((int64_t)x1 * x1) +
+                                    (uint64_t)((int64_t)x2 * x2) + (uint64_t)((int64_t)x3 * x3);
+                const int32_t t1 = (int32_t)redux_add((uint32_t)(x0 + x1 + x2 + x3));
+                const uint32_t t2l = redux_add((uint32_t)(sq & 0xFFFF)), t2h = redux_add((uint32_t)(sq >> 16));
+                const uint32_t tc = redux_add((uint32_t)sat);
+                if (lane == 0) {                                    // one warp per row: no atomics
+                    const int64_t a1 = t1, a2 = (int64_t)t2h * 65536 + (int64_t)t2l;
+                    s.S12[n][0] += a1;
+                    s.S12[n][1] += a2;
+                    s.rowc[n] += 128 * (a1 - 256 * (int64_t)tc);
+                }
             }
-#pragma unroll
-            for (int o = 1; o < 4; o <<= 1) {        // the row's four threads are adjacent lanes
-                S1 += __shfl_xor_sync(0xffffffffu, S1, o);
-                S2 += __shfl_xor_sync(0xffffffffu, S2, o);
-                rc += __shfl_xor_sync(0xffffffffu, rc, o);
-            }
-            if (cg == 0) { s.S1[n] = S1; s.S2[n] = S2; s.rowc[n] = rc; }
+            if (kb == 0) stamp(a, ph, 10);
         }
+        stamp(a, ph, 11);
         fence_proxy_async();
         __syncthreads();
+        stamp(a, ph, 1);
         // ---- MMAs ----
         if (warp == 1 && lane == 0) {
             bool ok = true;
+            #pragma unroll 1
             for (int kb = 0; kb < kps; kb++) {
                 const uint32_t par = (t.wwait >> kb) & 1;
                 t.wwait ^= 1u << kb;
@@ -237,88 +323,101 @@ B2_DEV void bank_round(const MegaArgs& a, int bi, const MegaBank& bk, const Unit
             }
             tc_fence_after();
             if (ok)
+                #pragma unroll 1
                 for (int kb = 0; kb < kps; kb++)
                     mma_kblock2(saddr(smem + kb * WST), saddr(xplanes + kb * XST), tmem, kb == 0);
             mma_commit(&s.accbar);                   // arrives once the issued MMAs (if any) are done
         }
         __syncwarp();
+        if (tid == 0 && ks > 1) {                    // my incoming slices: (ks - 1) peers x (rows x 1 KB + rows x 16 B)
+            mbar_expect_tx(&s.rbar, (uint32_t)((ks - 1) * (n1 - n0) * (1024 + 16)));
+        }
         int64_t colc = 0;
         {
-            const int j = u.mt * 128 + (warp & 3) * 32 + lane;
-            for (int kb = 0; kb < kps; kb++) colc += __ldg(bk.colcorr_kb + (size_t)(u.kk * kps + kb) * bk.nout_pad + j);
+            const int jc = u.mt * 128 + (warp & 3) * 32 + lane;
+#pragma unroll 1
+            for (int kb = 0; kb < kps; kb++) colc += __ldg(bk.colcorr_kb + (size_t)(u.kk * kps + kb) * bk.nout_pad + jc);
         }
         // one decision for the whole CTA: the TMEM loads below are warp-aligned
         const bool ok = __syncthreads_and(mbar_wait(&s.accbar, t.acc & 1, a.err));
         t.acc++;
         tc_fence_after();
-        // ---- corrected partial piles -> P ----
+        stamp(a, ph, 2);
+        // ---- corrected partial piles -> P: warp w reads TMEM lane quadrant w % 4 (columns), rows 16 (w / 4) .. +16 ----
         {
-            const int m = (warp & 3) * 32 + lane, r0 = (warp >> 2) * 32;
-            int64_t p[32];
+            const int mm = (warp & 3) * 32 + lane, r0 = (warp >> 2) * 16;
+            int64_t p[16];
             if (ok) {
-                const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + r0;
-                int64_t t16[16];
-                tmem_piles16(trow, t16);
+                tmem_piles16(tmem + ((uint32_t)((warp & 3) * 32) << 16) + r0, p);
 #pragma unroll
-                for (int q = 0; q < 16; q++) p[q] = t16[q];
-                tmem_piles16(trow + 16, t16);
-#pragma unroll
-                for (int q = 0; q < 16; q++) p[16 + q] = t16[q];
-                const unsigned long long satrows = s.satrows;
-#pragma unroll
-                for (int q = 0; q < 32; q++) p[q] += colc + s.rowc[r0 + q];
-                if ((satrows >> r0) & 0xffffffffull)      // rare: rows of this warp with +32768 entries
-                    for (int q = 0; q < 32; q++) {
-                        const int n = r0 + q;
-                        if (!((satrows >> n) & 1)) continue;
-                        int64_t add = 0;
-                        for (int kb = 0; kb < kps; kb++)
-                            for (int w = 0; w < 4; w++) {
-                                uint32_t bits = s.sat[n][kb * 4 + w];
-                                while (bits) {
-                                    const int k = w * 32 + __ffs(bits) - 1;
-                                    bits &= bits - 1;
-                                    const uint8_t* A = smem + kb * WST;
-                                    const int off = (int)sw128(m, k >> 4) + (k & 15);
-                                    const int64_t wv = 256 * (int64_t)(int8_t)A[off] + (int64_t)(int8_t)A[A_BYTES + off] + 128;
-                                    add += 256 * wv;
-                                }
-                            }
-#pragma unroll
-                        for (int v = 0; v < 32; v++)
-                            if (v == q) p[v] += add;
-                    }
+                for (int q = 0; q < 16; q++) p[q] += colc + s.rowc[r0 + q];
             } else {
 #pragma unroll
-                for (int q = 0; q < 32; q++) p[q] = 0;
+                for (int q = 0; q < 16; q++) p[q] = 0;
             }
             tc_fence_before();
             __syncthreads();                         // every read of the planes and of TMEM is done
 #pragma unroll
-            for (int q = 0; q < 32; q++) P[(r0 + q) * 128 + m] = p[q];
+            for (int q = 0; q < 16; q++) P[(r0 + q) * 128 + mm] = p[q];
+            // rare: a row with +32768 entries in this K range gets 256 * w[k][j] for each (the bank's int16 weights)
+            const unsigned long long satrows = ok ? s.satrows : 0ull;
+            const int jj = u.mt * 128 + mm;
+            if (((satrows >> r0) & 0xffffull) && jj < bk.nout)
+#pragma unroll 1
+                for (int q = 0; q < 16; q++) {
+                    const int n = r0 + q;
+                    if (!((satrows >> n) & 1)) continue;
+                    int64_t add = 0;
+#pragma unroll 1
+                    for (int kb = 0; kb < kps; kb++)
+#pragma unroll 1
+                        for (int w = 0; w < 4; w++) {
+                            uint32_t bits = s.sat[n][kb * 4 + w];
+                            while (bits) {
+                                const int kk = w * 32 + __ffs(bits) - 1;
+                                bits &= bits - 1;
+                                const int i = (u.kk * kps + kb) * 128 + kk;
+                                add += 256 * (int64_t)__ldg(bk.w16 + (size_t)i * bk.nout + jj);
+                            }
+                        }
+                    P[n * 128 + mm] += add;
+                }
         }
+        fence_proxy_async();                         // P and S12 are read by the bulk copies below
     }
-    cluster_sync();                                  // the cluster's partial tiles and row sums are written
-    if (u.on) {
-        // ---- my slice of rows: sum over my sub-group's CTAs, finish ----
-        const int n0 = u.kk * BN / ks, n1 = (u.kk + 1) * BN / ks;
-        const int g0 = u.g * ks;
-        uint32_t peer[MEGA_CS];
-        {
-            const uint32_t pbase = saddr(P);
-#pragma unroll
-            for (int p = 0; p < MEGA_CS; p++) peer[p] = p < ks ? mapa(pbase, g0 + p) : 0;
+    cluster_sync();                                  // every P written; every CTA's weights and planes are dead
+    stamp(a, ph, 3);
+    if (u.on && ks > 1) {
+        if (tid == 0) {
+            const uint32_t rb_local = saddr(RB), r12_local = saddr(R12), bar_local = saddr(&s.rbar);
+            #pragma unroll 1
+            for (int p = 0; p < ks; p++) {
+                if (p == u.kk) continue;
+                const int p0 = p * BN / ks, p1 = (p + 1) * BN / ks;
+                const uint32_t rk = (uint32_t)(g0 + p);
+                const uint32_t dst = mapa(rb_local + (uint32_t)(u.kk * SR * 1024), rk);
+                const uint32_t d12 = mapa(r12_local + (uint32_t)((u.kk * BN + p0) * 16), rk);
+                const uint32_t bar = mapa(bar_local, rk);
+                bulk_s2c(dst, P + (size_t)p0 * 128, (uint32_t)((p1 - p0) * 1024), bar);
+                bulk_s2c(d12, &s.S12[p0][0], (uint32_t)((p1 - p0) * 16), bar);
+            }
         }
+        const bool got = mbar_wait(&s.rbar, t.rpar & 1, a.err);
+        (void)got;
+    }
+    if (u.on && ks > 1) t.rpar++;
+    cluster_sync();                                  // every slice arrived: every CTA's outgoing copies are done
+    stamp(a, ph, 12);
+    if (u.on) {
+        // ---- my slice of rows: the gauge's row terms, then sum the partial piles and finish ----
         if (tid < n1 - n0) {
             const int n = n0 + tid;
             int64_t LS = 0, e2 = 0;
             if (GAUGED && n < a.rows) {
-                const uint32_t o1 = saddr(&s.S1[n]), o2 = saddr(&s.S2[n]);
-                int64_t S1 = 0, S2 = 0;
-                for (int p = 0; p < ks; p++) {
-                    S1 += ld_dsmem(mapa(o1, g0 + p));
-                    S2 += ld_dsmem(mapa(o2, g0 + p));
-                }
+                int64_t S1 = s.S12[n][0], S2 = s.S12[n][1];
+                #pragma unroll 1
+                for (int p = 0; p < ks; p++)
+                    if (p != u.kk) { S1 += R12[(p * BN + n) * 2]; S2 += R12[(p * BN + n) * 2 + 1]; }
                 LS = gauge_LS(S1, S2, -16 + s.sh[n], a.LOG2, a.log768, a.eps40);
                 e2 = __ldg(a.EXP2 + (wsub(0, LS) & 0xFFFF));
             }
@@ -326,103 +425,71 @@ B2_DEV void bank_round(const MegaArgs& a, int bi, const MegaBank& bk, const Unit
             s.e2[n] = e2;
         }
         __syncthreads();
-        const int m = tid & 127, ro = tid >> 7;
-        const int j = u.mt * 128 + m;
+        stamp(a, ph, 13);
         const bool jv = j < bk.nout;
         const int64_t e_j = jv ? (int64_t)__ldg(bk.e + j) : 0, b_j = jv ? __ldg(bk.b + j) : 0;
-        const int nit = (n1 - n0 + 1) >> 1;
+        const int nit = (n1 - n0 + 3) >> 2;          // rows per thread (n0 + ro + 4 it)
         const int H = a.kv.H, dm = H * 64;
-        for (int it0 = 0; it0 < nit; it0 += 4) {
-            int64_t sums[4];
-            {
-                int64_t tt[4][MEGA_CS];
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int n = n0 + 2 * (it0 + q) + ro;
-                    const bool ld = jv && it0 + q < nit && n < n1 && n < a.rows;
-                    const uint32_t off = (uint32_t)(n * 128 + m) * 8;
-#pragma unroll
-                    for (int p = 0; p < MEGA_CS; p++) tt[q][p] = (ld && p < ks) ? ld_dsmem(peer[p] + off) : 0;
-                }
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    int64_t v = 0;
-#pragma unroll
-                    for (int p = 0; p < MEGA_CS; p++) v = wadd(v, tt[q][p]);
-                    sums[q] = v;
-                }
+#pragma unroll 1
+        for (int it = 0; it < nit; it++) {
+            const int n = n0 + 4 * it + ro;
+            const bool valid = jv && n < n1 && n < a.rows;
+            int64_t val = 0;
+            if (valid) {
+                val = P[(size_t)n * 128 + m];
+#pragma unroll 1
+                for (int p = 0; p < ks; p++)
+                    if (p != u.kk) val = wadd(val, RB[((size_t)p * SR + (n - n0)) * 128 + m]);
+                val = epi_rt(EPI, val, e_j, b_j, -16 + s.sh[n], s.LS[n], s.e2[n], a.PHI);
             }
-            int64_t vals[4];
-            bool valids[4];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-                const int n = n0 + 2 * (it0 + q) + ro;
-                valids[q] = jv && it0 + q < nit && n < n1 && n < a.rows;
-                vals[q] = valids[q] ? epi_value<EPI>(sums[q], e_j, b_j, -16 + s.sh[n], s.LS[n], s.e2[n], a.PHI) : 0;
-            }
+            if (it == 0) stamp(a, ph, 14);
             if (HEADS) {
                 // heads16: each 64-column half of the tile is one head part (q, k or v of one head); a row's OR over
-                // the part is the OR over its two warps
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const uint64_t w = warp_or64(valids[q] ? mag(vals[q]) : 0);
-                    if (lane == 0) s.hor[warp][q] = w;
-                }
+                // the part is the OR over its two warps (w, w ^ 1)
+                const uint64_t w = warp_or64(valid ? mag(val) : 0);
+                if (lane == 0) s.hor[warp][it & 1] = w;
                 __syncthreads();
-                uint64_t por[4];
-#pragma unroll
-                for (int q = 0; q < 4; q++) por[q] = s.hor[warp][q] | s.hor[warp ^ 1][q];
-                __syncthreads();
+                const uint64_t por = s.hor[warp][it & 1] | s.hor[warp ^ 1][it & 1];
                 const int part = 2 * u.mt + (m >> 6), kind = part / H, hh = part % H, dd = m & 63;
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int n = n0 + 2 * (it0 + q) + ro;
-                    const bool valid = valids[q];
-                    const int64_t val = vals[q];
-                    const int sh = to16_shift(por[q]);
-                    const int32_t x = (int32_t)rshift(val, sh);
-                    if (kind == 0) {
-                        if (valid) {
-                            a.q16[(size_t)n * dm + hh * 64 + dd] = x;
-                            if (dd == 0) a.qexp[n * H + hh] = -16 + sh;
+                const int sh = to16_shift(por);
+                const int32_t x = (int32_t)rshift(val, sh);
+                if (kind == 0) {
+                    if (valid) {
+                        a.q16[(size_t)n * dm + hh * 64 + dd] = x;
+                        if (dd == 0) a.qexp[n * H + hh] = -16 + sh;
+                    }
+                } else {
+                    const int pos = valid ? s.pos[n] : 0;
+                    const bool pv = valid && pos >= 0 && pos < a.kv.lim;
+                    if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
+                    const size_t idx = pv ? kv_index(s.slot[n], layer, hh, pos, a.kv.L, H, a.kv.ctx) : 0;
+                    if (kind == 1) {
+                        const uint32_t sat = __ballot_sync(0xffffffffu, pv && x == 32768);
+                        if (pv) {
+                            a.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
+                            if (lane == 0) reinterpret_cast<uint32_t*>(&a.kv.kmask[idx])[dd >> 5] = sat;
+                            if (dd == 0) a.kv.kexp[idx] = -16 + sh;
                         }
-                    } else {
-                        const int pos = valid ? ldcg_i32(a.row_pos + n) : 0;
-                        const bool pv = valid && pos >= 0 && pos < a.kv.lim;
-                        if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
-                        const size_t idx = pv ? kv_index(ldcg_i32(a.row_slot + n), layer, hh, pos, a.kv.L, H, a.kv.ctx) : 0;
-                        if (kind == 1) {
-                            const uint32_t sat = __ballot_sync(0xffffffffu, pv && x == 32768);
-                            if (pv) {
-                                a.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
-                                if (lane == 0) reinterpret_cast<uint32_t*>(&a.kv.kmask[idx])[dd >> 5] = sat;
-                                if (dd == 0) a.kv.kexp[idx] = -16 + sh;
-                            }
-                        } else if (pv) {
-                            if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
-                            a.kv.v[idx * 64 + dd] = (int32_t)val;
-                        }
+                    } else if (pv) {
+                        if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
+                        a.kv.v[idx * 64 + dd] = (int32_t)val;
                     }
                 }
             } else {
-#pragma unroll
-                for (int q = 0; q < 4; q++) {
-                    const int n = n0 + 2 * (it0 + q) + ro;
-                    const bool valid = valids[q];
-                    int64_t o = vals[q];
-                    if (valid) {
-                        int64_t* dst = out + (size_t)n * ldo + j;
-                        if (EPI == EPI_PLAIN_ADD) o = wadd(ldcg(dst), o);
-                        *dst = o;
-                    }
-                    const uint64_t wor = warp_or64(valid ? mag(o) : 0);
-                    if (lane == 0 && or_out && valid) atomicOr((unsigned long long*)&or_out[n], (unsigned long long)wor);
+                int64_t o = val;
+                if (valid) {
+                    if (EPI == EPI_PLAIN_ADD) o = wadd(ldcg(out + (size_t)n * ldo + j), o);
+                    out[(size_t)n * ldo + j] = o;
                 }
+                const uint64_t wor = warp_or64(valid ? mag(o) : 0);
+                if (lane == 0 && or_out && valid) atomicOr((unsigned long long*)&or_out[n], (unsigned long long)wor);
             }
         }
         if (HEADS) fence_async_global();             // the key/value append is read by bulk copies next phase
     }
-    cluster_sync();                                  // no CTA reuses its shared memory while a peer may read it
+    stamp(a, ph, 4);
+    __syncthreads();
+    stamp(a, ph, 5);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -431,11 +498,11 @@ B2_DEV void bank_round(const MegaArgs& a, int bi, const MegaBank& bk, const Unit
 // ---------------------------------------------------------------------------------------------------------------------
 B2_DEV void att_issue(const MegaArgs& a, int layer, int unit, int slot, uint8_t* smem, Sh& s, Track& t) {
     const int r = unit / a.H, h = unit % a.H;
-    const int p = ldcg_i32(a.row_pos + r);
+    const int p = s.pos[r];
     if (p < 0 || p >= a.kv.lim || is_dead(a.err)) return;
     const int nkr = (p + 1 + 3) & ~3;
     uint8_t* base_s = smem + ATT_BASE + (size_t)slot * s.slot_bytes;
-    const size_t base = kv_index(ldcg_i32(a.row_slot + r), layer, h, 0, a.kv.L, a.kv.H, a.kv.ctx);
+    const size_t base = kv_index(s.slot[r], layer, h, 0, a.kv.L, a.kv.H, a.kv.ctx);
     fence_async_global();
     mbar_expect_tx(&s.abar[slot], (uint32_t)nkr * (128 + 256 + 8 + 4));
     t.aarm[slot]++;
@@ -445,33 +512,43 @@ B2_DEV void att_issue(const MegaArgs& a, int layer, int unit, int slot, uint8_t*
     bulk_g2s(base_s + (size_t)nkr * 392, a.kv.kexp + base, (uint32_t)nkr * 4, &s.abar[slot]);
 }
 
-B2_DEV void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* smem, Sh& s, Track& t) {
+__device__ __noinline__ void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* smem, Sh& s, Track& t, int ph) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int grp = wid >> 3, gt = tid & 255, gw = wid & 7;    // two groups of 8 warps work on different units
     const int G = gridDim.x, cid = blockIdx.x;
     const int nunits = a.rows * a.H;
     const int my = cid < nunits ? (nunits - cid + G - 1) / G : 0;
     if (!my) return;
-    // slots sized for the longest run among my units
+    // slots sized for the longest run among my units; each group gets half of them
     if (tid == 0) {
         int nk = 1;
-        for (int i = 0; i < my; i++) {
-            const int p = ldcg_i32(a.row_pos + (cid + i * G) / a.H);
-            nk = max(nk, min(max(p + 1, 1), a.kv.lim));
-        }
+#pragma unroll 1
+        for (int i = 0; i < my; i++) nk = max(nk, min(s.pos[(cid + i * G) / a.H] + 1, a.kv.lim));
         const int bytes = (((nk + 3) & ~3) * KEY_BYTES + 127) & ~127;
-        int ns = (DYN - ATT_BASE) / bytes;
-        ns = min(ns, min(MAX_SLOTS, my));
         s.slot_bytes = bytes;
-        s.nslots = max(ns, 1);
-        for (int i = 0; i < s.nslots; i++) att_issue(a, layer, cid + i * G, i, smem, s, t);
+        s.nslots = max(1, min((DYN - ATT_BASE) / bytes, MAX_SLOTS));
     }
     __syncthreads();
     const int NS = s.nslots;
+    const bool two = NS >= 2 && my >= 2;            // both groups at work
+    const int nsg = two ? NS / 2 : NS;              // slots per group
+    const int myg = two ? (my - grp + 1) / 2 : (grp == 0 ? my : 0);   // my group's units: i = grp + 2k (or all)
+    const int step = two ? 2 : 1;
+    if (!myg) return;                               // (group 1 when one slot is all that fits)
+    const int bar_id = 1 + grp;
+    if (gt == 0) {
+#pragma unroll 1
+        for (int k2 = 0; k2 < min(nsg, myg); k2++)
+            att_issue(a, layer, cid + (grp + step * k2) * G, grp + (two ? 2 * k2 : k2), smem, s, t);
+    }
     const int d = a.H * 64;
-    for (int i = 0; i < my; i++) {
-        const int unit = cid + i * G, slot = i % NS;
+    int64_t (*red)[66] = s.red[grp];
+#pragma unroll 1
+    for (int k2 = 0; k2 < myg; k2++) {
+        const int unit = cid + (grp + step * k2) * G;
+        const int slot = grp + (two ? 2 * (k2 % nsg) : (k2 % nsg));
         const int r = unit / a.H, h = unit % a.H;
-        const int p = ldcg_i32(a.row_pos + r);
+        const int p = s.pos[r];
         const bool pv = p >= 0 && p < a.kv.lim;
         const int nk = p + 1, nkr = (nk + 3) & ~3;
         uint8_t* sb = smem + ATT_BASE + (size_t)slot * s.slot_bytes;
@@ -481,7 +558,7 @@ B2_DEV void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* s
         int32_t* KEs = reinterpret_cast<int32_t*>(sb + (size_t)nkr * 392);
         int64_t* SCs = reinterpret_cast<int64_t*>(sb + (size_t)nkr * 396);
         int32_t* AVs = reinterpret_cast<int32_t*>(sb + (size_t)nkr * 404);
-        if (tid < 64) s.qs[slot][tid] = pv ? __ldcg(a.q16 + (size_t)r * d + h * 64 + tid) : 0;
+        if (gt < 64) s.qs[slot][gt] = pv ? __ldcg(a.q16 + (size_t)r * d + h * 64 + gt) : 0;
         const int64_t eq = pv ? __ldcg(a.qexp + r * a.H + h) : 0;
         bool ok = pv;
         if (pv) {
@@ -489,14 +566,16 @@ B2_DEV void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* s
             t.await_ ^= 1u << slot;
             ok = mbar_wait(&s.abar[slot], par, a.err);
         }
-        ok = __syncthreads_and(ok);                  // one decision for the CTA: the block below synchronises
+        ok = group_and(bar_id, 256, ok);            // one decision for the group: the block below synchronises
+        if (k2 == 0 && grp == 0) stamp(a, ph, 1);
         if (ok) {
             // pass 1: scores, 8 lanes per key
             int qr[8];
 #pragma unroll
             for (int q = 0; q < 8; q++) qr[q] = s.qs[slot][(lane & 7) * 8 + q];
             int64_t lmax = INT64_MIN;
-            for (int c = wid; c * 4 < nk; c += 8) {
+#pragma unroll 1
+            for (int c = gw; c * 4 < nk; c += 8) {
                 const int key = c * 4 + (lane >> 3);
                 int64_t part = 0;
                 if (key < nk) {
@@ -517,37 +596,39 @@ B2_DEV void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* s
                 }
             }
             lmax = warp_max64(lmax);
-            if (lane == 0) s.red[wid][65] = lmax;
-            __syncthreads();
-            int64_t start = s.red[0][65];
+            if (lane == 0) red[gw][65] = lmax;
+            group_sync(bar_id, 256);
+            int64_t start = red[0][65];
 #pragma unroll
-            for (int k = 1; k < 8; k++) start = s.red[k][65] > start ? s.red[k][65] : start;
+            for (int q = 1; q < 8; q++) start = red[q][65] > start ? red[q][65] : start;
             // pass 1b: arrival weights and their total
             int64_t z = 0;
-            for (int q = tid; q < nk; q += NT) {
+#pragma unroll 1
+            for (int q = gt; q < nk; q += 256) {
                 const int64_t av = arrival(wsub(start, SCs[q]), a.ARR, a.alen, a.err);
                 AVs[q] = (int32_t)av;
                 z = wadd(z, av);
             }
             z = warp_sum64(z);
-            __syncthreads();
-            if (lane == 0) s.red[wid][64] = z;
+            group_sync(bar_id, 256);
+            if (lane == 0) red[gw][64] = z;
             // pass 2: 2 dims per lane, warps split the keys
             int64_t n0 = 0, n1 = 0;
-            for (int q = wid; q < nk; q += 8) {
+#pragma unroll 1
+            for (int q = gw; q < nk; q += 8) {
                 const int64_t av = AVs[q];
                 if (!av) continue;
                 const int2 vv = reinterpret_cast<const int2*>(Vs + (size_t)q * 64)[lane];
                 n0 = wadd(n0, wmul(av, vv.x));
                 n1 = wadd(n1, wmul(av, vv.y));
             }
-            s.red[wid][2 * lane] = n0;
-            s.red[wid][2 * lane + 1] = n1;
-            __syncthreads();
-            if (wid == 0) {
+            red[gw][2 * lane] = n0;
+            red[gw][2 * lane + 1] = n1;
+            group_sync(bar_id, 256);
+            if (gw == 0) {
                 int64_t t0 = 0, t1 = 0, zz = 0;
 #pragma unroll
-                for (int k = 0; k < 8; k++) { t0 = wadd(t0, s.red[k][2 * lane]); t1 = wadd(t1, s.red[k][2 * lane + 1]); zz = wadd(zz, s.red[k][64]); }
+                for (int q = 0; q < 8; q++) { t0 = wadd(t0, red[q][2 * lane]); t1 = wadd(t1, red[q][2 * lane + 1]); zz = wadd(zz, red[q][64]); }
                 const int64_t F = -log2fix(zz, a.LOG2);
                 const int64_t v0 = power(t0, F, a.EXP2), v1 = power(t1, F, a.EXP2);
                 int64_t* o = a.ATT + (size_t)r * d + h * 64;
@@ -557,16 +638,17 @@ B2_DEV void att_phase(const MegaArgs& a, int layer, uint64_t* or_out, uint8_t* s
                 if (lane == 0) atomicOr((unsigned long long*)&or_out[r], (unsigned long long)w);
             }
         }
-        __syncthreads();                             // the slot and s.red are free again
-        if (tid == 0 && i + NS < my) att_issue(a, layer, cid + (i + NS) * G, slot, smem, s, t);
+        group_sync(bar_id, 256);                     // the slot and red are free again
+        if (k2 == 0 && grp == 0) stamp(a, ph, 2);
+        if (gt == 0 && k2 + nsg < myg) att_issue(a, layer, cid + (grp + step * (k2 + nsg)) * G, slot, smem, s, t);
     }
 }
 
 // the embed phase: rows' position and word, R = wte + wpe, OR slot 0; the other OR slots cleared
-B2_DEV void embed_phase(const MegaArgs& a) {
+__device__ __noinline__ void embed_phase(const MegaArgs& a) {
     const int tid = threadIdx.x, G = gridDim.x, cid = blockIdx.x;
     const int d = a.d;
-    __shared__ uint64_t s_or[8];
+    __shared__ uint64_t s_or[NT / 32];
     for (int i = cid * NT + tid; i < 4 * a.L * BN; i += G * NT)
         if (i >= BN) a.OR[i] = 0;
     for (int r = cid; r < a.rows; r += G) {
@@ -586,7 +668,7 @@ B2_DEV void embed_phase(const MegaArgs& a) {
         __syncthreads();
         if (tid == 0) {
             uint64_t all = 0;
-            for (int k = 0; k < 8; k++) all |= s_or[k];
+            for (int k = 0; k < NT / 32; k++) all |= s_or[k];
             a.OR[r] = all;
         }
         __syncthreads();
@@ -604,6 +686,7 @@ __global__ void __launch_bounds__(NT, 1) k_decode_mega(const MegaArgs a) {
         for (int k = 0; k < MAXKPS; k++) mbar_init(&s.wbar[k], 1);
         mbar_init(&s.accbar, 1);
         for (int k = 0; k < MAX_SLOTS; k++) mbar_init(&s.abar[k], 1);
+        mbar_init(&s.rbar, 1);
         fence_mbar_init();
     }
     if (warp == 0) tmem_alloc(&s.tmem, 256);
@@ -614,13 +697,27 @@ __global__ void __launch_bounds__(NT, 1) k_decode_mega(const MegaArgs a) {
     const int L = a.L;
     uint32_t nbar = 0;
     const uint32_t G = gridDim.x;
+    int ph = 0;
+    stamp(a, 0, 0);
+#define SYNC()                                  \
+    do {                                        \
+        stamp(a, ph, 6);                        \
+        grid_sync(a.bar, ++nbar * G, a.err);    \
+        ph++;                                   \
+        stamp(a, ph, 0);                        \
+    } while (0)
     // layer 0's qkv weights while the rows are embedded
     {
         const MegaBank& b0 = a.banks[0];
         if (tid == 0) issue_weights(a, 0, b0, unit_of(b0, cluster, crank, 0, ncl), smem, s, t);
     }
     embed_phase(a);
-    grid_sync(a.bar, ++nbar * G, a.err);
+    SYNC();
+    if (tid < BN) {
+        s.pos[tid] = tid < a.rows ? ldcg_i32(a.row_pos + tid) : 0;
+        s.slot[tid] = tid < a.rows ? ldcg_i32(a.row_slot + tid) : 0;
+    }
+    __syncthreads();
     for (int l = 0; l < L; l++) {
         const int bq = 4 * l, bp = bq + 1, bf = bq + 2, bm = bq + 3;
         uint64_t* OR = a.OR;
@@ -629,61 +726,64 @@ __global__ void __launch_bounds__(NT, 1) k_decode_mega(const MegaArgs a) {
             const MegaBank& bk = a.banks[bq];
             const int nr = rounds_of(bk, ncl);
             for (int rd = 0; rd < nr; rd++)
-                bank_round<EPI_GAUGED, true>(a, bq, bk, unit_of(bk, cluster, crank, rd, ncl), rd == 0, a.R,
-                                             OR + (size_t)bq * BN, nullptr, nullptr, 0, l, smem, s, t);
+                bank_round(a, BankIO{bq, EPI_GAUGED, true, a.R, OR + (size_t)bq * BN, nullptr, nullptr, 0},
+                           unit_of(bk, cluster, crank, rd, ncl), rd == 0, l, smem, s, t, ph);
             // proj's weights (a 1-block bank, below the arrival's buffers) fly during the arrival
             const MegaBank& nb = a.banks[bp];
             if (tid == 0) issue_weights(a, bp, nb, unit_of(nb, cluster, crank, 0, ncl), smem, s, t);
         }
-        grid_sync(a.bar, ++nbar * G, a.err);
+        SYNC();
         // ---- the arrival ----
-        att_phase(a, l, OR + (size_t)bp * BN, smem, s, t);
-        grid_sync(a.bar, ++nbar * G, a.err);
+        att_phase(a, l, OR + (size_t)bp * BN, smem, s, t, ph);
+        SYNC();
         // ---- proj ----
         {
             const MegaBank& bk = a.banks[bp];
             const int nr = rounds_of(bk, ncl);
             for (int rd = 0; rd < nr; rd++)
-                bank_round<EPI_PLAIN_ADD, false>(a, bp, bk, unit_of(bk, cluster, crank, rd, ncl), rd == 0, a.ATT,
-                                                 OR + (size_t)bp * BN, OR + (size_t)bf * BN, a.R, a.d, l, smem, s, t);
+                bank_round(a, BankIO{bp, EPI_PLAIN_ADD, false, a.ATT, OR + (size_t)bp * BN, OR + (size_t)bf * BN, a.R, a.d},
+                           unit_of(bk, cluster, crank, rd, ncl), rd == 0, l, smem, s, t, ph);
             const MegaBank& nb = a.banks[bf];
             if (tid == 0) issue_weights(a, bf, nb, unit_of(nb, cluster, crank, 0, ncl), smem, s, t);
         }
-        grid_sync(a.bar, ++nbar * G, a.err);
+        SYNC();
         // ---- fc + bend ----
         {
             const MegaBank& bk = a.banks[bf];
             const int nr = rounds_of(bk, ncl);
             for (int rd = 0; rd < nr; rd++)
-                bank_round<EPI_GAUGED_EDGE, false>(a, bf, bk, unit_of(bk, cluster, crank, rd, ncl), rd == 0, a.R,
-                                                   OR + (size_t)bf * BN, OR + (size_t)bm * BN, a.HID, a.F, l, smem, s, t);
+                bank_round(a, BankIO{bf, EPI_GAUGED_EDGE, false, a.R, OR + (size_t)bf * BN, OR + (size_t)bm * BN, a.HID, a.F},
+                           unit_of(bk, cluster, crank, rd, ncl), rd == 0, l, smem, s, t, ph);
             const MegaBank& nb = a.banks[bm];
             if (tid == 0) issue_weights(a, bm, nb, unit_of(nb, cluster, crank, 0, ncl), smem, s, t);
         }
-        grid_sync(a.bar, ++nbar * G, a.err);
+        SYNC();
         // ---- mproj ----
         {
             const MegaBank& bk = a.banks[bm];
             const int nr = rounds_of(bk, ncl);
             uint64_t* nxt = l + 1 < L ? OR + (size_t)(bm + 1) * BN : nullptr;
             for (int rd = 0; rd < nr; rd++)
-                bank_round<EPI_PLAIN_ADD, false>(a, bm, bk, unit_of(bk, cluster, crank, rd, ncl), rd == 0, a.HID,
-                                                 OR + (size_t)bm * BN, nxt, a.R, a.d, l, smem, s, t);
+                bank_round(a, BankIO{bm, EPI_PLAIN_ADD, false, a.HID, OR + (size_t)bm * BN, nxt, a.R, a.d},
+                           unit_of(bk, cluster, crank, rd, ncl), rd == 0, l, smem, s, t, ph);
             if (l + 1 < L) {
                 const MegaBank& nb = a.banks[bm + 1];
                 if (tid == 0) issue_weights(a, bm + 1, nb, unit_of(nb, cluster, crank, 0, ncl), smem, s, t);
-                grid_sync(a.bar, ++nbar * G, a.err);
+                SYNC();
             }
         }
     }
+#undef SYNC
+    stamp(a, ph, 6);
     // drain anything still in flight (only after a timeout can there be any), then free TMEM
-    if (tid == 0) {
+    if (tid == 0)
         for (int k = 0; k < MAXKPS; k++)
             if (t.warm[k]) mbar_drain(&s.wbar[k], (t.warm[k] - 1) & 1);
+    if (tid == 0 || tid == 256)                      // each warp group's leader armed its own arrival slots
         for (int k = 0; k < MAX_SLOTS; k++)
             if (t.aarm[k]) mbar_drain(&s.abar[k], (t.aarm[k] - 1) & 1);
-    }
     if (tid == 32 && t.acc) mbar_drain(&s.accbar, (t.acc - 1) & 1);
+    if (tid == 64 && t.rpar) mbar_drain(&s.rbar, (t.rpar - 1) & 1);
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(s.tmem, 256);
@@ -728,6 +828,7 @@ int mega_plan(MegaPlan& p, const TcBank* tc, const int32_t* const* e, const int6
         m.e = e[i];
         m.b = b[i];
         m.colcorr_kb = t.colcorr_kb;
+        m.w16 = t.w16;
         m.nin = t.nin;
         m.nout = t.nout;
         m.nout_pad = t.nout_pad;

@@ -16,6 +16,7 @@ struct MegaBank {
     const int32_t* e;
     const int64_t* b;
     const int64_t* colcorr_kb;   // [nin / 128][nout_pad]
+    const int16_t* w16;          // [nin][nout] the bank as converted (the rare +32768 correction)
     int nin, nout, nout_pad, ntiles;
     int tpc, ks, kps;
 };
@@ -52,7 +53,11 @@ struct MegaArgs {
     int att_slot_bytes, att_slots;   // the arrival's per-(row, head) shared-memory buffers
     uint32_t* bar;                   // grid barrier counter, zero at launch
     uint32_t* err;
+    uint64_t* trace;                 // optional: %globaltimer stamps [CTA][phase][MEGA_STAMPS] (a profiling aid)
 };
+
+constexpr int MEGA_STAMPS = 16;
+constexpr int MEGA_MAX_PHASES = 64;
 
 struct MegaPlan {
     int ready = 0;
