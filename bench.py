@@ -8,7 +8,12 @@ Workload (per GPU): GPT-2 124M base2 (seeded random-init weights, converted exac
 key/value store growing 33 -> 160 positions; the timed loop runs those 127 steps as a cycle, rewinding the streams
 to their prompt (b2_rewind, part of the timed work) after each cycle, so any --steps replays C2 exactly.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config c2|c4|c5]
+
+--config c4 (the prompt pass, 32 x 512-id prompts, seed 3; a step = one whole prompt pass; roofline = the bank
+products' int8 tensor operations against twice the measured dense bf16 rate) and --config c5 (Pythia-160M decode,
+512 streams of 64-id prompts, seed 4, 128 words; a step = one decode step of all 512 streams) measure the other two
+workloads the same way; the driver's default is C2.
 
 value = 64 * N * K / (max over ranks of the CUDA-event time of the K steps). Weights (247 MB) exceed L2 (126 MB)
 and are streamed every step, so no L2 flush is needed between steps. e2e = the same K steps through b2_step_host
@@ -315,6 +320,182 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+
+# ---------------------------------------------------------------------------------------------------------------------
+# C4: the prompt pass (int8 tensor-pipe bound) and C5: Pythia-160M decode at 512 streams
+# ---------------------------------------------------------------------------------------------------------------------
+C4_B, C4_P, C4_SEED = 32, 512, 3
+C4_MACS_PER_ROW = 84_934_656            # int16 multiply-adds of the 48 layer banks per position
+C5_B, C5_P, C5_WORDS, C5_SEED, C5_V = 512, 64, 128, 4, 50304
+C5_WEIGHT_BYTES = 247_136_256
+
+
+def _dist(local_rank, world):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+    return dist
+
+
+def run_c4(args):
+    import numpy as np
+    import torch
+
+    rank, world, local_rank = env_rank()
+    torch.cuda.set_device(local_rank)
+    dist = _dist(local_rank, world)
+    from streaming_machine_b200 import convert, engine
+    from streaming_machine_b200.shard import max_over_ranks, stream_ids
+    M = convert.load_gpt2(0)
+    eng = engine.Engine(M, device=local_rank, n_streams=C4_B, max_ctx=C4_P)
+    ids = stream_ids(C4_SEED, C4_B, C4_P, rank, world, V)
+    ids_t = torch.as_tensor(ids.astype(np.int32).ravel(), device="cuda")
+    lens_t = torch.full((C4_B,), C4_P, dtype=torch.int32, device="cuda")
+    nxt = torch.empty(C4_B, dtype=torch.int32, device="cuda")
+
+    def one():
+        eng._call("b2_prefill", eng.h, ids_t.data_ptr(), lens_t.data_ptr(), C4_B, nxt.data_ptr(), None, eng._stream())
+
+    for _ in range(max(args.warmup, 1)):
+        one()
+    torch.cuda.synchronize()
+    eng.profile(False)
+    if dist:
+        dist.barrier(device_ids=[local_rank])
+    clk_proc, clk_path = clocks_start(local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        one()
+    ev1.record()
+    ev1.synchronize()
+    clocks = clocks_stop(clk_proc, clk_path)
+    launches, _ = eng.profile_read()
+    t_ms = max_over_ranks(ev0.elapsed_time(ev1), dist, device="cuda")
+    tokens = C4_B * C4_P * world * args.steps
+    value = tokens / (t_ms / 1000.0)
+    # end to end: host ids in, the next words back (Engine.prefill)
+    e0 = time.perf_counter()
+    for _ in range(args.steps):
+        eng.prefill(ids)
+    e2e_s = max_over_ranks(time.perf_counter() - e0, dist, device="cuda")
+    # per-class event time of one pass: the bank products' share
+    eng.profile(True)
+    one()
+    _, by = eng.profile_read()
+    eng.profile(False)
+    bank_ms = by["bank"][1]
+    ops = C4_B * C4_P * C4_MACS_PER_ROW * 4 * 2 + C4_B * 768 * V * 4 * 2      # int8 ops: 4 per int16 MAC, x2
+    with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+        pk = json.load(f)
+    peak = 2.0 * float(pk["bf16_tflops"])
+    achieved = ops / (bank_ms / 1000.0) / 1e12
+    line = {"metric": "prompt-pass tokens/sec/GPU (C4, bit-exact vs base2.py); % int8 tensor roofline",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": {"workload": "C4: GPT-2 124M base2 prompt pass, 32 streams x 512 ids per GPU (seed 3)",
+                       "l2": "no flush: each pass streams 2 x 247 MB of weight planes and ~1 GB of activations"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak, "unit": "TOPS (int8)",
+                         "frac": round(achieved / peak, 4), "traffic": None,
+                         "kernel": "bank products (k_bank_tiles), int8 ops per pass / their summed event time",
+                         "peak_kind": "2 x measured dense bf16 (int8 tensor rate is twice bf16's)",
+                         "bank_ms_per_pass": round(bank_ms, 3)},
+            "e2e": {"value": round(tokens / e2e_s, 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 4 * C4_B * C4_P, "d2h_bytes_per_step": 4 * C4_B},
+            "clocks": clocks, "gpu_launches": int(launches),
+            "kernel_ms_per_step": {k: round(v[1], 4) for k, v in by.items()}}
+    if rank == 0 and world == 1 and not args.no_cpu:
+        from oracle.oracle import Oracle
+        orc = Oracle(M)
+        n = 96
+        t0 = time.perf_counter()
+        orc.scores(ids[0][:n], n - 1, n)
+        dt = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": round(n / dt, 3), "unit": "tokens/s", "cores": os.cpu_count() or 1,
+                                "kind": "port", "sample": f"stream 0's first {n} prompt positions through the machine "
+                                                          "(teacher-forced, banks split over all threads)"}
+    eng.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def run_c5(args):
+    import numpy as np
+    import torch
+
+    rank, world, local_rank = env_rank()
+    torch.cuda.set_device(local_rank)
+    dist = _dist(local_rank, world)
+    from streaming_machine_b200 import convert, engine
+    from streaming_machine_b200.shard import max_over_ranks, stream_ids
+    PM = convert.load_pythia(0)
+    eng = engine.Engine(PM, device=local_rank, n_streams=C5_B, max_ctx=C5_P + C5_WORDS)
+    ids = stream_ids(C5_SEED, C5_B, C5_P, rank, world, C5_V)
+    cycle = C5_WORDS - 1
+    lens = torch.full((C5_B,), C5_P, dtype=torch.int32, device="cuda")
+    buf = torch.empty(C5_B * cycle, dtype=torch.int32, device="cuda")
+    first_t = torch.as_tensor(eng.prefill(ids), device="cuda")
+    pos = [0]
+
+    def steps(n):
+        while n > 0:
+            seg = min(n, cycle - pos[0])
+            eng.generate_device(C5_B, seg, buf[:C5_B * seg].view(C5_B, seg))
+            pos[0] += seg
+            n -= seg
+            if pos[0] == cycle:
+                eng.rewind(lens, first_t)
+                pos[0] = 0
+
+    steps(args.warmup)
+    torch.cuda.synchronize()
+    eng.profile(False)
+    if dist:
+        dist.barrier(device_ids=[local_rank])
+    clk_proc, clk_path = clocks_start(local_rank)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    steps(args.steps)
+    ev1.record()
+    ev1.synchronize()
+    clocks = clocks_stop(clk_proc, clk_path)
+    launches, _ = eng.profile_read()
+    t_ms = max_over_ranks(ev0.elapsed_time(ev1), dist, device="cuda")
+    value = C5_B * world * args.steps / (t_ms / 1000.0)
+    eng.prefill(ids)
+    pos[0] = 0
+    eng.profile(True)
+    eng.generate_device(C5_B, cycle, buf.view(C5_B, cycle))
+    _, by = eng.profile_read()
+    eng.profile(False)
+    bank_gbs = C5_WEIGHT_BYTES * cycle / (by["bank"][1] / 1000.0) / 1e9
+    peak, peak_kind = peaks()
+    line = {"metric": "Pythia-160M greedy tokens/sec/GPU (C5, bit-exact vs pythia_base2.py); % HBM roofline",
+            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int64", "data": "synthetic",
+            "config": {"workload": "C5: Pythia-160M base2 greedy decode, 512 streams per GPU, 64-id prompts (seed 4), "
+                                   "128 words (127 decode steps, store 65->192 positions)",
+                       "l2": "no flush: 247 MB of weights streamed per step exceed the 126 MB L2"},
+            "roofline": {"bound": "hbm", "achieved": round(bank_gbs, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(bank_gbs / peak, 4), "traffic": None,
+                         "kernel": "bank products, weight bytes per step / their summed event time",
+                         "peak_kind": peak_kind},
+            "clocks": clocks, "gpu_launches": int(launches),
+            "kernel_ms_per_step": {k: round(v[1] / cycle, 4) for k, v in by.items()}}
+    eng.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -322,11 +503,17 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--config", choices=("c2", "c4", "c5"), default="c2",
+                    help="c2 (default): the metric's batch-64 decode; c4: the prompt pass; c5: Pythia-160M decode")
     ap.add_argument("--quick", action="store_true",
                     help="profiling aid: prompt pass, --warmup and --steps decode steps, no other pass")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+    elif args.config == "c4":
+        run_c4(args)
+    elif args.config == "c5":
+        run_c5(args)
     else:
         run_ours(args)
 

@@ -79,6 +79,8 @@ struct b2_handle {
     TcRows tcr{};
     int32_t *head_rows = nullptr, *race_out = nullptr;
     uint64_t* row_or = nullptr;  // decode: per bank input, the OR of |x| over each row ([4L][FUSED_ROWS])
+    PrefillBlock* pf_blocks = nullptr;   // prompt pass: blocks of consecutive positions of one stream [max_rows]
+    int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
     int use_mega = 0;            // decode steps of <= 64 streams as one persistent kernel (B2_MEGA=1)
@@ -115,6 +117,7 @@ namespace {
 
 constexpr int FUSED_ROWS = 64;
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
+constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
 
 int fail(b2_handle* h, int code, const char* fmt, ...) {
     char buf[512];
@@ -297,12 +300,24 @@ int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows
                   gauge, h->LOG2, h->log768, h->eps40, pl);
 }
 
-// the arrival for `rows` rows at layer l: bulk-copy kernel while a stream's keys fit in shared memory
-int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st) {
+// the arrival for `rows` rows at layer l: in a prompt pass (blocks given) query blocks sharing key/value tiles;
+// otherwise one CTA per (row, head), by bulk copies while a stream's keys fit in shared memory
+int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st, int nblocks = 0) {
     AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
                 or_out, h->half};
     const bool py = h->cfg.kind == B2_PYTHIA;
     const dim3 grid(rows, h->cfg.n_head);
+    if (nblocks > 0 && h->pf_qb && !(h->flags & B2_ARRIVAL_FLOAT)) {
+        const dim3 g(nblocks, h->cfg.n_head);
+        const size_t sm = prefill_smem(h->pf_qb, h->max_ctx);
+        const PrefillBlock* bl = h->pf_blocks;
+        const int nkm = h->max_ctx;
+        if (h->pf_qb == 16)
+            return py ? launch(h, B2_PROF_ATTEND, "attend_prefill", k_attend_prefill<16, true>, g, 256, sm, st, aa, bl, nkm)
+                      : launch(h, B2_PROF_ATTEND, "attend_prefill", k_attend_prefill<16, false>, g, 256, sm, st, aa, bl, nkm);
+        return py ? launch(h, B2_PROF_ATTEND, "attend_prefill", k_attend_prefill<8, true>, g, 256, sm, st, aa, bl, nkm)
+                  : launch(h, B2_PROF_ATTEND, "attend_prefill", k_attend_prefill<8, false>, g, 256, sm, st, aa, bl, nkm);
+    }
     if (h->flags & B2_ARRIVAL_FLOAT) {
         aa.qf = py ? h->qraw : h->QKV;                    // GPT-2: q is the first third of the qkv row
         aa.ldq = py ? h->cfg.d_model : 3 * h->cfg.d_model;
@@ -332,7 +347,7 @@ int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows,
 // before either branch adds into it; the branch sums go into R in the order mproj, proj (wrapping int64 adds, so the
 // order does not change R). Buffers: g1 R in ATT until the qkv bank has read it, g2 R in HID until the fc bank has.
 int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
-                    int32_t* words_by_slot, cudaStream_t st) {
+                    int32_t* words_by_slot, cudaStream_t st, int nblocks) {
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
     int rc;
@@ -348,7 +363,7 @@ int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t*
                          (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err,
                          (const double*)h->cosf, (const double*)h->sinf, h->qraw)))
             return rc;
-        if ((rc = run_attend(h, rows, l, nullptr, st))) return rc;
+        if ((rc = run_attend(h, rows, l, nullptr, st, nblocks))) return rc;
         if ((rc = run_gauge(h, h->R, nullptr, rows, 2 * l + 1, h->HID, st))) return rc;
         if ((rc = run_quant(h, h->HID, d, nullptr, rows, 0, st))) return rc;
         if ((rc = run_bank(h, 4 * l + 2, EPI_PLAIN_EDGE, rows, h->HID, F, nullptr, st))) return rc;
@@ -367,8 +382,8 @@ int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t*
 // ---- all layers + head for the rows in the row table --------------------------------------------------------------
 // head rows: rows [0, nhead) of `hrows` (row indices) are scored; their logits go to out rows hmap (slot ids).
 int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, int nhead, int64_t* logits,
-             int32_t* words_by_slot, cudaStream_t st) {
-    if (h->cfg.kind == B2_PYTHIA) return run_rows_pythia(h, rows, hrows, hmap, nhead, logits, words_by_slot, st);
+             int32_t* words_by_slot, cudaStream_t st, int nblocks = 0) {
+    if (h->cfg.kind == B2_PYTHIA) return run_rows_pythia(h, rows, hrows, hmap, nhead, logits, words_by_slot, st, nblocks);
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
     int rc;
@@ -381,7 +396,7 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
         if ((rc = launch(h, B2_PROF_HEADS, "heads", k_heads, dim3(rows, 3 * H), 32, 0, st, h->QKV, rows, h->row_slot,
                          h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err)))
             return rc;
-        if ((rc = run_attend(h, rows, l, nullptr, st))) return rc;
+        if ((rc = run_attend(h, rows, l, nullptr, st, nblocks))) return rc;
         if ((rc = run_quant(h, h->ATT, d, nullptr, rows, 0, st))) return rc;
         if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, rows, h->R, d, nullptr, st))) return rc;
         if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
@@ -572,7 +587,11 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess) {
+        cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_prefill<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_prefill<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_prefill<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_prefill<8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess) {
         delete h;
         return B2_ERR_CUDA;
     }
@@ -792,7 +811,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->sigf, h->qraw, h->kv.kraw, h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
@@ -804,6 +823,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     h->sigf = nullptr;
     h->qraw = nullptr;
     h->kv.kraw = nullptr;
+    h->pf_blocks = nullptr;
     const int L = c.n_layer, H = c.n_head, d = c.d_model, F = c.d_ff;
     const int ctx_stride = (max_ctx + 15) / 16 * 16;
     size_t nkv = (size_t)n_streams * L * H * ctx_stride;
@@ -826,6 +846,8 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     int mr = n_streams > 2048 ? n_streams : 2048;   // rows per pass (prompt passes are chunked to this)
     h->max_rows = mr;
     if ((rc = dalloc(h, &h->row_slot, mr)) || (rc = dalloc(h, &h->row_pos, mr)) || (rc = dalloc(h, &h->row_tok, mr))) return rc;
+    if ((rc = dalloc(h, &h->pf_blocks, mr))) return rc;
+    h->pf_qb = prefill_smem(16, max_ctx) <= PF_SMEM_MAX ? 16 : (prefill_smem(8, max_ctx) <= PF_SMEM_MAX ? 8 : 0);
     if ((rc = dalloc(h, &h->R, (size_t)mr * d)) || (rc = dalloc(h, &h->QKV, (size_t)mr * 3 * d)) ||
         (rc = dalloc(h, &h->ATT, (size_t)mr * d)) || (rc = dalloc(h, &h->HID, (size_t)mr * F)))
         return rc;
@@ -899,7 +921,25 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
                 }
                 // head rows must stay valid until the chunk's kernels have read them
             }
-            rc = run_rows(h, rows, h->head_rows, h->head_rows + nh, nh, lg, h->race_out, st);
+            // the arrival's query blocks: runs of up to pf_qb consecutive positions of one stream
+            int nblocks = 0;
+            if (h->pf_qb) {
+                std::vector<PrefillBlock> bl;
+                for (int i = 0; i < rows;) {
+                    const size_t g = r0 + i;
+                    int n = 1;
+                    while (n < h->pf_qb && i + n < rows && rs[g + n] == rs[g] && rp[g + n] == rp[g] + n) n++;
+                    bl.push_back(PrefillBlock{i, n, rs[g], rp[g]});
+                    i += n;
+                }
+                nblocks = (int)bl.size();
+                if (cudaMemcpyAsync(h->pf_blocks, bl.data(), sizeof(PrefillBlock) * bl.size(), cudaMemcpyHostToDevice, st) !=
+                    cudaSuccess) {
+                    rc = fail(h, B2_ERR_CUDA, "prefill block table copy");
+                    break;
+                }
+            }
+            rc = run_rows(h, rows, h->head_rows, h->head_rows + nh, nh, lg, h->race_out, st, nblocks);
             if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = fail(h, B2_ERR_CUDA, "prefill chunk sync");
         }
     } while (0);

@@ -647,6 +647,179 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
+// the arrival in a prompt pass (base2.py:85-100; pythia_base2.py:125-141): a block of up to QB consecutive prompt
+// positions of one stream per CTA and head, so that each key / value tile brought into shared memory serves all QB
+// queries (per-row arrivals would read every earlier key once per row):
+//   pass 1  the score of every (query, key <= the query's position) pair into shared memory, each query's largest;
+//   pass 2  a = ARR[start - sc] (0 past the table), Z = sum a, per query;
+//   pass 3  num = sum a * v over value tiles, out = power(num, -log2fix(Z)).
+// The arithmetic is k_attend's, query by query (wrapping int64 sums; Pythia's exact power and range checks).
+// Shared memory: QB x max_ctx int64 (scores, then arrival weights) + the tiles (prefill_smem()).
+// ---------------------------------------------------------------------------------------------------------------------
+struct PrefillBlock {
+    int row0, nr, slot, pos0;      // rows row0 .. row0 + nr - 1 are positions pos0 .. of stream slot `slot`
+};
+constexpr int PF_KT = 64;          // keys per tile
+constexpr int PF_KROW = 66;        // int16 per key row in shared memory (64 + 2: conflict-free row-per-lane reads)
+inline size_t prefill_smem(int qb, int nkmax) {
+    return (size_t)qb * nkmax * 8 + (size_t)qb * 64 * 4 + (size_t)PF_KT * PF_KROW * 2 + PF_KT * 8 + PF_KT * 4 +
+           (size_t)PF_KT * 64 * 4;
+}
+
+template <int QB, bool PY>
+__global__ void __launch_bounds__(256) k_attend_prefill(AttnArgs a, const PrefillBlock* __restrict__ blocks, int nkmax) {
+    griddep_wait();
+    griddep_launch();
+    extern __shared__ __align__(16) uint8_t sm[];
+    __shared__ int64_t s_max[QB][2], s_eq[QB], s_Z[QB];
+    __shared__ uint64_t s_vm[QB];
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const PrefillBlock blk = blocks[blockIdx.x];
+    const int h = blockIdx.y, H = a.kv.H, d = H * 64;
+    const int nr = blk.nr, pos0 = blk.pos0, nk = pos0 + nr;
+    if (pos0 < 0 || nr < 1 || nr > QB || nk > a.kv.lim || nk > nkmax) return;   // flagged by the heads kernel
+    int64_t* S = reinterpret_cast<int64_t*>(sm);                          // [QB][nkmax]
+    int32_t* Qs = reinterpret_cast<int32_t*>(S + (size_t)QB * nkmax);      // [QB][64]
+    int16_t* Kt = reinterpret_cast<int16_t*>(Qs + QB * 64);               // [PF_KT][PF_KROW]
+    uint64_t* KMt = reinterpret_cast<uint64_t*>(Kt + PF_KT * PF_KROW);    // [PF_KT]
+    int32_t* KEt = reinterpret_cast<int32_t*>(KMt + PF_KT);               // [PF_KT]
+    int32_t* Vt = KEt + PF_KT;                                            // [PF_KT][64]
+    for (int i = tid; i < QB * 64; i += 256) {
+        const int q = i >> 6, t = i & 63;
+        Qs[i] = q < nr ? a.q16[(size_t)(blk.row0 + q) * d + h * 64 + t] : 0;
+    }
+    if (tid < QB) {
+        s_eq[tid] = tid < nr ? (int64_t)a.qexp[(blk.row0 + tid) * H + h] : 0;
+        s_vm[tid] = 0;
+    }
+    const size_t base = kv_index(blk.slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
+
+    // ---- pass 1: thread (key kl of the tile, query group qg): queries qg, qg + 4, .. ----
+    constexpr int QPT = QB / 4;
+    const int kl = tid & 63, qg = tid >> 6;
+    int64_t lmax[QPT];
+#pragma unroll
+    for (int i = 0; i < QPT; i++) lmax[i] = INT64_MIN;
+    for (int k0 = 0; k0 < nk; k0 += PF_KT) {
+        __syncthreads();                                                  // the previous tile is consumed
+        {
+            const int r = tid >> 2, c = tid & 3, key = k0 + r;
+            uint32_t* dst = reinterpret_cast<uint32_t*>(Kt + r * PF_KROW) + c * 8;
+            int4 v0 = make_int4(0, 0, 0, 0), v1 = make_int4(0, 0, 0, 0);
+            if (key < nk) {
+                const int4* src = reinterpret_cast<const int4*>(a.kv.k + (base + key) * 64) + c * 2;
+                v0 = src[0];
+                v1 = src[1];
+            }
+            dst[0] = v0.x; dst[1] = v0.y; dst[2] = v0.z; dst[3] = v0.w;
+            dst[4] = v1.x; dst[5] = v1.y; dst[6] = v1.z; dst[7] = v1.w;
+            if (tid < PF_KT) {
+                const int kk = k0 + tid;
+                KMt[tid] = kk < nk ? a.kv.kmask[base + kk] : 0;
+                KEt[tid] = kk < nk ? a.kv.kexp[base + kk] : 0;
+            }
+        }
+        __syncthreads();
+        const int key = k0 + kl;
+        if (key < nk) {
+            uint32_t kw[32];
+            const uint32_t* kr = reinterpret_cast<const uint32_t*>(Kt + kl * PF_KROW);
+#pragma unroll
+            for (int w = 0; w < 32; w++) kw[w] = kr[w];
+            const uint64_t mk0 = KMt[kl];
+            const int64_t ek = KEt[kl];
+#pragma unroll
+            for (int i = 0; i < QPT; i++) {
+                const int q = qg + 4 * i;
+                if (q >= nr || key > pos0 + q) continue;                 // causal: keys up to the query's own position
+                const int32_t* qr = Qs + q * 64;
+                int64_t dot = 0;
+#pragma unroll
+                for (int w = 0; w < 32; w++) {
+                    // |q|, |k| <= 32768: each product fits int32 (a pair's sum may not: (-32768)^2 * 2 = 2^31)
+                    dot += (int64_t)(qr[2 * w] * (int32_t)(int16_t)(kw[w] & 0xFFFF));
+                    dot += (int64_t)(qr[2 * w + 1] * (int32_t)(int16_t)(kw[w] >> 16));
+                }
+                uint64_t mk = mk0;
+                while (mk) { const int t = __ffsll((long long)mk) - 1; mk &= mk - 1; dot += 65536LL * qr[t]; }
+                const int64_t sc = score<PY>(dot, s_eq[q], ek, a);
+                S[(size_t)q * nkmax + key] = sc;
+                lmax[i] = sc > lmax[i] ? sc : lmax[i];
+            }
+        }
+    }
+    // each query's largest score: its 64 threads are warps 2 qg and 2 qg + 1
+#pragma unroll
+    for (int i = 0; i < QPT; i++) {
+        const int64_t m = warp_max64(lmax[i]);
+        if (lane == 0) s_max[qg + 4 * i][wid & 1] = m;
+    }
+    __syncthreads();
+
+    // ---- pass 2: arrival weights in place of the scores, Z per query (256 / QB threads per query) ----
+    constexpr int TPQ = 256 / QB;
+    {
+        const int q = tid / TPQ, sub = tid % TPQ;
+        int64_t z = 0;
+        if (q < nr) {
+            const int64_t start = s_max[q][0] > s_max[q][1] ? s_max[q][0] : s_max[q][1];
+            for (int key = sub; key <= pos0 + q; key += TPQ) {
+                const int64_t av = arrival(wsub(start, S[(size_t)q * nkmax + key]), a.ARR, a.alen, a.err);
+                S[(size_t)q * nkmax + key] = av;
+                z = wadd(z, av);
+            }
+        }
+#pragma unroll
+        for (int o = TPQ / 2; o > 0; o >>= 1) z = wadd(z, __shfl_xor_sync(0xffffffffu, z, o));
+        if (sub == 0 && q < QB) s_Z[q] = z;
+    }
+
+    // ---- pass 3: num = sum a v; thread (query q, DPT dims) ----
+    constexpr int DPT = 64 / TPQ;
+    const int q = tid / TPQ, dg = tid % TPQ;
+    int64_t num[DPT];
+#pragma unroll
+    for (int j = 0; j < DPT; j++) num[j] = 0;
+    uint64_t vm = 0;
+    for (int k0 = 0; k0 < nk; k0 += PF_KT) {
+        __syncthreads();                                                  // pass 2 / the previous value tile is done
+        for (int i = tid; i < PF_KT * 16; i += 256) {
+            const int r = i >> 4, c = i & 15, key = k0 + r;
+            reinterpret_cast<int4*>(Vt)[i] =
+                key < nk ? reinterpret_cast<const int4*>(a.kv.v + (base + key) * 64)[c] : make_int4(0, 0, 0, 0);
+        }
+        __syncthreads();
+        if (q < nr) {
+            const int kend = min(PF_KT, pos0 + q + 1 - k0);
+            for (int r = 0; r < kend; r++) {
+                const int64_t av = S[(size_t)q * nkmax + k0 + r];
+                if (!av) continue;
+                const int32_t* vr = Vt + r * 64 + dg * DPT;
+#pragma unroll
+                for (int j = 0; j < DPT; j++) {
+                    num[j] = wadd(num[j], wmul(av, vr[j]));
+                    if (PY) vm = max(vm, mag(vr[j]));
+                }
+            }
+        }
+    }
+    if (PY) {
+        __syncthreads();
+        if (q < nr) atomicMax((unsigned long long*)&s_vm[q], (unsigned long long)vm);
+        __syncthreads();
+    }
+    if (q < nr) {
+        const int64_t zz = s_Z[q];
+        const int64_t F = -log2fix(zz, a.LOG2);
+        bool bad = PY && (unsigned __int128)s_vm[q] * (unsigned __int128)(uint64_t)zz >= ((unsigned __int128)1 << 62);
+        int64_t* o = a.out + (size_t)(blk.row0 + q) * d + h * 64 + dg * DPT;
+#pragma unroll
+        for (int j = 0; j < DPT; j++) o[j] = PY ? power_exact(num[j], F, a.EXP2, &bad) : power(num[j], F, a.EXP2);
+        if (PY && bad) set_err(a.err, DERR_RANGE);
+    }
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
 // the race at the top (base2.py:34-40): argmax with ties to the lowest index; one CTA per scored row
 // ---------------------------------------------------------------------------------------------------------------------
 __global__ void __launch_bounds__(1024) k_race(const int64_t* __restrict__ logits, int ld, const int32_t* __restrict__ rows_map,
