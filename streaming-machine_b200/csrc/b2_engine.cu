@@ -83,6 +83,7 @@ struct b2_handle {
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
+    int fuse_heads = 1;          // GPT-2 decode: heads16 in the qkv bank's epilogue (B2_FUSE_HEADS=0: its own kernel)
     int use_mega = 0;            // decode steps of <= 64 streams as one persistent kernel (B2_MEGA=1)
     MegaPlan mega;
     uint64_t* mega_trace = nullptr;   // B2_MEGA_TRACE=<file>: the last step's phase timestamps, written at b2_destroy
@@ -256,12 +257,15 @@ int bank_float_stages(const b2_handle* h, int bi) {
 }
 
 // ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
-int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st) {
+// heads (GPT-2's qkv): the split-K decode kernel may do heads16 in its epilogue; *heads_done says whether it did
+int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st,
+             const TcHeads* heads = nullptr, bool* heads_done = nullptr) {
     const DevBank& bk = h->banks[bi];
+    if (heads_done) *heads_done = false;
     if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
         prof_begin(h, B2_PROF_BANK, st);
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && !h->prof.timing);
+                         h->pdl && !h->prof.timing, heads, heads_done);
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
@@ -392,8 +396,16 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
         return rc;
     for (int l = 0; l < L; l++) {
         if ((rc = run_quant(h, h->R, d, nullptr, rows, 1, st))) return rc;
-        if ((rc = run_bank(h, 4 * l + 0, EPI_GAUGED, rows, h->QKV, 3 * d, nullptr, st))) return rc;
-        if ((rc = launch(h, B2_PROF_HEADS, "heads", k_heads, dim3(rows, 3 * H), 32, 0, st, h->QKV, rows, h->row_slot,
+        // decode rows: heads16 in the qkv bank's epilogue where the split-K kernel runs (not with arrival=float,
+        // which also needs the keys at full width)
+        const TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
+        bool heads_done = false;
+        const bool want_heads = h->fuse_heads && !(h->flags & B2_ARRIVAL_FLOAT);
+        if ((rc = run_bank(h, 4 * l + 0, EPI_GAUGED, rows, h->QKV, 3 * d, nullptr, st, want_heads ? &hd : nullptr,
+                           &heads_done)))
+            return rc;
+        if (!heads_done &&
+            (rc = launch(h, B2_PROF_HEADS, "heads", k_heads, dim3(rows, 3 * H), 32, 0, st, h->QKV, rows, h->row_slot,
                          h->row_pos, l, h->kv, h->q16, h->qexp, h->d_err)))
             return rc;
         if ((rc = run_attend(h, rows, l, nullptr, st, nblocks))) return rc;
@@ -584,6 +596,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
+    if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||

@@ -33,6 +33,8 @@ struct TcArgs {
     const int16_t* w16;
     uint32_t* err;
     EpiArgs epi;
+    int heads;        // EPI_GAUGED on the split path: heads16 in the epilogue (hd), no q/k/v stores
+    TcHeads hd;
 };
 
 // the 16 MMAs of one K block: 4 K steps x {wh.xh -> A1, wh.xl + wl.xh -> A2, wl.xl -> A3}
@@ -68,6 +70,15 @@ B2_DEV RowData load_row(const TcArgs& a, int n) {
         if (a.epi.out_map) d.orow = a.epi.out_map[n];
     }
     return d;
+}
+
+// the finished value of (row n, column j): corrections, then the bank's epilogue
+template <int EPI>
+B2_DEV int64_t finish_value(const TcArgs& a, const RowData& r, int n, int j, int64_t pile, int64_t colc, int64_t e_j,
+                            int64_t b_j) {
+    pile += colc + r.rowc;
+    for (int u = 0; u < r.nsat; u++) pile += 256 * (int64_t)a.w16[(size_t)a.sat[(size_t)n * a.sat_ld + u] * a.nout + j];
+    return epi_value<EPI>(pile, e_j, b_j, r.ex, r.LS, r.e2, a.epi.PHI);
 }
 
 // the finished pile of (row n, column j): corrections, then the bank's epilogue, stored
@@ -165,7 +176,69 @@ __global__ void __launch_bounds__(256, 1)
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 256);   // TMEM is no longer needed
     cluster_sync();                   // every CTA's partial tile is written
-    {
+    if (EPI == EPI_GAUGED && a.heads) {
+        // heads16 (the Metal engine's heads16, base2_stream.swift:112-119; base2.py:93): each 64-column half of the
+        // tile is one head part (q, k or v of one head); a row's OR over the part is the OR over its two warps
+        __shared__ uint64_t s_hor[8];
+        const int ksz = a.ksplit;
+        const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
+        const int m = tid & 127;
+        const int j = mt * 128 + m;
+        const bool jv = j < a.nout && go;
+        const int64_t colc = jv ? a.colcorr[j] : 0;
+        const int64_t e_j = jv ? (int64_t)a.epi.e[j] : 0, b_j = jv ? a.epi.b[j] : 0;
+        uint32_t peer[MAX_SPLIT];
+        const uint32_t pbase = saddr(P);
+#pragma unroll
+        for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
+        const int H = a.hd.kv.H, dm = H * 64;
+        const int part = 2 * mt + (m >> 6), kind = part / H, hh = part % H, dd = m & 63;
+        for (int nb = n0; nb < n1; nb += 2) {
+            const int n = nb + (tid >> 7);
+            const bool valid = jv && n < n1 && n < a.rows;
+            int64_t val = 0;
+            if (valid) {
+                const uint32_t off = (uint32_t)(n * 128 + m) * 8;
+                int64_t t[MAX_SPLIT];
+#pragma unroll
+                for (int p = 0; p < MAX_SPLIT; p++) t[p] = p < ksz ? ld_dsmem(peer[p] + off) : 0;
+                int64_t v = 0;
+#pragma unroll
+                for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[p]);
+                val = finish_value<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
+            }
+            const uint64_t w = warp_or64(valid ? mag(val) : 0);
+            if (lane == 0) s_hor[warp] = w;
+            __syncthreads();
+            const uint64_t por = s_hor[warp] | s_hor[warp ^ 1];
+            __syncthreads();
+            // a warp is 32 columns of one part of one row: kind and validity are the same across it
+            const int sh = to16_shift(por);
+            const int32_t x = (int32_t)rshift(val, sh);
+            if (kind == 0) {
+                if (valid) {
+                    a.hd.q16[(size_t)n * dm + hh * 64 + dd] = x;
+                    if (dd == 0) a.hd.qexp[n * H + hh] = -16 + sh;
+                }
+            } else {
+                const int pos = valid ? a.hd.row_pos[n] : 0;
+                const bool pv = valid && pos >= 0 && pos < a.hd.kv.lim;
+                if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
+                const size_t idx = pv ? kv_index(a.hd.row_slot[n], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
+                if (kind == 1) {
+                    const uint32_t satb = __ballot_sync(0xffffffffu, pv && x == 32768);   // +32768: not an int16
+                    if (pv) {
+                        a.hd.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
+                        if (lane == 0) reinterpret_cast<uint32_t*>(&a.hd.kv.kmask[idx])[dd >> 5] = satb;
+                        if (dd == 0) a.hd.kv.kexp[idx] = -16 + sh;
+                    }
+                } else if (pv) {
+                    if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
+                    a.hd.kv.v[idx * 64 + dd] = (int32_t)val;
+                }
+            }
+        }
+    } else {
         const int ksz = a.ksplit;
         const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
         const int m = tid & 127;
@@ -851,7 +924,8 @@ void tc_rows_free(TcRows& r) {
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl) {
+            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done) {
+    if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
     // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
     int mi = -1;
@@ -891,6 +965,11 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     if (ksplit > 1) {
         a.ksplit = ksplit;
         a.kps = kb / ksplit;
+        if (heads && epi == EPI_GAUGED && !out_map) {
+            a.heads = 1;
+            a.hd = *heads;
+            if (heads_done) *heads_done = true;
+        }
         a.stages = a.kps;
         size_t smem = (size_t)(a.kps > 2 ? a.kps : 2) * STAGE + 1024;   // >= the 64 KB partial tile
         dim3 grid(mtiles, ksplit, 1);

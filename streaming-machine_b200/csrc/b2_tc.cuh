@@ -68,15 +68,27 @@ struct FusedArgs {
     uint32_t* err;
 };
 
+// the qkv bank's heads16 done in its decode epilogue (instead of storing q/k/v and a separate split kernel): q16 and
+// its exponent per head, k16 / mask / exponent and v appended to the key/value store at each row's position
+struct TcHeads {
+    int32_t* q16;
+    int32_t* qexp;
+    KV kv;
+    const int32_t* row_slot;
+    const int32_t* row_pos;
+    int layer;
+};
+
 int tc_min_rows_default();
 int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
 void tc_bank_free(TcBank& t);
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);
+// heads (optional, EPI_GAUGED): do heads16 in the epilogue when the split-K decode kernel runs; *heads_done tells
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl);
+            cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr);
 int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2
