@@ -268,20 +268,21 @@ __global__ void __launch_bounds__(256, 1)
 // ---------------------------------------------------------------------------------------------------------------------
 // Many tiles (the head; prompt passes): a persistent loop over 128-column x 64-row tiles. TMEM holds two accumulator
 // sets (columns 0 and 256) so the epilogue of one tile overlaps the loads and MMAs of the next; a ring of `stages`
-// K blocks feeds the MMAs. 384 threads: warp 0 lane 0 = TMA, warp 1 lane 0 = MMA, warps 4-11 = epilogue
-// (warp w reads TMEM lane quadrant w % 4, rows 32 * ((w - 4) / 4) .. + 32 of the tile).
+// K blocks feeds the MMAs. 640 threads: warp 0 lane 0 = TMA, warp 1 lane 0 = MMA, warps 4-19 = epilogue (the int64
+// epilogue is the bound, so it gets 16 warps: warp w reads TMEM lane quadrant w % 4, rows 16 * ((w - 4) / 4) .. + 16).
 // ---------------------------------------------------------------------------------------------------------------------
+constexpr int TILE_THREADS = 640;
 template <int EPI>
-__global__ void __launch_bounds__(384, 1)
+__global__ void __launch_bounds__(TILE_THREADS, 1)
     k_bank_tiles(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
                  const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
     constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
-    constexpr int NEPI = 8;
+    constexpr int NEPI = 16;
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full_bar[MAX_STAGES], empty_bar[MAX_STAGES], tfull[2], tempty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int s_dead;
-    __shared__ RowData s_row[NEPI][32];
+    __shared__ RowData s_row[NEPI][16];
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = a.stages, KB = a.kps;
@@ -350,13 +351,13 @@ __global__ void __launch_bounds__(384, 1)
             }
         }
     } else if (warp >= 4) {
-        const int e = warp - 4, quad = warp & 3, r0 = (e >> 2) * 32;
+        const int e = warp - 4, quad = warp & 3, r0 = (e >> 2) * 16;
         const uint32_t tq = (uint32_t)(quad * 32) << 16;
         for (int i = 0; i < my_tiles; i++) {
             const int b = i & 1, t = blockIdx.x + i * G;
             const int mt = t % a.mtiles, nt = t / a.mtiles;
-            // this warp's 32 rows of the tile, staged per warp while the accumulators fill
-            s_row[e][lane] = load_row<GAUGED>(a, nt * BN + r0 + lane);
+            // this warp's 16 rows of the tile, staged per warp while the accumulators fill
+            if (lane < 16) s_row[e][lane] = load_row<GAUGED>(a, nt * BN + r0 + lane);
             const int j = mt * 128 + quad * 32 + lane;
             const bool jv = j < a.nout;
             const int64_t colc = jv ? a.colcorr[j] : 0;
@@ -364,14 +365,13 @@ __global__ void __launch_bounds__(384, 1)
             __syncwarp();
             if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
             tc_fence_after();
-#pragma unroll 1
-            for (int c = 0; c < 2; c++) {
+            {
                 int64_t p[16];
-                tmem_piles16(tmem + b * 256 + tq + r0 + 16 * c, p);
+                tmem_piles16(tmem + b * 256 + tq + r0, p);
 #pragma unroll
                 for (int q = 0; q < 16; q++) {
-                    const int rr = 16 * c + q, n = nt * BN + r0 + rr;
-                    if (n < a.rows && jv) finish<EPI>(a, s_row[e][rr], n, j, p[q], colc, e_j, b_j);
+                    const int n = nt * BN + r0 + q;
+                    if (n < a.rows && jv) finish<EPI>(a, s_row[e][q], n, j, p[q], colc, e_j, b_j);
                 }
             }
             tc_fence_before();
@@ -983,7 +983,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         size_t smem = (size_t)MAX_STAGES * STAGE + 1024;
         int total = mtiles * ntiles;
         dim3 grid(total < 148 ? total : 148);
-        B2_EPI_SWITCH(epi, err = launch_k(k_bank_tiles<E>, grid, dim3(384), smem, 1, st, pdl, t, r.maps[mi].h,
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_tiles<E>, grid, dim3(TILE_THREADS), smem, 1, st, pdl, t, r.maps[mi].h,
                                           r.maps[mi].l, a);
                       break)
     }
