@@ -733,13 +733,14 @@ __global__ void __launch_bounds__(256) k_attend_prefill(AttnArgs a, const Prefil
                 const int q = qg + 4 * i;
                 if (q >= nr || key > pos0 + q) continue;                 // causal: keys up to the query's own position
                 const int32_t* qr = Qs + q * 64;
-                int64_t dot = 0;
+                int64_t d4[4] = {0, 0, 0, 0};                          // four independent sums (latency)
 #pragma unroll
                 for (int w = 0; w < 32; w++) {
                     // |q|, |k| <= 32768: each product fits int32 (a pair's sum may not: (-32768)^2 * 2 = 2^31)
-                    dot += (int64_t)(qr[2 * w] * (int32_t)(int16_t)(kw[w] & 0xFFFF));
-                    dot += (int64_t)(qr[2 * w + 1] * (int32_t)(int16_t)(kw[w] >> 16));
+                    d4[(2 * w) & 3] += (int64_t)(qr[2 * w] * (int32_t)(int16_t)(kw[w] & 0xFFFF));
+                    d4[(2 * w + 1) & 3] += (int64_t)(qr[2 * w + 1] * (int32_t)(int16_t)(kw[w] >> 16));
                 }
+                int64_t dot = (d4[0] + d4[1]) + (d4[2] + d4[3]);
                 uint64_t mk = mk0;
                 while (mk) { const int t = __ffsll((long long)mk) - 1; mk &= mk - 1; dot += 65536LL * qr[t]; }
                 const int64_t sc = score<PY>(dot, s_eq[q], ek, a);
