@@ -88,6 +88,9 @@ struct b2_handle {
     MegaPlan mega;
     uint64_t* mega_trace = nullptr;   // B2_MEGA_TRACE=<file>: the last step's phase timestamps, written at b2_destroy
     std::string mega_trace_path;
+    uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
+    std::string split_trace_path;
+    int split_idx = 0;                // split-K launches so far in this step
     int64_t* logits = nullptr;   // [n_slots][vocab]
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
@@ -119,6 +122,7 @@ namespace {
 constexpr int FUSED_ROWS = 64;
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
 constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
+constexpr int SPLIT_TRACE_LAUNCHES = 64, SPLIT_TRACE_SLOT = 160 * 8;   // B2_SPLIT_TRACE: launches x (CTAs x stamps)
 
 int fail(b2_handle* h, int code, const char* fmt, ...) {
     char buf[512];
@@ -264,8 +268,11 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
     if (heads_done) *heads_done = false;
     if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
         prof_begin(h, B2_PROF_BANK, st);
+        uint64_t* tr = nullptr;
+        if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) tr = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && !h->prof.timing, heads, heads_done);
+                         h->pdl && !h->prof.timing, heads, heads_done, tr);
+        h->split_idx++;
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
@@ -598,6 +605,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
+    if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
@@ -804,6 +812,11 @@ int b2_finalize(b2_handle* h) {
         }
         if (mega_plan(h->mega, tcs.data(), es.data(), bs.data(), h->cfg.n_layer)) mega_free(h->mega);
         cudaGetLastError();
+        if (!h->split_trace_path.empty() && !h->split_trace) {
+            const size_t n = (size_t)SPLIT_TRACE_LAUNCHES * SPLIT_TRACE_SLOT;
+            if (cudaMalloc(&h->split_trace, n * sizeof(uint64_t)) != cudaSuccess) h->split_trace = nullptr;
+            else cudaMemset(h->split_trace, 0, n * sizeof(uint64_t));
+        }
         if (h->mega.ready && !h->mega_trace_path.empty() && !h->mega_trace) {
             const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
             if (cudaMalloc(&h->mega_trace, n * sizeof(uint64_t)) != cudaSuccess) h->mega_trace = nullptr;
@@ -972,6 +985,7 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
 int step_core(b2_handle* h, int n, cudaStream_t st) {
+    h->split_idx = 0;
     if (mega_ok(h, n)) {
         int rc = run_mega(h, n, st);
         if (rc) return rc;
@@ -1243,6 +1257,17 @@ void b2_destroy(b2_handle* h) {
             }
         }
         cudaFree(h->mega_trace);
+    }
+    if (h->split_trace) {
+        const size_t n = (size_t)SPLIT_TRACE_LAUNCHES * SPLIT_TRACE_SLOT;
+        std::vector<uint64_t> t(n);
+        if (cudaMemcpy(t.data(), h->split_trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost) == cudaSuccess) {
+            if (FILE* f = fopen(h->split_trace_path.c_str(), "wb")) {
+                fwrite(t.data(), sizeof(uint64_t), n, f);
+                fclose(f);
+            }
+        }
+        cudaFree(h->split_trace);
     }
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
     mega_free(h->mega);

@@ -35,7 +35,14 @@ struct TcArgs {
     EpiArgs epi;
     int heads;        // EPI_GAUGED on the split path: heads16 in the epilogue (hd), no q/k/v stores
     TcHeads hd;
+    uint64_t* trace;  // optional (profiling aid): %globaltimer stamps [CTA][8] of this launch
 };
+
+// profiling aid: thread 0 of the CTA stamps step k
+B2_DEV void tstamp(const TcArgs& a, int k) {
+    if (a.trace && threadIdx.x == 0)
+        a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + k] = gtime();
+}
 
 // the 16 MMAs of one K block: 4 K steps x {wh.xh -> A1, wh.xl + wl.xh -> A2, wl.xl -> A3}
 B2_DEV void mma_kblock(uint32_t base, uint32_t tacc, bool first) {
@@ -112,6 +119,7 @@ __global__ void __launch_bounds__(256, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, ks = blockIdx.y;
     const uint32_t crank = cluster_rank();
+    tstamp(a, 0);
 
     if (tid == 0) {
         for (int kb = 0; kb < a.kps; kb++) mbar_init(&full_bar[kb], 1);
@@ -126,6 +134,7 @@ __global__ void __launch_bounds__(256, 1)
     tc_fence_after();
     const uint32_t tmem = tmem_slot;
     const bool dead = s_dead != 0;
+    tstamp(a, 1);
     if (tid == 0 && !dead) {          // weights: independent of earlier kernels
         for (int kb = 0; kb < a.kps; kb++) {
             uint8_t* st = smem + kb * STAGE;
@@ -137,6 +146,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     griddep_wait();
     griddep_launch();
+    tstamp(a, 2);
     if (tid == 0 && !dead) {
         for (int kb = 0; kb < a.kps; kb++) {
             uint8_t* st = smem + kb * STAGE;
@@ -159,6 +169,7 @@ __global__ void __launch_bounds__(256, 1)
     const bool ok = !dead && mbar_wait(&acc_bar, 0, a.err);
     tc_fence_after();
     __syncthreads();
+    tstamp(a, 3);
     const bool go = ok && !s_abort;
     if (go) {
         // this warp's quadrant (TMEM lanes = output columns) and row half
@@ -175,7 +186,9 @@ __global__ void __launch_bounds__(256, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 256);   // TMEM is no longer needed
+    tstamp(a, 4);
     cluster_sync();                   // every CTA's partial tile is written
+    tstamp(a, 5);
     if (EPI == EPI_GAUGED && a.heads) {
         // heads16 (the Metal engine's heads16, base2_stream.swift:112-119; base2.py:93): each 64-column half of the
         // tile is one head part (q, k or v of one head); a row's OR over the part is the OR over its two warps
@@ -262,7 +275,10 @@ __global__ void __launch_bounds__(256, 1)
             finish<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
         }
     }
+    __syncthreads();
+    tstamp(a, 6);
     cluster_sync();                   // no CTA leaves while a peer may still read its partial tile
+    tstamp(a, 7);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -924,7 +940,7 @@ void tc_rows_free(TcRows& r) {
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done) {
+            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace) {
     if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
     // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
@@ -965,6 +981,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     if (ksplit > 1) {
         a.ksplit = ksplit;
         a.kps = kb / ksplit;
+        a.trace = trace;
         if (heads && epi == EPI_GAUGED && !out_map) {
             a.heads = 1;
             a.hd = *heads;

@@ -88,7 +88,8 @@ void tc_rows_free(TcRows& r);
 // heads (optional, EPI_GAUGED): do heads16 in the epilogue when the split-K decode kernel runs; *heads_done tells
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr);
+            cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
+            uint64_t* trace = nullptr);
 int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2
