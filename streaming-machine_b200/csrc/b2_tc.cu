@@ -38,6 +38,25 @@ struct TcArgs {
     uint64_t* trace;  // optional (profiling aid): %globaltimer stamps [CTA][8] of this launch
 };
 
+B2_DEV void ld_dsmem2(uint32_t addr, uint64_t& a0, uint64_t& a1) {
+    asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(a0), "=l"(a1) : "r"(addr));
+}
+// bit i of e -> bit 2i, bit i of o -> bit 2i + 1
+B2_DEV uint64_t interleave32(uint32_t e, uint32_t o) {
+    uint64_t x = e, y = o;
+    x = (x | (x << 16)) & 0x0000FFFF0000FFFFull;
+    y = (y | (y << 16)) & 0x0000FFFF0000FFFFull;
+    x = (x | (x << 8)) & 0x00FF00FF00FF00FFull;
+    y = (y | (y << 8)) & 0x00FF00FF00FF00FFull;
+    x = (x | (x << 4)) & 0x0F0F0F0F0F0F0F0Full;
+    y = (y | (y << 4)) & 0x0F0F0F0F0F0F0F0Full;
+    x = (x | (x << 2)) & 0x3333333333333333ull;
+    y = (y | (y << 2)) & 0x3333333333333333ull;
+    x = (x | (x << 1)) & 0x5555555555555555ull;
+    y = (y | (y << 1)) & 0x5555555555555555ull;
+    return x | (y << 1);
+}
+
 // profiling aid: thread 0 of the CTA stamps step k
 B2_DEV void tstamp(const TcArgs& a, int k) {
     if (a.trace && threadIdx.x == 0)
@@ -189,90 +208,81 @@ __global__ void __launch_bounds__(256, 1)
     tstamp(a, 4);
     cluster_sync();                   // every CTA's partial tile is written
     tstamp(a, 5);
-    if (EPI == EPI_GAUGED && a.heads) {
-        // heads16 (the Metal engine's heads16, base2_stream.swift:112-119; base2.py:93): each 64-column half of the
-        // tile is one head part (q, k or v of one head); a row's OR over the part is the OR over its two warps
-        __shared__ uint64_t s_hor[8];
+    {
+        // my slice of rows, summed over the cluster. Thread (column pair cp, row group rg) takes columns 2 cp, 2 cp + 1
+        // and rows n0 + rg, n0 + rg + 4, ..: one 16-byte DSMEM load per peer and row (the rate of DSMEM operations,
+        // not its bandwidth, bounds this step). For the qkv bank with heads16 a head part's 64 columns are one warp.
         const int ksz = a.ksplit;
         const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
-        const int m = tid & 127;
-        const int j = mt * 128 + m;
-        const bool jv = j < a.nout && go;
-        const int64_t colc = jv ? a.colcorr[j] : 0;
-        const int64_t e_j = jv ? (int64_t)a.epi.e[j] : 0, b_j = jv ? a.epi.b[j] : 0;
+        const int cp = tid & 63, rg = tid >> 6;
+        const int j0 = mt * 128 + 2 * cp, j1 = j0 + 1;
+        const bool jv0 = j0 < a.nout && go, jv1 = j1 < a.nout && go;
+        const int64_t colc0 = jv0 ? a.colcorr[j0] : 0, colc1 = jv1 ? a.colcorr[j1] : 0;
+        const int64_t e0 = jv0 ? (int64_t)a.epi.e[j0] : 0, b0 = jv0 ? a.epi.b[j0] : 0;
+        const int64_t e1 = jv1 ? (int64_t)a.epi.e[j1] : 0, b1 = jv1 ? a.epi.b[j1] : 0;
         uint32_t peer[MAX_SPLIT];
         const uint32_t pbase = saddr(P);
 #pragma unroll
         for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
-        const int H = a.hd.kv.H, dm = H * 64;
-        const int part = 2 * mt + (m >> 6), kind = part / H, hh = part % H, dd = m & 63;
-        for (int nb = n0; nb < n1; nb += 2) {
-            const int n = nb + (tid >> 7);
-            const bool valid = jv && n < n1 && n < a.rows;
-            int64_t val = 0;
-            if (valid) {
-                const uint32_t off = (uint32_t)(n * 128 + m) * 8;
-                int64_t t[MAX_SPLIT];
+        const bool heads = EPI == EPI_GAUGED && a.heads;
+        const int H = heads ? a.hd.kv.H : 1, dm = H * 64;
+        const int part = 2 * mt + (cp >> 5), kind = part / H, hh = part % H, dd = (2 * cp) & 63;
+        for (int nb = n0; nb < n1; nb += 4) {
+            const int n = nb + rg;                   // the same for the whole warp
+            const bool rv = n < n1 && n < a.rows;
+            int64_t v0 = 0, v1 = 0;
+            if (rv && (jv0 || jv1)) {
+                const uint32_t off = (uint32_t)(n * 128 + 2 * cp) * 8;
+                uint64_t t0[MAX_SPLIT], t1[MAX_SPLIT];
 #pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) t[p] = p < ksz ? ld_dsmem(peer[p] + off) : 0;
-                int64_t v = 0;
+                for (int p = 0; p < MAX_SPLIT; p++) {
+                    t0[p] = 0;
+                    t1[p] = 0;
+                    if (p < ksz) ld_dsmem2(peer[p] + off, t0[p], t1[p]);
+                }
+                uint64_t s0 = 0, s1 = 0;
 #pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[p]);
-                val = finish_value<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
+                for (int p = 0; p < MAX_SPLIT; p++) { s0 += t0[p]; s1 += t1[p]; }
+                if (jv0) v0 = finish_value<EPI>(a, s_row[n], n, j0, (int64_t)s0, colc0, e0, b0);
+                if (jv1) v1 = finish_value<EPI>(a, s_row[n], n, j1, (int64_t)s1, colc1, e1, b1);
             }
-            const uint64_t w = warp_or64(valid ? mag(val) : 0);
-            if (lane == 0) s_hor[warp] = w;
-            __syncthreads();
-            const uint64_t por = s_hor[warp] | s_hor[warp ^ 1];
-            __syncthreads();
-            // a warp is 32 columns of one part of one row: kind and validity are the same across it
+            if (!heads) {
+                if (rv) {
+                    int64_t* o = a.epi.out + (size_t)s_row[n].orow * a.epi.ldo + j0;
+                    if (jv0) o[0] = EPI == EPI_PLAIN_ADD ? wadd(o[0], v0) : v0;
+                    if (jv1) o[1] = EPI == EPI_PLAIN_ADD ? wadd(o[1], v1) : v1;
+                }
+                continue;
+            }
+            // heads16 (the Metal engine's heads16, base2_stream.swift:112-119; base2.py:93): the row's OR over the part
+            const uint64_t por = warp_or64(rv ? (mag(v0) | mag(v1)) : 0);
             const int sh = to16_shift(por);
-            const int32_t x = (int32_t)rshift(val, sh);
+            const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
             if (kind == 0) {
-                if (valid) {
-                    a.hd.q16[(size_t)n * dm + hh * 64 + dd] = x;
+                if (rv) {
+                    *reinterpret_cast<int2*>(a.hd.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
                     if (dd == 0) a.hd.qexp[n * H + hh] = -16 + sh;
                 }
             } else {
-                const int pos = valid ? a.hd.row_pos[n] : 0;
-                const bool pv = valid && pos >= 0 && pos < a.hd.kv.lim;
-                if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
+                const int pos = rv ? a.hd.row_pos[n] : 0;
+                const bool pv = rv && pos >= 0 && pos < a.hd.kv.lim;
+                if (rv && !pv && dd == 0) set_err(a.err, DERR_POS);
                 const size_t idx = pv ? kv_index(a.hd.row_slot[n], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
                 if (kind == 1) {
-                    const uint32_t satb = __ballot_sync(0xffffffffu, pv && x == 32768);   // +32768: not an int16
+                    // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
+                    const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
+                    const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
                     if (pv) {
-                        a.hd.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
-                        if (lane == 0) reinterpret_cast<uint32_t*>(&a.hd.kv.kmask[idx])[dd >> 5] = satb;
+                        *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) =
+                            ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+                        if (lane == 0) a.hd.kv.kmask[idx] = interleave32(be, bo);
                         if (dd == 0) a.hd.kv.kexp[idx] = -16 + sh;
                     }
                 } else if (pv) {
-                    if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
-                    a.hd.kv.v[idx * 64 + dd] = (int32_t)val;
+                    if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
+                    *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
                 }
             }
-        }
-    } else {
-        const int ksz = a.ksplit;
-        const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
-        const int m = tid & 127;
-        const int j = mt * 128 + m;
-        const bool jv = j < a.nout && go;
-        const int64_t colc = jv ? a.colcorr[j] : 0;
-        const int64_t e_j = jv ? (int64_t)a.epi.e[j] : 0, b_j = jv ? a.epi.b[j] : 0;
-        uint32_t peer[MAX_SPLIT];
-        const uint32_t pbase = saddr(P);
-#pragma unroll
-        for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
-        for (int n = n0 + (tid >> 7); n < n1; n += 2) {
-            if (n >= a.rows || !jv) continue;
-            const uint32_t off = (uint32_t)(n * 128 + m) * 8;
-            int64_t t[MAX_SPLIT];
-#pragma unroll
-            for (int p = 0; p < MAX_SPLIT; p++) t[p] = p < ksz ? ld_dsmem(peer[p] + off) : 0;
-            int64_t v = 0;
-#pragma unroll
-            for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[p]);
-            finish<EPI>(a, s_row[n], n, j, v, colc, e_j, b_j);
         }
     }
     __syncthreads();
