@@ -454,6 +454,8 @@ FusedArgs fused_args(b2_handle* h, const DevBank& bk, const int64_t* X, const ui
 }
 
 int run_fused(b2_handle* h, int bi, int epi, FusedArgs a, cudaStream_t st) {
+    if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) a.trace = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
+    h->split_idx++;
     prof_begin(h, B2_PROF_BANK, st);
     int rc = tc_fused(h->banks[bi].tc, epi, a, st, h->pdl && !h->prof.timing);
     prof_end(h, B2_PROF_BANK, st);

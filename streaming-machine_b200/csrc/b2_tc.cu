@@ -425,6 +425,15 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
 //             key/value store.
 // ---------------------------------------------------------------------------------------------------------------------
 
+// to16 of one int64 (its two 32-bit halves) by the row's shift (0..49, base2.py:24-27): add half, shift
+B2_DEV int32_t to16v(int lo, int hi, int sh) {
+    const uint64_t x = ((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo;
+    return sh ? (int32_t)((int64_t)(x + (1ull << (sh - 1))) >> sh) : (int32_t)(int64_t)x;
+}
+B2_DEV uint32_t hbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)(x == 32768 ? 127 : (x >> 8)); }
+B2_DEV uint32_t lbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)((x & 255) - 128); }
+B2_DEV void st_shared_u16(uint32_t addr, uint32_t v) { asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((uint16_t)v) : "memory"); }
+
 template <int EPI>
 __global__ void __launch_bounds__(256, 2)
     k_bank_fused(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl, const FusedArgs a) {
@@ -438,7 +447,6 @@ __global__ void __launch_bounds__(256, 2)
     __shared__ int64_t s_S1[BN], s_S2[BN], s_rowc[BN];
     __shared__ uint32_t s_sat[BN][MAX_KPS * 4];       // +32768 entries: bit k of this CTA's K range, per row
     __shared__ int64_t s_LS[BN], s_e2[BN];
-    __shared__ uint64_t s_hor[8][4];
     __shared__ unsigned long long s_satrows;       // bit n: row n has a +32768 entry in this CTA's K range
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* xplanes = smem + a.kps * WSTAGE;         // [kps][2][BN x 128] activation planes
@@ -446,6 +454,9 @@ __global__ void __launch_bounds__(256, 2)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x, ks = blockIdx.y;
     const uint32_t crank = cluster_rank();
+    if (a.trace && tid == 0) a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + 0] = gtime();
+#define FSTAMP(k_) \
+    if (a.trace && tid == 0) a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + (k_)] = gtime();
 
     if (tid == 0) {
         for (int kb = 0; kb < a.kps; kb++) mbar_init(&full_bar[kb], 1);
@@ -478,66 +489,69 @@ __global__ void __launch_bounds__(256, 2)
     }
     griddep_wait();
     griddep_launch();
+    FSTAMP(1)
 
-    // ---- activations: to16 and the two byte planes, in shared memory ----
-    {
-        const int n = tid >> 2, cg = tid & 3;
-        const bool nv = n < a.rows;
-        const int sh = nv ? to16_shift(a.xor_in[n]) : 0;
-        if (cg == 0) s_sh[n] = sh;
-        int64_t S1 = 0, S2 = 0, rc = 0;
-        for (int kb = 0; kb < a.kps; kb++) {
-            const int k0 = (ks * a.kps + kb) * 128 + cg * 32;
-            uint32_t hw[8], lw[8];
-            uint32_t satw = 0;
-            int64_t s1 = 0;
-            int4 raw[16];
-            const int4* src = reinterpret_cast<const int4*>(a.X + (size_t)n * a.nin + k0);
+    // ---- activations: to16 with the row's shift, the two byte planes in shared memory, per-row sums. Warp w takes
+    //      rows w, w + 8, ..; lane l values 2l, 2l + 1, 64 + 2l, 65 + 2l of each K block: a row's 1 KB is read by the
+    //      whole warp (coalesced), four rows per round; the row sums by warp reduction (redux) ----
+    if (tid < BN) s_sh[tid] = tid < a.rows ? to16_shift(a.xor_in[tid]) : 0;
+    __syncthreads();
+    for (int kb = 0; kb < a.kps; kb++) {
+        const int kx = (ks * a.kps + kb) * 128;
+        const uint32_t bh = saddr(xplanes + kb * 2 * B_BYTES), bl = bh + B_BYTES;
+#pragma unroll 1
+        for (int g = 0; g < 2; g++) {
+            int4 ra[4], rb[4];
 #pragma unroll
-            for (int v = 0; v < 16; v++) raw[v] = nv ? src[v] : make_int4(0, 0, 0, 0);
-#pragma unroll
-            for (int v4 = 0; v4 < 8; v4++) {
-                const int4 raw0 = raw[2 * v4], raw1 = raw[2 * v4 + 1];
-                const int64_t xv[4] = {(int64_t)(((uint64_t)(uint32_t)raw0.y << 32) | (uint32_t)raw0.x),
-                                       (int64_t)(((uint64_t)(uint32_t)raw0.w << 32) | (uint32_t)raw0.z),
-                                       (int64_t)(((uint64_t)(uint32_t)raw1.y << 32) | (uint32_t)raw1.x),
-                                       (int64_t)(((uint64_t)(uint32_t)raw1.w << 32) | (uint32_t)raw1.z)};
-                uint32_t h = 0, l = 0;
-#pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int32_t q = (int32_t)rshift(xv[u], sh);
-                    const bool sat = q == 32768;
-                    h |= (uint32_t)(uint8_t)(int8_t)(sat ? 127 : (q >> 8)) << (8 * u);
-                    l |= (uint32_t)(uint8_t)(int8_t)((q & 255) - 128) << (8 * u);
-                    s1 += q;
-                    S2 += (int64_t)q * q;
-                    satw |= (uint32_t)sat << (v4 * 4 + u);
-                }
-                hw[v4] = h;
-                lw[v4] = l;
+            for (int i = 0; i < 4; i++) {
+                const int n = warp + 8 * (4 * g + i);
+                const int4* src = reinterpret_cast<const int4*>(a.X + (size_t)n * a.nin + kx);
+                ra[i] = n < a.rows ? src[lane] : make_int4(0, 0, 0, 0);
+                rb[i] = n < a.rows ? src[32 + lane] : make_int4(0, 0, 0, 0);
             }
-            S1 += s1;
-            rc += 128 * (s1 - 256 * (int64_t)__popc(satw));
-            s_sat[n][kb * 4 + cg] = satw;
-            if (satw) atomicOr(&s_satrows, 1ull << n);
-            const uint32_t bh = saddr(xplanes + kb * 2 * B_BYTES), bl = bh + B_BYTES;
-            st_shared_v4(bh + sw128(n, 2 * cg), hw[0], hw[1], hw[2], hw[3]);
-            st_shared_v4(bh + sw128(n, 2 * cg + 1), hw[4], hw[5], hw[6], hw[7]);
-            st_shared_v4(bl + sw128(n, 2 * cg), lw[0], lw[1], lw[2], lw[3]);
-            st_shared_v4(bl + sw128(n, 2 * cg + 1), lw[4], lw[5], lw[6], lw[7]);
-        }
-        // the row's four threads are adjacent lanes
 #pragma unroll
-        for (int o = 1; o < 4; o <<= 1) {
-            S1 += __shfl_xor_sync(0xffffffffu, S1, o);
-            S2 += __shfl_xor_sync(0xffffffffu, S2, o);
-            rc += __shfl_xor_sync(0xffffffffu, rc, o);
+            for (int i = 0; i < 4; i++) {
+                const int n = warp + 8 * (4 * g + i);
+                const int sh = s_sh[n];
+                const int32_t x0 = to16v(ra[i].x, ra[i].y, sh), x1 = to16v(ra[i].z, ra[i].w, sh);
+                const int32_t x2 = to16v(rb[i].x, rb[i].y, sh), x3 = to16v(rb[i].z, rb[i].w, sh);
+                const uint32_t o = (uint32_t)((2 * lane) & 15);
+                st_shared_u16(bh + sw128(n, lane >> 3) + o, hbyte(x0) | (hbyte(x1) << 8));
+                st_shared_u16(bh + sw128(n, 4 + (lane >> 3)) + o, hbyte(x2) | (hbyte(x3) << 8));
+                st_shared_u16(bl + sw128(n, lane >> 3) + o, lbyte(x0) | (lbyte(x1) << 8));
+                st_shared_u16(bl + sw128(n, 4 + (lane >> 3)) + o, lbyte(x2) | (lbyte(x3) << 8));
+                const int sat = (x0 == 32768) + (x1 == 32768) + (x2 == 32768) + (x3 == 32768);
+                if (sat) {                                         // rare: the +32768 list
+#pragma unroll 1
+                    for (int q = 0; q < 4; q++) {
+                        const int32_t xq = q == 0 ? x0 : q == 1 ? x1 : q == 2 ? x2 : x3;
+                        if (xq == 32768) {
+                            const int kk = q < 2 ? 2 * lane + q : 64 + 2 * lane + (q - 2);
+                            atomicOr(&s_sat[n][kb * 4 + (kk >> 5)], 1u << (kk & 31));
+                            atomicOr(&s_satrows, 1ull << n);
+                        }
+                    }
+                }
+                // S1 (|a lane's sum| < 2^17), S2 as 16-bit halves (a lane's sum of 4 squares <= 2^32), +32768 count
+                const uint64_t sq = (uint64_t)((int64_t)x0 * x0) + (uint64_t)((int64_t)x1 * x1) +
+                                    (uint64_t)((int64_t)x2 * x2) + (uint64_t)((int64_t)x3 * x3);
+                const int32_t t1 = (int32_t)__reduce_add_sync(0xffffffffu, (uint32_t)(x0 + x1 + x2 + x3));
+                const uint32_t t2l = __reduce_add_sync(0xffffffffu, (uint32_t)(sq & 0xFFFF));
+                const uint32_t t2h = __reduce_add_sync(0xffffffffu, (uint32_t)(sq >> 16));
+                const uint32_t tc = __reduce_add_sync(0xffffffffu, (uint32_t)sat);
+                if (lane == 0) {                                    // one warp per row: no atomics
+                    const int64_t a1 = t1, a2 = (int64_t)t2h * 65536 + (int64_t)t2l;
+                    s_S1[n] += a1;
+                    s_S2[n] += a2;
+                    s_rowc[n] += 128 * (a1 - 256 * (int64_t)tc);
+                }
+            }
         }
-        if (cg == 0) { s_S1[n] = S1; s_S2[n] = S2; s_rowc[n] = rc; }
     }
     fence_proxy_async();
     __syncthreads();
 
+    FSTAMP(2)
     if (warp == 1 && lane == 0 && !dead) {
         for (int kb = 0; kb < a.kps; kb++) {
             if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
@@ -570,6 +584,7 @@ __global__ void __launch_bounds__(256, 2)
     tc_fence_after();
     __syncthreads();
     const bool go = ok && !s_abort;
+    FSTAMP(3)
 
     // ---- this CTA's corrected partial piles -> P ----
     {
@@ -619,7 +634,9 @@ __global__ void __launch_bounds__(256, 2)
         }
     }
     tc_fence_before();
+    FSTAMP(4)
     cluster_sync();                   // every CTA's partial tile and partial row sums are written
+    FSTAMP(5)
 
     // ---- my slice of rows: sum over the cluster, finish ----
     const int ksz = a.ksplit;
@@ -652,105 +669,93 @@ __global__ void __launch_bounds__(256, 2)
     }
     __syncthreads();
     {
-        const int m = tid & 127, ro = tid >> 7;
-        const int j = mt * 128 + m;
-        const bool jv = j < a.nout && go;
-        const int64_t e_j = jv ? (int64_t)a.e[j] : 0, b_j = jv ? a.b[j] : 0;
-        const int nit = (n1 - n0 + 1) >> 1;
+        // thread (column pair cp, row group rg): columns 2 cp, 2 cp + 1, rows n0 + rg, n0 + rg + 4, ..; one 16-byte DSMEM
+        // load per peer and row. A warp is one row's 64 columns: for the qkv bank exactly one head part, for the
+        // others one atomicOr per warp publishes the next bank's row OR.
+        const int cp = tid & 63, rg = tid >> 6;
+        const int j0 = mt * 128 + 2 * cp, j1 = j0 + 1;
+        const bool jv0 = j0 < a.nout && go, jv1 = j1 < a.nout && go;
+        const int64_t e0 = jv0 ? (int64_t)a.e[j0] : 0, b0 = jv0 ? a.b[j0] : 0;
+        const int64_t e1 = jv1 ? (int64_t)a.e[j1] : 0, b1 = jv1 ? a.b[j1] : 0;
         const int H = a.kv.H, dm = H * 64;
-        for (int it0 = 0; it0 < nit; it0 += 4) {
-          int64_t sums[4];
-          {
-            int64_t t[4][MAX_SPLIT];
+        const bool heads = EPI == EPI_GAUGED && a.q16;
+        const int part = 2 * mt + (cp >> 5), kind = part / H, hh = part % H, dd = (2 * cp) & 63;
+        for (int nb = n0; nb < n1; nb += 4) {
+            const int n = nb + rg;                   // the same for the whole warp
+            const bool rv = n < n1 && n < a.rows;
+            int64_t v0 = 0, v1 = 0;
+            if (rv && (jv0 || jv1)) {
+                const uint32_t off = (uint32_t)(n * 128 + 2 * cp) * 8;
+                uint64_t t0[MAX_SPLIT], t1[MAX_SPLIT];
 #pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int n = n0 + 2 * (it0 + u) + ro;
-                const bool ld = jv && it0 + u < nit && n < n1 && n < a.rows;
-                const uint32_t off = (uint32_t)(n * 128 + m) * 8;
+                for (int p = 0; p < MAX_SPLIT; p++) {
+                    t0[p] = 0;
+                    t1[p] = 0;
+                    if (p < ksz) ld_dsmem2(peer[p] + off, t0[p], t1[p]);
+                }
+                uint64_t s0 = 0, s1 = 0;
 #pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) t[u][p] = (ld && p < ksz) ? ld_dsmem(peer[p] + off) : 0;
+                for (int p = 0; p < MAX_SPLIT; p++) { s0 += t0[p]; s1 += t1[p]; }
+                const int64_t exr = -16 + s_sh[n];
+                if (jv0) v0 = epi_value<EPI>((int64_t)s0, e0, b0, exr, s_LS[n], s_e2[n], a.PHI);
+                if (jv1) v1 = epi_value<EPI>((int64_t)s1, e1, b1, exr, s_LS[n], s_e2[n], a.PHI);
             }
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                int64_t v = 0;
-#pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) v = wadd(v, t[u][p]);
-                sums[u] = v;
-            }
-          }
-          int64_t vals[4];
-          bool valids[4];
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int n = n0 + 2 * (it0 + u) + ro;
-            valids[u] = jv && it0 + u < nit && n < n1 && n < a.rows;
-            vals[u] = valids[u] ? epi_value<EPI>(sums[u], e_j, b_j, -16 + s_sh[n], s_LS[n], s_e2[n], a.PHI) : 0;
-          }
-          if (EPI == EPI_GAUGED && a.q16) {
-            // heads16: each 64-column half of the tile is one head part (q, k or v of one head); its rows' OR of
-            // magnitudes over the part's two warps, for the group's four rows at once
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const uint64_t w = warp_or64(valids[u] ? mag(vals[u]) : 0);
-                if (lane == 0) s_hor[warp][u] = w;
-            }
-            __syncthreads();
-            uint64_t por[4];
-#pragma unroll
-            for (int u = 0; u < 4; u++) por[u] = s_hor[warp][u] | s_hor[warp ^ 1][u];
-            __syncthreads();
-            const int part = 2 * mt + (m >> 6), kind = part / H, hh = part % H, dd = m & 63;
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int n = n0 + 2 * (it0 + u) + ro;
-                const bool valid = valids[u];
-                const int64_t val = vals[u];
-                const int sh = to16_shift(por[u]);
-                const int32_t x = (int32_t)rshift(val, sh);
-                if (a.out && valid) a.out[(size_t)n * a.ldo + j] = val;
+            if (heads) {
+                // heads16: the row's OR over the part, to16, q16 / k16 + mask + exponent / v
+                const uint64_t por = warp_or64(rv ? (mag(v0) | mag(v1)) : 0);
+                const int sh = to16_shift(por);
+                const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
+                if (a.out && rv) {                   // the q/k/v values themselves (b2_bank's fused mode)
+                    if (jv0) a.out[(size_t)n * a.ldo + j0] = v0;
+                    if (jv1) a.out[(size_t)n * a.ldo + j1] = v1;
+                }
                 if (kind == 0) {
-                    if (valid) {
-                        a.q16[(size_t)n * dm + hh * 64 + dd] = x;
+                    if (rv) {
+                        *reinterpret_cast<int2*>(a.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
                         if (dd == 0) a.qexp[n * H + hh] = -16 + sh;
                     }
                 } else {
-                    const int pos = valid ? a.row_pos[n] : 0;
-                    const bool pv = valid && pos >= 0 && pos < a.kv.lim;
-                    if (valid && !pv && dd == 0) set_err(a.err, DERR_POS);
+                    const int pos = rv ? a.row_pos[n] : 0;
+                    const bool pv = rv && pos >= 0 && pos < a.kv.lim;
+                    if (rv && !pv && dd == 0) set_err(a.err, DERR_POS);
                     const size_t idx = pv ? kv_index(a.row_slot[n], a.layer, hh, pos, a.kv.L, H, a.kv.ctx) : 0;
                     if (kind == 1) {
-                        const uint32_t sat = __ballot_sync(0xffffffffu, pv && x == 32768);
+                        const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);   // +32768: not an int16
+                        const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
                         if (pv) {
-                            a.kv.k[idx * 64 + dd] = (int16_t)(uint16_t)(uint32_t)x;
-                            if (lane == 0) reinterpret_cast<uint32_t*>(&a.kv.kmask[idx])[dd >> 5] = sat;
+                            *reinterpret_cast<uint32_t*>(a.kv.k + idx * 64 + dd) =
+                                ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+                            if (lane == 0) a.kv.kmask[idx] = interleave32(be, bo);
                             if (dd == 0) a.kv.kexp[idx] = -16 + sh;
                         }
                     } else if (pv) {
-                        if (val != (int64_t)(int32_t)val) set_err(a.err, DERR_VOVF);
-                        a.kv.v[idx * 64 + dd] = (int32_t)val;
+                        if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
+                        *reinterpret_cast<int2*>(a.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
                     }
                 }
-            }
-          } else {
-#pragma unroll
-            for (int u = 0; u < 4; u++) {
-                const int n = n0 + 2 * (it0 + u) + ro;
-                const bool valid = valids[u];
-                int64_t o = vals[u];
-                if (valid) {
-                    int64_t* dst = a.out + (size_t)n * a.ldo + j;
-                    if (EPI == EPI_PLAIN_ADD) o = wadd(*dst, o);
-                    *dst = o;
+            } else {
+                int64_t o0 = v0, o1 = v1;
+                if (rv) {
+                    int64_t* dst = a.out + (size_t)n * a.ldo + j0;
+                    if (EPI == EPI_PLAIN_ADD) {
+                        if (jv0) o0 = wadd(dst[0], v0);
+                        if (jv1) o1 = wadd(dst[1], v1);
+                    }
+                    if (jv0) dst[0] = o0;
+                    if (jv1) dst[1] = o1;
                 }
-                if (EPI != EPI_GAUGED) {
-                    const uint64_t wor = warp_or64(valid ? mag(o) : 0);
-                    if (lane == 0 && a.or_out && valid) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
+                if (EPI != EPI_GAUGED) {              // the next bank's row OR (over this warp's 64 columns)
+                    const uint64_t wor = warp_or64(rv ? ((jv0 ? mag(o0) : 0) | (jv1 ? mag(o1) : 0)) : 0);
+                    if (lane == 0 && a.or_out && rv) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
                 }
             }
-          }
         }
     }
+    __syncthreads();
+    FSTAMP(6)
     cluster_sync();                   // no CTA leaves while a peer may still read its shared memory
+    FSTAMP(7)
+#undef FSTAMP
 }
 
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
@@ -1020,6 +1025,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
 int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl) {
     if (!t.ready || a.rows < 1 || a.rows > BN || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD))
         return (int)cudaErrorInvalidValue;
+    if ((uintptr_t)a.X & 15) return (int)cudaErrorMisalignedAddress;   // rows are read as 16-byte vectors
     const int mtiles = t.nout_pad / 128, kb = t.nin / 128;
     int ksplit = 1;
     for (int d = MAX_SPLIT; d >= 1; d--)

@@ -66,6 +66,7 @@ struct FusedArgs {
     int32_t* q16;
     int32_t* qexp;
     uint32_t* err;
+    uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8]
 };
 
 // the qkv bank's heads16 done in its decode epilogue (instead of storing q/k/v and a separate split kernel): q16 and
