@@ -163,6 +163,13 @@ __global__ void __launch_bounds__(256, 1)
             tma_load_2d(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128);
         }
     }
+    // this thread's two columns' constants (the bank's own data: read before the dependency wait)
+    const int cp = tid & 63, rg = tid >> 6;
+    const int j0 = mt * 128 + 2 * cp, j1 = j0 + 1;
+    const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
+    const int64_t colc0 = cv0 ? a.colcorr[j0] : 0, colc1 = cv1 ? a.colcorr[j1] : 0;
+    const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
+    const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
     griddep_wait();
     griddep_launch();
     tstamp(a, 2);
@@ -214,12 +221,7 @@ __global__ void __launch_bounds__(256, 1)
         // not its bandwidth, bounds this step). For the qkv bank with heads16 a head part's 64 columns are one warp.
         const int ksz = a.ksplit;
         const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
-        const int cp = tid & 63, rg = tid >> 6;
-        const int j0 = mt * 128 + 2 * cp, j1 = j0 + 1;
-        const bool jv0 = j0 < a.nout && go, jv1 = j1 < a.nout && go;
-        const int64_t colc0 = jv0 ? a.colcorr[j0] : 0, colc1 = jv1 ? a.colcorr[j1] : 0;
-        const int64_t e0 = jv0 ? (int64_t)a.epi.e[j0] : 0, b0 = jv0 ? a.epi.b[j0] : 0;
-        const int64_t e1 = jv1 ? (int64_t)a.epi.e[j1] : 0, b1 = jv1 ? a.epi.b[j1] : 0;
+        const bool jv0 = cv0 && go, jv1 = cv1 && go;
         uint32_t peer[MAX_SPLIT];
         const uint32_t pbase = saddr(P);
 #pragma unroll
@@ -289,6 +291,209 @@ __global__ void __launch_bounds__(256, 1)
     tstamp(a, 6);
     cluster_sync();                   // no CTA leaves while a peer may still read its partial tile
     tstamp(a, 7);
+}
+
+// ---------------------------------------------------------------------------------------------------------------------
+// Decode banks with at most 6 K blocks (nin <= 768) and rows <= 64: no K split, no cluster. CTA (mt, rh) owns 64
+// output columns and 32 rows (32 rh ..) over the whole K range, every K block resident (<= 6 x 24 KB; the weights
+// loaded before the dependency wait). Per K block the A operand is the two weight planes of its 64 columns stacked
+// (wh in rows 0-63, wl in rows 64-127: M = 128) and the B operand the two row planes of its 32 rows stacked (xh in
+// rows 0-31, xl in rows 32-63: N = 64), so ONE MMA (M128 N64 K32) per K step makes all four byte products in one
+// 128 x 64 int32 accumulator:
+//     D[o][r] = wh.xh (A1)   D[o][32 + r] = wh.xl   D[64 + o][r] = wl.xh   D[64 + o][32 + r] = wl.xl (A3)
+// 512 threads: warp 0 lane 0 = TMA, warp 1 lane 0 = MMA, warps 2-15 load the row data. Epilogue: warp w < 8 reads
+// TMEM lane quadrant w % 4, columns 16 (w / 4) .. + 16 of both halves, and parks H = 65536 A1 + 256 wh.xl (quadrants
+// 0, 1) or L = 256 wl.xh + A3 (quadrants 2, 3) in shared memory, [row][column]; then warp w finishes rows w, w + 16
+// (lane l: columns 2l, 2l + 1; for the qkv bank the tile is one head part, so heads16's OR is one warp's).
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int WIDE_THREADS = 512;
+constexpr int WIDE_MAX_KB = 6;
+constexpr int WIDE_ROWS = 32;
+constexpr int WIDE_A = 2 * 64 * 128;                    // [wh; wl] of one K block
+constexpr int WIDE_B = 2 * WIDE_ROWS * 128;             // [xh; xl]
+constexpr int WIDE_KBLOCK = WIDE_A + WIDE_B;
+__host__ __device__ inline int wide_smem_bytes(int nkb) {
+    return (nkb * WIDE_KBLOCK > 2 * WIDE_ROWS * 64 * 8 ? nkb * WIDE_KBLOCK : 2 * WIDE_ROWS * 64 * 8) + 1024;
+}
+
+template <int EPI>
+__global__ void __launch_bounds__(WIDE_THREADS, 1)
+    k_bank_wide(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
+                const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ uint64_t full_bar[WIDE_MAX_KB], acc_bar;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int s_dead, s_abort;
+    __shared__ RowData s_row[WIDE_ROWS];
+    __shared__ int32_t s_pos[WIDE_ROWS], s_slot[WIDE_ROWS];   // heads16: where each row's key / value goes
+    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    int64_t* HB = (int64_t*)smem;     // [32 rows][64 columns] H, over the K blocks once the MMAs are done
+    int64_t* LB = HB + WIDE_ROWS * 64;   // [32 rows][64 columns] L
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x;        // output columns 64 mt .. + 64
+    const int r0 = blockIdx.y * WIDE_ROWS;   // rows r0 .. + 32
+    const int nkb = a.kps;
+    tstamp(a, 0);
+
+    if (tid == 0) {
+        for (int kb = 0; kb < nkb; kb++) mbar_init(&full_bar[kb], 1);
+        mbar_init(&acc_bar, 1);
+        s_abort = 0;
+        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(&tmem_slot, 64);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_slot;
+    const bool dead = s_dead != 0;
+    tstamp(a, 1);
+    if (tid == 0 && !dead) {          // weights: independent of earlier kernels
+        for (int kb = 0; kb < nkb; kb++) {
+            uint8_t* st = smem + kb * WIDE_KBLOCK;
+            mbar_expect_tx(&full_bar[kb], WIDE_KBLOCK);
+            tma_load_2d(st, &mwh, &full_bar[kb], kb * 128, mt * 64);
+            tma_load_2d(st + 64 * 128, &mwl, &full_bar[kb], kb * 128, mt * 64);
+        }
+    }
+    // this lane's two columns' constants (the bank's own data: read before the dependency wait)
+    const int j0 = mt * 64 + 2 * lane, j1 = j0 + 1;
+    const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
+    const int64_t colc0 = cv0 ? a.colcorr[j0] : 0, colc1 = cv1 ? a.colcorr[j1] : 0;
+    const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
+    const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
+    const bool heads = EPI == EPI_GAUGED && a.heads;
+    griddep_wait();
+    griddep_launch();
+    tstamp(a, 2);
+    if (tid == 0 && !dead) {
+        for (int kb = 0; kb < nkb; kb++) {
+            uint8_t* st = smem + kb * WIDE_KBLOCK + WIDE_A;
+            tma_load_2d(st, &mxh, &full_bar[kb], kb * 128, r0);
+            tma_load_2d(st + WIDE_ROWS * 128, &mxl, &full_bar[kb], kb * 128, r0);
+        }
+    } else if (warp == 1 && lane == 0 && !dead) {
+        for (int kb = 0; kb < nkb; kb++) {
+            if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
+            tc_fence_after();
+            const uint32_t base = saddr(smem + kb * WIDE_KBLOCK);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++)
+                mma_i8(tmem, sdesc(base + kk * 32), sdesc(base + WIDE_A + kk * 32), IDESC, (kb || kk) ? 1u : 0u);
+        }
+        mma_commit(&acc_bar);
+    } else if (warp >= 2) {
+        for (int q = tid - 64; q < WIDE_ROWS; q += WIDE_THREADS - 64) {
+            s_row[q] = load_row<GAUGED>(a, r0 + q);
+            if (heads) {
+                s_pos[q] = r0 + q < a.rows ? a.hd.row_pos[r0 + q] : 0;
+                s_slot[q] = r0 + q < a.rows ? a.hd.row_slot[r0 + q] : 0;
+            }
+        }
+    }
+    __syncwarp();
+    __syncthreads();
+    const bool ok = !dead && mbar_wait(&acc_bar, 0, a.err);
+    tc_fence_after();
+    __syncthreads();
+    tstamp(a, 3);
+    const bool go = ok && !s_abort;
+    if (go && warp < 8) {
+        const int q = warp & 3, g = warp >> 2;
+        const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
+        uint32_t xh_part[16], xl_part[16];
+        tmem_ld16(taddr + 16 * g, xh_part);                  // columns r = 16 g .. + 16: the products with xh
+        tmem_ld16(taddr + WIDE_ROWS + 16 * g, xl_part);      // the same rows' products with xl
+        tmem_wait_ld();
+        const int o = (q & 1) * 32 + lane;
+        int64_t* dst = q < 2 ? HB : LB;
+        const int64_t sh = q < 2 ? 65536 : 256, sl = q < 2 ? 256 : 1;
+#pragma unroll
+        for (int i = 0; i < 16; i++)
+            dst[(16 * g + i) * 64 + o] = sh * (int64_t)(int32_t)xh_part[i] + sl * (int64_t)(int32_t)xl_part[i];
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 64);
+    tstamp(a, 4);
+
+    // ---- finish: warp w rows r0 + w, r0 + w + 16; lane l columns 2l, 2l + 1 of the tile ----
+    const bool jv0 = cv0 && go, jv1 = cv1 && go;
+    constexpr int RPW = WIDE_ROWS / (WIDE_THREADS / 32);   // rows per warp
+    int64_t v0[RPW], v1[RPW];
+#pragma unroll
+    for (int it = 0; it < RPW; it++) {
+        const int nl = warp + 16 * it, n = r0 + nl;
+        v0[it] = 0;
+        v1[it] = 0;
+        if (n < a.rows && (jv0 || jv1)) {
+            const longlong2 h = *reinterpret_cast<const longlong2*>(HB + nl * 64 + 2 * lane);
+            const longlong2 l = *reinterpret_cast<const longlong2*>(LB + nl * 64 + 2 * lane);
+            if (jv0) v0[it] = finish_value<EPI>(a, s_row[nl], n, j0, (int64_t)((uint64_t)h.x + (uint64_t)l.x), colc0, e0, b0);
+            if (jv1) v1[it] = finish_value<EPI>(a, s_row[nl], n, j1, (int64_t)((uint64_t)h.y + (uint64_t)l.y), colc1, e1, b1);
+        }
+    }
+    tstamp(a, 6);
+    if (!heads) {
+        int64_t old0[RPW], old1[RPW];
+        if (EPI == EPI_PLAIN_ADD) {                  // the residual, read for every row before any store
+#pragma unroll
+            for (int it = 0; it < RPW; it++) {
+                const int nl = warp + 16 * it, n = r0 + nl;
+                const int64_t* o = a.epi.out + (size_t)(n < a.rows ? s_row[nl].orow : 0) * a.epi.ldo + j0;
+                old0[it] = n < a.rows && jv0 ? o[0] : 0;
+                old1[it] = n < a.rows && jv1 ? o[1] : 0;
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < RPW; it++) {
+            const int nl = warp + 16 * it, n = r0 + nl;
+            if (n >= a.rows) continue;
+            int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j0;
+            if (jv0) o[0] = EPI == EPI_PLAIN_ADD ? wadd(old0[it], v0[it]) : v0[it];
+            if (jv1) o[1] = EPI == EPI_PLAIN_ADD ? wadd(old1[it], v1[it]) : v1[it];
+        }
+    } else {
+        // heads16 (base2_stream.swift:112-119; base2.py:93): the tile is head part mt, a row's OR is this warp's
+        const int H = a.hd.kv.H, dm = H * 64, kind = mt / H, hh = mt % H, dd = 2 * lane;
+#pragma unroll
+        for (int it = 0; it < RPW; it++) {
+            const int nl = warp + 16 * it, n = r0 + nl;
+            const bool rv = n < a.rows && go;
+            const uint64_t por = warp_or64(rv ? (mag(v0[it]) | mag(v1[it])) : 0);
+            const int sh = to16_shift(por);
+            const int32_t x0 = (int32_t)rshift(v0[it], sh), x1 = (int32_t)rshift(v1[it], sh);
+            if (kind == 0) {
+                if (rv) {
+                    *reinterpret_cast<int2*>(a.hd.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
+                    if (lane == 0) a.hd.qexp[n * H + hh] = -16 + sh;
+                }
+            } else {
+                const int pos = rv ? s_pos[nl] : 0;
+                const bool pv = rv && pos >= 0 && pos < a.hd.kv.lim;
+                if (rv && !pv && lane == 0) set_err(a.err, DERR_POS);
+                const size_t idx = pv ? kv_index(s_slot[nl], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
+                if (kind == 1) {
+                    // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
+                    const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
+                    const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
+                    if (pv) {
+                        *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+                        if (lane == 0) {
+                            a.hd.kv.kmask[idx] = interleave32(be, bo);
+                            a.hd.kv.kexp[idx] = -16 + sh;
+                        }
+                    }
+                } else if (pv) {
+                    if (v0[it] != (int64_t)(int32_t)v0[it] || v1[it] != (int64_t)(int32_t)v1[it]) set_err(a.err, DERR_VOVF);
+                    *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0[it], (int32_t)v1[it]);
+                }
+            }
+        }
+    }
+    tstamp(a, 5);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -825,7 +1030,7 @@ int make_map(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld, 
 
 template <class K>
 cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y, cudaStream_t st, bool pdl,
-                     const TcBank& t, const TcMap& xh, const TcMap& xl, const TcArgs& a) {
+                     const TcBank& t, const TcMap& xh, const TcMap& xl, const TcArgs& a, bool w64 = false) {
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = grid;
     cfg.blockDim = block;
@@ -847,8 +1052,8 @@ cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y
     }
     cfg.attrs = at;
     cfg.numAttrs = na;
-    return cudaLaunchKernelEx(&cfg, kernel, *reinterpret_cast<const CUtensorMap*>(t.map_wh.bytes),
-                              *reinterpret_cast<const CUtensorMap*>(t.map_wl.bytes),
+    return cudaLaunchKernelEx(&cfg, kernel, *reinterpret_cast<const CUtensorMap*>((w64 ? t.map_wh64 : t.map_wh).bytes),
+                              *reinterpret_cast<const CUtensorMap*>((w64 ? t.map_wl64 : t.map_wl).bytes),
                               *reinterpret_cast<const CUtensorMap*>(xh.bytes), *reinterpret_cast<const CUtensorMap*>(xl.bytes), a);
 }
 
@@ -865,8 +1070,12 @@ cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y
 
 int tc_min_rows_default() { return 1; }
 
+// decode banks with nin <= 768: k_bank_wide (1, default) or the split-K cluster kernel (B2_WIDE=0)
+static int tc_wide = 1;
+
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
 int tc_init() {
+    if (const char* v = getenv("B2_WIDE")) tc_wide = atoi(v);
     void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
                      (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>,
                      (void*)k_bank_split<EPI_PLAIN_EDGE>};
@@ -885,6 +1094,12 @@ int tc_init() {
     }
     for (void* f : tiles) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_STAGES * STAGE + 1024);
+        if (e != cudaSuccess) return (int)e;
+    }
+    void* wide[] = {(void*)k_bank_wide<EPI_GAUGED>, (void*)k_bank_wide<EPI_GAUGED_EDGE>, (void*)k_bank_wide<EPI_PLAIN_ADD>,
+                    (void*)k_bank_wide<EPI_PLAIN_OUT>, (void*)k_bank_wide<EPI_PLAIN_EDGE>};
+    for (void* f : wide) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem_bytes(WIDE_MAX_KB));
         if (e != cudaSuccess) return (int)e;
     }
     return 0;
@@ -908,6 +1123,8 @@ int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
     if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
     int rc = make_map(t.map_wh, t.wh, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wl, t.wl, nin, t.nout_pad, nin, 128);
+    if (!rc) rc = make_map(t.map_wh64, t.wh, nin, t.nout_pad, nin, 64);
+    if (!rc) rc = make_map(t.map_wl64, t.wl, nin, t.nout_pad, nin, 64);
     if (rc) return rc;
     t.ready = 1;
     return 0;
@@ -967,6 +1184,8 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         mi = r.nmaps;
         int rc = make_map(r.maps[mi].h, r.xh, t.nin, r.rows_cap, r.kmax, BN);
         if (!rc) rc = make_map(r.maps[mi].l, r.xl, t.nin, r.rows_cap, r.kmax, BN);
+        if (!rc) rc = make_map(r.maps[mi].h32, r.xh, t.nin, r.rows_cap, r.kmax, WIDE_ROWS);
+        if (!rc) rc = make_map(r.maps[mi].l32, r.xl, t.nin, r.rows_cap, r.kmax, WIDE_ROWS);
         if (rc) return rc;
         r.maps[mi].k = t.nin;
         r.maps[mi].bn = BN;
@@ -993,7 +1212,21 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         for (int d = MAX_SPLIT; d >= 2; d--)
             if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
     cudaError_t err;
-    if (ksplit > 1) {
+    if (tc_wide && ntiles == 1 && mtiles < 148 && kb <= WIDE_MAX_KB && t.nout % 64 == 0) {
+        // one CTA per 64 output columns over the whole K range (no split, no cluster)
+        a.ksplit = 1;
+        a.kps = kb;
+        a.trace = trace;
+        if (heads && epi == EPI_GAUGED && !out_map) {
+            a.heads = 1;
+            a.hd = *heads;
+            if (heads_done) *heads_done = true;
+        }
+        dim3 grid(t.nout / 64, (rows + WIDE_ROWS - 1) / WIDE_ROWS);
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E>, grid, dim3(WIDE_THREADS), wide_smem_bytes(kb), 1, st, pdl, t,
+                                          r.maps[mi].h32, r.maps[mi].l32, a, true);
+                      break)
+    } else if (ksplit > 1) {
         a.ksplit = ksplit;
         a.kps = kb / ksplit;
         a.trace = trace;

@@ -26,7 +26,8 @@ struct TcBank {
     int64_t* colcorr = nullptr;  // [nout_pad]  128*sum_i w[i][j] - 16384*nin
     int64_t* colcorr_kb = nullptr;  // [nin/128][nout_pad] the same per 128-input block
     const int16_t* w16 = nullptr;  // the reference-layout bank [nin][nout] (for the +32768 correction)
-    TcMap map_wh, map_wl;
+    TcMap map_wh, map_wl;        // box: 128 bytes of K x 128 outputs
+    TcMap map_wh64, map_wl64;    // box: 128 bytes of K x 64 outputs (k_bank_wide)
 };
 
 // Row-side buffers: the activations' planes and their corrections.
@@ -38,7 +39,7 @@ struct TcRows {
     int32_t* nsat = nullptr;    // [rows_cap]  entries equal to +32768
     int16_t* sat = nullptr;     // [rows_cap][kmax] their indices
     uint32_t* err = nullptr;    // device error word (shared with the engine)
-    struct { int k, bn; TcMap h, l; } maps[4];
+    struct { int k, bn; TcMap h, l, h32, l32; } maps[4];   // per K: boxes of 64 and of 32 rows
     int nmaps = 0;
 };
 
