@@ -79,6 +79,10 @@ struct b2_handle {
     TcRows tcr{};
     int32_t *head_rows = nullptr, *race_out = nullptr;
     uint64_t* row_or = nullptr;  // decode: per bank input, the OR of |x| over each row ([4L][FUSED_ROWS])
+    int64_t* wq_acc = nullptr;   // decode, rows quantised in the bank kernels: S1, S2 per bank input ([2][4L][FUSED_ROWS])
+    int32_t* wq_nsat = nullptr;  // the +32768 count per bank input ([4L][FUSED_ROWS])
+    unsigned long long* wq_ctr = nullptr;   // arrival counters per bank input and row half ([4L][2], never reset)
+    int wq = 1;                  // decode steps of <= 64 streams quantise in the bank kernels (B2_WQ=0: quant kernels)
     PrefillBlock* pf_blocks = nullptr;   // prompt pass: blocks of consecutive positions of one stream [max_rows]
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
@@ -263,7 +267,8 @@ int bank_float_stages(const b2_handle* h, int bi) {
 // ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
 // heads (GPT-2's qkv): the split-K decode kernel may do heads16 in its epilogue; *heads_done says whether it did
 int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st,
-             const TcHeads* heads = nullptr, bool* heads_done = nullptr) {
+             const TcHeads* heads = nullptr, bool* heads_done = nullptr, const TcQuant* quant = nullptr,
+             uint64_t* or_out = nullptr) {
     const DevBank& bk = h->banks[bi];
     if (heads_done) *heads_done = false;
     if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
@@ -271,12 +276,13 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         uint64_t* tr = nullptr;
         if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) tr = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && !h->prof.timing, heads, heads_done, tr);
+                         h->pdl && !h->prof.timing, heads, heads_done, tr, quant, or_out);
         h->split_idx++;
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
     }
+    if (quant || or_out) return fail(h, B2_ERR_STATE, "bank %d: in-kernel quantisation needs the tensor-core banks", bi);
     BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
     a.flt = bank_float_stages(h, bi);
     a.sig = h->sigf;
@@ -469,7 +475,7 @@ int run_decode(b2_handle* h, int n, cudaStream_t st) {
     uint64_t* OR = h->row_or;   // slot q of the step: OR[q * FUSED_ROWS + row]
     int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
                     h->row_slot, h->row_pos, h->row_tok, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, OR, 4 * L, FUSED_ROWS,
-                    h->d_err);
+                    (int64_t*)nullptr, (int32_t*)nullptr, h->d_err);
     if (rc) return rc;
     for (int l = 0; l < L; l++) {
         uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
@@ -494,6 +500,64 @@ int run_decode(b2_handle* h, int n, cudaStream_t st) {
     if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
     return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab, (const int32_t*)nullptr,
                   c.vocab, h->race_out);
+}
+
+// ---- a decode step with the rows quantised inside the bank kernels (n <= 64 streams, row r = slot r) -------------
+// Each bank input's row OR is published by its producer (embed, attention, the banks before: atomicOr), so the
+// k_bank_wide CTAs quantise the rows themselves (shared out, then an arrival counter) instead of waiting for a
+// quant kernel (the mproj bank's 24 K blocks split over 4-CTA clusters). Only the head keeps a quant kernel.
+TcQuant wq_args(b2_handle* h, int site, const int64_t* X, int ldx, const uint64_t* xor_in) {
+    TcQuant q;
+    q.X = X;
+    q.ldx = ldx;
+    q.xor_in = xor_in;
+    q.S1 = h->wq_acc + (size_t)site * FUSED_ROWS;
+    q.S2 = h->wq_acc + (size_t)(4 * h->cfg.n_layer + site) * FUSED_ROWS;
+    q.nsat = h->wq_nsat + (size_t)site * FUSED_ROWS;
+    q.ctr = h->wq_ctr + (size_t)site * 2;
+    q.LOG2 = h->LOG2;
+    q.log768 = h->log768;
+    q.eps40 = h->eps40;
+    return q;
+}
+
+int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, L = c.n_layer, F = c.d_ff;
+    uint64_t* OR = h->row_or;   // slot q of the step: OR[q * FUSED_ROWS + row]
+    int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
+                    h->row_slot, h->row_pos, h->row_tok, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, OR, 4 * L, FUSED_ROWS,
+                    h->wq_acc, h->wq_nsat, h->d_err);
+    if (rc) return rc;
+    for (int l = 0; l < L; l++) {
+        uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
+        const TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
+        bool heads_done = false;
+        TcQuant q = wq_args(h, 4 * l, h->R, d, o0);
+        if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &q))) return rc;
+        if (!heads_done) return fail(h, B2_ERR_STATE, "qkv bank %d: heads16 not done in its epilogue", l);
+        if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st))) return rc;
+        q = wq_args(h, 4 * l + 1, h->ATT, d, o0 + FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, o0 + 2 * FUSED_ROWS)))
+            return rc;
+        q = wq_args(h, 4 * l + 2, h->R, d, o0 + 2 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 2, EPI_GAUGED_EDGE, n, h->HID, F, nullptr, st, nullptr, nullptr, &q,
+                           o0 + 3 * FUSED_ROWS)))
+            return rc;
+        uint64_t* next = l + 1 < L ? o0 + 4 * FUSED_ROWS : nullptr;
+        q = wq_args(h, 4 * l + 3, h->HID, F, o0 + 3 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, next))) return rc;
+    }
+    if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
+    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab, (const int32_t*)nullptr,
+                  c.vocab, h->race_out);
+}
+
+bool wq_ok(const b2_handle* h, int n) {
+    const b2_config& c = h->cfg;
+    return h->wq && c.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS && !h->flags &&
+           h->fuse_heads && c.d_model % 128 == 0 && c.d_model <= 768 && h->banks[4 * c.n_layer - 1].tc.ready;
 }
 
 bool mega_ok(const b2_handle* h, int n) {
@@ -606,6 +670,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
+    if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
@@ -839,7 +904,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
@@ -864,6 +929,12 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((h->flags & B2_ARRIVAL_FLOAT) && (rc = dalloc(h, &h->kv.kraw, nkv * 64))) return rc;
     if ((rc = dalloc(h, &h->row_or, (size_t)4 * L * FUSED_ROWS))) return rc;
     CK(cudaMemset(h->row_or, 0, sizeof(uint64_t) * 4 * L * FUSED_ROWS));
+    if ((rc = dalloc(h, &h->wq_acc, (size_t)2 * 4 * L * FUSED_ROWS))) return rc;
+    if ((rc = dalloc(h, &h->wq_nsat, (size_t)4 * L * FUSED_ROWS))) return rc;
+    if ((rc = dalloc(h, &h->wq_ctr, (size_t)4 * L * 2))) return rc;
+    CK(cudaMemset(h->wq_acc, 0, sizeof(int64_t) * 2 * 4 * L * FUSED_ROWS));
+    CK(cudaMemset(h->wq_nsat, 0, sizeof(int32_t) * 4 * L * FUSED_ROWS));
+    CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * L * 2));
     if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_base, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_desc, 1))) return rc;
@@ -990,6 +1061,12 @@ int step_core(b2_handle* h, int n, cudaStream_t st) {
     h->split_idx = 0;
     if (mega_ok(h, n)) {
         int rc = run_mega(h, n, st);
+        if (rc) return rc;
+        return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
+                      h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
+    }
+    if (!fused_ok(h, n) && wq_ok(h, n)) {
+        int rc = run_decode_wq(h, n, st);
         if (rc) return rc;
         return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
                       h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);

@@ -864,7 +864,7 @@ __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const i
 __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, const int32_t* __restrict__ slot_tok,
                                int32_t* row_slot, int32_t* row_pos, int32_t* row_tok, const int64_t* __restrict__ wte,
                                const int64_t* __restrict__ wpe, int d, int V, int nctx, int64_t* __restrict__ R,
-                               uint64_t* or_buf, int nor, int or_ld, uint32_t* err) {
+                               uint64_t* or_buf, int nor, int or_ld, int64_t* acc, int32_t* accn, uint32_t* err) {
     griddep_wait();
     griddep_launch();
     __shared__ uint64_t s_or[8];
@@ -883,6 +883,13 @@ __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, cons
         o |= mag(v);
     }
     for (int q = 1 + threadIdx.x; q < nor; q += blockDim.x) or_buf[(size_t)q * or_ld + s] = 0;
+    // the in-kernel quantisation's per-row accumulators of every bank input ([2][nor][or_ld] S1, S2; [nor][or_ld])
+    if (acc)
+        for (int q = threadIdx.x; q < nor; q += blockDim.x) {
+            acc[(size_t)q * or_ld + s] = 0;
+            acc[(size_t)(nor + q) * or_ld + s] = 0;
+            accn[(size_t)q * or_ld + s] = 0;
+        }
     o = warp_or64(o);
     if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
     __syncthreads();

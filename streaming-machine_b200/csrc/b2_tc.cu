@@ -36,11 +36,31 @@ struct TcArgs {
     int heads;        // EPI_GAUGED on the split path: heads16 in the epilogue (hd), no q/k/v stores
     TcHeads hd;
     uint64_t* trace;  // optional (profiling aid): %globaltimer stamps [CTA][8] of this launch
+    TcQuant q;        // k_bank_wide: quantise the rows in the kernel (q.X set) instead of reading a quant kernel's
+    uint64_t* or_out; // optional: OR of |stored value| over each output row (atomicOr), for the next bank's q.xor_in
 };
 
 B2_DEV void ld_dsmem2(uint32_t addr, uint64_t& a0, uint64_t& a1) {
     asm volatile("ld.shared::cluster.v2.u64 {%0, %1}, [%2];" : "=l"(a0), "=l"(a1) : "r"(addr));
 }
+B2_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+B2_DEV unsigned long long atom_add_release_u64(unsigned long long* p, unsigned long long v) {
+    unsigned long long old;
+    asm volatile("atom.release.gpu.global.add.u64 %0, [%1], %2;" : "=l"(old) : "l"(p), "l"(v) : "memory");
+    return old;
+}
+B2_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// to16 of one int64 given as its two 32-bit halves, by the row's shift (0..49, base2.py:24-27): add half, shift
+B2_DEV int32_t to16_halves(int lo, int hi, int sh) {
+    const uint64_t x = ((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo;
+    return sh ? (int32_t)((int64_t)(x + (1ull << (sh - 1))) >> sh) : (int32_t)(int64_t)x;
+}
+B2_DEV uint32_t hibyte16(int32_t x) { return (uint32_t)(uint8_t)(int8_t)(x == 32768 ? 127 : (x >> 8)); }
+B2_DEV uint32_t lobyte16(int32_t x) { return (uint32_t)(uint8_t)(int8_t)((x & 255) - 128); }
 // bit i of e -> bit 2i, bit i of o -> bit 2i + 1
 B2_DEV uint64_t interleave32(uint32_t e, uint32_t o) {
     uint64_t x = e, y = o;
@@ -60,7 +80,7 @@ B2_DEV uint64_t interleave32(uint32_t e, uint32_t o) {
 // profiling aid: thread 0 of the CTA stamps step k
 B2_DEV void tstamp(const TcArgs& a, int k) {
     if (a.trace && threadIdx.x == 0)
-        a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + k] = gtime();
+        a.trace[(((size_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 + k] = gtime();
 }
 
 // the 16 MMAs of one K block: 4 K steps x {wh.xh -> A1, wh.xl + wl.xh -> A2, wl.xl -> A3}
@@ -249,10 +269,19 @@ __global__ void __launch_bounds__(256, 1)
                 if (jv1) v1 = finish_value<EPI>(a, s_row[n], n, j1, (int64_t)s1, colc1, e1, b1);
             }
             if (!heads) {
+                int64_t w0 = v0, w1 = v1;
                 if (rv) {
                     int64_t* o = a.epi.out + (size_t)s_row[n].orow * a.epi.ldo + j0;
-                    if (jv0) o[0] = EPI == EPI_PLAIN_ADD ? wadd(o[0], v0) : v0;
-                    if (jv1) o[1] = EPI == EPI_PLAIN_ADD ? wadd(o[1], v1) : v1;
+                    if (EPI == EPI_PLAIN_ADD) {
+                        if (jv0) w0 = wadd(o[0], v0);
+                        if (jv1) w1 = wadd(o[1], v1);
+                    }
+                    if (jv0) o[0] = w0;
+                    if (jv1) o[1] = w1;
+                }
+                if (a.or_out) {                      // the next bank's row OR over this warp's 64 columns
+                    const uint64_t wor = warp_or64(rv ? ((jv0 ? mag(w0) : 0) | (jv1 ? mag(w1) : 0)) : 0);
+                    if (lane == 0 && rv) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
                 }
                 continue;
             }
@@ -316,7 +345,7 @@ __host__ __device__ inline int wide_smem_bytes(int nkb) {
     return (nkb * WIDE_KBLOCK > 2 * WIDE_ROWS * 64 * 8 ? nkb * WIDE_KBLOCK : 2 * WIDE_ROWS * 64 * 8) + 1024;
 }
 
-template <int EPI>
+template <int EPI, bool QUANT>
 __global__ void __launch_bounds__(WIDE_THREADS, 1)
     k_bank_wide(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
                 const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
@@ -332,8 +361,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     int64_t* LB = HB + WIDE_ROWS * 64;   // [32 rows][64 columns] L
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mt = blockIdx.x;        // output columns 64 mt .. + 64
-    const int r0 = blockIdx.y * WIDE_ROWS;   // rows r0 .. + 32
-    const int nkb = a.kps;
+    const int kz = blockIdx.y, nz = gridDim.y;   // K range: blocks kz * kps .. + kps (cluster (1, nz, 1))
+    const int r0 = blockIdx.z * WIDE_ROWS;   // rows r0 .. + 32
+    const int nkb = a.kps, kb0 = kz * nkb;
     tstamp(a, 0);
 
     if (tid == 0) {
@@ -354,8 +384,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         for (int kb = 0; kb < nkb; kb++) {
             uint8_t* st = smem + kb * WIDE_KBLOCK;
             mbar_expect_tx(&full_bar[kb], WIDE_KBLOCK);
-            tma_load_2d(st, &mwh, &full_bar[kb], kb * 128, mt * 64);
-            tma_load_2d(st + 64 * 128, &mwl, &full_bar[kb], kb * 128, mt * 64);
+            tma_load_2d(st, &mwh, &full_bar[kb], (kb0 + kb) * 128, mt * 64);
+            tma_load_2d(st + 64 * 128, &mwl, &full_bar[kb], (kb0 + kb) * 128, mt * 64);
         }
     }
     // this lane's two columns' constants (the bank's own data: read before the dependency wait)
@@ -368,13 +398,81 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     griddep_wait();
     griddep_launch();
     tstamp(a, 2);
-    if (tid == 0 && !dead) {
+    if (QUANT) {
+        // the rows' to16 and byte planes, shared out over the CTAs of this row half: item (K block kb, rows
+        // r0 + 8g ..) goes to CTA mt, mt + ntx, ..; thread t takes row 8g + t / 64, values 2 (t % 64), + 1 of the K
+        // block. The row sums go to the per-row accumulators (atomics), +32768 entries to the row's list.
+        const int ntx = gridDim.x * nz, nitems = nkb * nz * 4, cid = mt + gridDim.x * kz;
+        const int c = 2 * (tid & 63);
+        for (int it0 = cid; it0 < nitems && !dead; it0 += 2 * ntx) {
+            // up to two items per pass, both rows' loads in flight together
+            int4 v[2];
+            int n[2], kbv[2], sh[2];
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                const int it = it0 + u * ntx;
+                kbv[u] = it >> 2;
+                n[u] = it < nitems ? r0 + 8 * (it & 3) + (tid >> 6) : a.rows;
+                v[u] = make_int4(0, 0, 0, 0);
+                sh[u] = 0;
+                if (n[u] < a.rows) {
+                    sh[u] = to16_shift(a.q.xor_in[n[u]]);
+                    v[u] = *reinterpret_cast<const int4*>(a.q.X + (size_t)n[u] * a.q.ldx + kbv[u] * 128 + c);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 2; u++) {
+                if (it0 + u * ntx >= nitems) break;        // the same for the whole CTA
+                const int nn = n[u], kb = kbv[u];
+                int32_t x0 = 0, x1 = 0;
+                if (nn < a.rows) {
+                    x0 = to16_halves(v[u].x, v[u].y, sh[u]);
+                    x1 = to16_halves(v[u].z, v[u].w, sh[u]);
+                    const size_t o = (size_t)nn * a.q.kmax + kb * 128 + c;
+                    *reinterpret_cast<uint16_t*>(a.q.xh + o) = (uint16_t)(hibyte16(x0) | (hibyte16(x1) << 8));
+                    *reinterpret_cast<uint16_t*>(a.q.xl + o) = (uint16_t)(lobyte16(x0) | (lobyte16(x1) << 8));
+                    if (x0 == 32768) a.q.sat[(size_t)nn * a.q.kmax + atomicAdd(a.q.nsat + nn, 1)] = (int16_t)(kb * 128 + c);
+                    if (x1 == 32768) a.q.sat[(size_t)nn * a.q.kmax + atomicAdd(a.q.nsat + nn, 1)] = (int16_t)(kb * 128 + c + 1);
+                }
+                // a row's 64 threads are two whole warps: warp sums, one atomic per warp and sum
+                const uint32_t sq = (uint32_t)(x0 * x0) + (uint32_t)(x1 * x1);   // <= 2^31
+                const int32_t t1 = (int32_t)__reduce_add_sync(0xffffffffu, (uint32_t)(x0 + x1));
+                const uint32_t t2l = __reduce_add_sync(0xffffffffu, sq & 0xFFFFu);
+                const uint32_t t2h = __reduce_add_sync(0xffffffffu, sq >> 16);
+                if (lane == 0 && nn < a.rows) {
+                    atomicAdd((unsigned long long*)(a.q.S1 + nn), (unsigned long long)(int64_t)t1);
+                    atomicAdd((unsigned long long*)(a.q.S2 + nn), (unsigned long long)t2h * 65536ull + t2l);
+                }
+            }
+        }
+        // arrival on this row half's counter, then wait for all ntx CTAs of it (their planes and sums are complete)
+        __syncthreads();
+        if (tid == 0) {   // the release add covers the whole CTA's writes above (they happen before it: bar.sync)
+            unsigned long long* ctr = a.q.ctr + blockIdx.z;
+            const unsigned long long arrival = atom_add_release_u64(ctr, 1);
+            const unsigned long long target = (arrival / ntx + 1) * ntx;
+            if (!dead) {
+                const uint64_t t0 = gtime();
+                while (ld_acquire_u64(ctr) < target) {
+                    if (gtime() - t0 > WAIT_NS || (*(volatile uint32_t*)a.err & DERR_TIMEOUT)) {
+                        atomicOr(a.err, DERR_TIMEOUT);
+                        s_abort = 1;
+                        break;
+                    }
+                }
+            }
+            fence_proxy_async_global();   // the planes were written through the generic proxy; TMA reads them next
+        }
+        __syncthreads();
+    }
+    tstamp(a, 6);
+    if (tid == 0 && !dead && !s_abort) {
         for (int kb = 0; kb < nkb; kb++) {
             uint8_t* st = smem + kb * WIDE_KBLOCK + WIDE_A;
-            tma_load_2d(st, &mxh, &full_bar[kb], kb * 128, r0);
-            tma_load_2d(st + WIDE_ROWS * 128, &mxl, &full_bar[kb], kb * 128, r0);
+            tma_load_2d(st, &mxh, &full_bar[kb], (kb0 + kb) * 128, r0);
+            tma_load_2d(st + WIDE_ROWS * 128, &mxl, &full_bar[kb], (kb0 + kb) * 128, r0);
         }
-    } else if (warp == 1 && lane == 0 && !dead) {
+    } else if (warp == 1 && lane == 0 && !dead && !s_abort) {
         for (int kb = 0; kb < nkb; kb++) {
             if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
             tc_fence_after();
@@ -386,7 +484,25 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         mma_commit(&acc_bar);
     } else if (warp >= 2) {
         for (int q = tid - 64; q < WIDE_ROWS; q += WIDE_THREADS - 64) {
-            s_row[q] = load_row<GAUGED>(a, r0 + q);
+            if (QUANT) {
+                RowData d{0, 0, 0, 0, 0, r0 + q};
+                const int n = r0 + q;
+                if (n < a.rows) {
+                    const int64_t ex = -16 + to16_shift(a.q.xor_in[n]);
+                    const int64_t S1 = a.q.S1[n], S2 = a.q.S2[n];
+                    const int32_t ns = a.q.nsat[n];
+                    d.ex = ex;
+                    if (GAUGED) {
+                        d.LS = gauge_LS(S1, S2, (int)ex, a.q.LOG2, a.q.log768, a.q.eps40);
+                        d.e2 = __ldg(a.epi.EXP2 + (wsub(0, d.LS) & 0xFFFF));
+                    }
+                    d.rowc = 128 * (S1 - 256 * (int64_t)ns);
+                    d.nsat = ns;
+                }
+                s_row[q] = d;
+            } else {
+                s_row[q] = load_row<GAUGED>(a, r0 + q);
+            }
             if (heads) {
                 s_pos[q] = r0 + q < a.rows ? a.hd.row_pos[r0 + q] : 0;
                 s_slot[q] = r0 + q < a.rows ? a.hd.row_slot[r0 + q] : 0;
@@ -418,6 +534,37 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 64);
     tstamp(a, 4);
+    if (nz > 1) {
+        // split K: P = H + L in place, then CTA kz of the cluster sums rows kz * 32 / nz .. of every CTA's P over DSMEM
+        // and finishes them (warp w: row w % 8 of the slice, columns 32 (w / 8) + lane). Plain banks only.
+        for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
+        cluster_sync();
+        const int rs = WIDE_ROWS / nz, nl = kz * rs + (warp & 7), col = 32 * (warp >> 3) + lane;
+        const int j = mt * 64 + col, n = r0 + nl;
+        const bool live = (warp & 7) < rs && (warp >> 3) < 2 && n < a.rows && j < a.nout && go;
+        int64_t w = 0;
+        if (live) {
+            const uint32_t off = saddr(HB + nl * 64 + col);
+            uint64_t t[8];
+#pragma unroll
+            for (int p = 0; p < 8; p++) t[p] = p < nz ? (uint64_t)ld_dsmem(mapa(off, (uint32_t)p)) : 0;
+            uint64_t sum = 0;
+#pragma unroll
+            for (int p = 0; p < 8; p++) sum += t[p];
+            const int64_t colc = a.colcorr[j];
+            const int64_t v = finish_value<EPI>(a, s_row[nl], n, j, (int64_t)sum, colc, (int64_t)a.epi.e[j], a.epi.b[j]);
+            int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j;
+            w = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
+            *o = w;
+        }
+        if (a.or_out && (warp & 7) < rs && (warp >> 3) < 2) {   // the next bank's row OR over these 32 columns
+            const uint64_t wor = warp_or64(live ? mag(w) : 0);
+            if (lane == 0 && n < a.rows && go) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
+        }
+        tstamp(a, 5);
+        cluster_sync();               // no CTA leaves while a peer may still read its P
+        return;
+    }
 
     // ---- finish: warp w rows r0 + w, r0 + w + 16; lane l columns 2l, 2l + 1 of the tile ----
     const bool jv0 = cv0 && go, jv1 = cv1 && go;
@@ -435,7 +582,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             if (jv1) v1[it] = finish_value<EPI>(a, s_row[nl], n, j1, (int64_t)((uint64_t)h.y + (uint64_t)l.y), colc1, e1, b1);
         }
     }
-    tstamp(a, 6);
+    tstamp(a, 7);
     if (!heads) {
         int64_t old0[RPW], old1[RPW];
         if (EPI == EPI_PLAIN_ADD) {                  // the residual, read for every row before any store
@@ -450,10 +597,18 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
 #pragma unroll
         for (int it = 0; it < RPW; it++) {
             const int nl = warp + 16 * it, n = r0 + nl;
-            if (n >= a.rows) continue;
-            int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j0;
-            if (jv0) o[0] = EPI == EPI_PLAIN_ADD ? wadd(old0[it], v0[it]) : v0[it];
-            if (jv1) o[1] = EPI == EPI_PLAIN_ADD ? wadd(old1[it], v1[it]) : v1[it];
+            const bool rv = n < a.rows;
+            const int64_t w0 = EPI == EPI_PLAIN_ADD ? wadd(old0[it], v0[it]) : v0[it];
+            const int64_t w1 = EPI == EPI_PLAIN_ADD ? wadd(old1[it], v1[it]) : v1[it];
+            if (rv) {
+                int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j0;
+                if (jv0) o[0] = w0;
+                if (jv1) o[1] = w1;
+            }
+            if (a.or_out) {                          // the next bank's row OR over this tile's 64 columns
+                const uint64_t wor = warp_or64(rv ? ((jv0 ? mag(w0) : 0) | (jv1 ? mag(w1) : 0)) : 0);
+                if (lane == 0 && rv) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
+            }
         }
     } else {
         // heads16 (base2_stream.swift:112-119; base2.py:93): the tile is head part mt, a row's OR is this warp's
@@ -519,6 +674,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     const int S = a.stages, KB = a.kps;
     const int total = a.mtiles * a.ntiles;
     const int G = gridDim.x;
+    tstamp(a, 0);
     const int my_tiles = blockIdx.x < total ? (total - blockIdx.x + G - 1) / G : 0;
     const int nkb = my_tiles * KB;
     const int npre = nkb < S ? nkb : S;
@@ -544,8 +700,10 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
             tma_load_2d(st + A_BYTES, &mwl, &full_bar[g], kx, (t % a.mtiles) * 128);
         }
     }
+    tstamp(a, 1);
     griddep_wait();
     griddep_launch();
+    tstamp(a, 2);
     if (dead) {
         // nothing was issued; fall through to the teardown
     } else if (warp == 0) {
@@ -613,6 +771,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 512);
+    tstamp(a, 7);
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -1096,8 +1255,10 @@ int tc_init() {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_STAGES * STAGE + 1024);
         if (e != cudaSuccess) return (int)e;
     }
-    void* wide[] = {(void*)k_bank_wide<EPI_GAUGED>, (void*)k_bank_wide<EPI_GAUGED_EDGE>, (void*)k_bank_wide<EPI_PLAIN_ADD>,
-                    (void*)k_bank_wide<EPI_PLAIN_OUT>, (void*)k_bank_wide<EPI_PLAIN_EDGE>};
+    void* wide[] = {(void*)k_bank_wide<EPI_GAUGED, false>,     (void*)k_bank_wide<EPI_GAUGED_EDGE, false>,
+                    (void*)k_bank_wide<EPI_PLAIN_ADD, false>,  (void*)k_bank_wide<EPI_PLAIN_OUT, false>,
+                    (void*)k_bank_wide<EPI_PLAIN_EDGE, false>, (void*)k_bank_wide<EPI_GAUGED, true>,
+                    (void*)k_bank_wide<EPI_GAUGED_EDGE, true>, (void*)k_bank_wide<EPI_PLAIN_ADD, true>};
     for (void* f : wide) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem_bytes(WIDE_MAX_KB));
         if (e != cudaSuccess) return (int)e;
@@ -1172,7 +1333,8 @@ void tc_rows_free(TcRows& r) {
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace) {
+            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
+            uint64_t* or_out) {
     if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
     // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
@@ -1206,13 +1368,49 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     a.w16 = t.w16;
     a.err = r.err;
     a.epi = EpiArgs{ex, LS, e, b, out, ldo, out_map, EXP2, PHI};
+    a.or_out = or_out;
     // split-K over a cluster when there is one row tile and too few output tiles to fill the GPU
     int ksplit = 1;
     if (ntiles == 1 && mtiles < 148)
         for (int d = MAX_SPLIT; d >= 2; d--)
             if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
     cudaError_t err;
-    if (tc_wide && ntiles == 1 && mtiles < 148 && kb <= WIDE_MAX_KB && t.nout % 64 == 0) {
+    // k_bank_wide: K split over nz CTAs of a cluster when one CTA cannot hold all K blocks
+    int wz = 1;
+    while (wz <= MAX_SPLIT && (kb % wz || kb / wz > WIDE_MAX_KB)) wz++;
+    const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
+    const bool wide_ok = ntiles == 1 && wz <= MAX_SPLIT && WIDE_ROWS % wz == 0 && t.nout % 64 == 0 &&
+                         (t.nout / 64) * wz * wrh <= 148;
+    if (quant) {                      // the rows quantised in the kernel: only k_bank_wide does that
+        if (!wide_ok || out_map || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD) ||
+            ((uintptr_t)quant->X & 15) || (quant->ldx & 1))
+            return (int)cudaErrorInvalidValue;
+        a.q = *quant;
+        a.q.xh = r.xh;
+        a.q.xl = r.xl;
+        a.q.sat = r.sat;
+        a.q.kmax = r.kmax;
+        if (wz > 1 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
+        a.ksplit = wz;
+        a.kps = kb / wz;
+        a.trace = trace;
+        if (heads && epi == EPI_GAUGED) {
+            a.heads = 1;
+            a.hd = *heads;
+            if (heads_done) *heads_done = true;
+        }
+        dim3 grid(t.nout / 64, wz, wrh);
+        const size_t sm = wide_smem_bytes(a.kps);
+        if (epi == EPI_GAUGED)
+            err = launch_k(k_bank_wide<EPI_GAUGED, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
+                           r.maps[mi].l32, a, true);
+        else if (epi == EPI_GAUGED_EDGE)
+            err = launch_k(k_bank_wide<EPI_GAUGED_EDGE, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
+                           r.maps[mi].l32, a, true);
+        else
+            err = launch_k(k_bank_wide<EPI_PLAIN_ADD, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
+                           r.maps[mi].l32, a, true);
+    } else if (tc_wide && wide_ok && wz == 1) {
         // one CTA per 64 output columns over the whole K range (no split, no cluster)
         a.ksplit = 1;
         a.kps = kb;
@@ -1222,8 +1420,8 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             a.hd = *heads;
             if (heads_done) *heads_done = true;
         }
-        dim3 grid(t.nout / 64, (rows + WIDE_ROWS - 1) / WIDE_ROWS);
-        B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E>, grid, dim3(WIDE_THREADS), wide_smem_bytes(kb), 1, st, pdl, t,
+        dim3 grid(t.nout / 64, 1, wrh);
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E, false>, grid, dim3(WIDE_THREADS), wide_smem_bytes(kb), 1, st, pdl, t,
                                           r.maps[mi].h32, r.maps[mi].l32, a, true);
                       break)
     } else if (ksplit > 1) {
@@ -1245,6 +1443,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.ksplit = 1;
         a.kps = kb;
         a.stages = MAX_STAGES;
+        a.trace = trace;
         size_t smem = (size_t)MAX_STAGES * STAGE + 1024;
         int total = mtiles * ntiles;
         dim3 grid(total < 148 ? total : 148);

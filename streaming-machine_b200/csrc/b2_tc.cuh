@@ -81,6 +81,25 @@ struct TcHeads {
     int layer;
 };
 
+// a decode bank's rows quantised inside k_bank_wide instead of by a quant kernel before it: the rows' int64 values
+// and their ORs (complete when the kernel starts), per-row accumulators for S1, S2 and the +32768 count (zero when
+// the kernel starts), and an arrival counter per 32-row half (only ever increases). tc_bank fills in the planes.
+struct TcQuant {
+    const int64_t* X = nullptr;
+    int ldx = 0;
+    const uint64_t* xor_in = nullptr;
+    int64_t* S1 = nullptr;
+    int64_t* S2 = nullptr;
+    int32_t* nsat = nullptr;
+    unsigned long long* ctr = nullptr;   // [2]
+    const int32_t* LOG2 = nullptr;
+    int64_t log768 = 0, eps40 = 0;
+    int8_t* xh = nullptr;
+    int8_t* xl = nullptr;
+    int16_t* sat = nullptr;
+    int kmax = 0;
+};
+
 int tc_min_rows_default();
 int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
@@ -91,7 +110,7 @@ void tc_rows_free(TcRows& r);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
-            uint64_t* trace = nullptr);
+            uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr);
 int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2
