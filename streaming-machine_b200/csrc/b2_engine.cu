@@ -93,6 +93,8 @@ struct b2_handle {
     uint64_t* mega_trace = nullptr;   // B2_MEGA_TRACE=<file>: the last step's phase timestamps, written at b2_destroy
     std::string mega_trace_path;
     uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
+    uint64_t* att_trace = nullptr;    // B2_ATT_TRACE=<file>: the decode arrival's stamps of the last step ([L][CTA][8])
+    std::string att_trace_path;
     std::string split_trace_path;
     int split_idx = 0;                // split-K launches so far in this step
     int64_t* logits = nullptr;   // [n_slots][vocab]
@@ -341,6 +343,7 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st,
         return launch(h, B2_PROF_ATTEND, "attend_float", k_attend_float, grid, 64, sizeof(double) * h->max_ctx, st, aa);
     }
     const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
+    if (h->att_trace && rows <= 64) aa.trace = h->att_trace + (size_t)l * 64 * h->cfg.n_head * 8;
     if (h->att_bulk && bulk <= ATT_BULK_MAX)
         return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, true>, grid, 128, bulk, st, aa)
                   : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, false>, grid, 128, bulk, st, aa);
@@ -673,6 +676,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
+    if (const char* v = getenv("B2_ATT_TRACE")) h->att_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
     if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
@@ -883,6 +887,11 @@ int b2_finalize(b2_handle* h) {
             const size_t n = (size_t)SPLIT_TRACE_LAUNCHES * SPLIT_TRACE_SLOT;
             if (cudaMalloc(&h->split_trace, n * sizeof(uint64_t)) != cudaSuccess) h->split_trace = nullptr;
             else cudaMemset(h->split_trace, 0, n * sizeof(uint64_t));
+        }
+        if (!h->att_trace_path.empty() && !h->att_trace) {
+            const size_t n = (size_t)h->cfg.n_layer * 64 * h->cfg.n_head * 8;
+            if (cudaMalloc(&h->att_trace, n * sizeof(uint64_t)) != cudaSuccess) h->att_trace = nullptr;
+            else cudaMemset(h->att_trace, 0, n * sizeof(uint64_t));
         }
         if (h->mega.ready && !h->mega_trace_path.empty() && !h->mega_trace) {
             const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
@@ -1347,6 +1356,17 @@ void b2_destroy(b2_handle* h) {
             }
         }
         cudaFree(h->split_trace);
+    }
+    if (h->att_trace) {
+        const size_t n = (size_t)h->cfg.n_layer * 64 * h->cfg.n_head * 8;
+        std::vector<uint64_t> t(n);
+        if (cudaMemcpy(t.data(), h->att_trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost) == cudaSuccess) {
+            if (FILE* f = fopen(h->att_trace_path.c_str(), "wb")) {
+                fwrite(t.data(), sizeof(uint64_t), n, f);
+                fclose(f);
+            }
+        }
+        cudaFree(h->att_trace);
     }
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
     mega_free(h->mega);

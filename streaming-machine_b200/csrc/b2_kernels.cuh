@@ -378,6 +378,7 @@ struct AttnArgs {
     int64_t half;           // Pythia: log2(head size) / 2 at 2^-16 (the score's 1/sqrt(64) as a power)
     const int64_t* qf;      // arrival=float: the queries at full width, row r's head h at qf[r * ldq + h * 64]
     int ldq;
+    uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8] (k_attend_bulk)
 };
 
 // the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
@@ -519,18 +520,26 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
-// the arrival with the stream's keys, values and their metadata for this head brought into shared memory by four
-// bulk async copies at once (the whole run of positions 0..pos is contiguous in the store), then:
+// the arrival with the stream's keys and their metadata for this head brought into shared memory by three bulk
+// async copies at once (the whole run of positions 0..pos is contiguous in the store) and its values prefetched into
+// L2 by a fourth, then:
 //   pass 1  scores (8 lanes per key, 16-byte shared loads), the largest;   pass 1b  a = ARR[start - sc], Z = sum a;
-//   pass 2  num = sum a * v (2 dims per lane, warps split the keys);       out = power(num, -log2fix(Z)).
-// Shared memory: 408 bytes per key (positions rounded up to 4). Used while the context fits; k_attend otherwise.
+//   pass 2  num = sum a * v (2 dims per lane, warps split the keys, values read from L2, four keys in flight);
+//   out = power(num, -log2fix(Z)).
+// Shared memory: 152 bytes per key (positions rounded up to 4), so that a decode step's (row, head) CTAs fit on the
+// GPU at once. Used while the context fits; k_attend otherwise.
 // ---------------------------------------------------------------------------------------------------------------------
-constexpr int ATT_BYTES_PER_KEY = 128 + 256 + 8 + 4 + 8 + 4;
+constexpr int ATT_BYTES_PER_KEY = 128 + 8 + 4 + 8 + 4;
 
 template <int NW, bool PY>
 __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
+    uint64_t* const tr = a.trace ? a.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
+#define ASTAMP(k_) \
+    if (tr && threadIdx.x == 0) tr[k_] = gtime();
+    ASTAMP(0)
     griddep_wait();
     griddep_launch();
+    ASTAMP(1)
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ uint64_t bar;
     __shared__ int32_t qs[64];
@@ -542,11 +551,10 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     if (p < 0 || p >= a.kv.lim) return;      // flagged by the qkv bank (DERR_POS); never read past the store
     const int nk = p + 1, nkr = (nk + 3) & ~3;
     int16_t* Ks = reinterpret_cast<int16_t*>(sm);
-    int32_t* Vs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 128);
-    uint64_t* KMs = reinterpret_cast<uint64_t*>(sm + (size_t)nkr * 384);
-    int32_t* KEs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 392);
-    int64_t* SCs = reinterpret_cast<int64_t*>(sm + (size_t)nkr * 396);
-    int32_t* AVs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 404);
+    uint64_t* KMs = reinterpret_cast<uint64_t*>(sm + (size_t)nkr * 128);
+    int32_t* KEs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 136);
+    int64_t* SCs = reinterpret_cast<int64_t*>(sm + (size_t)nkr * 140);
+    int32_t* AVs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 148);
     const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
     if (tid == 0) {
         mbar_init(&bar, 1);
@@ -554,16 +562,17 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     }
     __syncthreads();
     if (tid == 0) {
-        mbar_expect_tx(&bar, (uint32_t)nkr * (128 + 256 + 8 + 4));
+        mbar_expect_tx(&bar, (uint32_t)nkr * (128 + 8 + 4));
         bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)nkr * 128, &bar);
-        bulk_g2s(Vs, a.kv.v + base * 64, (uint32_t)nkr * 256, &bar);
         bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)nkr * 8, &bar);
         bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)nkr * 4, &bar);
+        bulk_prefetch_l2(a.kv.v + base * 64, (uint32_t)nkr * 256);
     }
     if (tid < 64) qs[tid] = a.q16[(size_t)r * d + h * 64 + tid];
     const int64_t eq = a.qexp[r * H + h];
     __syncthreads();
     if (!mbar_wait(&bar, 0, a.err)) return;
+    ASTAMP(2)
 
     // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of key c*4 + (lane>>3)
     int qr[8];
@@ -593,6 +602,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     lmax = warp_max64(lmax);
     if (lane == 0) red[wid][65] = lmax;
     __syncthreads();
+    ASTAMP(3)
     int64_t start = red[0][65];
 #pragma unroll
     for (int k = 1; k < NW; k++) start = red[k][65] > start ? red[k][65] : start;
@@ -606,15 +616,34 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     }
     z = warp_sum64(z);
     __syncthreads();                 // red[][65] read by everyone; AVs complete
+    ASTAMP(4)
     if (lane == 0) red[wid][64] = z;
 
-    // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin
+    // ---- pass 2: lane holds dims 2*lane, 2*lane+1; warps take keys round-robin, four keys' values in flight
+    //      (a key whose weight is 0 adds 0, as skipping it would; Pythia's largest |v| only over weighted keys)
     int64_t n0 = 0, n1 = 0;
     uint64_t vmax = 0;
-    for (int s = wid; s < nk; s += NW) {
+    const int2* Vg = reinterpret_cast<const int2*>(a.kv.v + base * 64);
+    int s = wid;
+    for (; s + 3 * NW < nk; s += 4 * NW) {
+        int2 vv[4];
+        int64_t av[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            av[u] = AVs[s + u * NW];
+            vv[u] = Vg[(size_t)(s + u * NW) * 32 + lane];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            n0 = wadd(n0, wmul(av[u], vv[u].x));
+            n1 = wadd(n1, wmul(av[u], vv[u].y));
+            if (PY && av[u]) vmax = max(vmax, max(mag(vv[u].x), mag(vv[u].y)));
+        }
+    }
+    for (; s < nk; s += NW) {
         const int64_t av = AVs[s];
         if (!av) continue;
-        const int2 vv = reinterpret_cast<const int2*>(Vs + (size_t)s * 64)[lane];
+        const int2 vv = Vg[(size_t)s * 32 + lane];
         n0 = wadd(n0, wmul(av, vv.x));
         n1 = wadd(n1, wmul(av, vv.y));
         if (PY) vmax = max(vmax, max(mag(vv.x), mag(vv.y)));
@@ -623,6 +652,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     red[wid][2 * lane + 1] = n1;
     if (PY) { vmax = warp_max_u64(vmax); if (lane == 0) red[wid][65] = (int64_t)vmax; }
     __syncthreads();
+    ASTAMP(5)
     if (wid == 0) {
         int64_t t0 = 0, t1 = 0, zz = 0;
         uint64_t vm = 0;
@@ -643,7 +673,9 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
             const uint64_t w = warp_or64(mag(v0) | mag(v1));
             if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)w);
         }
+        ASTAMP(6)
     }
+#undef ASTAMP
 }
 
 // ---------------------------------------------------------------------------------------------------------------------

@@ -43,6 +43,10 @@ B2_DEV bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t* err) {
     atomicOr(err, DERR_TIMEOUT);
     return false;
 }
+// bring `bytes` of global memory into L2 (no shared memory, no completion; address 16-byte aligned, bytes % 16 == 0)
+B2_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)src), "r"(bytes) : "memory");
+}
 // 1-D bulk copy global -> shared, completing on an mbarrier (both addresses 16-byte aligned, bytes % 16 == 0)
 B2_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(saddr(dst)),
