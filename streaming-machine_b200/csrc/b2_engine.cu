@@ -98,6 +98,10 @@ struct b2_handle {
     std::string split_trace_path;
     int split_idx = 0;                // split-K launches so far in this step
     int64_t* logits = nullptr;   // [n_slots][vocab]
+    int64_t* race_v = nullptr;   // decode: the head epilogue's race winners per row and 32-column group
+    int32_t* race_i = nullptr;
+    int race_ld = 0;
+    int want_logits = 1;         // this call's decode steps store the logits (a caller asked for them)
     uint32_t* d_err = nullptr;
     std::vector<void*> allocs;
 
@@ -109,6 +113,7 @@ struct b2_handle {
     cudaStream_t cap_stream = nullptr;
     struct StepGraph {
         int n = 0;
+        int want_logits = 0;
         cudaGraphExec_t exec = nullptr;
         int64_t cnt[B2_PROF_N] = {0};
     } graph;
@@ -270,7 +275,7 @@ int bank_float_stages(const b2_handle* h, int bi) {
 // heads (GPT-2's qkv): the split-K decode kernel may do heads16 in its epilogue; *heads_done says whether it did
 int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st,
              const TcHeads* heads = nullptr, bool* heads_done = nullptr, const TcQuant* quant = nullptr,
-             uint64_t* or_out = nullptr) {
+             uint64_t* or_out = nullptr, const TcRace* race = nullptr) {
     const DevBank& bk = h->banks[bi];
     if (heads_done) *heads_done = false;
     if (h->use_tc && rows >= h->tc_min_rows && bk.tc.ready) {
@@ -278,13 +283,13 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         uint64_t* tr = nullptr;
         if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) tr = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && !h->prof.timing, heads, heads_done, tr, quant, or_out);
+                         h->pdl && !h->prof.timing, heads, heads_done, tr, quant, or_out, race);
         h->split_idx++;
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
     }
-    if (quant || or_out) return fail(h, B2_ERR_STATE, "bank %d: in-kernel quantisation needs the tensor-core banks", bi);
+    if (quant || or_out || race) return fail(h, B2_ERR_STATE, "bank %d: this epilogue needs the tensor-core banks", bi);
     BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
     a.flt = bank_float_stages(h, bi);
     a.sig = h->sigf;
@@ -552,9 +557,13 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, next))) return rc;
     }
     if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
-    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
-    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab, (const int32_t*)nullptr,
-                  c.vocab, h->race_out);
+    // the race inside the head's epilogue (per 32-column group), the logits stored only when the caller wants them
+    const TcRace race{h->race_v, h->race_i, h->race_ld};
+    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->want_logits ? h->logits : nullptr, c.vocab, nullptr, st, nullptr,
+                       nullptr, nullptr, nullptr, &race)))
+        return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race_parts, n, 256, 0, st, (const int64_t*)h->race_v,
+                  (const int32_t*)h->race_i, h->race_ld, h->race_ld, h->race_out);
 }
 
 bool wq_ok(const b2_handle* h, int n) {
@@ -913,7 +922,8 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
+    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->race_v,
+                   h->race_i, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
     for (void* p : old) dfree(h, p);
@@ -941,6 +951,9 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((rc = dalloc(h, &h->wq_acc, (size_t)2 * 4 * L * FUSED_ROWS))) return rc;
     if ((rc = dalloc(h, &h->wq_nsat, (size_t)4 * L * FUSED_ROWS))) return rc;
     if ((rc = dalloc(h, &h->wq_ctr, (size_t)4 * L * 2))) return rc;
+    h->race_ld = 4 * ((c.vocab + 127) / 128);
+    if ((rc = dalloc(h, &h->race_v, (size_t)FUSED_ROWS * h->race_ld))) return rc;
+    if ((rc = dalloc(h, &h->race_i, (size_t)FUSED_ROWS * h->race_ld))) return rc;
     CK(cudaMemset(h->wq_acc, 0, sizeof(int64_t) * 2 * 4 * L * FUSED_ROWS));
     CK(cudaMemset(h->wq_nsat, 0, sizeof(int32_t) * 4 * L * FUSED_ROWS));
     CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * L * 2));
@@ -1096,7 +1109,7 @@ int step_core(b2_handle* h, int n, cudaStream_t st) {
 
 // the step captured once per stream count (on an internal stream), then replayed
 int step_graph(b2_handle* h, int n, cudaStream_t st) {
-    if (h->graph.exec && h->graph.n != n) drop_graph(h);
+    if (h->graph.exec && (h->graph.n != n || h->graph.want_logits != h->want_logits)) drop_graph(h);
     if (!h->graph.exec) {
         if (!h->cap_stream) CK(cudaStreamCreateWithFlags(&h->cap_stream, cudaStreamNonBlocking));
         CK(cudaStreamSynchronize(st));
@@ -1114,6 +1127,7 @@ int step_graph(b2_handle* h, int n, cudaStream_t st) {
         cudaGraphDestroy(g);
         if (e != cudaSuccess) { h->graph.exec = nullptr; return fail(h, B2_ERR_CUDA, "step graph: %s", cudaGetErrorString(e)); }
         h->graph.n = n;
+        h->graph.want_logits = h->want_logits;
     }
     CK(cudaGraphLaunch(h->graph.exec, st));
     for (int c = 0; c < B2_PROF_N; c++) { h->prof.cnt[c] += h->graph.cnt[c]; h->prof.launches += h->graph.cnt[c]; }
@@ -1122,6 +1136,7 @@ int step_graph(b2_handle* h, int n, cudaStream_t st) {
 
 // n_steps decode steps; the words of step t go to out[s * ld + t] (out may be NULL); logits of the last step copied out
 int run_steps(b2_handle* h, int n, int n_steps, int32_t* out, int ld, int64_t* logits, cudaStream_t st) {
+    h->want_logits = logits != nullptr;
     int rc = launch(h, B2_PROF_OTHER, "gen_begin", k_gen_begin, (n + 127) / 128, 128, 0, st, n, h->slot_len, h->gen_base,
                     h->gen_desc, out, ld);
     if (rc) return rc;

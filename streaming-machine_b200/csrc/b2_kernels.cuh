@@ -877,6 +877,29 @@ __global__ void __launch_bounds__(1024) k_race(const int64_t* __restrict__ logit
     }
 }
 
+// the race over a head epilogue's per-group winners (TcRace): row r's word is the best of v[r][0..nparts), ties to the
+// lowest column
+__global__ void __launch_bounds__(256) k_race_parts(const int64_t* __restrict__ pv, const int32_t* __restrict__ pi, int ld,
+                                                    int nparts, int32_t* __restrict__ out) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ int64_t sv[8];
+    __shared__ int si[8];
+    const int r = blockIdx.x;
+    int64_t v = INT64_MIN;
+    int i = 0x7fffffff;
+    for (int t = threadIdx.x; t < nparts; t += 256) race_merge(v, i, pv[(size_t)r * ld + t], pi[(size_t)r * ld + t]);
+    warp_race(v, i);
+    if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = v; si[threadIdx.x >> 5] = i; }
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        v = threadIdx.x < 8 ? sv[threadIdx.x] : INT64_MIN;
+        i = threadIdx.x < 8 ? si[threadIdx.x] : 0x7fffffff;
+        warp_race(v, i);
+        if (threadIdx.x == 0) out[r] = i;
+    }
+}
+
 // ---------------------------------------------------------------------------------------------------------------------
 // row bookkeeping for a decode step: one row per stream slot, at the slot's next position
 // ---------------------------------------------------------------------------------------------------------------------

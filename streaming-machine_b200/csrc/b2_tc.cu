@@ -38,6 +38,7 @@ struct TcArgs {
     uint64_t* trace;  // optional (profiling aid): %globaltimer stamps [CTA][8] of this launch
     TcQuant q;        // k_bank_wide: quantise the rows in the kernel (q.X set) instead of reading a quant kernel's
     uint64_t* or_out; // optional: OR of |stored value| over each output row (atomicOr), for the next bank's q.xor_in
+    TcRace race;      // k_bank_tiles: each 32-column group's race winner per row (race.v set); out may then be null
 };
 
 B2_DEV void ld_dsmem2(uint32_t addr, uint64_t& a0, uint64_t& a1) {
@@ -179,8 +180,9 @@ __global__ void __launch_bounds__(256, 1)
             uint8_t* st = smem + kb * STAGE;
             int kx = (ks * a.kps + kb) * 128;
             mbar_expect_tx(&full_bar[kb], STAGE);
-            tma_load_2d(st, &mwh, &full_bar[kb], kx, mt * 128);
-            tma_load_2d(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128);
+            const uint64_t pol = l2_evict_first();   // a decode step reads each weight once
+            tma_load_2d_hint(st, &mwh, &full_bar[kb], kx, mt * 128, pol);
+            tma_load_2d_hint(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128, pol);
         }
     }
     // this thread's two columns' constants (the bank's own data: read before the dependency wait)
@@ -384,8 +386,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         for (int kb = 0; kb < nkb; kb++) {
             uint8_t* st = smem + kb * WIDE_KBLOCK;
             mbar_expect_tx(&full_bar[kb], WIDE_KBLOCK);
-            tma_load_2d(st, &mwh, &full_bar[kb], (kb0 + kb) * 128, mt * 64);
-            tma_load_2d(st + 64 * 128, &mwl, &full_bar[kb], (kb0 + kb) * 128, mt * 64);
+            const uint64_t pol = l2_evict_first();   // a decode step reads each weight once
+            tma_load_2d_hint(st, &mwh, &full_bar[kb], (kb0 + kb) * 128, mt * 64, pol);
+            tma_load_2d_hint(st + 64 * 128, &mwl, &full_bar[kb], (kb0 + kb) * 128, mt * 64, pol);
         }
     }
     // this lane's two columns' constants (the bank's own data: read before the dependency wait)
@@ -672,6 +675,9 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int S = a.stages, KB = a.kps;
+    // one row tile (a decode step's head): each weight is read once, so it goes first from L2; prompt passes reuse
+    // each weight tile across row tiles
+    const uint64_t wpol = a.ntiles == 1 ? l2_evict_first() : l2_evict_normal();
     const int total = a.mtiles * a.ntiles;
     const int G = gridDim.x;
     tstamp(a, 0);
@@ -696,8 +702,8 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
             const int t = blockIdx.x + (g / KB) * G, kx = (g % KB) * 128;
             uint8_t* st = smem + g * STAGE;
             mbar_expect_tx(&full_bar[g], STAGE);
-            tma_load_2d(st, &mwh, &full_bar[g], kx, (t % a.mtiles) * 128);
-            tma_load_2d(st + A_BYTES, &mwl, &full_bar[g], kx, (t % a.mtiles) * 128);
+            tma_load_2d_hint(st, &mwh, &full_bar[g], kx, (t % a.mtiles) * 128, wpol);
+            tma_load_2d_hint(st + A_BYTES, &mwl, &full_bar[g], kx, (t % a.mtiles) * 128, wpol);
         }
     }
     tstamp(a, 1);
@@ -715,8 +721,8 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
                 if (g >= npre) {
                     if (!mbar_wait(&empty_bar[s], ((g / S) - 1) & 1, a.err)) break;
                     mbar_expect_tx(&full_bar[s], STAGE);
-                    tma_load_2d(st, &mwh, &full_bar[s], kx, mt * 128);
-                    tma_load_2d(st + A_BYTES, &mwl, &full_bar[s], kx, mt * 128);
+                    tma_load_2d_hint(st, &mwh, &full_bar[s], kx, mt * 128, wpol);
+                    tma_load_2d_hint(st + A_BYTES, &mwl, &full_bar[s], kx, mt * 128, wpol);
                 }
                 tma_load_2d(st + 2 * A_BYTES, &mxh, &full_bar[s], kx, nt * BN);
                 tma_load_2d(st + 2 * A_BYTES + B_BYTES, &mxl, &full_bar[s], kx, nt * BN);
@@ -754,13 +760,47 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
             __syncwarp();
             if (!mbar_wait(&tfull[b], (i >> 1) & 1, a.err)) break;
             tc_fence_after();
-            {
-                int64_t p[16];
-                tmem_piles16(tmem + b * 256 + tq + r0, p);
+            // four rows at a time (a rolled loop keeps the epilogue's code small: it runs once per tile per warp)
+            const uint32_t tb = tmem + b * 256 + tq + r0;
+#pragma unroll 1
+            for (int q0 = 0; q0 < 16; q0 += 4) {
+                int64_t p[4];
+                int ix[4];
+                tmem_piles4(tb + q0, p);
 #pragma unroll
-                for (int q = 0; q < 16; q++) {
-                    const int n = nt * BN + r0 + q;
-                    if (n < a.rows && jv) finish<EPI>(a, s_row[e][q], n, j, p[q], colc, e_j, b_j);
+                for (int u = 0; u < 4; u++) {
+                    const int q = q0 + u, n = nt * BN + r0 + q;
+                    const bool ok = n < a.rows && jv;
+                    if (a.race.v) {
+                        // the race inside the epilogue (greedy decoding): the row's largest value over this warp's 32
+                        // columns, ties to the lowest column (base2.py:114 argmax)
+                        p[u] = ok ? finish_value<EPI>(a, s_row[e][q], n, j, p[u], colc, e_j, b_j) : INT64_MIN;
+                        ix[u] = ok ? j : 0x7fffffff;
+                        if (ok && a.epi.out) a.epi.out[(size_t)s_row[e][q].orow * a.epi.ldo + j] = p[u];
+                    } else if (ok) {
+                        finish<EPI>(a, s_row[e][q], n, j, p[u], colc, e_j, b_j);
+                    }
+                }
+                if (a.race.v) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            const int64_t ov = __shfl_xor_sync(0xffffffffu, p[u], o);
+                            const int oi = __shfl_xor_sync(0xffffffffu, ix[u], o);
+                            race_merge(p[u], ix[u], ov, oi);
+                        }
+                    }
+                    if (lane < 4) {
+                        const int64_t v = lane == 0 ? p[0] : lane == 1 ? p[1] : lane == 2 ? p[2] : p[3];
+                        const int iv = lane == 0 ? ix[0] : lane == 1 ? ix[1] : lane == 2 ? ix[2] : ix[3];
+                        const int n = nt * BN + r0 + q0 + lane;
+                        if (n < a.rows) {
+                            const size_t o = (size_t)n * a.race.ld + mt * 4 + quad;
+                            a.race.v[o] = v;
+                            a.race.i[o] = iv;
+                        }
+                    }
                 }
             }
             tc_fence_before();
@@ -847,8 +887,9 @@ __global__ void __launch_bounds__(256, 2)
             uint8_t* st = smem + kb * WSTAGE;
             int kx = (ks * a.kps + kb) * 128;
             mbar_expect_tx(&full_bar[kb], WSTAGE);
-            tma_load_2d(st, &mwh, &full_bar[kb], kx, mt * 128);
-            tma_load_2d(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128);
+            const uint64_t pol = l2_evict_first();   // a decode step reads each weight once
+            tma_load_2d_hint(st, &mwh, &full_bar[kb], kx, mt * 128, pol);
+            tma_load_2d_hint(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128, pol);
         }
     }
     griddep_wait();
@@ -1334,7 +1375,7 @@ void tc_rows_free(TcRows& r) {
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
-            uint64_t* or_out) {
+            uint64_t* or_out, const TcRace* race) {
     if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
     // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
@@ -1374,6 +1415,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     if (ntiles == 1 && mtiles < 148)
         for (int d = MAX_SPLIT; d >= 2; d--)
             if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
+    if (race && !out && !race->v) return (int)cudaErrorInvalidValue;
     cudaError_t err;
     // k_bank_wide: K split over nz CTAs of a cluster when one CTA cannot hold all K blocks
     int wz = 1;
@@ -1444,6 +1486,10 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.kps = kb;
         a.stages = MAX_STAGES;
         a.trace = trace;
+        if (race) {
+            if (epi != EPI_GAUGED || race->ld < mtiles * 4) return (int)cudaErrorInvalidValue;
+            a.race = *race;
+        }
         size_t smem = (size_t)MAX_STAGES * STAGE + 1024;
         int total = mtiles * ntiles;
         dim3 grid(total < 148 ? total : 148);

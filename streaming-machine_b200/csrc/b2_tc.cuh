@@ -100,6 +100,14 @@ struct TcQuant {
     int kmax = 0;
 };
 
+// the race fused into a bank's epilogue (the head, greedy decoding): per row, the largest value over each 32-column
+// group and its column (ties to the lowest), v[row * ld + group], i[row * ld + group]; ld >= 4 * (nout_pad / 128)
+struct TcRace {
+    int64_t* v = nullptr;
+    int32_t* i = nullptr;
+    int ld = 0;
+};
+
 int tc_min_rows_default();
 int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
@@ -110,7 +118,8 @@ void tc_rows_free(TcRows& r);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
-            uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr);
+            uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
+            const TcRace* race = nullptr);
 int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2

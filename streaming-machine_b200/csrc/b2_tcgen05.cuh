@@ -18,6 +18,26 @@ B2_DEV void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0
         "l"((uint64_t)map), "r"(saddr(bar)), "r"(c0), "r"(c1)
         : "memory");
 }
+// the same with an L2 eviction-priority hint (a policy from l2_evict_first / l2_evict_normal)
+B2_DEV void tma_load_2d_hint(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, %4}], "
+        "[%2], %5;" ::"r"(saddr(dst)),
+        "l"((uint64_t)map), "r"(saddr(bar)), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+// L2 policies: data read once per step (a decode step's weights) goes first, so that what is reused (code, tables,
+// activations, recent keys) stays
+B2_DEV uint64_t l2_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+B2_DEV uint64_t l2_evict_normal() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
 B2_DEV void tmem_alloc(uint32_t* slot, uint32_t ncols) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(saddr(slot)), "r"(ncols) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
@@ -54,6 +74,11 @@ B2_DEV void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
+}
+B2_DEV void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(taddr));
 }
 B2_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
@@ -114,6 +139,18 @@ B2_DEV void tmem_piles16(uint32_t taddr, int64_t (&p)[16]) {
     tmem_wait_ld();
 #pragma unroll
     for (int q = 0; q < 16; q++)
+        p[q] = (int64_t)(int32_t)r1[q] * 65536 + (int64_t)(int32_t)r2[q] * 256 + (int64_t)(int32_t)r3[q];
+}
+
+// the same for 4 rows (columns n0..n0+3 of each accumulator)
+B2_DEV void tmem_piles4(uint32_t taddr, int64_t (&p)[4]) {
+    uint32_t r1[4], r2[4], r3[4];
+    tmem_ld4(taddr + 0 * BN, r1);
+    tmem_ld4(taddr + 1 * BN, r2);
+    tmem_ld4(taddr + 2 * BN, r3);
+    tmem_wait_ld();
+#pragma unroll
+    for (int q = 0; q < 4; q++)
         p[q] = (int64_t)(int32_t)r1[q] * 65536 + (int64_t)(int32_t)r2[q] * 256 + (int64_t)(int32_t)r3[q];
 }
 
