@@ -132,6 +132,7 @@ namespace {
 
 constexpr int FUSED_ROWS = 64;
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
+constexpr int ATT_NW = 8;                      // warps per (row, head) CTA of the bulk-copy arrival
 constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
 constexpr int SPLIT_TRACE_LAUNCHES = 64, SPLIT_TRACE_SLOT = 160 * 8;   // B2_SPLIT_TRACE: launches x (CTAs x stamps)
 
@@ -350,8 +351,8 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st,
     const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
     if (h->att_trace && rows <= 64) aa.trace = h->att_trace + (size_t)l * 64 * h->cfg.n_head * 8;
     if (h->att_bulk && bulk <= ATT_BULK_MAX)
-        return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, true>, grid, 128, bulk, st, aa)
-                  : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<4, false>, grid, 128, bulk, st, aa);
+        return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, true>, grid, ATT_NW * 32, bulk, st, aa)
+                  : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, false>, grid, ATT_NW * 32, bulk, st, aa);
     const size_t sm = sizeof(int64_t) * h->max_ctx;
     return py ? launch(h, B2_PROF_ATTEND, "attend", k_attend<4, true>, grid, 128, sm, st, aa)
               : launch(h, B2_PROF_ATTEND, "attend", k_attend<4, false>, grid, 128, sm, st, aa);
@@ -687,8 +688,8 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
     if (const char* v = getenv("B2_ATT_TRACE")) h->att_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
-    if (cudaFuncSetAttribute(k_attend_bulk<4, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attend_bulk<4, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+    if (cudaFuncSetAttribute(k_attend_bulk<ATT_NW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_bulk<ATT_NW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||

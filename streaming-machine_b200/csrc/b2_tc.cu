@@ -401,6 +401,23 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     griddep_wait();
     griddep_launch();
     tstamp(a, 2);
+    // the residual this thread adds to, final now that the wait has returned (in-kernel quantisation: no out_map)
+    constexpr int RPW = WIDE_ROWS / (WIDE_THREADS / 32);   // rows per warp in the finish
+    int64_t pre0[RPW], pre1[RPW], pres = 0;
+    if (QUANT && EPI == EPI_PLAIN_ADD) {
+        if (nz == 1) {
+#pragma unroll
+            for (int it = 0; it < RPW; it++) {
+                const int n = r0 + warp + 16 * it;
+                const int64_t* o = a.epi.out + (size_t)(n < a.rows ? n : 0) * a.epi.ldo + j0;
+                pre0[it] = n < a.rows && cv0 ? o[0] : 0;
+                pre1[it] = n < a.rows && cv1 ? o[1] : 0;
+            }
+        } else {
+            const int n = r0 + kz * (WIDE_ROWS / nz) + (warp & 7), j = mt * 64 + 32 * (warp >> 3) + lane;
+            if ((warp & 7) < WIDE_ROWS / nz && n < a.rows && j < a.nout) pres = a.epi.out[(size_t)n * a.epi.ldo + j];
+        }
+    }
     if (QUANT) {
         // the rows' to16 and byte planes, shared out over the CTAs of this row half: item (K block kb, rows
         // r0 + 8g ..) goes to CTA mt, mt + ntx, ..; thread t takes row 8g + t / 64, values 2 (t % 64), + 1 of the K
@@ -557,7 +574,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             const int64_t colc = a.colcorr[j];
             const int64_t v = finish_value<EPI>(a, s_row[nl], n, j, (int64_t)sum, colc, (int64_t)a.epi.e[j], a.epi.b[j]);
             int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j;
-            w = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
+            w = EPI == EPI_PLAIN_ADD ? wadd(QUANT ? pres : *o, v) : v;
             *o = w;
         }
         if (a.or_out && (warp & 7) < rs && (warp >> 3) < 2) {   // the next bank's row OR over these 32 columns
@@ -571,7 +588,6 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
 
     // ---- finish: warp w rows r0 + w, r0 + w + 16; lane l columns 2l, 2l + 1 of the tile ----
     const bool jv0 = cv0 && go, jv1 = cv1 && go;
-    constexpr int RPW = WIDE_ROWS / (WIDE_THREADS / 32);   // rows per warp
     int64_t v0[RPW], v1[RPW];
 #pragma unroll
     for (int it = 0; it < RPW; it++) {
@@ -592,6 +608,11 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
 #pragma unroll
             for (int it = 0; it < RPW; it++) {
                 const int nl = warp + 16 * it, n = r0 + nl;
+                if (QUANT) {
+                    old0[it] = pre0[it];
+                    old1[it] = pre1[it];
+                    continue;
+                }
                 const int64_t* o = a.epi.out + (size_t)(n < a.rows ? s_row[nl].orow : 0) * a.epi.ldo + j0;
                 old0[it] = n < a.rows && jv0 ? o[0] : 0;
                 old1[it] = n < a.rows && jv1 ? o[1] : 0;
