@@ -286,7 +286,7 @@ def run_ours(args):
     att_bytes = B * KV_BYTES_PER_KEY * keys
     att_gbs = att_bytes / (att_ms / 1000.0) / 1e9
     traffic = None       # DRAM bytes per bank launch from the committed ncu summary of the same kernel
-    tp = os.path.join(ROOT, "profiles", "bank_split_decode_c2.md")
+    tp = os.path.join(ROOT, "profiles", "bank_wide_decode_c2.md")
     if os.path.exists(tp):
         import re
         mt = re.search(r"bank_dram_bytes_per_launch_avg:\s*(\d+)", open(tp).read())
