@@ -569,8 +569,12 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
 
 bool wq_ok(const b2_handle* h, int n) {
     const b2_config& c = h->cfg;
-    return h->wq && c.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS && !h->flags &&
-           h->fuse_heads && c.d_model % 128 == 0 && c.d_model <= 768 && h->banks[4 * c.n_layer - 1].tc.ready;
+    if (!(h->wq && c.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS && !h->flags &&
+          h->fuse_heads))
+        return false;
+    for (int bi = 0; bi < 4 * c.n_layer; bi++)
+        if (!wide_fits(h->banks[bi].tc, n)) return false;
+    return true;
 }
 
 bool mega_ok(const b2_handle* h, int n) {

@@ -1293,10 +1293,19 @@ int tc_min_rows_default() { return 1; }
 
 // decode banks with nin <= 768: k_bank_wide (1, default) or the split-K cluster kernel (B2_WIDE=0)
 static int tc_wide = 1;
+// the device's SMs: k_bank_wide's CTAs of a row half wait for one another (arrival counter), so a launch must fit
+// on the GPU at once (one CTA per SM at its shared memory)
+static int tc_sms = 148;
 
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
 int tc_init() {
     if (const char* v = getenv("B2_WIDE")) tc_wide = atoi(v);
+    {
+        int dev = 0, sms = 0;
+        if (cudaGetDevice(&dev) == cudaSuccess &&
+            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
+            tc_sms = sms;
+    }
     void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
                      (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>,
                      (void*)k_bank_split<EPI_PLAIN_EDGE>};
@@ -1393,6 +1402,18 @@ void tc_rows_free(TcRows& r) {
     r.nmaps = 0;
 }
 
+// k_bank_wide takes this bank for `rows` rows (<= 64): the K split over wz CTAs of a cluster when one CTA cannot hold
+// all K blocks, 64-column tiles, and every CTA on the GPU at once
+bool wide_fits(const TcBank& t, int rows, int* wz_out) {
+    const int kb = t.nin / 128;
+    int wz = 1;
+    while (wz <= MAX_SPLIT && (kb % wz || kb / wz > WIDE_MAX_KB)) wz++;
+    if (wz_out) *wz_out = wz;
+    const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
+    return t.ready && rows >= 1 && rows <= BN && wz <= MAX_SPLIT && WIDE_ROWS % wz == 0 && t.nout % 64 == 0 &&
+           (t.nout / 64) * wz * wrh <= tc_sms;
+}
+
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
@@ -1438,12 +1459,9 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
     if (race && !out && !race->v) return (int)cudaErrorInvalidValue;
     cudaError_t err;
-    // k_bank_wide: K split over nz CTAs of a cluster when one CTA cannot hold all K blocks
     int wz = 1;
-    while (wz <= MAX_SPLIT && (kb % wz || kb / wz > WIDE_MAX_KB)) wz++;
+    const bool wide_ok = wide_fits(t, rows, &wz);
     const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
-    const bool wide_ok = ntiles == 1 && wz <= MAX_SPLIT && WIDE_ROWS % wz == 0 && t.nout % 64 == 0 &&
-                         (t.nout / 64) * wz * wrh <= 148;
     if (quant) {                      // the rows quantised in the kernel: only k_bank_wide does that
         if (!wide_ok || out_map || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD) ||
             ((uintptr_t)quant->X & 15) || (quant->ldx & 1))

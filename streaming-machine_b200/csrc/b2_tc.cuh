@@ -115,6 +115,8 @@ void tc_bank_free(TcBank& t);
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);
 // heads (optional, EPI_GAUGED): do heads16 in the epilogue when the split-K decode kernel runs; *heads_done tells
+// whether k_bank_wide takes this bank for `rows` decode rows (the in-kernel quantisation needs it)
+bool wide_fits(const TcBank& t, int rows, int* wz = nullptr);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
