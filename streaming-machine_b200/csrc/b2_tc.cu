@@ -403,12 +403,18 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     tstamp(a, 2);
     // the residual this thread adds to, final now that the wait has returned (in-kernel quantisation: no out_map)
     constexpr int RPW = WIDE_ROWS / (WIDE_THREADS / 32);   // rows per warp in the finish
+    // the finish's rows: warp w takes rows w, w + 16 of the 32 (no split) or row 16 kz + w (2-CTA split, each CTA
+    // finishing half of the rows); 4- and 8-CTA splits finish 8-row slices with one column per thread (plain banks)
+    const int nrpw = nz == 1 ? RPW : 1;
     int64_t pre0[RPW], pre1[RPW], pres = 0;
     if (QUANT && EPI == EPI_PLAIN_ADD) {
-        if (nz == 1) {
+        if (nz <= 2) {
 #pragma unroll
             for (int it = 0; it < RPW; it++) {
-                const int n = r0 + warp + 16 * it;
+                pre0[it] = 0;
+                pre1[it] = 0;
+                if (it >= nrpw) break;
+                const int n = r0 + (nz == 1 ? warp + 16 * it : 16 * kz + warp);
                 const int64_t* o = a.epi.out + (size_t)(n < a.rows ? n : 0) * a.epi.ldo + j0;
                 pre0[it] = n < a.rows && cv0 ? o[0] : 0;
                 pre1[it] = n < a.rows && cv1 ? o[1] : 0;
@@ -554,7 +560,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 64);
     tstamp(a, 4);
-    if (nz > 1) {
+    if (nz > 2) {
         // split K: P = H + L in place, then CTA kz of the cluster sums rows kz * 32 / nz .. of every CTA's P over DSMEM
         // and finishes them (warp w: row w % 8 of the slice, columns 32 (w / 8) + lane). Plain banks only.
         for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
@@ -586,19 +592,37 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         return;
     }
 
-    // ---- finish: warp w rows r0 + w, r0 + w + 16; lane l columns 2l, 2l + 1 of the tile ----
+    if (nz == 2) {                    // P = H + L in place; the pair's tiles are complete after the barrier
+        for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
+        cluster_sync();
+    }
+
+    // ---- finish: lane l columns 2l, 2l + 1 of the tile ----
     const bool jv0 = cv0 && go, jv1 = cv1 && go;
     int64_t v0[RPW], v1[RPW];
 #pragma unroll
     for (int it = 0; it < RPW; it++) {
-        const int nl = warp + 16 * it, n = r0 + nl;
         v0[it] = 0;
         v1[it] = 0;
+        if (it >= nrpw) break;
+        const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
         if (n < a.rows && (jv0 || jv1)) {
-            const longlong2 h = *reinterpret_cast<const longlong2*>(HB + nl * 64 + 2 * lane);
-            const longlong2 l = *reinterpret_cast<const longlong2*>(LB + nl * 64 + 2 * lane);
-            if (jv0) v0[it] = finish_value<EPI>(a, s_row[nl], n, j0, (int64_t)((uint64_t)h.x + (uint64_t)l.x), colc0, e0, b0);
-            if (jv1) v1[it] = finish_value<EPI>(a, s_row[nl], n, j1, (int64_t)((uint64_t)h.y + (uint64_t)l.y), colc1, e1, b1);
+            uint64_t p0, p1;
+            if (nz == 1) {
+                const longlong2 h = *reinterpret_cast<const longlong2*>(HB + nl * 64 + 2 * lane);
+                const longlong2 l = *reinterpret_cast<const longlong2*>(LB + nl * 64 + 2 * lane);
+                p0 = (uint64_t)h.x + (uint64_t)l.x;
+                p1 = (uint64_t)h.y + (uint64_t)l.y;
+            } else {                      // this row's two partial tiles, over DSMEM
+                const uint32_t off = saddr(HB + nl * 64 + 2 * lane);
+                uint64_t a0, a1, c0, c1;
+                ld_dsmem2(mapa(off, 0), a0, a1);
+                ld_dsmem2(mapa(off, 1), c0, c1);
+                p0 = a0 + c0;
+                p1 = a1 + c1;
+            }
+            if (jv0) v0[it] = finish_value<EPI>(a, s_row[nl], n, j0, (int64_t)p0, colc0, e0, b0);
+            if (jv1) v1[it] = finish_value<EPI>(a, s_row[nl], n, j1, (int64_t)p1, colc1, e1, b1);
         }
     }
     tstamp(a, 7);
@@ -607,7 +631,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         if (EPI == EPI_PLAIN_ADD) {                  // the residual, read for every row before any store
 #pragma unroll
             for (int it = 0; it < RPW; it++) {
-                const int nl = warp + 16 * it, n = r0 + nl;
+                const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
                 if (QUANT) {
                     old0[it] = pre0[it];
                     old1[it] = pre1[it];
@@ -620,7 +644,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         }
 #pragma unroll
         for (int it = 0; it < RPW; it++) {
-            const int nl = warp + 16 * it, n = r0 + nl;
+            if (it >= nrpw) break;
+            const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
             const bool rv = n < a.rows;
             const int64_t w0 = EPI == EPI_PLAIN_ADD ? wadd(old0[it], v0[it]) : v0[it];
             const int64_t w1 = EPI == EPI_PLAIN_ADD ? wadd(old1[it], v1[it]) : v1[it];
@@ -639,7 +664,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         const int H = a.hd.kv.H, dm = H * 64, kind = mt / H, hh = mt % H, dd = 2 * lane;
 #pragma unroll
         for (int it = 0; it < RPW; it++) {
-            const int nl = warp + 16 * it, n = r0 + nl;
+            if (it >= nrpw) break;
+            const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
             const bool rv = n < a.rows && go;
             const uint64_t por = warp_or64(rv ? (mag(v0[it]) | mag(v1[it])) : 0);
             const int sh = to16_shift(por);
@@ -673,6 +699,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
         }
     }
     tstamp(a, 5);
+    if (nz == 2) cluster_sync();     // no CTA leaves while its pair may still read its P
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
@@ -1296,10 +1323,14 @@ static int tc_wide = 1;
 // the device's SMs: k_bank_wide's CTAs of a row half wait for one another (arrival counter), so a launch must fit
 // on the GPU at once (one CTA per SM at its shared memory)
 static int tc_sms = 148;
+// the in-kernel-quantising decode banks split a 768-input bank over this many CTAs when the launch still fits
+// (2: half the K blocks, MMAs, quantisation and finish per CTA, one DSMEM pair sum; 1: B2_WIDE_KZ=1)
+static int tc_wide_kz = 2;
 
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
 int tc_init() {
     if (const char* v = getenv("B2_WIDE")) tc_wide = atoi(v);
+    if (const char* v = getenv("B2_WIDE_KZ")) tc_wide_kz = atoi(v);
     {
         int dev = 0, sms = 0;
         if (cudaGetDevice(&dev) == cudaSuccess &&
@@ -1471,7 +1502,10 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.q.xl = r.xl;
         a.q.sat = r.sat;
         a.q.kmax = r.kmax;
-        if (wz > 1 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
+        int qz = wz;
+        if (qz == 1 && tc_wide_kz == 2 && kb % 2 == 0 && (t.nout / 64) * 2 * wrh <= tc_sms) qz = 2;
+        if (qz > 2 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
+        wz = qz;
         a.ksplit = wz;
         a.kps = kb / wz;
         a.trace = trace;
