@@ -1,7 +1,7 @@
 """Generate the golden vectors that pin the oracle to the reference machine.
 
-Runs ONLY in a container where the reference checkout exists (its path is the first argument, default
-/root/reference). It does what the reference's own harness does (`judge5.py:11-12`): exec `base2.py`'s source up to
+Runs ONLY where a checkout of the reference exists (its path is the first argument, or the environment variable
+B2_REFERENCE). It does what the reference's own harness does (`judge5.py:11-12`): exec `base2.py`'s source up to
 its tokenizer line to get the machine as a namespace, after exec'ing `base2_convert.py` with
 `GPT2LMHeadModel.from_pretrained` patched to hand back the seeded random-init weights of
 `streaming_machine_b200.convert.gpt2_seeded_state` (no checkpoint, no network).
@@ -12,7 +12,7 @@ Writes into this directory:
   gpt2_layer0.npz        one layer's banks, attention and edge on a 6-position prompt
   gpt2_logits_c1.npz     C1's greedy tokens and the full int64 logits at every generated position
 
-    python tests/golden/make_golden.py [/root/reference]
+    python tests/golden/make_golden.py <reference checkout>
 """
 import hashlib
 import json
@@ -85,7 +85,9 @@ def greedy(J, ids, n):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2_REFERENCE", "")
+    if not ref or not os.path.isdir(ref):
+        sys.exit("usage: give the reference checkout's path (first argument or B2_REFERENCE)")
     t0 = time.time()
     sd = convert.gpt2_seeded_state(0)
     mine = convert.convert_gpt2(sd)

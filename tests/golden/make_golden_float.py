@@ -1,7 +1,7 @@
 """Golden vectors for the float stage switches (base2.py `gauge=/edge=/arrival= float`, base2.py:66-69, 79-80,
 89-92, 110-113; pythia_base2.py `gauge=/turn=/edge=/arrival= float`, :102-104, 118-120, 130-133, 144-146).
 
-Runs ONLY where the reference checkout exists (first argument, default /root/reference). Loads the reference
+Runs ONLY where a checkout of the reference exists (first argument, or B2_REFERENCE). Loads the reference
 machines exactly as make_golden.py and make_golden_pythia.py do, once per switch setting, and records what each
 switched stage gives on the inputs of the integer layer-0 fixtures, plus a few greedy words with the switches on:
 
@@ -10,7 +10,7 @@ switched stage gives on the inputs of the integer layer-0 fixtures, plus a few g
   pythia_float.npz   gauge (ln1.0, ln1.3), turn, edge, attention with their switch; 3 greedy words of C5 stream 0's
                      first 16 ids for each switch alone and all four together
 
-    python tests/golden/make_golden_float.py [/root/reference]
+    python tests/golden/make_golden_float.py <reference checkout>
 """
 import os
 import sys
@@ -80,7 +80,9 @@ def pythia(ref, t0):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2_REFERENCE", "")
+    if not ref or not os.path.isdir(ref):
+        sys.exit("usage: give the reference checkout's path (first argument or B2_REFERENCE)")
     t0 = time.time()
     gpt2(ref, t0)
     pythia(ref, t0)

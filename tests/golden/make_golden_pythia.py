@@ -1,6 +1,6 @@
 """Golden vectors for the Pythia-160M variant (config 5), from the reference's own foundation0/pythia_base2.py.
 
-Runs ONLY where the reference checkout exists (first argument, default /root/reference). In a temporary directory
+Runs ONLY where a checkout of the reference exists (first argument, or B2_REFERENCE). In a temporary directory
 holding copies of the reference's two Pythia-160M config.json files, it execs `foundation0/pythia_convert.py` with
 `safetensors.safe_open` patched to serve `streaming_machine_b200.convert.pythia_seeded_state(0)` as both the start
 and the finished checkpoint, then execs `foundation0/pythia_base2.py` (size=160m, not as __main__) from the same
@@ -10,7 +10,7 @@ directory, and records:
   pythia_micro.npz        turn (rotary), gauge, power past 2^45 (exact big-int path), attention on a short sequence
   pythia_layer0.npz       one layer branch by branch on a 6-id prompt
 
-    python tests/golden/make_golden_pythia.py [/root/reference]
+    python tests/golden/make_golden_pythia.py <reference checkout>
 """
 import hashlib
 import json
@@ -66,7 +66,9 @@ def load_reference(ref, sd, work, argv=()):
 
 
 def main():
-    ref = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("B2_REFERENCE", "")
+    if not ref or not os.path.isdir(ref):
+        sys.exit("usage: give the reference checkout's path (first argument or B2_REFERENCE)")
     t0 = time.time()
     sd = convert.pythia_seeded_state(0)
     mine = convert.convert_pythia(sd)
