@@ -416,11 +416,28 @@ static int nthreads(int want) {
 #endif
 }
 
+/* A 64-bit digest of one row of scores: the sum over v of logit[v] * key(v) modulo 2^64, key(v) = splitmix64(v) | 1
+ * (the SplitMix64 finaliser of Steele, Lea and Flood, 2014). Odd keys make any single differing score change the
+ * digest. Lets a parity test compare every generated position of every stream without storing the scores. */
+static inline u64 hkey(u64 v) {
+    u64 z = v + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return (z ^ (z >> 31)) | 1ull;
+}
+u64 b2o_logit_hash(const i64 *lg, i64 V) {
+    u64 h = 0;
+    for (i64 v = 0; v < V; v++) h += (u64)lg[v] * hkey((u64)v);
+    return h;
+}
+
 /* Greedy generation for B independent streams of equal prompt length P (base2.py:122-123: each new word is the
  * race at the last position, fed back in). tokens: [B][n_new]; logits (optional): [B][n_new][V], the scores each
- * token was raced on. Streams run in parallel over threads; a single stream splits each bank over threads.
- * Returns 0, or -1 when memory is short or a position passes the context. */
-int b2o_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+ * token was raced on; hashes (optional): [B][n_new], their digests (b2o_logit_hash). Streams run in parallel over
+ * threads; a single stream splits each bank over threads. Returns 0, or -1 when memory is short or a position
+ * passes the context. */
+static int gen_core(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, u64 *hashes,
+                    int threads) {
     const model_t *m = (const model_t *)mv;
     int ctx = P + n_new;
     if (ctx > m->ctx || P < 1) return -1;
@@ -437,10 +454,18 @@ int b2o_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t 
             tok = position(m, &c, &s, ctx, P - 1 + t, tok, lg, par);
             tokens[(size_t)b * n_new + t] = tok;
             if (logits) memcpy(logits + ((size_t)b * n_new + t) * m->V, lg, sizeof(i64) * m->V);
+            if (hashes) hashes[(size_t)b * n_new + t] = b2o_logit_hash(lg, m->V);
         }
         cache_free(&c); scratch_free(&s); free(lg);
     }
     return err;
+}
+int b2o_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+    return gen_core(mv, ids, B, P, n_new, tokens, logits, NULL, threads);
+}
+int b2o_generate_digest(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, u64 *hashes,
+                        int threads) {
+    return gen_core(mv, ids, B, P, n_new, tokens, NULL, hashes, threads);
 }
 
 /* Teacher-forced scores (the judge5.py:15-23 pattern): one stream's P ids, the head's scores at positions
@@ -776,8 +801,10 @@ static int pposition(const pmodel_t *m, cache_t *c, pscratch_t *s, int ctx, int 
     return (int)race1(logits, m->V);
 }
 
-/* greedy words for B streams of equal prompt length (the loop of pythia_base2.py:175), logits optional */
-int b2p_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+/* greedy words for B streams of equal prompt length (the loop of pythia_base2.py:175), logits and their digests
+ * (b2o_logit_hash) optional */
+static int pgen_core(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, u64 *hashes,
+                     int threads) {
     const pmodel_t *m = (const pmodel_t *)mv;
     int ctx = P + n_new;
     if (ctx > m->ctx || P < 1) return -1;
@@ -795,10 +822,18 @@ int b2p_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t 
             if (tok == -2) { err = -2; break; }
             tokens[(size_t)b * n_new + t] = tok;
             if (logits) memcpy(logits + ((size_t)b * n_new + t) * m->V, lg, sizeof(i64) * m->V);
+            if (hashes) hashes[(size_t)b * n_new + t] = b2o_logit_hash(lg, m->V);
         }
         cache_free(&c); pscratch_free(&s); free(lg);
     }
     return err;
+}
+int b2p_generate(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, i64 *logits, int threads) {
+    return pgen_core(mv, ids, B, P, n_new, tokens, logits, NULL, threads);
+}
+int b2p_generate_digest(void *mv, const int32_t *ids, int B, int P, int n_new, int32_t *tokens, u64 *hashes,
+                        int threads) {
+    return pgen_core(mv, ids, B, P, n_new, tokens, NULL, hashes, threads);
 }
 
 /* teacher-forced scores at positions [first, last) of one stream (pythia_base2.py:151-160 with last) */

@@ -73,6 +73,13 @@ def lib():
         L.b2o_attention.restype = c_int
         L.b2o_generate.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, ctypes.c_void_p, c_int]
         L.b2o_generate.restype = c_int
+        _u64p = np.ctypeslib.ndpointer(np.uint64, flags="C_CONTIGUOUS")
+        L.b2o_generate_digest.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, _u64p, c_int]
+        L.b2o_generate_digest.restype = c_int
+        L.b2p_generate_digest.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i32p, _u64p, c_int]
+        L.b2p_generate_digest.restype = c_int
+        L.b2o_logit_hash.argtypes = [_i64p, c_i64]
+        L.b2o_logit_hash.restype = ctypes.c_uint64
         L.b2o_scores.argtypes = [c_vp, _i32p, c_int, c_int, c_int, _i64p]
         L.b2o_scores.restype = c_int
         L.b2o_greedy_recompute.argtypes = [c_vp, _i32p, c_int, c_int, _i32p, c_int]
@@ -121,6 +128,23 @@ def to16(X, e):
     x16, sh = np.empty_like(X), np.empty(X.shape[0], np.int64)
     lib().b2o_to16(X, X.shape[0], X.shape[1], int(e) if np.ndim(e) == 0 else 0, x16, sh)
     return x16, (sh if np.ndim(e) == 0 else sh + np.asarray(e, np.int64))
+
+
+def logit_hash_keys(V: int) -> np.ndarray:
+    """The digest's per-word keys (b2o_logit_hash in base2_oracle.c): SplitMix64 of the word index, forced odd."""
+    with np.errstate(over="ignore"):
+        z = np.arange(V, dtype=np.uint64) + np.uint64(0x9E3779B97F4A7C15)
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return (z ^ (z >> np.uint64(31))) | np.uint64(1)
+
+
+def logit_hash(lg) -> np.ndarray:
+    """Digest of each row of scores [..., V]: sum of logit * key modulo 2^64 (as uint64)."""
+    lg = np.ascontiguousarray(lg, dtype=np.int64)
+    k = logit_hash_keys(lg.shape[-1])
+    with np.errstate(over="ignore"):
+        return (lg.view(np.uint64) * k).sum(axis=-1, dtype=np.uint64)
 
 
 def race(v):
@@ -250,6 +274,16 @@ class Oracle:
             raise RuntimeError(f"oracle generate failed ({rc})")
         return (tok, lg) if logits else tok
 
+    def generate_digest(self, ids, n_new: int, threads: int = 0):
+        """Greedy words [B, n_new] and the digest (logit_hash) of the scores each was raced on [B, n_new]."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), dtype=np.int32)
+        B, P = ids.shape
+        tok = np.empty((B, n_new), np.int32)
+        hs = np.empty((B, n_new), np.uint64)
+        if lib().b2o_generate_digest(self.h, ids, B, P, n_new, tok, hs, threads):
+            raise RuntimeError("oracle generate_digest failed")
+        return tok, hs
+
     def forward(self, ids) -> int:
         """base2.py:102-114: the word after ids."""
         return int(self.generate(np.asarray(ids)[None, :], 1)[0, 0])
@@ -364,6 +398,16 @@ class PythiaOracle:
         if rc:
             raise RuntimeError(f"pythia oracle generate failed ({rc})")
         return (tok, lg) if logits else tok
+
+    def generate_digest(self, ids, n_new: int, threads: int = 0):
+        """Greedy words [B, n_new] and the digest (logit_hash) of the scores each was raced on [B, n_new]."""
+        ids = np.ascontiguousarray(np.atleast_2d(ids), dtype=np.int32)
+        B, P = ids.shape
+        tok = np.empty((B, n_new), np.int32)
+        hs = np.empty((B, n_new), np.uint64)
+        if lib().b2p_generate_digest(self.h, ids, B, P, n_new, tok, hs, threads):
+            raise RuntimeError("pythia oracle generate_digest failed")
+        return tok, hs
 
     def scores(self, ids, first: int, last: int):
         ids = np.ascontiguousarray(ids, dtype=np.int32)
