@@ -71,7 +71,9 @@ int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t*
 int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n);
 
 /* A scalar by its npz key: "log2_768", "eps40" (base2_convert.py:60-61); Pythia: "eps40", "half_log2_hs", "rot"
- * (16) and each norm's gain exponent "ln1.<l>.ge", "ln2.<l>.ge", "lnf.ge". */
+ * (16) and each norm's gain exponent "ln1.<l>.ge", "ln2.<l>.ge", "lnf.ge". One engine setting besides: "wait_ns",
+ * how long a device-side wait (a TMA or bulk-copy completion, a counter other CTAs raise) may take before the
+ * kernel gives up, flags the call and returns (default 0 = 0.5 s); it may be set at any time. */
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v);
 
 /* All arrays given: build the device layouts. */
@@ -138,6 +140,11 @@ int b2_profile_read(b2_handle* h, int64_t* launches, int64_t* counts, double* ms
 
 /* Wait for queued work and report any device-side check that failed since the last call. */
 int b2_sync(b2_handle* h);
+
+/* Self-check of failure detection: one kernel waits, through the engine's bounded wait, for a copy that never comes.
+ * After the "wait_ns" limit it gives up; the call returns B2_ERR_DEVICE ("bounded wait gave up") and the handle
+ * stays usable. No reference counterpart (the reference's machine has no device waits, base2.py:102-114). */
+int b2_check_wait(b2_handle* h, void* stream);
 
 const char* b2_last_error(const b2_handle* h);
 void b2_destroy(b2_handle* h);

@@ -647,7 +647,12 @@ int read_device_error(b2_handle* h) {
     if (e & DERR_POS) return fail(h, B2_ERR_CTX, "a position passed the context (device check, bits 0x%x)", e);
     if (e & DERR_VOVF) return fail(h, B2_ERR_VALUE, "a value-store entry did not fit int32 (device check, bits 0x%x)", e);
     if (e & DERR_INDEX) return fail(h, B2_ERR_VALUE, "an arrival index fell below the table (device check, bits 0x%x)", e);
-    if (e & DERR_TIMEOUT) return fail(h, B2_ERR_DEVICE, "a tensor-core kernel's bounded wait gave up (device check, bits 0x%x)", e);
+    if (e & DERR_TIMEOUT) {
+        // some CTAs of a quantising bank never arrived: its counters are out of step with the launches, so they start
+        // again from zero (nothing is in flight: every caller synchronised before reading the error word)
+        if (h->wq_ctr) CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * h->cfg.n_layer * 2));
+        return fail(h, B2_ERR_DEVICE, "a device kernel's bounded wait gave up (device check, bits 0x%x)", e);
+    }
     if (e & DERR_RANGE)
         return fail(h, B2_ERR_VALUE, "a value passed the range the reference asserts (turn input >= 2^31, a power or the "
                     "arrival's sum past int64; device check, bits 0x%x)", e);
@@ -701,8 +706,9 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
         delete h;
         return B2_ERR_CUDA;
     }
-    if (dalloc(h, &h->d_err, 1)) { delete h; return B2_ERR_NOMEM; }
-    cudaMemset(h->d_err, 0, sizeof(uint32_t));
+    // the error word [0], then (as a uint64 at [2]) the bounded waits' limit in ns (0: the kernels' default)
+    if (dalloc(h, &h->d_err, 4)) { delete h; return B2_ERR_NOMEM; }
+    cudaMemset(h->d_err, 0, 4 * sizeof(uint32_t));
     *out = h;
     return B2_OK;
 }
@@ -785,6 +791,14 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
 
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v) {
     if (!h || !name) return B2_ERR_ARG;
+    if (!strcmp(name, "wait_ns")) {   // the bounded device waits' limit (not a model scalar: finalize state unchanged)
+        if (v < 0) return fail(h, B2_ERR_ARG, "wait_ns = %lld is negative", (long long)v);
+        CK(cudaSetDevice(h->device));
+        CK(cudaDeviceSynchronize());
+        const uint64_t u = (uint64_t)v;
+        CK(cudaMemcpy(h->d_err + 2, &u, sizeof u, cudaMemcpyHostToDevice));
+        return B2_OK;
+    }
     const char* part = nullptr;
     const int ni = norm_index(h, name, &part);
     if (!strcmp(name, "log2_768")) { h->log768 = v; h->have_scalar[0] = true; }
@@ -1340,6 +1354,16 @@ int b2_profile_read(b2_handle* h, int64_t* launches, int64_t* counts, double* ms
         if (ms) ms[c] = t;
     }
     return B2_OK;
+}
+
+int b2_check_wait(b2_handle* h, void* stream) {
+    if (!h) return B2_ERR_ARG;
+    CK(cudaSetDevice(h->device));
+    cudaStream_t st = (cudaStream_t)stream;
+    int rc = launch(h, B2_PROF_OTHER, "wait_check", k_wait_check, 1, 32, 0, st, h->d_err);
+    if (rc) return rc;
+    CK(cudaStreamSynchronize(st));
+    return read_device_error(h);
 }
 
 int b2_sync(b2_handle* h) {

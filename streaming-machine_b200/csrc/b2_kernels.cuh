@@ -990,6 +990,20 @@ __global__ void k_gen_begin(int n, const int32_t* __restrict__ slot_len, int32_t
 }
 
 // after the race: the word goes straight back in (base2_stream.swift:143-146); stream lengths advance
+// b2_check_wait: the bounded wait of every TMA / bulk-copy completion (mbar_wait) on an mbarrier that expects 16
+// bytes no copy will ever bring (a flag nothing sets). The wait gives up after the handle's limit and sets
+// DERR_TIMEOUT; nothing faults and the context stays usable.
+__global__ void k_wait_check(uint32_t* err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        fence_mbar_init();
+        mbar_expect_tx(&bar, 16);
+        mbar_wait(&bar, 0, err);
+    }
+    __syncwarp();
+}
+
 __global__ void k_decode_commit(int n, const int32_t* __restrict__ word, int32_t* slot_len, int32_t* slot_tok,
                                 const GenDesc* __restrict__ desc, const int32_t* __restrict__ base) {
     griddep_wait();

@@ -87,9 +87,9 @@ B2_DEV void grid_sync(uint32_t* bar, uint32_t target, uint32_t* err) {
         __threadfence();
         red_release(bar, 1);
         if (!is_dead(err)) {
-            const uint64_t t0 = gtime();
+            const uint64_t t0 = gtime(), lim = wait_limit(err);
             while (ld_acquire(bar) < target) {
-                if (gtime() - t0 > WAIT_NS) { atomicOr(err, DERR_TIMEOUT); break; }
+                if (gtime() - t0 > lim) { atomicOr(err, DERR_TIMEOUT); break; }
                 if (is_dead(err)) break;
             }
         }

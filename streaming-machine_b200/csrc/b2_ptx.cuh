@@ -25,23 +25,35 @@ B2_DEV bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
         : "memory");
     return ok != 0;
 }
-// bounded wait: gives up after WAIT_NS of wall time (%globaltimer), sets DERR_TIMEOUT and returns false
+// bounded waits: each gives up after a limit of wall time (%globaltimer), sets DERR_TIMEOUT and returns false.
+// The limit lives beside the handle's error word (err[2..3], a uint64 in ns; 0 = WAIT_NS), so a caller can shorten it
+// (b2_set_scalar "wait_ns") without rebuilding; every kernel that waits gets the handle's error word.
 constexpr uint64_t WAIT_NS = 500ull * 1000 * 1000;
 B2_DEV uint64_t gtime() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
+B2_DEV uint64_t wait_limit(const uint32_t* err) {
+    const uint64_t v = *(const volatile uint64_t*)(err + 2);
+    return v ? v : WAIT_NS;
+}
 B2_DEV bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t* err) {
     if (mbar_try_wait(bar, phase)) return true;
-    const uint64_t t0 = gtime();
+    const uint64_t t0 = gtime(), lim = wait_limit(err);
     for (;;) {
         for (int i = 0; i < 256; i++)
             if (mbar_try_wait(bar, phase)) return true;
-        if (gtime() - t0 > WAIT_NS || (*(volatile uint32_t*)err & DERR_TIMEOUT)) break;
+        if (gtime() - t0 > lim || (*(volatile uint32_t*)err & DERR_TIMEOUT)) break;
     }
     atomicOr(err, DERR_TIMEOUT);
     return false;
+}
+// b2_profile mode 2 (in-kernel stamps): a kernel that takes a stamp slot records when its dependent work starts (the
+// first CTA out of griddepcontrol.wait); the unit of work's accumulate kernel turns consecutive starts into durations.
+// Costs one atomic per CTA and leaves the launches, graph and programmatic overlap as they are.
+B2_DEV void stamp_begin(uint64_t* slot) {
+    if (slot && threadIdx.x == 0 && threadIdx.y == 0) atomicMin((unsigned long long*)slot, (unsigned long long)gtime());
 }
 // bring `bytes` of global memory into L2 (no shared memory, no completion; address 16-byte aligned, bytes % 16 == 0)
 B2_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {

@@ -10,6 +10,8 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
+#include <mutex>
+
 #include "b2_epi.cuh"
 #include "b2_ptx.cuh"
 #include "b2_tc.cuh"
@@ -478,9 +480,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             const unsigned long long arrival = atom_add_release_u64(ctr, 1);
             const unsigned long long target = (arrival / ntx + 1) * ntx;
             if (!dead) {
-                const uint64_t t0 = gtime();
+                const uint64_t t0 = gtime(), lim = wait_limit(a.err);
                 while (ld_acquire_u64(ctr) < target) {
-                    if (gtime() - t0 > WAIT_NS || (*(volatile uint32_t*)a.err & DERR_TIMEOUT)) {
+                    if (gtime() - t0 > lim || (*(volatile uint32_t*)a.err & DERR_TIMEOUT)) {
                         atomicOr(a.err, DERR_TIMEOUT);
                         s_abort = 1;
                         break;
@@ -1320,9 +1322,23 @@ int tc_min_rows_default() { return 1; }
 
 // decode banks with nin <= 768: k_bank_wide (1, default) or the split-K cluster kernel (B2_WIDE=0)
 static int tc_wide = 1;
-// the device's SMs: k_bank_wide's CTAs of a row half wait for one another (arrival counter), so a launch must fit
-// on the GPU at once (one CTA per SM at its shared memory)
-static int tc_sms = 148;
+// k_bank_wide's CTAs of a row half wait for one another (arrival counter), so a launch must fit on the GPU at once.
+// Per device (filled by tc_init with that device current): how many k_bank_wide CTAs can be resident at once when
+// launched as clusters of 1, 2 or 4 (cudaOccupancyMaxActiveClusters at the kernel's largest shared memory, so GPC
+// partitioning is accounted for, not just the SM count).
+constexpr int TC_MAX_DEVICES = 64;
+struct WideCaps {
+    int ready = 0;
+    int ctas[MAX_SPLIT + 1] = {0};
+};
+static WideCaps tc_caps[TC_MAX_DEVICES];
+static std::mutex tc_caps_mu;
+static const WideCaps& wide_caps() {
+    static const WideCaps none{};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= TC_MAX_DEVICES) return none;
+    return tc_caps[dev];
+}
 // the in-kernel-quantising decode banks split a 768-input bank over this many CTAs when the launch still fits
 // (2: half the K blocks, MMAs, quantisation and finish per CTA, one DSMEM pair sum; 1: B2_WIDE_KZ=1)
 static int tc_wide_kz = 2;
@@ -1331,12 +1347,6 @@ static int tc_wide_kz = 2;
 int tc_init() {
     if (const char* v = getenv("B2_WIDE")) tc_wide = atoi(v);
     if (const char* v = getenv("B2_WIDE_KZ")) tc_wide_kz = atoi(v);
-    {
-        int dev = 0, sms = 0;
-        if (cudaGetDevice(&dev) == cudaSuccess &&
-            cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
-            tc_sms = sms;
-    }
     void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
                      (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>,
                      (void*)k_bank_split<EPI_PLAIN_EDGE>};
@@ -1364,6 +1374,34 @@ int tc_init() {
     for (void* f : wide) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem_bytes(WIDE_MAX_KB));
         if (e != cudaSuccess) return (int)e;
+    }
+    // this device's co-residency for k_bank_wide launches (cluster sizes 1, 2, 4)
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return (int)e;
+    if (dev < 0 || dev >= TC_MAX_DEVICES) return (int)cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(tc_caps_mu);
+    if (!tc_caps[dev].ready) {
+        WideCaps c{};
+        for (int cz = 1; cz <= 4; cz *= 2) {
+            cudaLaunchConfig_t cfg{};
+            cfg.gridDim = dim3(1, cz, 1);
+            cfg.blockDim = dim3(WIDE_THREADS);
+            cfg.dynamicSmemBytes = wide_smem_bytes(WIDE_MAX_KB);
+            cudaLaunchAttribute at[1];
+            at[0].id = cudaLaunchAttributeClusterDimension;
+            at[0].val.clusterDim.x = 1;
+            at[0].val.clusterDim.y = cz;
+            at[0].val.clusterDim.z = 1;
+            cfg.attrs = at;
+            cfg.numAttrs = 1;
+            int nc = 0;
+            e = cudaOccupancyMaxActiveClusters(&nc, (void*)k_bank_wide<EPI_PLAIN_ADD, true>, &cfg);
+            if (e != cudaSuccess) return (int)e;
+            c.ctas[cz] = nc * cz;
+        }
+        c.ready = 1;
+        tc_caps[dev] = c;
     }
     return 0;
 }
@@ -1441,8 +1479,22 @@ bool wide_fits(const TcBank& t, int rows, int* wz_out) {
     while (wz <= MAX_SPLIT && (kb % wz || kb / wz > WIDE_MAX_KB)) wz++;
     if (wz_out) *wz_out = wz;
     const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
-    return t.ready && rows >= 1 && rows <= BN && wz <= MAX_SPLIT && WIDE_ROWS % wz == 0 && t.nout % 64 == 0 &&
-           (t.nout / 64) * wz * wrh <= tc_sms;
+    const WideCaps& c = wide_caps();
+    return t.ready && c.ready && rows >= 1 && rows <= BN && wz <= 4 && WIDE_ROWS % wz == 0 && t.nout % 64 == 0 &&
+           (t.nout / 64) * wz * wrh <= c.ctas[wz];
+}
+
+// the K split of the in-kernel-quantising k_bank_wide for this bank: a function of the bank alone, never of the
+// step's row count, because the per-(bank, row half) arrival counter assumes every launch at a site adds the same
+// number of arrivals (the CTAs along x and K). A 768-input bank goes to a CTA pair when a 64-row launch of pairs
+// still fits the device at once (qkv, proj); otherwise (fc) it stays unsplit.
+static int wide_quant_split(const TcBank& t) {
+    int wz = 1;
+    wide_fits(t, BN, &wz);
+    const int kb = t.nin / 128;
+    const WideCaps& c = wide_caps();
+    if (wz == 1 && tc_wide_kz == 2 && kb % 2 == 0 && (t.nout / 64) * 2 * (BN / WIDE_ROWS) <= c.ctas[2]) wz = 2;
+    return wz;
 }
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
@@ -1502,9 +1554,9 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.q.xl = r.xl;
         a.q.sat = r.sat;
         a.q.kmax = r.kmax;
-        int qz = wz;
-        if (qz == 1 && tc_wide_kz == 2 && kb % 2 == 0 && (t.nout / 64) * 2 * wrh <= tc_sms) qz = 2;
+        const int qz = wide_quant_split(t);
         if (qz > 2 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
+        if ((t.nout / 64) * qz * wrh > wide_caps().ctas[qz]) return (int)cudaErrorInvalidValue;
         wz = qz;
         a.ksplit = wz;
         a.kps = kb / wz;

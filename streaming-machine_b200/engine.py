@@ -26,7 +26,8 @@ STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_CTX", 5:
 # every symbol include/base2.h declares
 EXPORTS = ("b2_create", "b2_set_bank", "b2_set_array", "b2_set_scalar", "b2_finalize", "b2_alloc_streams",
            "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_gauge", "b2_bank_noalloc",
-           "b2_rewind", "b2_profile", "b2_profile_read", "b2_sync", "b2_last_error", "b2_destroy", "b2_abi_version")
+           "b2_rewind", "b2_profile", "b2_profile_read", "b2_sync", "b2_check_wait", "b2_last_error", "b2_destroy",
+           "b2_abi_version")
 PROF_CLASSES = ("bank", "attend", "quant", "heads", "race", "other")
 
 
@@ -66,6 +67,7 @@ def lib():
         L.b2_profile.argtypes = [vp, ctypes.c_int]
         L.b2_profile_read.argtypes = [vp, vp, vp, vp]
         L.b2_sync.argtypes = [vp]
+        L.b2_check_wait.argtypes = [vp, vp]
         L.b2_last_error.argtypes = [vp]
         L.b2_last_error.restype = cp
         L.b2_destroy.argtypes = [vp]
@@ -198,6 +200,27 @@ class Engine:
         o = out.cpu().numpy()
         return (o, lg.cpu().numpy()) if logits else o
 
+    def prefill_device(self, prompts, logits: bool = False):
+        """prefill() with the words (and scores) left on the device as torch tensors."""
+        prompts = [list(map(int, p)) for p in prompts]
+        n = len(prompts)
+        ids = self._i32(np.concatenate([np.asarray(p, np.int32) for p in prompts]))
+        lens = self._i32([len(p) for p in prompts])
+        nxt = self.torch.empty(n, dtype=self.torch.int32, device=self.device)
+        lg = self.torch.empty((n, self.V), dtype=self.torch.int64, device=self.device) if logits else None
+        self._call("b2_prefill", self.h, ids.data_ptr(), lens.data_ptr(), n, nxt.data_ptr(),
+                   lg.data_ptr() if logits else None, self._stream())
+        return nxt, lg
+
+    def step_device(self, n: int | None = None, logits: bool = False):
+        """One new position for streams 0..n-1 with each stream's last word fed back on the device; the words (and
+        scores) as torch tensors on the device, nothing copied to the host."""
+        n = n if n is not None else self.n_streams
+        out = self.torch.empty(n, dtype=self.torch.int32, device=self.device)
+        lg = self.torch.empty((n, self.V), dtype=self.torch.int64, device=self.device) if logits else None
+        self._call("b2_step", self.h, None, n, out.data_ptr(), lg.data_ptr() if logits else None, self._stream())
+        return out, lg
+
     def generate_device(self, n: int, n_steps: int, out=None):
         """n_steps decode steps with on-device feedback; returns the [n, n_steps] int32 device tensor."""
         out = out if out is not None else self.torch.empty((n, n_steps), dtype=self.torch.int32, device=self.device)
@@ -262,3 +285,12 @@ class Engine:
 
     def sync(self):
         self._call("b2_sync", self.h)
+
+    def set_wait_limit(self, ns: int):
+        """How long a device-side wait may take before the kernel gives up and the call reports B2_ERR_DEVICE
+        (0 = the default, 0.5 s)."""
+        self._call("b2_set_scalar", self.h, b"wait_ns", int(ns))
+
+    def check_wait(self):
+        """Run the bounded-wait self-check (a wait nothing satisfies): raises B2Error(ERR_DEVICE) once it gives up."""
+        self._call("b2_check_wait", self.h, self._stream())
