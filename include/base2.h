@@ -104,8 +104,7 @@ int b2_step_host(b2_handle* h, const int32_t* tok_in, int32_t n_streams, int32_t
 
 /* One bank on given rows, for unit parity (base2.py:62-76): mode 0 = gauged_bank, 1 = gauged_bank then edge,
  * 2 = plain_bank, 3 = plain_bank then edge (Pythia's fc, pythia_base2.py:166; Pythia takes modes 2 and 3 only).
- * X [rows][nin] int64, out [rows][nout] int64 (device pointers). mode | 8 runs the decode step's fused kernel instead
- * (GPT-2, rows <= 64, layer banks only; mode 1 only on fc banks). */
+ * X [rows][nin] int64, out [rows][nout] int64 (device pointers). */
 int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int64_t* out, int32_t mode, void* stream);
 
 /* Pythia's layer norm on given rows (pythia_base2.py:100-110, gauge(R, name)): name "ln1.<l>", "ln2.<l>" or "lnf";

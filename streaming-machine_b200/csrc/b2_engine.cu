@@ -16,7 +16,6 @@
 
 #include "../../include/base2.h"
 #include "b2_kernels.cuh"
-#include "b2_mega.cuh"
 #include "b2_tc.cuh"
 
 using namespace b2;
@@ -86,12 +85,7 @@ struct b2_handle {
     PrefillBlock* pf_blocks = nullptr;   // prompt pass: blocks of consecutive positions of one stream [max_rows]
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
-    int fused = 0;               // decode steps of <= FUSED_ROWS streams use the fused tensor-core banks (B2_FUSED=1)
     int fuse_heads = 1;          // GPT-2 decode: heads16 in the qkv bank's epilogue (B2_FUSE_HEADS=0: its own kernel)
-    int use_mega = 0;            // decode steps of <= 64 streams as one persistent kernel (B2_MEGA=1)
-    MegaPlan mega;
-    uint64_t* mega_trace = nullptr;   // B2_MEGA_TRACE=<file>: the last step's phase timestamps, written at b2_destroy
-    std::string mega_trace_path;
     uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
     uint64_t* att_trace = nullptr;    // B2_ATT_TRACE=<file>: the decode arrival's stamps of the last step ([L][CTA][8])
     std::string att_trace_path;
@@ -444,73 +438,6 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
     return launch(h, B2_PROF_RACE, "race", k_race, nhead, 1024, 0, st, logits, c.vocab, hmap, c.vocab, words_by_slot);
 }
 
-// ---- a decode step with the fused banks (n <= FUSED_ROWS streams, row r = slot r) ---------------------------------------
-FusedArgs fused_args(b2_handle* h, const DevBank& bk, const int64_t* X, const uint64_t* xor_in, uint64_t* or_out,
-                     int64_t* out, int ldo, int n) {
-    FusedArgs a{};
-    a.rows = n;
-    a.X = X;
-    a.xor_in = xor_in;
-    a.or_out = or_out;
-    a.e = bk.e;
-    a.b = bk.b;
-    a.out = out;
-    a.ldo = ldo;
-    a.EXP2 = h->EXP2;
-    a.PHI = h->PHI;
-    a.LOG2 = h->LOG2;
-    a.log768 = h->log768;
-    a.eps40 = h->eps40;
-    a.row_slot = h->row_slot;
-    a.row_pos = h->row_pos;
-    a.kv = h->kv;
-    a.err = h->d_err;
-    return a;
-}
-
-int run_fused(b2_handle* h, int bi, int epi, FusedArgs a, cudaStream_t st) {
-    if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) a.trace = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
-    h->split_idx++;
-    prof_begin(h, B2_PROF_BANK, st);
-    int rc = tc_fused(h->banks[bi].tc, epi, a, st, h->pdl && !h->prof.timing);
-    prof_end(h, B2_PROF_BANK, st);
-    if (rc) return fail(h, B2_ERR_CUDA, "fused bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
-    return B2_OK;
-}
-
-int run_decode(b2_handle* h, int n, cudaStream_t st) {
-    const b2_config& c = h->cfg;
-    const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
-    uint64_t* OR = h->row_or;   // slot q of the step: OR[q * FUSED_ROWS + row]
-    int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
-                    h->row_slot, h->row_pos, h->row_tok, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, OR, 4 * L, FUSED_ROWS,
-                    (int64_t*)nullptr, (int32_t*)nullptr, h->d_err);
-    if (rc) return rc;
-    for (int l = 0; l < L; l++) {
-        uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
-        FusedArgs q = fused_args(h, h->banks[4 * l], h->R, o0, nullptr, nullptr, 0, n);
-        q.layer = l;
-        q.q16 = h->q16;
-        q.qexp = h->qexp;
-        if ((rc = run_fused(h, 4 * l, EPI_GAUGED, q, st))) return rc;
-        if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st))) return rc;
-        if ((rc = run_fused(h, 4 * l + 1, EPI_PLAIN_ADD,
-                            fused_args(h, h->banks[4 * l + 1], h->ATT, o0 + FUSED_ROWS, o0 + 2 * FUSED_ROWS, h->R, d, n), st)))
-            return rc;
-        if ((rc = run_fused(h, 4 * l + 2, EPI_GAUGED_EDGE,
-                            fused_args(h, h->banks[4 * l + 2], h->R, o0 + 2 * FUSED_ROWS, o0 + 3 * FUSED_ROWS, h->HID, F, n), st)))
-            return rc;
-        uint64_t* next = l + 1 < L ? o0 + 4 * FUSED_ROWS : nullptr;
-        if ((rc = run_fused(h, 4 * l + 3, EPI_PLAIN_ADD,
-                            fused_args(h, h->banks[4 * l + 3], h->HID, o0 + 3 * FUSED_ROWS, next, h->R, d, n), st)))
-            return rc;
-    }
-    if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
-    if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
-    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab, (const int32_t*)nullptr,
-                  c.vocab, h->race_out);
-}
-
 // ---- a decode step with the rows quantised inside the bank kernels (n <= 64 streams, row r = slot r) -------------
 // Each bank input's row OR is published by its producer (embed, attention, the banks before: atomicOr), so the
 // k_bank_wide CTAs quantise the rows themselves (shared out, then an arrival counter) instead of waiting for a
@@ -577,60 +504,6 @@ bool wq_ok(const b2_handle* h, int n) {
     return true;
 }
 
-bool mega_ok(const b2_handle* h, int n) {
-    return h->use_mega && h->mega.ready && h->cfg.kind == B2_GPT2 && !h->flags && n <= 64 && h->tc_min_rows <= 1 &&
-           mega_att_slot_bytes(h->max_ctx) > 0;
-}
-
-// the decode step for n <= 64 streams (row r = slot r) as one persistent kernel, then the head and the race
-int run_mega(b2_handle* h, int n, cudaStream_t st) {
-    const b2_config& c = h->cfg;
-    MegaArgs a{};
-    a.L = c.n_layer;
-    a.H = c.n_head;
-    a.d = c.d_model;
-    a.F = c.d_ff;
-    a.rows = n;
-    a.slot_len = h->slot_len;
-    a.slot_tok = h->slot_tok;
-    a.row_slot = h->row_slot;
-    a.row_pos = h->row_pos;
-    a.row_tok = h->row_tok;
-    a.wte = h->wte;
-    a.wpe = h->wpe;
-    a.vocab = c.vocab;
-    a.nctx = c.n_ctx;
-    a.R = h->R;
-    a.ATT = h->ATT;
-    a.HID = h->HID;
-    a.OR = h->row_or;
-    a.q16 = h->q16;
-    a.qexp = h->qexp;
-    a.kv = h->kv;
-    a.EXP2 = h->EXP2;
-    a.PHI = h->PHI;
-    a.LOG2 = h->LOG2;
-    a.ARR = h->ARR;
-    a.alen = h->alen;
-    a.log768 = h->log768;
-    a.eps40 = h->eps40;
-    a.err = h->d_err;
-    a.trace = h->mega_trace;
-    prof_begin(h, B2_PROF_BANK, st);
-    int rc = mega_launch(h->mega, a, st);
-    prof_end(h, B2_PROF_BANK, st);
-    if (rc) return fail(h, B2_ERR_CUDA, "decode-step kernel: %s", cudaGetErrorString((cudaError_t)rc));
-    if ((rc = run_quant(h, h->R, c.d_model, nullptr, n, 1, st))) return rc;
-    if ((rc = run_bank(h, 4 * c.n_layer, EPI_GAUGED, n, h->logits, c.vocab, nullptr, st))) return rc;
-    return launch(h, B2_PROF_RACE, "race", k_race, n, 1024, 0, st, (const int64_t*)h->logits, c.vocab,
-                  (const int32_t*)nullptr, c.vocab, h->race_out);
-}
-
-bool fused_avail(const b2_handle* h, int n) {
-    return h->cfg.kind == B2_GPT2 && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS;
-}
-bool fused_ok(const b2_handle* h, int n) { return h->fused && fused_avail(h, n); }
-
 int ensure_ready(b2_handle* h) {
     if (!h) return B2_ERR_ARG;
     if (!h->finalized) return fail(h, B2_ERR_STATE, "b2_finalize has not been called");
@@ -688,12 +561,9 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (cfg->kind == B2_PYTHIA) h->norms.resize(2 * cfg->n_layer + 1);
     if (const char* v = getenv("B2_PDL")) h->pdl = atoi(v);
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
-    if (const char* v = getenv("B2_FUSED")) h->fused = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
-    if (const char* v = getenv("B2_MEGA")) h->use_mega = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
-    if (const char* v = getenv("B2_MEGA_TRACE")) h->mega_trace_path = v;
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
     if (const char* v = getenv("B2_ATT_TRACE")) h->att_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
@@ -898,18 +768,7 @@ int b2_finalize(b2_handle* h) {
     }
     CK(cudaDeviceSynchronize());
     h->tc_min_rows = tc_ok ? tc_min_rows_default() : (1 << 30);
-    mega_free(h->mega);
     if (tc_ok && h->cfg.kind == B2_GPT2 && !h->flags) {
-        // the one-kernel decode step; without it (a plan that does not fit) decode runs as separate launches
-        std::vector<TcBank> tcs;
-        std::vector<const int32_t*> es;
-        std::vector<const int64_t*> bs;
-        for (int i = 0; i < 4 * h->cfg.n_layer; i++) {
-            tcs.push_back(h->banks[i].tc);
-            es.push_back(h->banks[i].e);
-            bs.push_back(h->banks[i].b);
-        }
-        if (mega_plan(h->mega, tcs.data(), es.data(), bs.data(), h->cfg.n_layer)) mega_free(h->mega);
         cudaGetLastError();
         if (!h->split_trace_path.empty() && !h->split_trace) {
             const size_t n = (size_t)SPLIT_TRACE_LAUNCHES * SPLIT_TRACE_SLOT;
@@ -920,11 +779,6 @@ int b2_finalize(b2_handle* h) {
             const size_t n = (size_t)h->cfg.n_layer * 64 * h->cfg.n_head * 8;
             if (cudaMalloc(&h->att_trace, n * sizeof(uint64_t)) != cudaSuccess) h->att_trace = nullptr;
             else cudaMemset(h->att_trace, 0, n * sizeof(uint64_t));
-        }
-        if (h->mega.ready && !h->mega_trace_path.empty() && !h->mega_trace) {
-            const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
-            if (cudaMalloc(&h->mega_trace, n * sizeof(uint64_t)) != cudaSuccess) h->mega_trace = nullptr;
-            else cudaMemset(h->mega_trace, 0, n * sizeof(uint64_t));
         }
     }
     const char* env = getenv("B2_TC_MIN_ROWS");
@@ -1100,20 +954,8 @@ namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
 int step_core(b2_handle* h, int n, cudaStream_t st) {
     h->split_idx = 0;
-    if (mega_ok(h, n)) {
-        int rc = run_mega(h, n, st);
-        if (rc) return rc;
-        return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
-                      h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
-    }
-    if (!fused_ok(h, n) && wq_ok(h, n)) {
+    if (wq_ok(h, n)) {
         int rc = run_decode_wq(h, n, st);
-        if (rc) return rc;
-        return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
-                      h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
-    }
-    if (fused_ok(h, n)) {
-        int rc = run_decode(h, n, st);
         if (rc) return rc;
         return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
                       h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
@@ -1203,24 +1045,12 @@ int b2_bank(b2_handle* h, const char* name, const int64_t* X, int32_t rows, int6
     int rc = ensure_ready(h);
     if (rc) return rc;
     int bi = bank_index(h, name);
-    const int fusedm = mode & 8;
-    mode &= 7;
     if (bi < 0 || !X || !out || rows < 1 || rows > h->max_rows || mode < 0 || mode > 3)
         return fail(h, B2_ERR_ARG, "b2_bank: bad argument");
-    if (h->cfg.kind == B2_PYTHIA && (mode < 2 || fusedm))
+    if (h->cfg.kind == B2_PYTHIA && mode < 2)
         return fail(h, B2_ERR_ARG, "b2_bank: Pythia's banks are plain (modes 2 and 3); its norm is b2_gauge");
     cudaStream_t st = (cudaStream_t)stream;
     const DevBank& bk = h->banks[bi];
-    if (fusedm) {
-        // the fused decode kernel on its own: rows <= 64, not the head, q/k/v values returned (no key/value append)
-        if (rows > FUSED_ROWS || bi == 4 * h->cfg.n_layer || !fused_avail(h, rows) || mode == 3 || (mode == 1) != (bi % 4 == 2))
-            return fail(h, B2_ERR_ARG, "b2_bank: the fused kernel takes <= %d rows of a layer bank", FUSED_ROWS);
-        uint64_t* xor_in = h->row_or;
-        if ((rc = launch(h, B2_PROF_QUANT, "row_or", k_row_or, rows, 256, 0, st, X, bk.nin, rows, xor_in))) return rc;
-        if (mode == 2) CK(cudaMemsetAsync(out, 0, sizeof(int64_t) * rows * bk.nout, st));
-        FusedArgs a = fused_args(h, bk, X, xor_in, nullptr, out, bk.nout, rows);
-        return run_fused(h, bi, mode == 0 ? EPI_GAUGED : (mode == 1 ? EPI_GAUGED_EDGE : EPI_PLAIN_ADD), a, st);
-    }
     if ((rc = run_quant(h, X, bk.nin, nullptr, rows, mode < 2, st))) return rc;
     const int epi[4] = {EPI_GAUGED, EPI_GAUGED_EDGE, EPI_PLAIN_OUT, EPI_PLAIN_EDGE};
     return run_bank(h, bi, epi[mode], rows, out, bk.nout, nullptr, st);
@@ -1379,17 +1209,6 @@ void b2_destroy(b2_handle* h) {
     cudaDeviceSynchronize();
     drop_graph(h);
     if (h->cap_stream) cudaStreamDestroy(h->cap_stream);
-    if (h->mega_trace) {
-        const size_t n = (size_t)MEGA_CS * h->mega.nclusters * MEGA_MAX_PHASES * MEGA_STAMPS;
-        std::vector<uint64_t> t(n);
-        if (cudaMemcpy(t.data(), h->mega_trace, n * sizeof(uint64_t), cudaMemcpyDeviceToHost) == cudaSuccess) {
-            if (FILE* f = fopen(h->mega_trace_path.c_str(), "wb")) {
-                fwrite(t.data(), sizeof(uint64_t), n, f);
-                fclose(f);
-            }
-        }
-        cudaFree(h->mega_trace);
-    }
     if (h->split_trace) {
         const size_t n = (size_t)SPLIT_TRACE_LAUNCHES * SPLIT_TRACE_SLOT;
         std::vector<uint64_t> t(n);
@@ -1413,7 +1232,6 @@ void b2_destroy(b2_handle* h) {
         cudaFree(h->att_trace);
     }
     for (auto& bk : h->banks) tc_bank_free(bk.tc);
-    mega_free(h->mega);
     tc_rows_free(h->tcr);
     for (int c = 0; c < B2_PROF_N; c++)
         for (auto& p : h->prof.ev[c]) { cudaEventDestroy(p.first); cudaEventDestroy(p.second); }

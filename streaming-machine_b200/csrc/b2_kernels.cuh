@@ -955,24 +955,6 @@ __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, cons
     }
 }
 
-// the OR of |X| over each row (the fused banks' to16 shift when called on their own, b2_bank)
-__global__ void k_row_or(const int64_t* __restrict__ X, int n, int rows, uint64_t* out) {
-    griddep_wait();
-    griddep_launch();
-    __shared__ uint64_t s_or[8];
-    const int r = blockIdx.x;
-    if (r >= rows) return;
-    uint64_t o = 0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) o |= mag(X[(size_t)r * n + i]);
-    o = warp_or64(o);
-    if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        uint64_t all = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); w++) all |= s_or[w];
-        out[r] = all;
-    }
-}
 
 // where a decode step's words go: out[s * ld + (slot_len[s] - base[s])], set once per call (k_gen_begin), so one
 // captured step graph serves every call and every position

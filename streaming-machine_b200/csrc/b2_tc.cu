@@ -864,355 +864,6 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     tstamp(a, 7);
 }
 
-// ---------------------------------------------------------------------------------------------------------------------
-// Decode banks, fused (rows <= 64): the previous bank's output arrives as int64 values plus, per row, the OR of their
-// magnitudes (published by its producer with atomicOr). Each CTA of a (1, ksplit, 1) cluster owns 1-3 K blocks:
-//   prologue  weights by TMA (before the dependency wait); the activations of its K range read from global, to16'd with
-//             the row's shift and split into the two signed byte planes straight into SWIZZLE_128B shared memory;
-//             partial S1, S2 (the gauge), the row correction and a bit mask of +32768 entries, per row;
-//   MMA       16 per K block into three TMEM accumulators;
-//   partial   65536*A1 + 256*A2 + A3 + this K range's column and row corrections + 256*w for its +32768 entries
-//             (w read back from its own shared-memory planes), parked in shared memory;
-//   reduce    after a cluster barrier each CTA sums a 1/ksplit slice of the rows over DSMEM (and the row's S1, S2),
-//             finishes them (gauge, power, bias, bend or residual add) and publishes the next bank's row OR; the qkv
-//             bank instead splits its rows into q16 / k16 / v (the Metal engine's heads16) and appends k, v to the
-//             key/value store.
-// ---------------------------------------------------------------------------------------------------------------------
-
-// to16 of one int64 (its two 32-bit halves) by the row's shift (0..49, base2.py:24-27): add half, shift
-B2_DEV int32_t to16v(int lo, int hi, int sh) {
-    const uint64_t x = ((uint64_t)(uint32_t)hi << 32) | (uint32_t)lo;
-    return sh ? (int32_t)((int64_t)(x + (1ull << (sh - 1))) >> sh) : (int32_t)(int64_t)x;
-}
-B2_DEV uint32_t hbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)(x == 32768 ? 127 : (x >> 8)); }
-B2_DEV uint32_t lbyte(int32_t x) { return (uint32_t)(uint8_t)(int8_t)((x & 255) - 128); }
-B2_DEV void st_shared_u16(uint32_t addr, uint32_t v) { asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "h"((uint16_t)v) : "memory"); }
-
-template <int EPI>
-__global__ void __launch_bounds__(256, 2)
-    k_bank_fused(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl, const FusedArgs a) {
-    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
-    constexpr int WSTAGE = 2 * A_BYTES;               // weight planes of one K block
-    extern __shared__ uint8_t smem_raw[];
-    __shared__ uint64_t full_bar[MAX_KPS], acc_bar;
-    __shared__ uint32_t tmem_slot;
-    __shared__ int s_dead, s_abort;
-    __shared__ int s_sh[BN];
-    __shared__ int64_t s_S1[BN], s_S2[BN], s_rowc[BN];
-    __shared__ uint32_t s_sat[BN][MAX_KPS * 4];       // +32768 entries: bit k of this CTA's K range, per row
-    __shared__ int64_t s_LS[BN], s_e2[BN];
-    __shared__ unsigned long long s_satrows;       // bit n: row n has a +32768 entry in this CTA's K range
-    uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* xplanes = smem + a.kps * WSTAGE;         // [kps][2][BN x 128] activation planes
-    int64_t* P = (int64_t*)smem;                      // [BN][128] partial tile, over everything once used
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x, ks = blockIdx.y;
-    const uint32_t crank = cluster_rank();
-    if (a.trace && tid == 0) a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + 0] = gtime();
-#define FSTAMP(k_) \
-    if (a.trace && tid == 0) a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + (k_)] = gtime();
-
-    if (tid == 0) {
-        for (int kb = 0; kb < a.kps; kb++) mbar_init(&full_bar[kb], 1);
-        mbar_init(&acc_bar, 1);
-        s_abort = 0;
-        s_satrows = 0;
-        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
-        fence_mbar_init();
-    }
-    if (tid < BN) {
-        s_S1[tid] = 0;
-        s_S2[tid] = 0;
-        s_rowc[tid] = 0;
-        for (int w = 0; w < MAX_KPS * 4; w++) s_sat[tid][w] = 0;
-    }
-    if (warp == 0) tmem_alloc(&tmem_slot, 256);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    const uint32_t tmem = tmem_slot;
-    const bool dead = s_dead != 0;
-    if (tid == 0 && !dead) {          // weights: independent of earlier kernels
-        for (int kb = 0; kb < a.kps; kb++) {
-            uint8_t* st = smem + kb * WSTAGE;
-            int kx = (ks * a.kps + kb) * 128;
-            mbar_expect_tx(&full_bar[kb], WSTAGE);
-            const uint64_t pol = l2_evict_first();   // a decode step reads each weight once
-            tma_load_2d_hint(st, &mwh, &full_bar[kb], kx, mt * 128, pol);
-            tma_load_2d_hint(st + A_BYTES, &mwl, &full_bar[kb], kx, mt * 128, pol);
-        }
-    }
-    griddep_wait();
-    griddep_launch();
-    FSTAMP(1)
-
-    // ---- activations: to16 with the row's shift, the two byte planes in shared memory, per-row sums. Warp w takes
-    //      rows w, w + 8, ..; lane l values 2l, 2l + 1, 64 + 2l, 65 + 2l of each K block: a row's 1 KB is read by the
-    //      whole warp (coalesced), four rows per round; the row sums by warp reduction (redux) ----
-    if (tid < BN) s_sh[tid] = tid < a.rows ? to16_shift(a.xor_in[tid]) : 0;
-    __syncthreads();
-    for (int kb = 0; kb < a.kps; kb++) {
-        const int kx = (ks * a.kps + kb) * 128;
-        const uint32_t bh = saddr(xplanes + kb * 2 * B_BYTES), bl = bh + B_BYTES;
-#pragma unroll 1
-        for (int g = 0; g < 2; g++) {
-            int4 ra[4], rb[4];
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int n = warp + 8 * (4 * g + i);
-                const int4* src = reinterpret_cast<const int4*>(a.X + (size_t)n * a.nin + kx);
-                ra[i] = n < a.rows ? src[lane] : make_int4(0, 0, 0, 0);
-                rb[i] = n < a.rows ? src[32 + lane] : make_int4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int i = 0; i < 4; i++) {
-                const int n = warp + 8 * (4 * g + i);
-                const int sh = s_sh[n];
-                const int32_t x0 = to16v(ra[i].x, ra[i].y, sh), x1 = to16v(ra[i].z, ra[i].w, sh);
-                const int32_t x2 = to16v(rb[i].x, rb[i].y, sh), x3 = to16v(rb[i].z, rb[i].w, sh);
-                const uint32_t o = (uint32_t)((2 * lane) & 15);
-                st_shared_u16(bh + sw128(n, lane >> 3) + o, hbyte(x0) | (hbyte(x1) << 8));
-                st_shared_u16(bh + sw128(n, 4 + (lane >> 3)) + o, hbyte(x2) | (hbyte(x3) << 8));
-                st_shared_u16(bl + sw128(n, lane >> 3) + o, lbyte(x0) | (lbyte(x1) << 8));
-                st_shared_u16(bl + sw128(n, 4 + (lane >> 3)) + o, lbyte(x2) | (lbyte(x3) << 8));
-                const int sat = (x0 == 32768) + (x1 == 32768) + (x2 == 32768) + (x3 == 32768);
-                if (sat) {                                         // rare: the +32768 list
-#pragma unroll 1
-                    for (int q = 0; q < 4; q++) {
-                        const int32_t xq = q == 0 ? x0 : q == 1 ? x1 : q == 2 ? x2 : x3;
-                        if (xq == 32768) {
-                            const int kk = q < 2 ? 2 * lane + q : 64 + 2 * lane + (q - 2);
-                            atomicOr(&s_sat[n][kb * 4 + (kk >> 5)], 1u << (kk & 31));
-                            atomicOr(&s_satrows, 1ull << n);
-                        }
-                    }
-                }
-                // S1 (|a lane's sum| < 2^17), S2 as 16-bit halves (a lane's sum of 4 squares <= 2^32), +32768 count
-                const uint64_t sq = (uint64_t)((int64_t)x0 * x0) + (uint64_t)((int64_t)x1 * x1) +
-                                    (uint64_t)((int64_t)x2 * x2) + (uint64_t)((int64_t)x3 * x3);
-                const int32_t t1 = (int32_t)__reduce_add_sync(0xffffffffu, (uint32_t)(x0 + x1 + x2 + x3));
-                const uint32_t t2l = __reduce_add_sync(0xffffffffu, (uint32_t)(sq & 0xFFFF));
-                const uint32_t t2h = __reduce_add_sync(0xffffffffu, (uint32_t)(sq >> 16));
-                const uint32_t tc = __reduce_add_sync(0xffffffffu, (uint32_t)sat);
-                if (lane == 0) {                                    // one warp per row: no atomics
-                    const int64_t a1 = t1, a2 = (int64_t)t2h * 65536 + (int64_t)t2l;
-                    s_S1[n] += a1;
-                    s_S2[n] += a2;
-                    s_rowc[n] += 128 * (a1 - 256 * (int64_t)tc);
-                }
-            }
-        }
-    }
-    fence_proxy_async();
-    __syncthreads();
-
-    FSTAMP(2)
-    if (warp == 1 && lane == 0 && !dead) {
-        for (int kb = 0; kb < a.kps; kb++) {
-            if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
-        }
-        tc_fence_after();
-        for (int kb = 0; kb < a.kps && !s_abort; kb++) {
-            // A planes at smem + kb * WSTAGE, B planes at xplanes + kb * 2 * B_BYTES
-            const uint32_t abase = saddr(smem + kb * WSTAGE), bbase = saddr(xplanes + kb * 2 * B_BYTES);
-#pragma unroll
-            for (int kk = 0; kk < 4; kk++) {
-                uint64_t ah = sdesc(abase + kk * 32), al = sdesc(abase + A_BYTES + kk * 32);
-                uint64_t bh = sdesc(bbase + kk * 32), bl = sdesc(bbase + B_BYTES + kk * 32);
-                uint32_t acc = (kb || kk) ? 1u : 0u;
-                mma_i8(tmem + 0 * BN, ah, bh, IDESC, acc);
-                mma_i8(tmem + 1 * BN, ah, bl, IDESC, acc);
-                mma_i8(tmem + 1 * BN, al, bh, IDESC, 1);
-                mma_i8(tmem + 2 * BN, al, bl, IDESC, acc);
-            }
-        }
-        mma_commit(&acc_bar);
-    }
-    __syncwarp();
-    // this CTA's share of the column correction, fetched while the MMAs run
-    int64_t colc = 0;
-    {
-        const int j = mt * 128 + (warp & 3) * 32 + lane;
-        for (int kb = 0; kb < a.kps; kb++) colc += a.colcorr_kb[(size_t)(ks * a.kps + kb) * a.nout_pad + j];
-    }
-    const bool ok = !dead && mbar_wait(&acc_bar, 0, a.err);
-    tc_fence_after();
-    __syncthreads();
-    const bool go = ok && !s_abort;
-    FSTAMP(3)
-
-    // ---- this CTA's corrected partial piles -> P ----
-    {
-        const int m = (warp & 3) * 32 + lane, r0 = (warp >> 2) * 32;
-        int64_t p[32];
-        if (go) {
-            const uint32_t trow = tmem + ((uint32_t)((warp & 3) * 32) << 16) + r0;
-            int64_t t16[16];
-            tmem_piles16(trow, t16);
-#pragma unroll
-            for (int q = 0; q < 16; q++) p[q] = t16[q];
-            tmem_piles16(trow + 16, t16);
-#pragma unroll
-            for (int q = 0; q < 16; q++) p[16 + q] = t16[q];
-            const unsigned long long satrows = s_satrows;
-#pragma unroll
-            for (int q = 0; q < 32; q++) p[q] += colc + s_rowc[r0 + q];
-            if ((satrows >> r0) & 0xffffffffull)          // rare: rows of this warp with +32768 entries
-            for (int q = 0; q < 32; q++) {
-                const int n = r0 + q;
-                if (!((satrows >> n) & 1)) continue;
-                int64_t add = 0;
-                for (int kb = 0; kb < a.kps; kb++)
-                    for (int w = 0; w < 4; w++) {
-                        uint32_t bits = s_sat[n][kb * 4 + w];
-                        while (bits) {
-                            const int k = w * 32 + __ffs(bits) - 1;
-                            bits &= bits - 1;
-                            const uint8_t* A = smem + kb * WSTAGE;
-                            const int off = (int)sw128(m, k >> 4) + (k & 15);
-                            const int64_t wv = 256 * (int64_t)(int8_t)A[off] + (int64_t)(int8_t)A[A_BYTES + off] + 128;
-                            add += 256 * wv;
-                        }
-                    }
-                // rare: add into the register file through a fully unrolled select (no dynamic indexing)
-#pragma unroll
-                for (int u = 0; u < 32; u++)
-                    if (u == q) p[u] += add;
-            }
-        }
-        tc_fence_before();
-        __syncthreads();              // every read of the planes and of TMEM is done: P may overwrite them
-        if (warp == 0) tmem_dealloc(tmem, 256);   // free TMEM now: the next kernel's CTAs may allocate early
-        if (go) {
-#pragma unroll
-            for (int q = 0; q < 32; q++) P[(r0 + q) * 128 + m] = p[q];
-        }
-    }
-    tc_fence_before();
-    FSTAMP(4)
-    cluster_sync();                   // every CTA's partial tile and partial row sums are written
-    FSTAMP(5)
-
-    // ---- my slice of rows: sum over the cluster, finish ----
-    const int ksz = a.ksplit;
-    const int n0 = (int)crank * BN / ksz, n1 = ((int)crank + 1) * BN / ksz;
-    uint32_t peer[MAX_SPLIT];
-    {
-        const uint32_t pbase = saddr(P);
-#pragma unroll
-        for (int p = 0; p < MAX_SPLIT; p++) peer[p] = p < ksz ? mapa(pbase, p) : 0;
-    }
-    if (tid < n1 - n0) {
-        const int n = n0 + tid;
-        int64_t LS = 0, e2 = 0;
-        if (GAUGED && n < a.rows) {
-            const uint32_t o1 = saddr(&s_S1[n]), o2 = saddr(&s_S2[n]);
-            int64_t t1[MAX_SPLIT], t2[MAX_SPLIT];
-#pragma unroll
-            for (int p = 0; p < MAX_SPLIT; p++) {
-                t1[p] = p < ksz ? ld_dsmem(mapa(o1, p)) : 0;
-                t2[p] = p < ksz ? ld_dsmem(mapa(o2, p)) : 0;
-            }
-            int64_t S1 = 0, S2 = 0;
-#pragma unroll
-            for (int p = 0; p < MAX_SPLIT; p++) { S1 += t1[p]; S2 += t2[p]; }
-            LS = gauge_LS(S1, S2, -16 + s_sh[n], a.LOG2, a.log768, a.eps40);
-            e2 = __ldg(a.EXP2 + (wsub(0, LS) & 0xFFFF));
-        }
-        s_LS[n] = LS;
-        s_e2[n] = e2;
-    }
-    __syncthreads();
-    {
-        // thread (column pair cp, row group rg): columns 2 cp, 2 cp + 1, rows n0 + rg, n0 + rg + 4, ..; one 16-byte DSMEM
-        // load per peer and row. A warp is one row's 64 columns: for the qkv bank exactly one head part, for the
-        // others one atomicOr per warp publishes the next bank's row OR.
-        const int cp = tid & 63, rg = tid >> 6;
-        const int j0 = mt * 128 + 2 * cp, j1 = j0 + 1;
-        const bool jv0 = j0 < a.nout && go, jv1 = j1 < a.nout && go;
-        const int64_t e0 = jv0 ? (int64_t)a.e[j0] : 0, b0 = jv0 ? a.b[j0] : 0;
-        const int64_t e1 = jv1 ? (int64_t)a.e[j1] : 0, b1 = jv1 ? a.b[j1] : 0;
-        const int H = a.kv.H, dm = H * 64;
-        const bool heads = EPI == EPI_GAUGED && a.q16;
-        const int part = 2 * mt + (cp >> 5), kind = part / H, hh = part % H, dd = (2 * cp) & 63;
-        for (int nb = n0; nb < n1; nb += 4) {
-            const int n = nb + rg;                   // the same for the whole warp
-            const bool rv = n < n1 && n < a.rows;
-            int64_t v0 = 0, v1 = 0;
-            if (rv && (jv0 || jv1)) {
-                const uint32_t off = (uint32_t)(n * 128 + 2 * cp) * 8;
-                uint64_t t0[MAX_SPLIT], t1[MAX_SPLIT];
-#pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) {
-                    t0[p] = 0;
-                    t1[p] = 0;
-                    if (p < ksz) ld_dsmem2(peer[p] + off, t0[p], t1[p]);
-                }
-                uint64_t s0 = 0, s1 = 0;
-#pragma unroll
-                for (int p = 0; p < MAX_SPLIT; p++) { s0 += t0[p]; s1 += t1[p]; }
-                const int64_t exr = -16 + s_sh[n];
-                if (jv0) v0 = epi_value<EPI>((int64_t)s0, e0, b0, exr, s_LS[n], s_e2[n], a.PHI);
-                if (jv1) v1 = epi_value<EPI>((int64_t)s1, e1, b1, exr, s_LS[n], s_e2[n], a.PHI);
-            }
-            if (heads) {
-                // heads16: the row's OR over the part, to16, q16 / k16 + mask + exponent / v
-                const uint64_t por = warp_or64(rv ? (mag(v0) | mag(v1)) : 0);
-                const int sh = to16_shift(por);
-                const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
-                if (a.out && rv) {                   // the q/k/v values themselves (b2_bank's fused mode)
-                    if (jv0) a.out[(size_t)n * a.ldo + j0] = v0;
-                    if (jv1) a.out[(size_t)n * a.ldo + j1] = v1;
-                }
-                if (kind == 0) {
-                    if (rv) {
-                        *reinterpret_cast<int2*>(a.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
-                        if (dd == 0) a.qexp[n * H + hh] = -16 + sh;
-                    }
-                } else {
-                    const int pos = rv ? a.row_pos[n] : 0;
-                    const bool pv = rv && pos >= 0 && pos < a.kv.lim;
-                    if (rv && !pv && dd == 0) set_err(a.err, DERR_POS);
-                    const size_t idx = pv ? kv_index(a.row_slot[n], a.layer, hh, pos, a.kv.L, H, a.kv.ctx) : 0;
-                    if (kind == 1) {
-                        const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);   // +32768: not an int16
-                        const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
-                        if (pv) {
-                            *reinterpret_cast<uint32_t*>(a.kv.k + idx * 64 + dd) =
-                                ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
-                            if (lane == 0) a.kv.kmask[idx] = interleave32(be, bo);
-                            if (dd == 0) a.kv.kexp[idx] = -16 + sh;
-                        }
-                    } else if (pv) {
-                        if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
-                        *reinterpret_cast<int2*>(a.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
-                    }
-                }
-            } else {
-                int64_t o0 = v0, o1 = v1;
-                if (rv) {
-                    int64_t* dst = a.out + (size_t)n * a.ldo + j0;
-                    if (EPI == EPI_PLAIN_ADD) {
-                        if (jv0) o0 = wadd(dst[0], v0);
-                        if (jv1) o1 = wadd(dst[1], v1);
-                    }
-                    if (jv0) dst[0] = o0;
-                    if (jv1) dst[1] = o1;
-                }
-                if (EPI != EPI_GAUGED) {              // the next bank's row OR (over this warp's 64 columns)
-                    const uint64_t wor = warp_or64(rv ? ((jv0 ? mag(o0) : 0) | (jv1 ? mag(o1) : 0)) : 0);
-                    if (lane == 0 && a.or_out && rv) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
-                }
-            }
-        }
-    }
-    __syncthreads();
-    FSTAMP(6)
-    cluster_sync();                   // no CTA leaves while a peer may still read its shared memory
-    FSTAMP(7)
-#undef FSTAMP
-}
-
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
 __global__ void k_weight_planes(const int16_t* __restrict__ w, int nin, int nout, int8_t* __restrict__ wh,
                                 int8_t* __restrict__ wl) {
@@ -1242,7 +893,7 @@ __global__ void k_colcorr(const int16_t* __restrict__ w, int nin, int nout, int 
     cc[j] = j < nout ? 128 * s - 16384 * (int64_t)nin : 0;
 }
 
-// per 128-input block: 128 * sum_{i in block} w[i][j] - 16384 * 128 (the fused decode banks add their blocks' share)
+// per 128-input block: 128 * sum_{i in block} w[i][j] - 16384 * 128 (a CTA over part of the K range adds its blocks' share)
 __global__ void k_colcorr_kb(const int16_t* __restrict__ w, int nin, int nout, int nout_pad, int64_t* __restrict__ cc) {
     int j = blockIdx.x * blockDim.x + threadIdx.x, kb = blockIdx.y;
     if (j >= nout_pad) return;
@@ -1354,12 +1005,6 @@ int tc_init() {
                      (void*)k_bank_tiles<EPI_PLAIN_ADD>, (void*)k_bank_tiles<EPI_PLAIN_OUT>,
                      (void*)k_bank_tiles<EPI_PLAIN_EDGE>};
     for (void* f : split) {
-        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
-        if (e != cudaSuccess) return (int)e;
-    }
-    void* fused[] = {(void*)k_bank_fused<EPI_GAUGED>, (void*)k_bank_fused<EPI_GAUGED_EDGE>,
-                     (void*)k_bank_fused<EPI_PLAIN_ADD>};
-    for (void* f : fused) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, MAX_KPS * STAGE + 1024);
         if (e != cudaSuccess) return (int)e;
     }
@@ -1622,52 +1267,6 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
                                           r.maps[mi].l, a);
                       break)
     }
-    return (int)err;
-}
-
-int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl) {
-    if (!t.ready || a.rows < 1 || a.rows > BN || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD))
-        return (int)cudaErrorInvalidValue;
-    if ((uintptr_t)a.X & 15) return (int)cudaErrorMisalignedAddress;   // rows are read as 16-byte vectors
-    const int mtiles = t.nout_pad / 128, kb = t.nin / 128;
-    int ksplit = 1;
-    for (int d = MAX_SPLIT; d >= 1; d--)
-        if (kb % d == 0 && kb / d <= MAX_KPS && mtiles * d <= 160) { ksplit = d; break; }
-    if (kb / ksplit > MAX_KPS) return (int)cudaErrorInvalidValue;
-    a.nin = t.nin;
-    a.nout = t.nout;
-    a.nout_pad = t.nout_pad;
-    a.kps = kb / ksplit;
-    a.ksplit = ksplit;
-    a.colcorr_kb = t.colcorr_kb;
-    size_t smem = (size_t)(a.kps * STAGE > 64 * 1024 ? a.kps * STAGE : 64 * 1024) + 1024;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(mtiles, ksplit, 1);
-    cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[2];
-    int na = 0;
-    if (pdl) {
-        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[na].val.programmaticStreamSerializationAllowed = 1;
-        na++;
-    }
-    if (ksplit > 1) {
-        at[na].id = cudaLaunchAttributeClusterDimension;
-        at[na].val.clusterDim.x = 1;
-        at[na].val.clusterDim.y = ksplit;
-        at[na].val.clusterDim.z = 1;
-        na++;
-    }
-    cfg.attrs = at;
-    cfg.numAttrs = na;
-    const CUtensorMap& mh = *reinterpret_cast<const CUtensorMap*>(t.map_wh.bytes);
-    const CUtensorMap& ml = *reinterpret_cast<const CUtensorMap*>(t.map_wl.bytes);
-    cudaError_t err;
-    if (epi == EPI_GAUGED) err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_GAUGED>, mh, ml, a);
-    else if (epi == EPI_GAUGED_EDGE) err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_GAUGED_EDGE>, mh, ml, a);
-    else err = cudaLaunchKernelEx(&cfg, k_bank_fused<EPI_PLAIN_ADD>, mh, ml, a);
     return (int)err;
 }
 

@@ -44,32 +44,6 @@ struct TcRows {
 };
 
 
-// a decode bank with its quantisation fused in (rows <= 64); see k_bank_fused in b2_tc.cu
-struct FusedArgs {
-    int nin, nout, rows, kps, ksplit;
-    const int64_t* X;            // [rows][nin] the bank's input
-    const uint64_t* xor_in;      // [rows] OR of |X| over the row
-    uint64_t* or_out;            // [rows] OR of |output row| for the next bank (EPI_PLAIN_ADD / EPI_GAUGED_EDGE)
-    const int64_t* colcorr_kb;   // [nin / 128][nout_pad]
-    int nout_pad;
-    const int32_t* e;
-    const int64_t* b;
-    int64_t* out;                // R (PLAIN_ADD), H (GAUGED_EDGE), the q/k/v values (GAUGED, optional)
-    int ldo;
-    const int32_t* EXP2;
-    const int32_t* PHI;
-    const int32_t* LOG2;
-    int64_t log768, eps40;
-    const int32_t* row_slot;     // qkv: where each row's key/value goes
-    const int32_t* row_pos;
-    int layer;
-    KV kv;
-    int32_t* q16;
-    int32_t* qexp;
-    uint32_t* err;
-    uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8]
-};
-
 // the qkv bank's heads16 done in its decode epilogue (instead of storing q/k/v and a separate split kernel): q16 and
 // its exponent per head, k16 / mask / exponent and v appended to the key/value store at each row's position
 struct TcHeads {
@@ -122,6 +96,5 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
             uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
             const TcRace* race = nullptr);
-int tc_fused(const TcBank& t, int epi, FusedArgs a, cudaStream_t st, bool pdl);
 
 }  // namespace b2

@@ -1,6 +1,6 @@
 // b2_tcgen05.cuh -- PTX wrappers for the 5th-generation tensor cores (tcgen05 MMA kind::i8, TMEM), 2-D TMA tile
 // loads, thread-block clusters (DSMEM) and the shared-memory operand layout (K-major, SWIZZLE_128B), shared by the
-// bank kernels (b2_tc.cu) and the decode-step kernel (b2_mega.cu). Every function is inline.
+// bank kernels (b2_tc.cu). Every function is inline.
 #pragma once
 #include <cuda.h>
 #include <stdint.h>
