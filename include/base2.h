@@ -129,9 +129,13 @@ int b2_bank_noalloc(b2_handle* h, const char* name, const int64_t* X, int32_t ro
  * error (B2_ERR_CTX). The reference has no counterpart: its machine recomputes every prefix (base2.py:123). */
 int b2_rewind(b2_handle* h, int32_t n_streams, const int32_t* lens, const int32_t* last_tok, void* stream);
 
-/* Profiling. B2_PROF_* kernel classes; b2_profile(h, timing) resets the counters and, with timing != 0, brackets
- * every launch with CUDA events on its stream. b2_profile_read fills launches (total kernel launches since the
- * reset) and, per class, the launch count and summed event time in ms (arrays of B2_PROF_N). */
+/* Profiling. B2_PROF_* kernel classes; b2_profile(h, mode) resets the counters. mode 1 brackets every launch with
+ * CUDA events on its stream (launches then run without programmatic overlap and outside the step graph); mode 2
+ * leaves launches, step graph and overlap as they are and has each bank, arrival, quantisation and heads kernel
+ * stamp the start of its dependent work (%globaltimer, first CTA); a kernel's duration is then its start to the next
+ * stamped start, so unstamped kernels count towards the stamped one before them. b2_profile_read fills launches
+ * (total kernel launches since the reset) and, per class, the launch count and the summed time in ms (arrays of
+ * B2_PROF_N). No reference counterpart beyond the Metal engine's bench modes (base2_stream_fr2.swift:1060-1149). */
 enum { B2_PROF_BANK = 0, B2_PROF_ATTEND = 1, B2_PROF_QUANT = 2, B2_PROF_HEADS = 3, B2_PROF_RACE = 4, B2_PROF_OTHER = 5,
        B2_PROF_N = 6 };
 int b2_profile(b2_handle* h, int timing);

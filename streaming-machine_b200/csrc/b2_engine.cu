@@ -112,7 +112,13 @@ struct b2_handle {
         int64_t cnt[B2_PROF_N] = {0};
     } graph;
 
-    // launch accounting / per-class event timing (b2_profile)
+    // b2_profile mode 2: start stamps per launch, slots [class][STAMP_PER_CLASS] (device), the per-class summed
+    // durations and counts ([B2_PROF_N][2], device), the next free slot of each class in the current unit of work
+    uint64_t* stamp_slots = nullptr;
+    uint64_t* stamp_tot = nullptr;
+    int stamp_next[B2_PROF_N] = {0};
+
+    // launch accounting / per-class event timing (b2_profile mode 1) or in-kernel stamps (mode 2)
     struct Prof {
         int timing = 0;
         int64_t launches = 0;
@@ -223,14 +229,21 @@ cudaEvent_t prof_event(b2_handle* h) {
 void prof_begin(b2_handle* h, int cls, cudaStream_t st, int n = 1) {
     h->prof.launches += n;
     h->prof.cnt[cls] += n;
-    if (h->prof.timing) {
+    if (h->prof.timing == 1) {
         cudaEvent_t a = prof_event(h), b = prof_event(h);
         cudaEventRecord(a, st);
         h->prof.ev[cls].push_back({a, b});
     }
 }
 void prof_end(b2_handle* h, int cls, cudaStream_t st) {
-    if (h->prof.timing) cudaEventRecord(h->prof.ev[cls].back().second, st);
+    if (h->prof.timing == 1) cudaEventRecord(h->prof.ev[cls].back().second, st);
+}
+
+// mode 2: the stamp slot of the next launch of class cls (nullptr when not stamping or out of slots)
+constexpr int STAMP_PER_CLASS = 4096;
+uint64_t* stamp_slot(b2_handle* h, int cls) {
+    if (h->prof.timing != 2 || !h->stamp_slots || h->stamp_next[cls] >= STAMP_PER_CLASS) return nullptr;
+    return h->stamp_slots + (size_t)cls * STAMP_PER_CLASS + h->stamp_next[cls]++;
 }
 
 // every launch: counted per class, bracketed by events when timing, programmatic (PDL) unless timing
@@ -247,11 +260,25 @@ int launch(b2_handle* h, int cls, const char* what, void (*kernel)(KArgs...), di
     at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
-    cfg.numAttrs = (h->pdl && !h->prof.timing) ? 1 : 0;
+    cfg.numAttrs = (h->pdl && h->prof.timing != 1) ? 1 : 0;
     cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, ((KArgs)args)...);
     prof_end(h, cls, st);
     if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "launch %s: %s", what, cudaGetErrorString(e));
     return B2_OK;
+}
+
+// mode 2: a unit of work (decode step, prompt-pass chunk) clears its slots first and turns them into per-class
+// durations last (k_stamp_reset / k_stamp_accum)
+int stamp_open(b2_handle* h, cudaStream_t st) {
+    if (h->prof.timing != 2 || !h->stamp_slots) return B2_OK;
+    for (int c = 0; c < B2_PROF_N; c++) h->stamp_next[c] = 0;
+    return launch(h, B2_PROF_OTHER, "stamp_reset", k_stamp_reset, 1, 1024, 0, st, h->stamp_slots,
+                  (int)(B2_PROF_N * STAMP_PER_CLASS));
+}
+int stamp_close(b2_handle* h, cudaStream_t st) {
+    if (h->prof.timing != 2 || !h->stamp_slots) return B2_OK;
+    return launch(h, B2_PROF_OTHER, "stamp_accum", k_stamp_accum, 1, 1024, 0, st, (const uint64_t*)h->stamp_slots,
+                  (int)(B2_PROF_N * STAMP_PER_CLASS), STAMP_PER_CLASS, h->stamp_tot);
 }
 
 // the float stages (B2_*_FLOAT) that bank bi's epilogue takes: GPT-2's gauged banks and head (gauge), its fc (tanh
@@ -278,7 +305,8 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         uint64_t* tr = nullptr;
         if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) tr = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && !h->prof.timing, heads, heads_done, tr, quant, or_out, race);
+                         h->pdl && h->prof.timing != 1, heads, heads_done, tr, quant, or_out, race,
+                         stamp_slot(h, B2_PROF_BANK));
         h->split_idx++;
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
@@ -312,6 +340,7 @@ int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows
     PlaneOut pl{};
     if (h->use_tc && rows >= h->tc_min_rows)
         pl = PlaneOut{h->tcr.xh, h->tcr.xl, h->tcr.kmax, h->tcr.rowcorr, h->tcr.nsat, h->tcr.sat};
+    pl.stamp = stamp_slot(h, B2_PROF_QUANT);
     if (n > 1024)
         return launch(h, B2_PROF_QUANT, "quant", k_quant<512>, rows, 512, 0, st, X, n, src_rows, rows, h->x16, h->ex, h->LS,
                       gauge, h->LOG2, h->log768, h->eps40, pl);
@@ -324,6 +353,7 @@ int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows
 int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st, int nblocks = 0) {
     AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
                 or_out, h->half};
+    aa.stamp = stamp_slot(h, B2_PROF_ATTEND);
     const bool py = h->cfg.kind == B2_PYTHIA;
     const dim3 grid(rows, h->cfg.n_head);
     if (nblocks > 0 && h->pf_qb && !(h->flags & B2_ARRIVAL_FLOAT)) {
@@ -360,7 +390,7 @@ int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows,
                       src_rows, rows, (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out);
     return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, rows, 256, 0, st, X, h->cfg.d_model, src_rows, rows,
                   (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2, (const int32_t*)h->EXP2,
-                  h->eps40, h->d_err);
+                  h->eps40, h->d_err, stamp_slot(h, B2_PROF_QUANT));
 }
 
 // Pythia's layers + head (pythia_base2.py:161-169): the parallel residual R <- R + A(g1 R) + M(g2 R). Both norms read R
@@ -381,7 +411,7 @@ int run_rows_pythia(b2_handle* h, int rows, const int32_t* hrows, const int32_t*
         if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(rows, 3 * H), 32, 0, st,
                          (const int64_t*)h->QKV, rows, (const int32_t*)h->row_slot, (const int32_t*)h->row_pos, l, h->kv,
                          (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err,
-                         (const double*)h->cosf, (const double*)h->sinf, h->qraw)))
+                         (const double*)h->cosf, (const double*)h->sinf, h->qraw, stamp_slot(h, B2_PROF_HEADS))))
             return rc;
         if ((rc = run_attend(h, rows, l, nullptr, st, nblocks))) return rc;
         if ((rc = run_gauge(h, h->R, nullptr, rows, 2 * l + 1, h->HID, st))) return rc;
@@ -933,7 +963,9 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
                     break;
                 }
             }
-            rc = run_rows(h, rows, h->head_rows, h->head_rows + nh, nh, lg, h->race_out, st, nblocks);
+            rc = stamp_open(h, st);
+            if (!rc) rc = run_rows(h, rows, h->head_rows, h->head_rows + nh, nh, lg, h->race_out, st, nblocks);
+            if (!rc) rc = stamp_close(h, st);
             if (!rc && cudaStreamSynchronize(st) != cudaSuccess) rc = fail(h, B2_ERR_CUDA, "prefill chunk sync");
         }
     } while (0);
@@ -952,8 +984,7 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 
 namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
-int step_core(b2_handle* h, int n, cudaStream_t st) {
-    h->split_idx = 0;
+int step_body(b2_handle* h, int n, cudaStream_t st) {
     if (wq_ok(h, n)) {
         int rc = run_decode_wq(h, n, st);
         if (rc) return rc;
@@ -966,6 +997,13 @@ int step_core(b2_handle* h, int n, cudaStream_t st) {
     if ((rc = run_rows(h, n, nullptr, nullptr, n, h->logits, h->race_out, st))) return rc;
     return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
                   h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);
+}
+int step_core(b2_handle* h, int n, cudaStream_t st) {
+    h->split_idx = 0;
+    int rc = stamp_open(h, st);
+    if (!rc) rc = step_body(h, n, st);
+    if (!rc) rc = stamp_close(h, st);
+    return rc;
 }
 
 // the step captured once per stream count (on an internal stream), then replayed
@@ -1002,7 +1040,7 @@ int run_steps(b2_handle* h, int n, int n_steps, int32_t* out, int ld, int64_t* l
                     h->gen_desc, out, ld);
     if (rc) return rc;
     for (int t = 0; t < n_steps; t++) {
-        rc = (h->use_graph && !h->prof.timing) ? step_graph(h, n, st) : step_core(h, n, st);
+        rc = (h->use_graph && h->prof.timing != 1) ? step_graph(h, n, st) : step_core(h, n, st);
         if (rc) return rc;
     }
     if (logits) CK(cudaMemcpyAsync(logits, h->logits, sizeof(int64_t) * n * h->cfg.vocab, cudaMemcpyDeviceToDevice, st));
@@ -1165,6 +1203,14 @@ int b2_profile(b2_handle* h, int timing) {
         h->prof.cnt[c] = 0;
     }
     h->prof.launches = 0;
+    if (timing < 0 || timing > 2) return fail(h, B2_ERR_ARG, "b2_profile: mode %d (0 counts, 1 events, 2 stamps)", timing);
+    if (timing == 2) {
+        int rc;
+        if (!h->stamp_slots && (rc = dalloc(h, &h->stamp_slots, (size_t)B2_PROF_N * STAMP_PER_CLASS))) return rc;
+        if (!h->stamp_tot && (rc = dalloc(h, &h->stamp_tot, (size_t)2 * B2_PROF_N))) return rc;
+        CK(cudaMemset(h->stamp_tot, 0, sizeof(uint64_t) * 2 * B2_PROF_N));
+    }
+    if ((timing == 2) != (h->prof.timing == 2)) drop_graph(h);   // a captured step holds (or lacks) the stamp kernels
     h->prof.timing = timing;
     return B2_OK;
 }
@@ -1174,6 +1220,15 @@ int b2_profile_read(b2_handle* h, int64_t* launches, int64_t* counts, double* ms
     CK(cudaSetDevice(h->device));
     CK(cudaDeviceSynchronize());
     if (launches) *launches = h->prof.launches;
+    if (h->prof.timing == 2) {   // stamps: ms = the summed durations of the stamped launches of each class
+        uint64_t tot[2 * B2_PROF_N];
+        CK(cudaMemcpy(tot, h->stamp_tot, sizeof tot, cudaMemcpyDeviceToHost));
+        for (int c = 0; c < B2_PROF_N; c++) {
+            if (counts) counts[c] = h->prof.cnt[c];
+            if (ms) ms[c] = (double)tot[2 * c] * 1e-6;
+        }
+        return B2_OK;
+    }
     for (int c = 0; c < B2_PROF_N; c++) {
         if (counts) counts[c] = h->prof.cnt[c];
         double t = 0;

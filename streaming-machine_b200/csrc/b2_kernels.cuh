@@ -43,6 +43,7 @@ struct PlaneOut {
     int64_t* rowcorr;
     int32_t* nsat;
     int16_t* sat;
+    uint64_t* stamp = nullptr;   // b2_profile mode 2
 };
 
 template <int NT>
@@ -51,6 +52,7 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
                                               int64_t* __restrict__ LS, int gauge, const int32_t* __restrict__ LOG2,
                                               int64_t log768, int64_t eps40, PlaneOut pl) {
     griddep_wait();
+    stamp_begin(pl.stamp);
     griddep_launch();
     __shared__ uint64_t s_or[NT / 32];
     __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
@@ -115,8 +117,9 @@ __global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, 
                                                  int rows, const int64_t* __restrict__ g, int64_t ge,
                                                  const int64_t* __restrict__ b, int64_t* __restrict__ out,
                                                  const int32_t* __restrict__ LOG2, const int32_t* __restrict__ EXP2,
-                                                 int64_t eps40, uint32_t* err) {
+                                                 int64_t eps40, uint32_t* err, uint64_t* stamp) {
     griddep_wait();
+    stamp_begin(stamp);
     griddep_launch();
     __shared__ uint64_t s_or[NT / 32];
     __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
@@ -174,8 +177,9 @@ __global__ void k_heads_pythia(const int64_t* __restrict__ QKV, int rows, const 
                                const int32_t* __restrict__ row_pos, int layer, KV kv, int rot,
                                const int32_t* __restrict__ COS, const int32_t* __restrict__ SIN, int32_t* __restrict__ q16,
                                int32_t* __restrict__ qexp, uint32_t* err, const double* __restrict__ cosf,
-                               const double* __restrict__ sinf, int64_t* __restrict__ qraw) {
+                               const double* __restrict__ sinf, int64_t* __restrict__ qraw, uint64_t* stamp) {
     griddep_wait();
+    stamp_begin(stamp);
     griddep_launch();
     const int r = blockIdx.x, part = blockIdx.y, lane = threadIdx.x;
     const int H = kv.H, d = H * 64, h = part / 3, kind = part % 3;
@@ -379,6 +383,7 @@ struct AttnArgs {
     const int64_t* qf;      // arrival=float: the queries at full width, row r's head h at qf[r * ldq + h * 64]
     int ldq;
     uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8] (k_attend_bulk)
+    uint64_t* stamp = nullptr;   // b2_profile mode 2
 };
 
 // the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
@@ -399,6 +404,7 @@ B2_DEV int64_t score(int64_t dot, int64_t eq, int64_t ek, const AttnArgs& a) {
 template <int NW, bool PY>
 __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     extern __shared__ int64_t sc[];           // [pos + 1]
     __shared__ int32_t qs[64];
@@ -538,6 +544,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     if (tr && threadIdx.x == 0) tr[k_] = gtime();
     ASTAMP(0)
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     ASTAMP(1)
     extern __shared__ __align__(16) uint8_t sm[];
@@ -701,6 +708,7 @@ inline size_t prefill_smem(int qb, int nkmax) {
 template <int QB, bool PY>
 __global__ void __launch_bounds__(256) k_attend_prefill(AttnArgs a, const PrefillBlock* __restrict__ blocks, int nkmax) {
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ int64_t s_max[QB][2], s_eq[QB], s_Z[QB];
@@ -984,6 +992,36 @@ __global__ void k_wait_check(uint32_t* err) {
         mbar_wait(&bar, 0, err);
     }
     __syncwarp();
+}
+
+// b2_profile mode 2: a unit of work (a decode step, a prompt-pass chunk) begins by clearing its stamp slots ...
+__global__ void k_stamp_reset(uint64_t* slots, int n) {
+    griddep_wait();
+    griddep_launch();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) slots[i] = ~0ull;
+}
+// ... and ends by turning them into durations: slots are grouped by kernel class (per_class each); a stamped kernel
+// lasted from its start to the next stamped start of any class (or to this kernel's own start), so a kernel without a
+// slot is counted in the stamped one before it. tot[2c] += ns, tot[2c + 1] += launches of class c.
+__global__ void __launch_bounds__(1024) k_stamp_accum(const uint64_t* slots, int n, int per_class, uint64_t* tot) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ uint64_t t_end;
+    if (threadIdx.x == 0) t_end = gtime();
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const uint64_t s = slots[i];
+        if (s == ~0ull) continue;
+        uint64_t next = t_end;
+        for (int j = 0; j < n; j++) {
+            const uint64_t u = slots[j];
+            if (u != ~0ull && u > s && u < next) next = u;
+        }
+        if (next <= s) continue;
+        const int c = i / per_class;
+        atomicAdd((unsigned long long*)&tot[2 * c], (unsigned long long)(next - s));
+        atomicAdd((unsigned long long*)&tot[2 * c + 1], 1ull);
+    }
 }
 
 __global__ void k_decode_commit(int n, const int32_t* __restrict__ word, int32_t* slot_len, int32_t* slot_tok,

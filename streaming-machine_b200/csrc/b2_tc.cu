@@ -41,6 +41,7 @@ struct TcArgs {
     TcQuant q;        // k_bank_wide: quantise the rows in the kernel (q.X set) instead of reading a quant kernel's
     uint64_t* or_out; // optional: OR of |stored value| over each output row (atomicOr), for the next bank's q.xor_in
     TcRace race;      // k_bank_tiles: each 32-column group's race winner per row (race.v set); out may then be null
+    uint64_t* stamp;  // b2_profile mode 2
 };
 
 B2_DEV void ld_dsmem2(uint32_t addr, uint64_t& a0, uint64_t& a1) {
@@ -195,6 +196,7 @@ __global__ void __launch_bounds__(256, 1)
     const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
     const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     tstamp(a, 2);
     if (tid == 0 && !dead) {
@@ -401,6 +403,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
     const bool heads = EPI == EPI_GAUGED && a.heads;
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     tstamp(a, 2);
     // the residual this thread adds to, final now that the wait has returned (in-kernel quantisation: no out_map)
@@ -758,6 +761,7 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     }
     tstamp(a, 1);
     griddep_wait();
+    stamp_begin(a.stamp);
     griddep_launch();
     tstamp(a, 2);
     if (dead) {
@@ -1145,7 +1149,7 @@ static int wide_quant_split(const TcBank& t) {
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
-            uint64_t* or_out, const TcRace* race) {
+            uint64_t* or_out, const TcRace* race, uint64_t* stamp) {
     if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
     // the row planes' tensor maps for K = nin (box: 128 bytes x 64 rows), made once
@@ -1180,6 +1184,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     a.err = r.err;
     a.epi = EpiArgs{ex, LS, e, b, out, ldo, out_map, EXP2, PHI};
     a.or_out = or_out;
+    a.stamp = stamp;
     // split-K over a cluster when there is one row tile and too few output tiles to fill the GPU
     int ksplit = 1;
     if (ntiles == 1 && mtiles < 148)

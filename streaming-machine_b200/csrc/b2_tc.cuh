@@ -95,6 +95,6 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
             uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
-            const TcRace* race = nullptr);
+            const TcRace* race = nullptr, uint64_t* stamp = nullptr);
 
 }  // namespace b2
