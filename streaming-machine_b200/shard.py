@@ -23,6 +23,14 @@ def stream_ids(seed: int, streams_per_rank: int, prompt_len: int, rank: int, wor
     return ids[rank * streams_per_rank:(rank + 1) * streams_per_rank]
 
 
+def partition(n_streams: int, rank: int, world: int) -> tuple[int, int]:
+    """This rank's half-open block [lo, hi) of n_streams streams split as evenly as possible over world ranks (a
+    fixed total shared out: strong scaling; every stream computed once, on exactly one rank)."""
+    base, extra = divmod(n_streams, world)
+    lo = rank * base + min(rank, extra)
+    return lo, lo + base + (1 if rank < extra else 0)
+
+
 def max_over_ranks(x: float, dist=None, device=None) -> float:
     """The largest x over all ranks (the job's time is its slowest rank's)."""
     if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:
