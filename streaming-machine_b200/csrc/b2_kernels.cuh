@@ -384,6 +384,7 @@ struct AttnArgs {
     int ldq;
     uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8] (k_attend_bulk)
     uint64_t* stamp = nullptr;   // b2_profile mode 2
+    RowTiles tout{};             // decode (row-tile path): the output also as row tiles, each row's OR in tout.orow
 };
 
 // the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
@@ -676,7 +677,9 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         if (PY && bad) set_err(a.err, DERR_RANGE);
         o[2 * lane] = v0;
         o[2 * lane + 1] = v1;
-        if (a.or_out) {
+        if (a.tout.y) {
+            rt_store2(a.tout, r, h * 64, v0, v1, true);   // proj's input, and the row's OR
+        } else if (a.or_out) {
             const uint64_t w = warp_or64(mag(v0) | mag(v1));
             if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)w);
         }
@@ -927,7 +930,7 @@ __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const i
 __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, const int32_t* __restrict__ slot_tok,
                                int32_t* row_slot, int32_t* row_pos, int32_t* row_tok, const int64_t* __restrict__ wte,
                                const int64_t* __restrict__ wpe, int d, int V, int nctx, int64_t* __restrict__ R,
-                               uint64_t* or_buf, int nor, int or_ld, int64_t* acc, int32_t* accn, uint32_t* err) {
+                               uint64_t* or_buf, int nor, int or_ld, RowTiles rt, uint32_t* err) {
     griddep_wait();
     griddep_launch();
     __shared__ uint64_t s_or[8];
@@ -940,19 +943,19 @@ __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, cons
     const int64_t* a = wte + (size_t)tok * d;
     const int64_t* b = wpe + (size_t)pos * d;
     uint64_t o = 0;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    // a warp takes 32 consecutive columns at a time: one row-tile chunk (d is a multiple of 32)
+    for (int i0 = threadIdx.x & ~31; i0 < d; i0 += blockDim.x) {
+        const int i = i0 + (threadIdx.x & 31);
         const int64_t v = wadd(__ldg(a + i), __ldg(b + i));
         R[(size_t)s * d + i] = v;
         o |= mag(v);
+        if (rt.y) {
+            RowTiles t = rt;
+            t.orow = nullptr;         // the row's OR is written whole below
+            rt_store1(t, s, i0, v, true);
+        }
     }
     for (int q = 1 + threadIdx.x; q < nor; q += blockDim.x) or_buf[(size_t)q * or_ld + s] = 0;
-    // the in-kernel quantisation's per-row accumulators of every bank input ([2][nor][or_ld] S1, S2; [nor][or_ld])
-    if (acc)
-        for (int q = threadIdx.x; q < nor; q += blockDim.x) {
-            acc[(size_t)q * or_ld + s] = 0;
-            acc[(size_t)(nor + q) * or_ld + s] = 0;
-            accn[(size_t)q * or_ld + s] = 0;
-        }
     o = warp_or64(o);
     if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
     __syncthreads();
@@ -1000,25 +1003,36 @@ __global__ void k_stamp_reset(uint64_t* slots, int n) {
     griddep_launch();
     for (int i = threadIdx.x; i < n; i += blockDim.x) slots[i] = ~0ull;
 }
-// ... and ends by turning them into durations: slots are grouped by kernel class (per_class each); a stamped kernel
-// lasted from its start to the next stamped start of any class (or to this kernel's own start), so a kernel without a
-// slot is counted in the stamped one before it. tot[2c] += ns, tot[2c + 1] += launches of class c.
-__global__ void __launch_bounds__(1024) k_stamp_accum(const uint64_t* slots, int n, int per_class, uint64_t* tot) {
+// ... and ends by turning them into durations: a stamped kernel lasted from its start to the next stamped start of any
+// class (or to this kernel's own start), so a kernel without a slot is counted in the stamped one before it.
+// tot[2c] += ns, tot[2c + 1] += launches of class c.
+struct StampUse {
+    int n[8];   // slots used per class in this unit of work
+};
+__global__ void __launch_bounds__(1024) k_stamp_accum(const uint64_t* slots, StampUse use, int per_class, uint64_t* tot) {
     griddep_wait();
     griddep_launch();
     __shared__ uint64_t t_end;
-    if (threadIdx.x == 0) t_end = gtime();
+    __shared__ int off[9];
+    if (threadIdx.x == 0) {
+        t_end = gtime();
+        off[0] = 0;
+        for (int c = 0; c < 8; c++) off[c + 1] = off[c] + use.n[c];
+    }
     __syncthreads();
+    const int n = off[8];
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const uint64_t s = slots[i];
+        int c = 0;
+        while (i >= off[c + 1]) c++;
+        const uint64_t s = slots[(size_t)c * per_class + (i - off[c])];
         if (s == ~0ull) continue;
         uint64_t next = t_end;
-        for (int j = 0; j < n; j++) {
-            const uint64_t u = slots[j];
-            if (u != ~0ull && u > s && u < next) next = u;
-        }
+        for (int cc = 0; cc < 8; cc++)
+            for (int j = 0; j < use.n[cc]; j++) {
+                const uint64_t u = slots[(size_t)cc * per_class + j];
+                if (u != ~0ull && u > s && u < next) next = u;
+            }
         if (next <= s) continue;
-        const int c = i / per_class;
         atomicAdd((unsigned long long*)&tot[2 * c], (unsigned long long)(next - s));
         atomicAdd((unsigned long long*)&tot[2 * c + 1], 1ull);
     }
