@@ -87,6 +87,7 @@ struct b2_handle {
     PrefillBlock* pf_blocks = nullptr;   // prompt pass: blocks of consecutive positions of one stream [max_rows]
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
+    int early_keys = 1;          // decode arrival: earlier positions' keys copied before the dependency wait (B2_EARLY_KEYS=0)
     int fuse_heads = 1;          // GPT-2 decode: heads16 in the qkv bank's epilogue (B2_FUSE_HEADS=0: its own kernel)
     uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
     uint64_t* att_trace = nullptr;    // B2_ATT_TRACE=<file>: the decode arrival's stamps of the last step ([L][CTA][8])
@@ -356,10 +357,11 @@ int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows
 // the arrival for `rows` rows at layer l: in a prompt pass (blocks given) query blocks sharing key/value tiles;
 // otherwise one CTA per (row, head), by bulk copies while a stream's keys fit in shared memory
 int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st, int nblocks = 0,
-               RowTiles tout = RowTiles{}) {
+               RowTiles tout = RowTiles{}, bool decode = false) {
     AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
                 or_out, h->half};
     aa.tout = tout;
+    aa.early = decode && h->early_keys;
     aa.stamp = stamp_slot(h, B2_PROF_ATTEND);
     const bool py = h->cfg.kind == B2_PYTHIA;
     const dim3 grid(rows, h->cfg.n_head);
@@ -518,7 +520,7 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         TcTiles t = tile_args(h, tiles_of(h, T_R, o0), none, true);
         if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &t))) return rc;
         if (!heads_done) return fail(h, B2_ERR_STATE, "qkv bank %d: heads16 not done in its epilogue", l);
-        if ((rc = run_attend(h, n, l, nullptr, st, 0, tiles_of(h, T_ATT, o0 + FUSED_ROWS)))) return rc;
+        if ((rc = run_attend(h, n, l, nullptr, st, 0, tiles_of(h, T_ATT, o0 + FUSED_ROWS), true))) return rc;
         t = tile_args(h, tiles_of(h, T_ATT, o0 + FUSED_ROWS), tiles_of(h, T_R, o0 + 2 * FUSED_ROWS), true);
         if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &t))) return rc;
         t = tile_args(h, tiles_of(h, T_R, o0 + 2 * FUSED_ROWS), tiles_of(h, T_HID, o0 + 3 * FUSED_ROWS), false);
@@ -601,6 +603,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_PDL")) h->pdl = atoi(v);
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
+    if (const char* v = getenv("B2_EARLY_KEYS")) h->early_keys = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;

@@ -385,6 +385,8 @@ struct AttnArgs {
     uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8] (k_attend_bulk)
     uint64_t* stamp = nullptr;   // b2_profile mode 2
     RowTiles tout{};             // decode (row-tile path): the output also as row tiles, each row's OR in tout.orow
+    int early = 0;               // decode: keys before a row's own position come from earlier steps (k_attend_bulk
+                                 // copies them before its dependency wait, the row's own key after it)
 };
 
 // the score of one key: GPT-2 rshift(q.k, -(eq + ek - 3 + 10)) (base2.py:94); Pythia power(q.k, (eq + ek + 10)*65536
@@ -544,10 +546,6 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
 #define ASTAMP(k_) \
     if (tr && threadIdx.x == 0) tr[k_] = gtime();
     ASTAMP(0)
-    griddep_wait();
-    stamp_begin(a.stamp);
-    griddep_launch();
-    ASTAMP(1)
     extern __shared__ __align__(16) uint8_t sm[];
     __shared__ uint64_t bar;
     __shared__ int32_t qs[64];
@@ -555,9 +553,18 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     const int r = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int H = a.kv.H, d = H * 64;
-    const int slot = a.row_slot[r], p = a.row_pos[r];
+    // decode (a.early): the row table and every key before the row's own position were written at least two launches
+    // back (the step's first kernel, earlier steps), so they are read, and the keys copied, before the dependency wait;
+    // L2 reads, never the non-coherent path. The row's own key (this step's qkv bank) is read after the wait.
+    if (!a.early) {
+        griddep_wait();
+        stamp_begin(a.stamp);
+        griddep_launch();
+    }
+    const int slot = __ldcg(a.row_slot + r), p = __ldcg(a.row_pos + r);
     if (p < 0 || p >= a.kv.lim) return;      // flagged by the qkv bank (DERR_POS); never read past the store
     const int nk = p + 1, nkr = (nk + 3) & ~3;
+    const int ncp = a.early ? (p + 3) & ~3 : nkr;   // positions copied in bulk (from the store's start)
     int16_t* Ks = reinterpret_cast<int16_t*>(sm);
     uint64_t* KMs = reinterpret_cast<uint64_t*>(sm + (size_t)nkr * 128);
     int32_t* KEs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 136);
@@ -570,16 +577,32 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     }
     __syncthreads();
     if (tid == 0) {
-        mbar_expect_tx(&bar, (uint32_t)nkr * (128 + 8 + 4));
-        bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)nkr * 128, &bar);
-        bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)nkr * 8, &bar);
-        bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)nkr * 4, &bar);
-        bulk_prefetch_l2(a.kv.v + base * 64, (uint32_t)nkr * 256);
+        mbar_expect_tx(&bar, (uint32_t)ncp * (128 + 8 + 4));
+        if (ncp) {
+            bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)ncp * 128, &bar);
+            bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)ncp * 8, &bar);
+            bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)ncp * 4, &bar);
+            bulk_prefetch_l2(a.kv.v + base * 64, (uint32_t)ncp * 256);
+        }
     }
+    if (a.early) {
+        griddep_wait();
+        stamp_begin(a.stamp);
+        griddep_launch();
+    }
+    ASTAMP(1)
     if (tid < 64) qs[tid] = a.q16[(size_t)r * d + h * 64 + tid];
     const int64_t eq = a.qexp[r * H + h];
-    __syncthreads();
     if (!mbar_wait(&bar, 0, a.err)) return;
+    if (a.early && wid == 0) {       // the row's own key, after the bulk copy (which may have covered its slot)
+        const size_t e = base + p;
+        reinterpret_cast<uint32_t*>(Ks + (size_t)p * 64)[lane] = __ldcg(reinterpret_cast<const unsigned int*>(a.kv.k + e * 64) + lane);
+        if (lane == 0) {
+            KMs[p] = __ldcg((const unsigned long long*)a.kv.kmask + e);
+            KEs[p] = __ldcg(a.kv.kexp + e);
+        }
+    }
+    __syncthreads();
     ASTAMP(2)
 
     // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of key c*4 + (lane>>3)

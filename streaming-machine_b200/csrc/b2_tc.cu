@@ -466,20 +466,34 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
                 sc[kb] = __ldcg((const signed char*)a.t.in.s + (size_t)n * (a.t.in.ld >> 5) + (k >> 5));
             }
         }
+        // a rolled loop (each CTA runs this code once per launch, so its size costs instruction fetches): K block kb is
+        // always in slot 0 of the load arrays, which shift down by one per block
         int64_t S1 = 0, S2 = 0;
         int bad = 0;
         const int lim = sh ? sh - 1 : 0;
+        const uint32_t bb0 = saddr(smem + WIDE_A), chunk = (uint32_t)(kq >> 4), part = kq & 15;
+        const uint32_t oh = sw128(q, chunk) + part, ol = sw128(WIDE_ROWS + q, chunk) + part;
+#pragma unroll 1
+        for (int kb = 0; kb < nkb; kb++) {
+            const int y[8] = {ya[0].x, ya[0].y, ya[0].z, ya[0].w, yb[0].x, yb[0].y, yb[0].z, yb[0].w};
+            const int sck = sc[0];
 #pragma unroll
-        for (int kb = 0; kb < WIDE_MAX_KB; kb++) {
-            if (kb >= nkb) break;
-            const int y[8] = {ya[kb].x, ya[kb].y, ya[kb].z, ya[kb].w, yb[kb].x, yb[kb].y, yb[kb].z, yb[kb].w};
-            bad |= sc[kb] > lim;
+            for (int u = 0; u + 1 < WIDE_MAX_KB; u++) {
+                ya[u] = ya[u + 1];
+                yb[u] = yb[u + 1];
+                sc[u] = sc[u + 1];
+            }
+            bad |= sck > lim;
+            // x16 = (Y + 1) >> 1 with Y = y >> (sh - 1 - sc) (17 significant bits: 32-bit arithmetic; the shift saturates
+            // at 31, where y's sign alone is left); sh = 0: x16 = y; sh >= 48: the wrap of rt_to16, per value
+            const int t = sh ? min(sh - 1 - sck, 31) : 0;
             uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
 #pragma unroll
             for (int i = 0; i < 8; i++) {
-                const int32_t x = nv ? rt_to16(y[i], sc[kb], sh) : 0;
+                int32_t x = 0;
+                if (nv) x = sh >= 48 ? rt_to16(y[i], sck, sh) : (sh ? ((y[i] >> t) + 1) >> 1 : y[i]);
                 S1 += x;
-                S2 += (int64_t)x * x;
+                S2 += (int64_t)(uint32_t)(x * x);
                 if (x == 32768) {   // rare: listed for the correction 256 * w (per CTA, over its own K range)
                     const int u = atomicAdd(&s_nsat[q], 1);
                     if (u < a.t.sat_ld)
@@ -490,10 +504,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
                 if (i < 4) { h0 |= hb << (8 * i); l0 |= lb << (8 * i); }
                 else { h1 |= hb << (8 * (i - 4)); l1 |= lb << (8 * (i - 4)); }
             }
-            const uint32_t bb = saddr(smem + kb * WIDE_KBLOCK + WIDE_A), chunk = (uint32_t)(kq >> 4), part = kq & 15;
-            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + sw128(q, chunk) + part), "r"(h0), "r"(h1) : "memory");
-            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + sw128(WIDE_ROWS + q, chunk) + part), "r"(l0), "r"(l1)
-                         : "memory");
+            const uint32_t bb = bb0 + (uint32_t)kb * WIDE_KBLOCK;
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + oh), "r"(h0), "r"(h1) : "memory");
+            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + ol), "r"(l0), "r"(l1) : "memory");
         }
         if (bad && nv) set_err(a.err, DERR_RANGE);   // a row whose OR sets bit 63 (a value of -2^63): not computed
         // the row's sums over its half warp
