@@ -78,12 +78,10 @@ struct b2_handle {
     TcRows tcr{};
     int32_t *head_rows = nullptr, *race_out = nullptr;
     uint64_t* row_or = nullptr;  // decode: per bank input, the OR of |x| over each row ([4L][FUSED_ROWS])
-    // decode steps of <= 64 streams: the bank inputs as row tiles (RowTiles): the residual R (qkv's and fc's input),
-    // the arrival's output (proj's), fc's bent output (mproj's); y [FUSED_ROWS][ld] int32, s [FUSED_ROWS][ld / 32]
-    int32_t *rt_y[3] = {nullptr, nullptr, nullptr};
-    int8_t* rt_s[3] = {nullptr, nullptr, nullptr};
-    int16_t* rt_sat = nullptr;   // the banks' per-CTA lists of +32768 entries ([RT_SAT_CTAS][32][RT_SAT_LD])
-    int wq = 1;                  // decode steps of <= 64 streams take row tiles in the bank kernels (B2_WQ=0: quant kernels)
+    int64_t* wq_acc = nullptr;   // decode, rows quantised in the bank kernels: S1, S2 per bank input ([2][4L][FUSED_ROWS])
+    int32_t* wq_nsat = nullptr;  // the +32768 count per bank input ([4L][FUSED_ROWS])
+    unsigned long long* wq_ctr = nullptr;   // arrival counters per bank input and row half ([4L][2], never reset)
+    int wq = 1;                  // decode steps of <= 64 streams quantise in the bank kernels (B2_WQ=0: quant kernels)
     PrefillBlock* pf_blocks = nullptr;   // prompt pass: blocks of consecutive positions of one stream [max_rows]
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
@@ -134,7 +132,6 @@ struct b2_handle {
 namespace {
 
 constexpr int FUSED_ROWS = 64;
-constexpr int RT_SAT_CTAS = 160, RT_SAT_LD = 768;   // k_bank_wide's +32768 scratch: CTAs per launch, entries per row
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
 constexpr int ATT_NW = 8;                      // warps per (row, head) CTA of the bulk-copy arrival
 constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
@@ -302,7 +299,7 @@ int bank_float_stages(const b2_handle* h, int bi) {
 // ---- one bank over `rows` rows whose x16/ex/LS are ready -------------------------------------------------------------
 // heads (GPT-2's qkv): the split-K decode kernel may do heads16 in its epilogue; *heads_done says whether it did
 int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, const int32_t* out_map, cudaStream_t st,
-             const TcHeads* heads = nullptr, bool* heads_done = nullptr, const TcTiles* tiles = nullptr,
+             const TcHeads* heads = nullptr, bool* heads_done = nullptr, const TcQuant* quant = nullptr,
              uint64_t* or_out = nullptr, const TcRace* race = nullptr) {
     const DevBank& bk = h->banks[bi];
     if (heads_done) *heads_done = false;
@@ -311,14 +308,14 @@ int run_bank(b2_handle* h, int bi, int epi, int rows, int64_t* out, int ldo, con
         uint64_t* tr = nullptr;
         if (h->split_trace && h->split_idx < SPLIT_TRACE_LAUNCHES) tr = h->split_trace + (size_t)h->split_idx * SPLIT_TRACE_SLOT;
         int rc = tc_bank(bk.tc, h->tcr, epi, rows, h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI, st,
-                         h->pdl && h->prof.timing != 1, heads, heads_done, tr, tiles, or_out, race,
+                         h->pdl && h->prof.timing != 1, heads, heads_done, tr, quant, or_out, race,
                          stamp_slot(h, B2_PROF_BANK));
         h->split_idx++;
         prof_end(h, B2_PROF_BANK, st);
         if (rc) return fail(h, B2_ERR_CUDA, "tensor-core bank %d: %s", bi, cudaGetErrorString((cudaError_t)rc));
         return check_launch(h, "tc_bank");
     }
-    if (tiles || or_out || race) return fail(h, B2_ERR_STATE, "bank %d: this epilogue needs the tensor-core banks", bi);
+    if (quant || or_out || race) return fail(h, B2_ERR_STATE, "bank %d: this epilogue needs the tensor-core banks", bi);
     BankArgs a{h->x16, bk.w, bk.nin, bk.nout, rows, {h->ex, h->LS, bk.e, bk.b, out, ldo, out_map, h->EXP2, h->PHI}};
     a.flt = bank_float_stages(h, bi);
     a.sig = h->sigf;
@@ -356,11 +353,9 @@ int run_quant_int(b2_handle* h, const int64_t* X, int n, const int32_t* src_rows
 
 // the arrival for `rows` rows at layer l: in a prompt pass (blocks given) query blocks sharing key/value tiles;
 // otherwise one CTA per (row, head), by bulk copies while a stream's keys fit in shared memory
-int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st, int nblocks = 0,
-               RowTiles tout = RowTiles{}, bool decode = false) {
+int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st, int nblocks = 0, bool decode = false) {
     AttnArgs aa{h->row_slot, h->row_pos, rows, l, h->kv, h->q16, h->qexp, h->ARR, h->alen, h->LOG2, h->EXP2, h->ATT, h->d_err,
                 or_out, h->half};
-    aa.tout = tout;
     aa.early = decode && h->early_keys;
     aa.stamp = stamp_slot(h, B2_PROF_ATTEND);
     const bool py = h->cfg.kind == B2_PYTHIA;
@@ -477,58 +472,51 @@ int run_rows(b2_handle* h, int rows, const int32_t* hrows, const int32_t* hmap, 
     return launch(h, B2_PROF_RACE, "race", k_race, nhead, 1024, 0, st, logits, c.vocab, hmap, c.vocab, words_by_slot);
 }
 
-// ---- a decode step with row tiles between the banks (n <= 64 streams, row r = slot r) ---------------------------
-// Every bank input's producer (embed, the arrival, proj, fc, mproj) writes it as row tiles and ORs each row's
-// magnitudes into its slot of row_or, so each k_bank_wide CTA converts its own rows over its own K range when it
-// starts (no quantisation kernel, no wait between the CTAs). Only the head keeps a quant kernel.
-RowTiles tiles_of(b2_handle* h, int which, uint64_t* orow) {
-    RowTiles t;
-    t.y = h->rt_y[which];
-    t.s = h->rt_s[which];
-    t.orow = orow;
-    t.ld = which == 2 ? h->cfg.d_ff : h->cfg.d_model;
-    return t;
-}
-TcTiles tile_args(b2_handle* h, RowTiles in, RowTiles out, bool out_i64) {
-    TcTiles t;
-    t.in = in;
-    t.out = out;
-    t.out_i64 = out_i64;
-    t.LOG2 = h->LOG2;
-    t.log768 = h->log768;
-    t.eps40 = h->eps40;
-    t.sat = h->rt_sat;
-    t.sat_ld = RT_SAT_LD;
-    t.sat_ctas = RT_SAT_CTAS;
-    return t;
+// ---- a decode step with the rows quantised inside the bank kernels (n <= 64 streams, row r = slot r) -------------
+// Each bank input's row OR is published by its producer (embed, attention, the banks before: atomicOr), so the
+// k_bank_wide CTAs quantise the rows themselves (shared out, then an arrival counter) instead of waiting for a
+// quant kernel (the mproj bank's 24 K blocks split over 4-CTA clusters). Only the head keeps a quant kernel.
+TcQuant wq_args(b2_handle* h, int site, const int64_t* X, int ldx, const uint64_t* xor_in) {
+    TcQuant q;
+    q.X = X;
+    q.ldx = ldx;
+    q.xor_in = xor_in;
+    q.S1 = h->wq_acc + (size_t)site * FUSED_ROWS;
+    q.S2 = h->wq_acc + (size_t)(4 * h->cfg.n_layer + site) * FUSED_ROWS;
+    q.nsat = h->wq_nsat + (size_t)site * FUSED_ROWS;
+    q.ctr = h->wq_ctr + (size_t)site * 2;
+    q.LOG2 = h->LOG2;
+    q.log768 = h->log768;
+    q.eps40 = h->eps40;
+    return q;
 }
 
 int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, F = c.d_ff;
     uint64_t* OR = h->row_or;   // slot q of the step: OR[q * FUSED_ROWS + row]
-    enum { T_R = 0, T_ATT = 1, T_HID = 2 };
     int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
                     h->row_slot, h->row_pos, h->row_tok, h->wte, h->wpe, d, c.vocab, c.n_ctx, h->R, OR, 4 * L, FUSED_ROWS,
-                    tiles_of(h, T_R, OR), h->d_err);
+                    h->wq_acc, h->wq_nsat, h->d_err);
     if (rc) return rc;
-    const RowTiles none{};
     for (int l = 0; l < L; l++) {
         uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
         const TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
         bool heads_done = false;
-        TcTiles t = tile_args(h, tiles_of(h, T_R, o0), none, true);
-        if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &t))) return rc;
+        TcQuant q = wq_args(h, 4 * l, h->R, d, o0);
+        if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &q))) return rc;
         if (!heads_done) return fail(h, B2_ERR_STATE, "qkv bank %d: heads16 not done in its epilogue", l);
-        if ((rc = run_attend(h, n, l, nullptr, st, 0, tiles_of(h, T_ATT, o0 + FUSED_ROWS), true))) return rc;
-        t = tile_args(h, tiles_of(h, T_ATT, o0 + FUSED_ROWS), tiles_of(h, T_R, o0 + 2 * FUSED_ROWS), true);
-        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &t))) return rc;
-        t = tile_args(h, tiles_of(h, T_R, o0 + 2 * FUSED_ROWS), tiles_of(h, T_HID, o0 + 3 * FUSED_ROWS), false);
-        if ((rc = run_bank(h, 4 * l + 2, EPI_GAUGED_EDGE, n, h->HID, F, nullptr, st, nullptr, nullptr, &t))) return rc;
-        // mproj: R += ..., as row tiles for the next layer's qkv (the head reads the int64 R)
-        t = tile_args(h, tiles_of(h, T_HID, o0 + 3 * FUSED_ROWS),
-                      l + 1 < L ? tiles_of(h, T_R, o0 + 4 * FUSED_ROWS) : none, true);
-        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &t))) return rc;
+        if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st, 0, true))) return rc;
+        q = wq_args(h, 4 * l + 1, h->ATT, d, o0 + FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, o0 + 2 * FUSED_ROWS)))
+            return rc;
+        q = wq_args(h, 4 * l + 2, h->R, d, o0 + 2 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 2, EPI_GAUGED_EDGE, n, h->HID, F, nullptr, st, nullptr, nullptr, &q,
+                           o0 + 3 * FUSED_ROWS)))
+            return rc;
+        uint64_t* next = l + 1 < L ? o0 + 4 * FUSED_ROWS : nullptr;
+        q = wq_args(h, 4 * l + 3, h->HID, F, o0 + 3 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, next))) return rc;
     }
     if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
     // the race inside the head's epilogue (per 32-column group), the logits stored only when the caller wants them
@@ -566,7 +554,12 @@ int read_device_error(b2_handle* h) {
     if (e & DERR_POS) return fail(h, B2_ERR_CTX, "a position passed the context (device check, bits 0x%x)", e);
     if (e & DERR_VOVF) return fail(h, B2_ERR_VALUE, "a value-store entry did not fit int32 (device check, bits 0x%x)", e);
     if (e & DERR_INDEX) return fail(h, B2_ERR_VALUE, "an arrival index fell below the table (device check, bits 0x%x)", e);
-    if (e & DERR_TIMEOUT) return fail(h, B2_ERR_DEVICE, "a device kernel's bounded wait gave up (device check, bits 0x%x)", e);
+    if (e & DERR_TIMEOUT) {
+        // some CTAs of a quantising bank never arrived: its counters are out of step with the launches, so they start
+        // again from zero (nothing is in flight: every caller synchronised before reading the error word)
+        if (h->wq_ctr) CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * h->cfg.n_layer * 2));
+        return fail(h, B2_ERR_DEVICE, "a device kernel's bounded wait gave up (device check, bits 0x%x)", e);
+    }
     if (e & DERR_RANGE)
         return fail(h, B2_ERR_VALUE, "a value passed the range the reference asserts (turn input >= 2^31, a power or the "
                     "arrival's sum past int64; device check, bits 0x%x)", e);
@@ -837,8 +830,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->rt_y[0], h->rt_y[1], h->rt_y[2], h->rt_s[0],
-                   h->rt_s[1], h->rt_s[2], h->rt_sat, h->race_v,
+    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->race_v,
                    h->race_i, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
@@ -864,15 +856,15 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     if ((h->flags & B2_ARRIVAL_FLOAT) && (rc = dalloc(h, &h->kv.kraw, nkv * 64))) return rc;
     if ((rc = dalloc(h, &h->row_or, (size_t)4 * L * FUSED_ROWS))) return rc;
     CK(cudaMemset(h->row_or, 0, sizeof(uint64_t) * 4 * L * FUSED_ROWS));
-    for (int k = 0; k < 3; k++) {
-        const int ld = k == 2 ? F : d;
-        if ((rc = dalloc(h, &h->rt_y[k], (size_t)FUSED_ROWS * ld)) || (rc = dalloc(h, &h->rt_s[k], (size_t)FUSED_ROWS * ld / 32)))
-            return rc;
-    }
-    if ((rc = dalloc(h, &h->rt_sat, (size_t)RT_SAT_CTAS * 32 * RT_SAT_LD))) return rc;
+    if ((rc = dalloc(h, &h->wq_acc, (size_t)2 * 4 * L * FUSED_ROWS))) return rc;
+    if ((rc = dalloc(h, &h->wq_nsat, (size_t)4 * L * FUSED_ROWS))) return rc;
+    if ((rc = dalloc(h, &h->wq_ctr, (size_t)4 * L * 2))) return rc;
     h->race_ld = 4 * ((c.vocab + 127) / 128);
     if ((rc = dalloc(h, &h->race_v, (size_t)FUSED_ROWS * h->race_ld))) return rc;
     if ((rc = dalloc(h, &h->race_i, (size_t)FUSED_ROWS * h->race_ld))) return rc;
+    CK(cudaMemset(h->wq_acc, 0, sizeof(int64_t) * 2 * 4 * L * FUSED_ROWS));
+    CK(cudaMemset(h->wq_nsat, 0, sizeof(int32_t) * 4 * L * FUSED_ROWS));
+    CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * L * 2));
     if ((rc = dalloc(h, &h->slot_len, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_base, n_streams))) return rc;
     if ((rc = dalloc(h, &h->gen_desc, 1))) return rc;

@@ -64,64 +64,6 @@ B2_DEV int64_t epi_value(int64_t pile, int64_t e_j, int64_t b_j, int64_t exr, in
     return EPI == EPI_PLAIN_EDGE ? edge(v, PHI) : v;     // pythia_base2.py:156 edge(plain(..., fc))
 }
 
-// A decode bank's input rows in the compact form their producer writes ("row tiles"). For each row and each chunk of
-// 32 columns: the values shifted right by s_c = max(bit_length(OR of the chunk's magnitudes) - 16, 0) as int32 (17
-// significant bits at most) and s_c itself; and per row the OR of all its magnitudes (atomicOr by the producers).
-// Since s_c <= sh - 1 for the row's to16 shift sh >= 1 (the chunk's OR is part of the row's), X >> (sh - 1) and so
-// to16's rounded shift are recovered exactly from y (rt_to16), at half the bytes of the int64 values.
-struct RowTiles {
-    int32_t* y = nullptr;      // [rows][ld]
-    int8_t* s = nullptr;       // [rows][ld / 32]
-    uint64_t* orow = nullptr;  // [rows]
-    int ld = 0;
-};
-
-B2_DEV int rt_shift(uint64_t orv) {
-    const int top = bitlen((int64_t)orv);       // numpy's signed reading of the OR, as to16_shift
-    return top > 16 ? top - 16 : 0;
-}
-
-// x16 = rshift(X, sh) (base2.py:24-27: add half, arithmetic shift, the add wrapping past 2^63 as numpy's int64 does)
-// from y = X >> sc, given sc <= max(sh - 1, 0). With Y = X >> (sh - 1): (X + 2^(sh-1)) >> sh = (Y + 1) >> 1; the add
-// wraps exactly when Y = 2^(64 - sh) - 1, and the wrapped result is 2^(64 - sh) smaller.
-B2_DEV int32_t rt_to16(int32_t y, int sc, int sh) {
-    if (sh == 0) return y;
-    const int64_t yf = (int64_t)y >> (sh - 1 - sc);
-    int64_t x = (yf + 1) >> 1;
-    if (sh >= 48 && yf == (1ll << (64 - sh)) - 1) x -= 1ll << (64 - sh);
-    return (int32_t)x;
-}
-
-// a full warp stores row n's columns col0 + 2 lane, + 1 (col0 a multiple of 64) as row tiles, and ORs the row's
-// magnitudes into t.orow[n]; rv (row valid) is the same for the whole warp
-B2_DEV void rt_store2(const RowTiles& t, int n, int col0, int64_t v0, int64_t v1, bool rv) {
-    const int lane = threadIdx.x & 31;
-    uint64_t o = rv ? (mag(v0) | mag(v1)) : 0;
-#pragma unroll
-    for (int k = 8; k > 0; k >>= 1) o |= __shfl_xor_sync(0xffffffffu, o, k);    // the lane's 32-column half
-    const int s = rt_shift(o);
-    const uint64_t all = o | __shfl_xor_sync(0xffffffffu, o, 16);
-    if (!rv) return;
-    *reinterpret_cast<int2*>(t.y + (size_t)n * t.ld + col0 + 2 * lane) = make_int2((int32_t)(v0 >> s), (int32_t)(v1 >> s));
-    if ((lane & 15) == 0) t.s[(size_t)n * (t.ld >> 5) + (col0 >> 5) + (lane >> 4)] = (int8_t)s;
-    if (lane == 0 && t.orow) atomicOr((unsigned long long*)&t.orow[n], (unsigned long long)all);
-}
-
-// the same with one column per lane: row n's columns col0 + lane (col0 a multiple of 32)
-B2_DEV void rt_store1(const RowTiles& t, int n, int col0, int64_t v, bool rv) {
-    const int lane = threadIdx.x & 31;
-    uint64_t o = rv ? mag(v) : 0;
-#pragma unroll
-    for (int k = 16; k > 0; k >>= 1) o |= __shfl_xor_sync(0xffffffffu, o, k);
-    if (!rv) return;
-    const int s = rt_shift(o);
-    t.y[(size_t)n * t.ld + col0 + lane] = (int32_t)(v >> s);
-    if (lane == 0) {
-        t.s[(size_t)n * (t.ld >> 5) + (col0 >> 5)] = (int8_t)s;
-        if (t.orow) atomicOr((unsigned long long*)&t.orow[n], (unsigned long long)o);
-    }
-}
-
 // PDL: wait for the kernels this one depends on (no-op without programmatic launch), and let the next one start
 B2_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 B2_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

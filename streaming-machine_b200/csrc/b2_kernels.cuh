@@ -384,7 +384,6 @@ struct AttnArgs {
     int ldq;
     uint64_t* trace = nullptr;   // optional (profiling aid): %globaltimer stamps [CTA][8] (k_attend_bulk)
     uint64_t* stamp = nullptr;   // b2_profile mode 2
-    RowTiles tout{};             // decode (row-tile path): the output also as row tiles, each row's OR in tout.orow
     int early = 0;               // decode: keys before a row's own position come from earlier steps (k_attend_bulk
                                  // copies them before its dependency wait, the row's own key after it)
 };
@@ -700,9 +699,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         if (PY && bad) set_err(a.err, DERR_RANGE);
         o[2 * lane] = v0;
         o[2 * lane + 1] = v1;
-        if (a.tout.y) {
-            rt_store2(a.tout, r, h * 64, v0, v1, true);   // proj's input, and the row's OR
-        } else if (a.or_out) {
+        if (a.or_out) {
             const uint64_t w = warp_or64(mag(v0) | mag(v1));
             if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)w);
         }
@@ -953,7 +950,7 @@ __global__ void k_decode_rows(int n, const int32_t* __restrict__ tok_in, const i
 __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, const int32_t* __restrict__ slot_tok,
                                int32_t* row_slot, int32_t* row_pos, int32_t* row_tok, const int64_t* __restrict__ wte,
                                const int64_t* __restrict__ wpe, int d, int V, int nctx, int64_t* __restrict__ R,
-                               uint64_t* or_buf, int nor, int or_ld, RowTiles rt, uint32_t* err) {
+                               uint64_t* or_buf, int nor, int or_ld, int64_t* acc, int32_t* accn, uint32_t* err) {
     griddep_wait();
     griddep_launch();
     __shared__ uint64_t s_or[8];
@@ -966,19 +963,19 @@ __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, cons
     const int64_t* a = wte + (size_t)tok * d;
     const int64_t* b = wpe + (size_t)pos * d;
     uint64_t o = 0;
-    // a warp takes 32 consecutive columns at a time: one row-tile chunk (d is a multiple of 32)
-    for (int i0 = threadIdx.x & ~31; i0 < d; i0 += blockDim.x) {
-        const int i = i0 + (threadIdx.x & 31);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
         const int64_t v = wadd(__ldg(a + i), __ldg(b + i));
         R[(size_t)s * d + i] = v;
         o |= mag(v);
-        if (rt.y) {
-            RowTiles t = rt;
-            t.orow = nullptr;         // the row's OR is written whole below
-            rt_store1(t, s, i0, v, true);
-        }
     }
     for (int q = 1 + threadIdx.x; q < nor; q += blockDim.x) or_buf[(size_t)q * or_ld + s] = 0;
+    // the in-kernel quantisation's per-row accumulators of every bank input ([2][nor][or_ld] S1, S2; [nor][or_ld])
+    if (acc)
+        for (int q = threadIdx.x; q < nor; q += blockDim.x) {
+            acc[(size_t)q * or_ld + s] = 0;
+            acc[(size_t)(nor + q) * or_ld + s] = 0;
+            accn[(size_t)q * or_ld + s] = 0;
+        }
     o = warp_or64(o);
     if ((threadIdx.x & 31) == 0) s_or[threadIdx.x >> 5] = o;
     __syncthreads();

@@ -38,9 +38,7 @@ struct TcArgs {
     int heads;        // EPI_GAUGED on the split path: heads16 in the epilogue (hd), no q/k/v stores
     TcHeads hd;
     uint64_t* trace;  // optional (profiling aid): %globaltimer stamps [CTA][8] of this launch
-    TcTiles t;        // k_bank_wide<E, true>: the rows from their producer's row tiles, converted by each CTA
-    const int64_t* colcorr_kb;   // [nin / 128][nout_pad] the column corrections per 128-input block
-    int nout_pad;
+    TcQuant q;        // k_bank_wide: quantise the rows in the kernel (q.X set) instead of reading a quant kernel's
     uint64_t* or_out; // optional: OR of |stored value| over each output row (atomicOr), for the next bank's q.xor_in
     TcRace race;      // k_bank_tiles: each 32-column group's race winner per row (race.v set); out may then be null
     uint64_t* stamp;  // b2_profile mode 2
@@ -353,7 +351,7 @@ __host__ __device__ inline int wide_smem_bytes(int nkb) {
     return (nkb * WIDE_KBLOCK > 2 * WIDE_ROWS * 64 * 8 ? nkb * WIDE_KBLOCK : 2 * WIDE_ROWS * 64 * 8) + 1024;
 }
 
-template <int EPI, bool TILES>
+template <int EPI, bool QUANT>
 __global__ void __launch_bounds__(WIDE_THREADS, 1)
     k_bank_wide(const __grid_constant__ CUtensorMap mwh, const __grid_constant__ CUtensorMap mwl,
                 const __grid_constant__ CUtensorMap mxh, const __grid_constant__ CUtensorMap mxl, const TcArgs a) {
@@ -361,12 +359,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     extern __shared__ uint8_t smem_raw[];
     __shared__ uint64_t full_bar[WIDE_MAX_KB], acc_bar;
     __shared__ uint32_t tmem_slot;
-    __shared__ int s_dead, s_anysat;
+    __shared__ int s_dead, s_abort;
     __shared__ RowData s_row[WIDE_ROWS];
     __shared__ int32_t s_pos[WIDE_ROWS], s_slot[WIDE_ROWS];   // heads16: where each row's key / value goes
-    __shared__ int64_t s_part[WIDE_ROWS][3];                  // row tiles: this CTA's S1, S2 and +32768 count per row
-    __shared__ int s_sh[WIDE_ROWS], s_nsat[WIDE_ROWS];
-    __shared__ int64_t s_colc[64];                            // row tiles: the columns' correction over this K range
     uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     int64_t* HB = (int64_t*)smem;     // [32 rows][64 columns] H, over the K blocks once the MMAs are done
     int64_t* LB = HB + WIDE_ROWS * 64;   // [32 rows][64 columns] L
@@ -375,14 +370,12 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     const int kz = blockIdx.y, nz = gridDim.y;   // K range: blocks kz * kps .. + kps (cluster (1, nz, 1))
     const int r0 = blockIdx.z * WIDE_ROWS;   // rows r0 .. + 32
     const int nkb = a.kps, kb0 = kz * nkb;
-    const int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
     tstamp(a, 0);
 
-    if (tid < WIDE_ROWS) s_nsat[tid] = 0;
     if (tid == 0) {
         for (int kb = 0; kb < nkb; kb++) mbar_init(&full_bar[kb], 1);
         mbar_init(&acc_bar, 1);
-        s_anysat = 0;
+        s_abort = 0;
         s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
         fence_mbar_init();
     }
@@ -396,7 +389,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     if (tid == 0 && !dead) {          // weights: independent of earlier kernels
         for (int kb = 0; kb < nkb; kb++) {
             uint8_t* st = smem + kb * WIDE_KBLOCK;
-            mbar_expect_tx(&full_bar[kb], TILES ? WIDE_A : WIDE_KBLOCK);
+            mbar_expect_tx(&full_bar[kb], WIDE_KBLOCK);
             const uint64_t pol = l2_evict_first();   // a decode step reads each weight once
             tma_load_2d_hint(st, &mwh, &full_bar[kb], (kb0 + kb) * 128, mt * 64, pol);
             tma_load_2d_hint(st + 64 * 128, &mwl, &full_bar[kb], (kb0 + kb) * 128, mt * 64, pol);
@@ -408,25 +401,18 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     const int64_t colc0 = cv0 ? a.colcorr[j0] : 0, colc1 = cv1 ? a.colcorr[j1] : 0;
     const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
     const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
-    if (TILES && tid < 64) {          // the column correction over this CTA's K blocks only (the partners add theirs)
-        const int j = mt * 64 + tid;
-        int64_t c = 0;
-        if (j < a.nout)
-            for (int kb = 0; kb < nkb; kb++) c += a.colcorr_kb[(size_t)(kb0 + kb) * a.nout_pad + j];
-        s_colc[tid] = c;
-    }
     const bool heads = EPI == EPI_GAUGED && a.heads;
     griddep_wait();
     stamp_begin(a.stamp);
     griddep_launch();
     tstamp(a, 2);
-    // the residual this thread adds to, final now that the wait has returned (row tiles: no out_map)
+    // the residual this thread adds to, final now that the wait has returned (in-kernel quantisation: no out_map)
     constexpr int RPW = WIDE_ROWS / (WIDE_THREADS / 32);   // rows per warp in the finish
     // the finish's rows: warp w takes rows w, w + 16 of the 32 (no split) or row 16 kz + w (2-CTA split, each CTA
     // finishing half of the rows); 4- and 8-CTA splits finish 8-row slices with one column per thread (plain banks)
     const int nrpw = nz == 1 ? RPW : 1;
     int64_t pre0[RPW], pre1[RPW], pres = 0;
-    if (TILES && EPI == EPI_PLAIN_ADD) {
+    if (QUANT && EPI == EPI_PLAIN_ADD) {
         if (nz <= 2) {
 #pragma unroll
             for (int it = 0; it < RPW; it++) {
@@ -443,101 +429,83 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             if ((warp & 7) < WIDE_ROWS / nz && n < a.rows && j < a.nout) pres = a.epi.out[(size_t)n * a.epi.ldo + j];
         }
     }
-    if (TILES) {
-        // the rows' to16 from their tiles, straight into the B operand (K-major SWIZZLE_128B, xh rows 0-31, xl rows
-        // 32-63) of every K block of this CTA: a half warp per row, 8 inputs of each K block per thread, all of a
-        // thread's loads in flight together; the row's S1, S2 and +32768 entries over this K range on the way
-        const int q = tid >> 4, kq = (tid & 15) * 8, n = r0 + q;
-        const bool nv = n < a.rows && !dead;
-        const uint64_t orv = nv ? (uint64_t)__ldcg((const unsigned long long*)a.t.in.orow + n) : 0;
-        const int sh = to16_shift(orv);
-        int4 ya[WIDE_MAX_KB], yb[WIDE_MAX_KB];
-        int sc[WIDE_MAX_KB];
+    if (QUANT) {
+        // the rows' to16 and byte planes, shared out over the CTAs of this row half: item (K block kb, rows
+        // r0 + 8g ..) goes to CTA mt, mt + ntx, ..; thread t takes row 8g + t / 64, values 2 (t % 64), + 1 of the K
+        // block. The row sums go to the per-row accumulators (atomics), +32768 entries to the row's list.
+        const int ntx = gridDim.x * nz, nitems = nkb * nz * 4, cid = mt + gridDim.x * kz;
+        const int c = 2 * (tid & 63);
+        for (int it0 = cid; it0 < nitems && !dead; it0 += 2 * ntx) {
+            // up to two items per pass, both rows' loads in flight together
+            int4 v[2];
+            int n[2], kbv[2], sh[2];
 #pragma unroll
-        for (int kb = 0; kb < WIDE_MAX_KB; kb++) {
-            ya[kb] = make_int4(0, 0, 0, 0);
-            yb[kb] = ya[kb];
-            sc[kb] = 0;
-            if (kb < nkb && nv) {
-                const int k = (kb0 + kb) * 128 + kq;
-                const int4* p = reinterpret_cast<const int4*>(a.t.in.y + (size_t)n * a.t.in.ld + k);
-                ya[kb] = __ldcg(p);
-                yb[kb] = __ldcg(p + 1);
-                sc[kb] = __ldcg((const signed char*)a.t.in.s + (size_t)n * (a.t.in.ld >> 5) + (k >> 5));
-            }
-        }
-        // a rolled loop (each CTA runs this code once per launch, so its size costs instruction fetches): K block kb is
-        // always in slot 0 of the load arrays, which shift down by one per block
-        int64_t S1 = 0, S2 = 0;
-        int bad = 0;
-        const int lim = sh ? sh - 1 : 0;
-        const uint32_t bb0 = saddr(smem + WIDE_A), chunk = (uint32_t)(kq >> 4), part = kq & 15;
-        const uint32_t oh = sw128(q, chunk) + part, ol = sw128(WIDE_ROWS + q, chunk) + part;
-#pragma unroll 1
-        for (int kb = 0; kb < nkb; kb++) {
-            const int y[8] = {ya[0].x, ya[0].y, ya[0].z, ya[0].w, yb[0].x, yb[0].y, yb[0].z, yb[0].w};
-            const int sck = sc[0];
-#pragma unroll
-            for (int u = 0; u + 1 < WIDE_MAX_KB; u++) {
-                ya[u] = ya[u + 1];
-                yb[u] = yb[u + 1];
-                sc[u] = sc[u + 1];
-            }
-            bad |= sck > lim;
-            // x16 = (Y + 1) >> 1 with Y = y >> (sh - 1 - sc) (17 significant bits: 32-bit arithmetic; the shift saturates
-            // at 31, where y's sign alone is left); sh = 0: x16 = y; sh >= 48: the wrap of rt_to16, per value
-            const int t = sh ? min(sh - 1 - sck, 31) : 0;
-            uint32_t h0 = 0, h1 = 0, l0 = 0, l1 = 0;
-#pragma unroll
-            for (int i = 0; i < 8; i++) {
-                int32_t x = 0;
-                if (nv) x = sh >= 48 ? rt_to16(y[i], sck, sh) : (sh ? ((y[i] >> t) + 1) >> 1 : y[i]);
-                S1 += x;
-                S2 += (int64_t)(uint32_t)(x * x);
-                if (x == 32768) {   // rare: listed for the correction 256 * w (per CTA, over its own K range)
-                    const int u = atomicAdd(&s_nsat[q], 1);
-                    if (u < a.t.sat_ld)
-                        a.t.sat[((size_t)cta * WIDE_ROWS + q) * a.t.sat_ld + u] = (int16_t)((kb0 + kb) * 128 + kq + i);
-                    s_anysat = 1;
+            for (int u = 0; u < 2; u++) {
+                const int it = it0 + u * ntx;
+                kbv[u] = it >> 2;
+                n[u] = it < nitems ? r0 + 8 * (it & 3) + (tid >> 6) : a.rows;
+                v[u] = make_int4(0, 0, 0, 0);
+                sh[u] = 0;
+                if (n[u] < a.rows) {
+                    sh[u] = to16_shift(a.q.xor_in[n[u]]);
+                    v[u] = *reinterpret_cast<const int4*>(a.q.X + (size_t)n[u] * a.q.ldx + kbv[u] * 128 + c);
                 }
-                const uint32_t hb = hibyte16(x), lb = lobyte16(x);
-                if (i < 4) { h0 |= hb << (8 * i); l0 |= lb << (8 * i); }
-                else { h1 |= hb << (8 * (i - 4)); l1 |= lb << (8 * (i - 4)); }
             }
-            const uint32_t bb = bb0 + (uint32_t)kb * WIDE_KBLOCK;
-            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + oh), "r"(h0), "r"(h1) : "memory");
-            asm volatile("st.shared.v2.b32 [%0], {%1, %2};" ::"r"(bb + ol), "r"(l0), "r"(l1) : "memory");
-        }
-        if (bad && nv) set_err(a.err, DERR_RANGE);   // a row whose OR sets bit 63 (a value of -2^63): not computed
-        // the row's sums over its half warp
 #pragma unroll
-        for (int k = 8; k > 0; k >>= 1) {
-            S1 = wadd(S1, __shfl_xor_sync(0xffffffffu, S1, k));
-            S2 = wadd(S2, __shfl_xor_sync(0xffffffffu, S2, k));
+            for (int u = 0; u < 2; u++) {
+                if (it0 + u * ntx >= nitems) break;        // the same for the whole CTA
+                const int nn = n[u], kb = kbv[u];
+                int32_t x0 = 0, x1 = 0;
+                if (nn < a.rows) {
+                    x0 = to16_halves(v[u].x, v[u].y, sh[u]);
+                    x1 = to16_halves(v[u].z, v[u].w, sh[u]);
+                    const size_t o = (size_t)nn * a.q.kmax + kb * 128 + c;
+                    *reinterpret_cast<uint16_t*>(a.q.xh + o) = (uint16_t)(hibyte16(x0) | (hibyte16(x1) << 8));
+                    *reinterpret_cast<uint16_t*>(a.q.xl + o) = (uint16_t)(lobyte16(x0) | (lobyte16(x1) << 8));
+                    if (x0 == 32768) a.q.sat[(size_t)nn * a.q.kmax + atomicAdd(a.q.nsat + nn, 1)] = (int16_t)(kb * 128 + c);
+                    if (x1 == 32768) a.q.sat[(size_t)nn * a.q.kmax + atomicAdd(a.q.nsat + nn, 1)] = (int16_t)(kb * 128 + c + 1);
+                }
+                // a row's 64 threads are two whole warps: warp sums, one atomic per warp and sum
+                const uint32_t sq = (uint32_t)(x0 * x0) + (uint32_t)(x1 * x1);   // <= 2^31
+                const int32_t t1 = (int32_t)__reduce_add_sync(0xffffffffu, (uint32_t)(x0 + x1));
+                const uint32_t t2l = __reduce_add_sync(0xffffffffu, sq & 0xFFFFu);
+                const uint32_t t2h = __reduce_add_sync(0xffffffffu, sq >> 16);
+                if (lane == 0 && nn < a.rows) {
+                    atomicAdd((unsigned long long*)(a.q.S1 + nn), (unsigned long long)(int64_t)t1);
+                    atomicAdd((unsigned long long*)(a.q.S2 + nn), (unsigned long long)t2h * 65536ull + t2l);
+                }
+            }
         }
-        fence_proxy_async();          // the planes were written by threads; the MMAs read them through the async proxy
-        __syncthreads();              // s_nsat counts complete
-        if ((tid & 15) == 0) {
-            s_part[q][0] = S1;
-            s_part[q][1] = S2;
-            s_part[q][2] = s_nsat[q];
-            s_sh[q] = sh;
+        // arrival on this row half's counter, then wait for all ntx CTAs of it (their planes and sums are complete)
+        __syncthreads();
+        if (tid == 0) {   // the release add covers the whole CTA's writes above (they happen before it: bar.sync)
+            unsigned long long* ctr = a.q.ctr + blockIdx.z;
+            const unsigned long long arrival = atom_add_release_u64(ctr, 1);
+            const unsigned long long target = (arrival / ntx + 1) * ntx;
+            if (!dead) {
+                const uint64_t t0 = gtime(), lim = wait_limit(a.err);
+                while (ld_acquire_u64(ctr) < target) {
+                    if (gtime() - t0 > lim || (*(volatile uint32_t*)a.err & DERR_TIMEOUT)) {
+                        atomicOr(a.err, DERR_TIMEOUT);
+                        s_abort = 1;
+                        break;
+                    }
+                }
+            }
+            fence_proxy_async_global();   // the planes were written through the generic proxy; TMA reads them next
         }
         __syncthreads();
-        // the pair's gauge needs both halves' sums: exchange them now (arrive here, wait below) so the row data is
-        // ready while the MMAs run
-        if (GAUGED && nz == 2) asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
     }
     tstamp(a, 6);
-    if (!TILES && tid == 0 && !dead) {
+    if (tid == 0 && !dead && !s_abort) {
         for (int kb = 0; kb < nkb; kb++) {
             uint8_t* st = smem + kb * WIDE_KBLOCK + WIDE_A;
             tma_load_2d(st, &mxh, &full_bar[kb], (kb0 + kb) * 128, r0);
             tma_load_2d(st + WIDE_ROWS * 128, &mxl, &full_bar[kb], (kb0 + kb) * 128, r0);
         }
-    } else if (warp == 1 && lane == 0 && !dead) {
+    } else if (warp == 1 && lane == 0 && !dead && !s_abort) {
         for (int kb = 0; kb < nkb; kb++) {
-            if (!mbar_wait(&full_bar[kb], 0, a.err)) break;
+            if (!mbar_wait(&full_bar[kb], 0, a.err)) { s_abort = 1; break; }
             tc_fence_after();
             const uint32_t base = saddr(smem + kb * WIDE_KBLOCK);
 #pragma unroll
@@ -545,29 +513,22 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
                 mma_i8(tmem, sdesc(base + kk * 32), sdesc(base + WIDE_A + kk * 32), IDESC, (kb || kk) ? 1u : 0u);
         }
         mma_commit(&acc_bar);
-    }
-    __syncwarp();
-    if (TILES && GAUGED && nz == 2) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-    if (warp >= 2) {
+    } else if (warp >= 2) {
         for (int q = tid - 64; q < WIDE_ROWS; q += WIDE_THREADS - 64) {
-            if (TILES) {
+            if (QUANT) {
                 RowData d{0, 0, 0, 0, 0, r0 + q};
                 const int n = r0 + q;
                 if (n < a.rows) {
-                    const int64_t ex = -16 + s_sh[q];
-                    int64_t S1 = s_part[q][0], S2 = s_part[q][1];
+                    const int64_t ex = -16 + to16_shift(a.q.xor_in[n]);
+                    const int64_t S1 = a.q.S1[n], S2 = a.q.S2[n];
+                    const int32_t ns = a.q.nsat[n];
                     d.ex = ex;
-                    d.rowc = 128 * (S1 - 256 * s_part[q][2]);   // this CTA's share (its K range) of the row correction
                     if (GAUGED) {
-                        if (nz == 2) {          // the whole row's sums for the gauge
-                            const uint32_t off = saddr(&s_part[q][0]);
-                            S1 = wadd(S1, ld_dsmem(mapa(off, (uint32_t)(kz ^ 1))));
-                            S2 = wadd(S2, ld_dsmem(mapa(off + 8, (uint32_t)(kz ^ 1))));
-                        }
-                        d.LS = gauge_LS(S1, S2, (int)ex, a.t.LOG2, a.t.log768, a.t.eps40);
+                        d.LS = gauge_LS(S1, S2, (int)ex, a.q.LOG2, a.q.log768, a.q.eps40);
                         d.e2 = __ldg(a.epi.EXP2 + (wsub(0, d.LS) & 0xFFFF));
                     }
-                    d.nsat = s_nsat[q] < a.t.sat_ld ? s_nsat[q] : a.t.sat_ld;
+                    d.rowc = 128 * (S1 - 256 * (int64_t)ns);
+                    d.nsat = ns;
                 }
                 s_row[q] = d;
             } else {
@@ -585,7 +546,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     tc_fence_after();
     __syncthreads();
     tstamp(a, 3);
-    if (ok && warp < 8) {
+    const bool go = ok && !s_abort;
+    if (go && warp < 8) {
         const int q = warp & 3, g = warp >> 2;
         const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16);
         uint32_t xh_part[16], xl_part[16];
@@ -603,37 +565,14 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, 64);
     tstamp(a, 4);
-    if (TILES) {
-        // this CTA's partial pile over its K range, complete with its share of the corrections: P = H + L + the
-        // columns' and the row's corrections (+ 256 w for its +32768 entries); the pair / cluster sums the partials
-        for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS)
-            HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i] + (uint64_t)s_row[i >> 6].rowc + (uint64_t)s_colc[i & 63]);
-        if (s_anysat) {               // rare: warp w adds rows w, w + 16's listed entries to their 64 columns
-            __syncthreads();
-            for (int rr = warp; rr < WIDE_ROWS; rr += WIDE_THREADS / 32) {
-                const int ns = s_row[rr].nsat;
-                for (int u = 0; u < ns; u++) {
-                    const int i = a.t.sat[((size_t)cta * WIDE_ROWS + rr) * a.t.sat_ld + u];
-                    for (int c = lane; c < 64; c += 32) {
-                        const int j = mt * 64 + c;
-                        if (j < a.nout) HB[rr * 64 + c] += 256 * (int64_t)a.w16[(size_t)i * a.nout + j];
-                    }
-                }
-            }
-        }
-        __syncthreads();
-    }
-    const bool go = ok;
     if (nz > 2) {
         // split K: P = H + L in place, then CTA kz of the cluster sums rows kz * 32 / nz .. of every CTA's P over DSMEM
         // and finishes them (warp w: row w % 8 of the slice, columns 32 (w / 8) + lane). Plain banks only.
-        if (!TILES)
-            for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
+        for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
         cluster_sync();
         const int rs = WIDE_ROWS / nz, nl = kz * rs + (warp & 7), col = 32 * (warp >> 3) + lane;
         const int j = mt * 64 + col, n = r0 + nl;
-        const bool slice = (warp & 7) < rs && (warp >> 3) < 2;
-        const bool live = slice && n < a.rows && j < a.nout && go;
+        const bool live = (warp & 7) < rs && (warp >> 3) < 2 && n < a.rows && j < a.nout && go;
         int64_t w = 0;
         if (live) {
             const uint32_t off = saddr(HB + nl * 64 + col);
@@ -643,20 +582,15 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             uint64_t sum = 0;
 #pragma unroll
             for (int p = 0; p < 8; p++) sum += t[p];
-            const int64_t v = TILES ? epi_value<EPI>((int64_t)sum, (int64_t)a.epi.e[j], a.epi.b[j], s_row[nl].ex,
-                                                     s_row[nl].LS, s_row[nl].e2, a.epi.PHI)
-                                    : finish_value<EPI>(a, s_row[nl], n, j, (int64_t)sum, a.colcorr[j], (int64_t)a.epi.e[j],
-                                                        a.epi.b[j]);
+            const int64_t colc = a.colcorr[j];
+            const int64_t v = finish_value<EPI>(a, s_row[nl], n, j, (int64_t)sum, colc, (int64_t)a.epi.e[j], a.epi.b[j]);
             int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j;
-            w = EPI == EPI_PLAIN_ADD ? wadd(TILES ? pres : *o, v) : v;
-            if (!TILES || a.t.out_i64) *o = w;
+            w = EPI == EPI_PLAIN_ADD ? wadd(QUANT ? pres : *o, v) : v;
+            *o = w;
         }
-        if (slice) {                  // the next bank's input: row tiles (and the row's OR) over these 32 columns
-            if (TILES && a.t.out.y) rt_store1(a.t.out, n, mt * 64 + 32 * (warp >> 3), w, n < a.rows && go);
-            else if (a.or_out) {
-                const uint64_t wor = warp_or64(live ? mag(w) : 0);
-                if (lane == 0 && n < a.rows && go) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
-            }
+        if (a.or_out && (warp & 7) < rs && (warp >> 3) < 2) {   // the next bank's row OR over these 32 columns
+            const uint64_t wor = warp_or64(live ? mag(w) : 0);
+            if (lane == 0 && n < a.rows && go) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
         }
         tstamp(a, 5);
         cluster_sync();               // no CTA leaves while a peer may still read its P
@@ -664,8 +598,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     }
 
     if (nz == 2) {                    // P = H + L in place; the pair's tiles are complete after the barrier
-        if (!TILES)
-            for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
+        for (int i = tid; i < WIDE_ROWS * 64; i += WIDE_THREADS) HB[i] = (int64_t)((uint64_t)HB[i] + (uint64_t)LB[i]);
         cluster_sync();
     }
 
@@ -682,14 +615,9 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             uint64_t p0, p1;
             if (nz == 1) {
                 const longlong2 h = *reinterpret_cast<const longlong2*>(HB + nl * 64 + 2 * lane);
-                if (TILES) {
-                    p0 = (uint64_t)h.x;
-                    p1 = (uint64_t)h.y;
-                } else {
-                    const longlong2 l = *reinterpret_cast<const longlong2*>(LB + nl * 64 + 2 * lane);
-                    p0 = (uint64_t)h.x + (uint64_t)l.x;
-                    p1 = (uint64_t)h.y + (uint64_t)l.y;
-                }
+                const longlong2 l = *reinterpret_cast<const longlong2*>(LB + nl * 64 + 2 * lane);
+                p0 = (uint64_t)h.x + (uint64_t)l.x;
+                p1 = (uint64_t)h.y + (uint64_t)l.y;
             } else {                      // this row's two partial tiles, over DSMEM
                 const uint32_t off = saddr(HB + nl * 64 + 2 * lane);
                 uint64_t a0, a1, c0, c1;
@@ -698,14 +626,8 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
                 p0 = a0 + c0;
                 p1 = a1 + c1;
             }
-            const RowData& rd = s_row[nl];
-            if (TILES) {
-                if (jv0) v0[it] = epi_value<EPI>((int64_t)p0, e0, b0, rd.ex, rd.LS, rd.e2, a.epi.PHI);
-                if (jv1) v1[it] = epi_value<EPI>((int64_t)p1, e1, b1, rd.ex, rd.LS, rd.e2, a.epi.PHI);
-            } else {
-                if (jv0) v0[it] = finish_value<EPI>(a, rd, n, j0, (int64_t)p0, colc0, e0, b0);
-                if (jv1) v1[it] = finish_value<EPI>(a, rd, n, j1, (int64_t)p1, colc1, e1, b1);
-            }
+            if (jv0) v0[it] = finish_value<EPI>(a, s_row[nl], n, j0, (int64_t)p0, colc0, e0, b0);
+            if (jv1) v1[it] = finish_value<EPI>(a, s_row[nl], n, j1, (int64_t)p1, colc1, e1, b1);
         }
     }
     tstamp(a, 7);
@@ -715,7 +637,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
 #pragma unroll
             for (int it = 0; it < RPW; it++) {
                 const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
-                if (TILES) {
+                if (QUANT) {
                     old0[it] = pre0[it];
                     old1[it] = pre1[it];
                     continue;
@@ -732,14 +654,12 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             const bool rv = n < a.rows;
             const int64_t w0 = EPI == EPI_PLAIN_ADD ? wadd(old0[it], v0[it]) : v0[it];
             const int64_t w1 = EPI == EPI_PLAIN_ADD ? wadd(old1[it], v1[it]) : v1[it];
-            if (rv && (!TILES || a.t.out_i64)) {
+            if (rv) {
                 int64_t* o = a.epi.out + (size_t)s_row[nl].orow * a.epi.ldo + j0;
                 if (jv0) o[0] = w0;
                 if (jv1) o[1] = w1;
             }
-            if (TILES && a.t.out.y) {
-                rt_store2(a.t.out, n, mt * 64, w0, w1, rv && go);   // the next bank's input, and the row's OR
-            } else if (a.or_out) {                   // the next bank's row OR over this tile's 64 columns
+            if (a.or_out) {                          // the next bank's row OR over this tile's 64 columns
                 const uint64_t wor = warp_or64(rv ? ((jv0 ? mag(w0) : 0) | (jv1 ? mag(w1) : 0)) : 0);
                 if (lane == 0 && rv) atomicOr((unsigned long long*)&a.or_out[n], (unsigned long long)wor);
             }
@@ -1074,8 +994,8 @@ static const WideCaps& wide_caps() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= TC_MAX_DEVICES) return none;
     return tc_caps[dev];
 }
-// the row-tile decode banks split a 768-input bank over this many CTAs when the launch still fits
-// (2: half the K blocks, MMAs, conversion and finish per CTA, one DSMEM pair sum; 1: B2_WIDE_KZ=1)
+// the in-kernel-quantising decode banks split a 768-input bank over this many CTAs when the launch still fits
+// (2: half the K blocks, MMAs, quantisation and finish per CTA, one DSMEM pair sum; 1: B2_WIDE_KZ=1)
 static int tc_wide_kz = 2;
 
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
@@ -1213,9 +1133,10 @@ bool wide_fits(const TcBank& t, int rows, int* wz_out) {
            (t.nout / 64) * wz * wrh <= c.ctas[wz];
 }
 
-// the K split of the row-tile k_bank_wide for this bank: a function of the bank alone (the same for every row count).
-// A 768-input bank goes to a CTA pair when a 64-row launch of pairs still fits the device at once (qkv, proj);
-// otherwise (fc) it stays unsplit; 3,072 inputs (mproj) go to 4-CTA clusters.
+// the K split of the in-kernel-quantising k_bank_wide for this bank: a function of the bank alone, never of the
+// step's row count, because the per-(bank, row half) arrival counter assumes every launch at a site adds the same
+// number of arrivals (the CTAs along x and K). A 768-input bank goes to a CTA pair when a 64-row launch of pairs
+// still fits the device at once (qkv, proj); otherwise (fc) it stays unsplit.
 static int wide_quant_split(const TcBank& t) {
     int wz = 1;
     wide_fits(t, BN, &wz);
@@ -1227,7 +1148,7 @@ static int wide_quant_split(const TcBank& t) {
 
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
-            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcTiles* tiles,
+            cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
             uint64_t* or_out, const TcRace* race, uint64_t* stamp) {
     if (heads_done) *heads_done = false;
     if (!t.ready || rows < 1 || rows > r.rows_cap || t.nin > r.kmax) return (int)cudaErrorInvalidValue;
@@ -1274,20 +1195,18 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     int wz = 1;
     const bool wide_ok = wide_fits(t, rows, &wz);
     const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
-    if (tiles) {                      // the rows as row tiles converted by each CTA: only k_bank_wide does that
+    if (quant) {                      // the rows quantised in the kernel: only k_bank_wide does that
         if (!wide_ok || out_map || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD) ||
-            !tiles->in.y || !tiles->in.s || !tiles->in.orow || (tiles->in.ld & 31) || ((uintptr_t)tiles->in.y & 15) ||
-            (tiles->out.y && ((tiles->out.ld & 31) || ((uintptr_t)tiles->out.y & 7))) || !tiles->sat ||
-            (!tiles->out_i64 && !tiles->out.y))
+            ((uintptr_t)quant->X & 15) || (quant->ldx & 1))
             return (int)cudaErrorInvalidValue;
-        a.t = *tiles;
-        a.colcorr_kb = t.colcorr_kb;
-        a.nout_pad = t.nout_pad;
+        a.q = *quant;
+        a.q.xh = r.xh;
+        a.q.xl = r.xl;
+        a.q.sat = r.sat;
+        a.q.kmax = r.kmax;
         const int qz = wide_quant_split(t);
         if (qz > 2 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
-        const int nctas = (t.nout / 64) * qz * wrh;
-        if (nctas > wide_caps().ctas[qz] || nctas > tiles->sat_ctas || t.nin / qz > tiles->sat_ld)
-            return (int)cudaErrorInvalidValue;
+        if ((t.nout / 64) * qz * wrh > wide_caps().ctas[qz]) return (int)cudaErrorInvalidValue;
         wz = qz;
         a.ksplit = wz;
         a.kps = kb / wz;

@@ -55,18 +55,23 @@ struct TcHeads {
     int layer;
 };
 
-// a decode bank whose input rows arrive as row tiles (RowTiles, b2_epi.cuh) written by their producer: each
-// k_bank_wide CTA converts its own rows over its own K range (to16, the byte planes in shared memory, the gauge's
-// sums), so no quantisation pass or wait runs between the banks. The bank's output goes to the next bank as row tiles
-// (out.y set; out.orow gets the rows' ORs) and, when out_i64, as int64 values too (the residual, the head's input).
-struct TcTiles {
-    RowTiles in;
-    RowTiles out;
-    bool out_i64 = true;
-    const int32_t* LOG2 = nullptr;   // the gauge (gauged banks)
+// a decode bank's rows quantised inside k_bank_wide instead of by a quant kernel before it: the rows' int64 values
+// and their ORs (complete when the kernel starts), per-row accumulators for S1, S2 and the +32768 count (zero when
+// the kernel starts), and an arrival counter per 32-row half (only ever increases). tc_bank fills in the planes.
+struct TcQuant {
+    const int64_t* X = nullptr;
+    int ldx = 0;
+    const uint64_t* xor_in = nullptr;
+    int64_t* S1 = nullptr;
+    int64_t* S2 = nullptr;
+    int32_t* nsat = nullptr;
+    unsigned long long* ctr = nullptr;   // [2]
+    const int32_t* LOG2 = nullptr;
     int64_t log768 = 0, eps40 = 0;
-    int16_t* sat = nullptr;          // scratch for the rare +32768 entries: [CTA][32 rows][sat_ld], per launch
-    int sat_ld = 0, sat_ctas = 0;
+    int8_t* xh = nullptr;
+    int8_t* xl = nullptr;
+    int16_t* sat = nullptr;
+    int kmax = 0;
 };
 
 // the race fused into a bank's epilogue (the head, greedy decoding): per row, the largest value over each 32-column
@@ -83,13 +88,13 @@ int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
 void tc_bank_free(TcBank& t);
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);
-// heads (optional, EPI_GAUGED): do heads16 in the epilogue when a decode kernel runs; *heads_done tells whether it
-// did. wide_fits: whether k_bank_wide takes this bank for `rows` decode rows (the row-tile path needs it)
+// heads (optional, EPI_GAUGED): do heads16 in the epilogue when the split-K decode kernel runs; *heads_done tells
+// whether k_bank_wide takes this bank for `rows` decode rows (the in-kernel quantisation needs it)
 bool wide_fits(const TcBank& t, int rows, int* wz = nullptr);
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
-            uint64_t* trace = nullptr, const TcTiles* tiles = nullptr, uint64_t* or_out = nullptr,
+            uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
             const TcRace* race = nullptr, uint64_t* stamp = nullptr);
 
 }  // namespace b2
