@@ -86,6 +86,8 @@ struct b2_handle {
     int pf_qb = 0;                       // queries per block (16 or 8, by the context's shared memory; 0: per-row)
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int early_keys = 1;          // decode arrival: earlier positions' keys copied before the dependency wait (B2_EARLY_KEYS=0)
+    int att_split = 1;           // few (row, head) units with long contexts: keys split over a cluster (B2_ATT_SPLIT=0)
+    int sms = 148;               // the device's SM count
     int fuse_heads = 1;          // GPT-2 decode: heads16 in the qkv bank's epilogue (B2_FUSE_HEADS=0: its own kernel)
     uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
     uint64_t* att_trace = nullptr;    // B2_ATT_TRACE=<file>: the decode arrival's stamps of the last step ([L][CTA][8])
@@ -134,6 +136,7 @@ namespace {
 constexpr int FUSED_ROWS = 64;
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
 constexpr int ATT_NW = 8;                      // warps per (row, head) CTA of the bulk-copy arrival
+constexpr int ATT_CS = 4;                      // CTAs per (row, head) cluster when the arrival splits the keys
 constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
 constexpr int SPLIT_TRACE_LAUNCHES = 64, SPLIT_TRACE_SLOT = 160 * 8;   // B2_SPLIT_TRACE: launches x (CTAs x stamps)
 
@@ -377,10 +380,37 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st,
         return launch(h, B2_PROF_ATTEND, "attend_float", k_attend_float, grid, 64, sizeof(double) * h->max_ctx, st, aa);
     }
     const size_t bulk = (size_t)((h->max_ctx + 3) & ~3) * ATT_BYTES_PER_KEY;
+    // few (row, head) units with long contexts: each unit's keys split over a cluster of ATT_CS CTAs, so the launch
+    // fills the GPU in one wave with small CTAs (their largest score and sums combined over DSMEM)
+    const size_t bulk_cs = (size_t)((((h->max_ctx + ATT_CS - 1) / ATT_CS) + 3) & ~3) * ATT_BYTES_PER_KEY;
+    const bool split = h->att_bulk && h->att_split && bulk_cs <= ATT_BULK_MAX &&
+                       ((rows * h->cfg.n_head < 2 * h->sms && h->max_ctx >= 256) || bulk > ATT_BULK_MAX);
+    if (split) {
+        prof_begin(h, B2_PROF_ATTEND, st);
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(rows, h->cfg.n_head, ATT_CS);
+        cfg.blockDim = dim3(ATT_NW * 32);
+        cfg.dynamicSmemBytes = bulk_cs;
+        cfg.stream = st;
+        cudaLaunchAttribute at[2];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = ATT_CS;
+        at[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[1].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = (h->pdl && h->prof.timing != 1) ? 2 : 1;
+        const cudaError_t e = py ? cudaLaunchKernelEx(&cfg, k_attend_bulk<ATT_NW, true, ATT_CS>, aa)
+                                 : cudaLaunchKernelEx(&cfg, k_attend_bulk<ATT_NW, false, ATT_CS>, aa);
+        prof_end(h, B2_PROF_ATTEND, st);
+        if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "launch attend_bulk (split): %s", cudaGetErrorString(e));
+        return B2_OK;
+    }
     if (h->att_trace && rows <= 64) aa.trace = h->att_trace + (size_t)l * 64 * h->cfg.n_head * 8;
     if (h->att_bulk && bulk <= ATT_BULK_MAX)
-        return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, true>, grid, ATT_NW * 32, bulk, st, aa)
-                  : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, false>, grid, ATT_NW * 32, bulk, st, aa);
+        return py ? launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, true, 1>, grid, ATT_NW * 32, bulk, st, aa)
+                  : launch(h, B2_PROF_ATTEND, "attend_bulk", k_attend_bulk<ATT_NW, false, 1>, grid, ATT_NW * 32, bulk, st, aa);
     const size_t sm = sizeof(int64_t) * h->max_ctx;
     return py ? launch(h, B2_PROF_ATTEND, "attend", k_attend<4, true>, grid, 128, sm, st, aa)
               : launch(h, B2_PROF_ATTEND, "attend", k_attend<4, false>, grid, 128, sm, st, aa);
@@ -597,13 +627,17 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_GRAPH")) h->use_graph = atoi(v);
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (const char* v = getenv("B2_EARLY_KEYS")) h->early_keys = atoi(v);
+    if (const char* v = getenv("B2_ATT_SPLIT")) h->att_split = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
     if (const char* v = getenv("B2_ATT_TRACE")) h->att_trace_path = v;
     if (cudaSetDevice(device) != cudaSuccess) { delete h; return B2_ERR_CUDA; }
-    if (cudaFuncSetAttribute(k_attend_bulk<ATT_NW, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
-        cudaFuncSetAttribute(k_attend_bulk<ATT_NW, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+    if (cudaFuncSetAttribute(k_attend_bulk<ATT_NW, false, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_bulk<ATT_NW, true, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_bulk<ATT_NW, false, ATT_CS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaFuncSetAttribute(k_attend_bulk<ATT_NW, true, ATT_CS>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ATT_BULK_MAX) != cudaSuccess ||
+        cudaDeviceGetAttribute(&h->sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||
         cudaFuncSetAttribute(k_attend_prefill<8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM_MAX) != cudaSuccess ||

@@ -539,9 +539,9 @@ __global__ void __launch_bounds__(NW * 32) k_attend(AttnArgs a) {
 // ---------------------------------------------------------------------------------------------------------------------
 constexpr int ATT_BYTES_PER_KEY = 128 + 8 + 4 + 8 + 4;
 
-template <int NW, bool PY>
+template <int NW, bool PY, int CS>
 __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
-    uint64_t* const tr = a.trace ? a.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
+    uint64_t* const tr = a.trace && CS == 1 ? a.trace + ((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 : nullptr;
 #define ASTAMP(k_) \
     if (tr && threadIdx.x == 0) tr[k_] = gtime();
     ASTAMP(0)
@@ -549,6 +549,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     __shared__ uint64_t bar;
     __shared__ int32_t qs[64];
     __shared__ int64_t red[NW][66];
+    __shared__ int64_t s_max, s_part[66];          // CS > 1: this CTA's largest score; its sums (64 dims, Z, max |v|)
     const int r = blockIdx.x, h = blockIdx.y;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int H = a.kv.H, d = H * 64;
@@ -561,27 +562,32 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         griddep_launch();
     }
     const int slot = __ldcg(a.row_slot + r), p = __ldcg(a.row_pos + r);
-    if (p < 0 || p >= a.kv.lim) return;      // flagged by the qkv bank (DERR_POS); never read past the store
-    const int nk = p + 1, nkr = (nk + 3) & ~3;
-    const int ncp = a.early ? (p + 3) & ~3 : nkr;   // positions copied in bulk (from the store's start)
+    if (p < 0 || p >= a.kv.lim) return;      // flagged by the qkv bank (DERR_POS); never read past the store (the
+                                             // whole cluster returns: the row is the same for all its CTAs)
+    const int nk = p + 1;
+    // CS > 1: the CTAs of a cluster share the row's keys, rank c taking [k0, k0 + nl) (chunks of a multiple of 4 keys)
+    const int c = CS > 1 ? (int)cluster_rank() : 0;
+    const int chunk = CS > 1 ? (((nk + CS - 1) / CS + 3) & ~3) : nk;
+    const int k0 = c * chunk, nl = max(0, min(nk - k0, chunk));
+    const int nkr = (nl + 3) & ~3;           // keys this CTA copies and holds (from k0, a multiple of 4)
     int16_t* Ks = reinterpret_cast<int16_t*>(sm);
     uint64_t* KMs = reinterpret_cast<uint64_t*>(sm + (size_t)nkr * 128);
     int32_t* KEs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 136);
     int64_t* SCs = reinterpret_cast<int64_t*>(sm + (size_t)nkr * 140);
     int32_t* AVs = reinterpret_cast<int32_t*>(sm + (size_t)nkr * 148);
-    const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx);
+    const size_t base = kv_index(slot, a.layer, h, 0, a.kv.L, H, a.kv.ctx) + k0;
     if (tid == 0) {
         mbar_init(&bar, 1);
         fence_mbar_init();
     }
     __syncthreads();
     if (tid == 0) {
-        mbar_expect_tx(&bar, (uint32_t)ncp * (128 + 8 + 4));
-        if (ncp) {
-            bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)ncp * 128, &bar);
-            bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)ncp * 8, &bar);
-            bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)ncp * 4, &bar);
-            bulk_prefetch_l2(a.kv.v + base * 64, (uint32_t)ncp * 256);
+        mbar_expect_tx(&bar, (uint32_t)nkr * (128 + 8 + 4));
+        if (nkr) {
+            bulk_g2s(Ks, a.kv.k + base * 64, (uint32_t)nkr * 128, &bar);
+            bulk_g2s(KMs, a.kv.kmask + base, (uint32_t)nkr * 8, &bar);
+            bulk_g2s(KEs, a.kv.kexp + base, (uint32_t)nkr * 4, &bar);
+            bulk_prefetch_l2(a.kv.v + base * 64, (uint32_t)nkr * 256);
         }
     }
     if (a.early) {
@@ -592,27 +598,30 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     ASTAMP(1)
     if (tid < 64) qs[tid] = a.q16[(size_t)r * d + h * 64 + tid];
     const int64_t eq = a.qexp[r * H + h];
-    if (!mbar_wait(&bar, 0, a.err)) return;
-    if (a.early && wid == 0) {       // the row's own key, after the bulk copy (which may have covered its slot)
-        const size_t e = base + p;
-        reinterpret_cast<uint32_t*>(Ks + (size_t)p * 64)[lane] = __ldcg(reinterpret_cast<const unsigned int*>(a.kv.k + e * 64) + lane);
+    // a wait that gives up flags the call (DERR_TIMEOUT); a cluster's CTAs still meet at every barrier
+    const bool copied = mbar_wait(&bar, 0, a.err);
+    if (CS == 1 && !copied) return;
+    const int pl = p - k0;                   // the row's own key, local index (this CTA's when 0 <= pl < nl)
+    if (a.early && wid == 0 && pl >= 0 && pl < nl) {   // after the bulk copy (which may have covered its slot)
+        const size_t e = base + pl;
+        reinterpret_cast<uint32_t*>(Ks + (size_t)pl * 64)[lane] = __ldcg(reinterpret_cast<const unsigned int*>(a.kv.k + e * 64) + lane);
         if (lane == 0) {
-            KMs[p] = __ldcg((const unsigned long long*)a.kv.kmask + e);
-            KEs[p] = __ldcg(a.kv.kexp + e);
+            KMs[pl] = __ldcg((const unsigned long long*)a.kv.kmask + e);
+            KEs[pl] = __ldcg(a.kv.kexp + e);
         }
     }
     __syncthreads();
     ASTAMP(2)
 
-    // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of key c*4 + (lane>>3)
+    // ---- pass 1: lane holds 8 dims ((lane&7)*8..) of key cc*4 + (lane>>3)
     int qr[8];
 #pragma unroll
     for (int t = 0; t < 8; t++) qr[t] = qs[(lane & 7) * 8 + t];
     int64_t lmax = INT64_MIN;
-    for (int c = wid; c * 4 < nk; c += NW) {
-        const int key = c * 4 + (lane >> 3);
+    for (int cc = wid; cc * 4 < nl; cc += NW) {
+        const int key = cc * 4 + (lane >> 3);
         int64_t part = 0;
-        if (key < nk) {
+        if (key < nl) {
             const int4 raw = reinterpret_cast<const int4*>(Ks + (size_t)key * 64)[lane & 7];
             const int16_t* kk = reinterpret_cast<const int16_t*>(&raw);
 #pragma unroll
@@ -621,7 +630,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         part += __shfl_xor_sync(0xffffffffu, part, 1);
         part += __shfl_xor_sync(0xffffffffu, part, 2);
         part += __shfl_xor_sync(0xffffffffu, part, 4);
-        if ((lane & 7) == 0 && key < nk) {
+        if ((lane & 7) == 0 && key < nl) {
             uint64_t m = KMs[key];
             while (m) { const int t = __ffsll((long long)m) - 1; m &= m - 1; part += 65536LL * qs[t]; }
             const int64_t s = score<PY>(part, eq, (int64_t)KEs[key], a);
@@ -636,10 +645,20 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     int64_t start = red[0][65];
 #pragma unroll
     for (int k = 1; k < NW; k++) start = red[k][65] > start ? red[k][65] : start;
+    if (CS > 1) {                            // the row's largest score over the cluster's CTAs
+        if (tid == 0) s_max = start;
+        cluster_sync();
+        const uint32_t off = saddr(&s_max);
+#pragma unroll
+        for (int q = 0; q < CS; q++) {
+            const int64_t m = ld_dsmem(mapa(off, (uint32_t)q));
+            start = m > start ? m : start;
+        }
+    }
 
     // ---- pass 1b: the arrival weights and their total
     int64_t z = 0;
-    for (int s = tid; s < nk; s += NW * 32) {
+    for (int s = tid; s < nl; s += NW * 32) {
         const int64_t av = arrival(wsub(start, SCs[s]), a.ARR, a.alen, a.err);
         AVs[s] = (int32_t)av;
         z = wadd(z, av);
@@ -655,7 +674,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     uint64_t vmax = 0;
     const int2* Vg = reinterpret_cast<const int2*>(a.kv.v + base * 64);
     int s = wid;
-    for (; s + 3 * NW < nk; s += 4 * NW) {
+    for (; s + 3 * NW < nl; s += 4 * NW) {
         int2 vv[4];
         int64_t av[4];
 #pragma unroll
@@ -670,7 +689,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
             if (PY && av[u]) vmax = max(vmax, max(mag(vv[u].x), mag(vv[u].y)));
         }
     }
-    for (; s < nk; s += NW) {
+    for (; s < nl; s += NW) {
         const int64_t av = AVs[s];
         if (!av) continue;
         const int2 vv = Vg[(size_t)s * 32 + lane];
@@ -683,14 +702,37 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
     if (PY) { vmax = warp_max_u64(vmax); if (lane == 0) red[wid][65] = (int64_t)vmax; }
     __syncthreads();
     ASTAMP(5)
+    int64_t t0 = 0, t1 = 0, zz = 0;
+    uint64_t vm = 0;
     if (wid == 0) {
-        int64_t t0 = 0, t1 = 0, zz = 0;
-        uint64_t vm = 0;
 #pragma unroll
         for (int k = 0; k < NW; k++) {
             t0 = wadd(t0, red[k][2 * lane]); t1 = wadd(t1, red[k][2 * lane + 1]); zz = wadd(zz, red[k][64]);
             if (PY) vm = max(vm, (uint64_t)red[k][65]);
         }
+    }
+    if (CS > 1) {                            // the cluster's sums (wrapping int64 adds: any order gives the same bits)
+        if (wid == 0) {
+            s_part[2 * lane] = t0;
+            s_part[2 * lane + 1] = t1;
+            if (lane == 0) { s_part[64] = zz; s_part[65] = (int64_t)vm; }
+        }
+        cluster_sync();
+        if (c == 0 && wid == 0) {
+            t0 = t1 = zz = 0;
+            vm = 0;
+            const uint32_t o0 = saddr(&s_part[2 * lane]), o1 = saddr(&s_part[2 * lane + 1]), oz = saddr(&s_part[64]),
+                           ov = saddr(&s_part[65]);
+#pragma unroll
+            for (int q = 0; q < CS; q++) {
+                t0 = wadd(t0, ld_dsmem(mapa(o0, (uint32_t)q)));
+                t1 = wadd(t1, ld_dsmem(mapa(o1, (uint32_t)q)));
+                zz = wadd(zz, ld_dsmem(mapa(oz, (uint32_t)q)));
+                if (PY) vm = max(vm, (uint64_t)ld_dsmem(mapa(ov, (uint32_t)q)));
+            }
+        }
+    }
+    if (wid == 0 && c == 0) {
         const int64_t F = -log2fix(zz, a.LOG2);
         int64_t* o = a.out + (size_t)r * d + h * 64;
         bool bad = PY && (unsigned __int128)vm * (unsigned __int128)(uint64_t)zz >= ((unsigned __int128)1 << 62);
@@ -705,6 +747,7 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         }
         ASTAMP(6)
     }
+    if (CS > 1) cluster_sync();              // no CTA leaves while rank 0 may still read its sums
 #undef ASTAMP
 }
 

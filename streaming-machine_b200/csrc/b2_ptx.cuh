@@ -55,6 +55,25 @@ B2_DEV bool mbar_wait(uint64_t* bar, uint32_t phase, uint32_t* err) {
 B2_DEV void stamp_begin(uint64_t* slot) {
     if (slot && threadIdx.x == 0 && threadIdx.y == 0) atomicMin((unsigned long long*)slot, (unsigned long long)gtime());
 }
+// thread-block clusters: rank, barrier (all threads), another CTA's shared memory (DSMEM)
+B2_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+B2_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+B2_DEV uint32_t mapa(uint32_t addr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+    return r;
+}
+B2_DEV int64_t ld_dsmem(uint32_t addr) {
+    uint64_t v;
+    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr));
+    return (int64_t)v;
+}
 // bring `bytes` of global memory into L2 (no shared memory, no completion; address 16-byte aligned, bytes % 16 == 0)
 B2_DEV void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((uint64_t)src), "r"(bytes) : "memory");

@@ -83,24 +83,6 @@ B2_DEV void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
 B2_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // cluster helpers
-B2_DEV uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-B2_DEV void cluster_sync() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-B2_DEV uint32_t mapa(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-B2_DEV int64_t ld_dsmem(uint32_t addr) {
-    uint64_t v;
-    asm volatile("ld.shared::cluster.u64 %0, [%1];" : "=l"(v) : "r"(addr));
-    return (int64_t)v;
-}
 B2_DEV void mbar_arrive(uint64_t* bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(saddr(bar)) : "memory");
 }
