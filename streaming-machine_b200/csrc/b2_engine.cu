@@ -417,14 +417,15 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st,
 }
 
 // Pythia's layer norm (pythia_base2.py:100-110) of rows of X (gathered by src_rows when given) into out [rows][d]
-int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows, int ni, int64_t* out, cudaStream_t st) {
+int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows, int ni, int64_t* out, cudaStream_t st,
+              uint64_t* or_out = nullptr) {
     const b2_handle::Norm& nm = h->norms[ni];
     if (h->flags & B2_GAUGE_FLOAT)
         return launch(h, B2_PROF_QUANT, "gauge_ln_float", k_gauge_ln_float<256>, rows, 256, 0, st, X, h->cfg.d_model,
                       src_rows, rows, (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out);
     return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, rows, 256, 0, st, X, h->cfg.d_model, src_rows, rows,
                   (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2, (const int32_t*)h->EXP2,
-                  h->eps40, h->d_err, stamp_slot(h, B2_PROF_QUANT));
+                  h->eps40, h->d_err, stamp_slot(h, B2_PROF_QUANT), or_out);
 }
 
 // Pythia's layers + head (pythia_base2.py:161-169): the parallel residual R <- R + A(g1 R) + M(g2 R). Both norms read R
@@ -556,6 +557,60 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         return rc;
     return launch(h, B2_PROF_RACE, "race", k_race_parts, n, 256, 0, st, (const int64_t*)h->race_v,
                   (const int32_t*)h->race_i, h->race_ld, h->race_ld, h->race_out);
+}
+
+// Pythia-160M (pythia_base2.py:161-169) the same way: both norms publish their rows' ORs, the four banks quantise
+// their rows in the kernel, so a layer is 8 launches (norm, qkv, turn + key/value append, arrival, norm, fc + bend,
+// mproj, proj) instead of 12. The second norm's output goes to the QKV buffer (free once the turn has read it): fc
+// writes its 3,072 columns into HID while other CTAs may still be quantising their rows of its input.
+int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
+    uint64_t* OR = h->row_or;
+    int rc = launch(h, B2_PROF_OTHER, "embed_decode", k_embed_decode, n, 256, 0, st, n, h->slot_len, h->slot_tok,
+                    h->row_slot, h->row_pos, h->row_tok, h->wte, (const int64_t*)nullptr, d, c.vocab, c.n_ctx, h->R, OR,
+                    4 * L, FUSED_ROWS, h->wq_acc, h->wq_nsat, h->d_err);
+    if (rc) return rc;
+    for (int l = 0; l < L; l++) {
+        uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
+        // attention branch: g1 R -> qkv -> turn and key/value append -> arrival
+        if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l, h->ATT, st, o0))) return rc;
+        TcQuant q = wq_args(h, 4 * l, h->ATT, d, o0);
+        if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, n, h->QKV, 3 * d, nullptr, st, nullptr, nullptr, &q))) return rc;
+        if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(n, 3 * H), 32, 0, st,
+                         (const int64_t*)h->QKV, n, (const int32_t*)h->row_slot, (const int32_t*)h->row_pos, l, h->kv,
+                         (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err,
+                         (const double*)nullptr, (const double*)nullptr, (int64_t*)nullptr, stamp_slot(h, B2_PROF_HEADS))))
+            return rc;
+        if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st, 0, true))) return rc;
+        // MLP branch from the same R: g2 R -> fc + bend -> mproj; then both branches into R (mproj, proj)
+        if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l + 1, h->QKV, st, o0 + 2 * FUSED_ROWS))) return rc;
+        q = wq_args(h, 4 * l + 2, h->QKV, d, o0 + 2 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 2, EPI_PLAIN_EDGE, n, h->HID, F, nullptr, st, nullptr, nullptr, &q,
+                           o0 + 3 * FUSED_ROWS)))
+            return rc;
+        q = wq_args(h, 4 * l + 3, h->HID, F, o0 + 3 * FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q))) return rc;
+        q = wq_args(h, 4 * l + 1, h->ATT, d, o0 + FUSED_ROWS);
+        if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q))) return rc;
+    }
+    if ((rc = run_gauge(h, h->R, nullptr, n, 2 * L, h->ATT, st))) return rc;
+    if ((rc = run_quant(h, h->ATT, d, nullptr, n, 0, st))) return rc;
+    const TcRace race{h->race_v, h->race_i, h->race_ld};
+    if ((rc = run_bank(h, 4 * L, EPI_PLAIN_OUT, n, h->want_logits ? h->logits : nullptr, c.vocab, nullptr, st, nullptr,
+                       nullptr, nullptr, nullptr, &race)))
+        return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race_parts, n, 256, 0, st, (const int64_t*)h->race_v,
+                  (const int32_t*)h->race_i, h->race_ld, h->race_ld, h->race_out);
+}
+
+bool wq_pythia_ok(const b2_handle* h, int n) {
+    const b2_config& c = h->cfg;
+    if (!(h->wq && c.kind == B2_PYTHIA && h->use_tc && h->tc_min_rows <= 1 && n <= FUSED_ROWS && !h->flags))
+        return false;
+    for (int bi = 0; bi < 4 * c.n_layer; bi++)
+        if (!wide_fits(h->banks[bi].tc, n)) return false;
+    return true;
 }
 
 bool wq_ok(const b2_handle* h, int n) {
@@ -1024,8 +1079,8 @@ int b2_prefill(b2_handle* h, const int32_t* ids, const int32_t* lens, int32_t n_
 namespace {
 // one decode step for slots 0..n-1 (row r = slot r); words into the call's GenDesc, words by slot into race_out
 int step_body(b2_handle* h, int n, cudaStream_t st) {
-    if (wq_ok(h, n)) {
-        int rc = run_decode_wq(h, n, st);
+    if (wq_ok(h, n) || wq_pythia_ok(h, n)) {
+        int rc = h->cfg.kind == B2_PYTHIA ? run_decode_wq_pythia(h, n, st) : run_decode_wq(h, n, st);
         if (rc) return rc;
         return launch(h, B2_PROF_OTHER, "decode_commit", k_decode_commit, (n + 127) / 128, 128, 0, st, n, h->race_out,
                       h->slot_len, h->slot_tok, h->gen_desc, h->gen_base);

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, 
                                                  int rows, const int64_t* __restrict__ g, int64_t ge,
                                                  const int64_t* __restrict__ b, int64_t* __restrict__ out,
                                                  const int32_t* __restrict__ LOG2, const int32_t* __restrict__ EXP2,
-                                                 int64_t eps40, uint32_t* err, uint64_t* stamp) {
+                                                 int64_t eps40, uint32_t* err, uint64_t* stamp, uint64_t* or_out) {
     griddep_wait();
     stamp_begin(stamp);
     griddep_launch();
@@ -160,11 +160,26 @@ __global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, 
     __syncthreads();
     const int64_t F = s_F, S1 = s_S1;
     bool bad = false;
+    uint64_t oo = 0;
     for (int i = threadIdx.x; i < d; i += NT) {
         const int64_t c = wsub(wmul(d, rshift(x[i], sh)), S1);
-        out[(size_t)r * d + i] = wadd(power_exact(wmul(c, g[i]), F, EXP2, &bad), b[i]);
+        const int64_t v = wadd(power_exact(wmul(c, g[i]), F, EXP2, &bad), b[i]);
+        out[(size_t)r * d + i] = v;
+        oo |= mag(v);
     }
     if (bad) set_err(err, DERR_RANGE);
+    if (or_out) {                            // the next bank's to16 shift: the OR of the row's magnitudes
+        oo = warp_or64(oo);
+        __syncthreads();                     // s_or's earlier values were read above
+        if (lane == 0) s_or[wid] = oo;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            uint64_t w = 0;
+#pragma unroll
+            for (int k = 0; k < NT / 32; k++) w |= s_or[k];
+            or_out[r] = w;
+        }
+    }
 }
 
 // Pythia's q/k/v split (pythia_base2.py:116-134): one warp per (row, part of 3H), parts ordered per head q, k, v.
@@ -1004,10 +1019,10 @@ __global__ void k_embed_decode(int n, const int32_t* __restrict__ slot_len, cons
     if (tok < 0 || tok >= V) { if (threadIdx.x == 0) set_err(err, DERR_TOKEN); tok = 0; }
     if (pos < 0 || pos >= nctx) { if (threadIdx.x == 0) set_err(err, DERR_POS); pos = 0; }
     const int64_t* a = wte + (size_t)tok * d;
-    const int64_t* b = wpe + (size_t)pos * d;
+    const int64_t* b = wpe ? wpe + (size_t)pos * d : nullptr;   // Pythia: no position table
     uint64_t o = 0;
     for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const int64_t v = wadd(__ldg(a + i), __ldg(b + i));
+        const int64_t v = b ? wadd(__ldg(a + i), __ldg(b + i)) : __ldg(a + i);
         R[(size_t)s * d + i] = v;
         o |= mag(v);
     }

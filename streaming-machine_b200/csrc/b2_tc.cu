@@ -1019,7 +1019,8 @@ int tc_init() {
     void* wide[] = {(void*)k_bank_wide<EPI_GAUGED, false>,     (void*)k_bank_wide<EPI_GAUGED_EDGE, false>,
                     (void*)k_bank_wide<EPI_PLAIN_ADD, false>,  (void*)k_bank_wide<EPI_PLAIN_OUT, false>,
                     (void*)k_bank_wide<EPI_PLAIN_EDGE, false>, (void*)k_bank_wide<EPI_GAUGED, true>,
-                    (void*)k_bank_wide<EPI_GAUGED_EDGE, true>, (void*)k_bank_wide<EPI_PLAIN_ADD, true>};
+                    (void*)k_bank_wide<EPI_GAUGED_EDGE, true>, (void*)k_bank_wide<EPI_PLAIN_ADD, true>,
+                    (void*)k_bank_wide<EPI_PLAIN_OUT, true>,   (void*)k_bank_wide<EPI_PLAIN_EDGE, true>};
     for (void* f : wide) {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem_bytes(WIDE_MAX_KB));
         if (e != cudaSuccess) return (int)e;
@@ -1196,7 +1197,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     const bool wide_ok = wide_fits(t, rows, &wz);
     const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
     if (quant) {                      // the rows quantised in the kernel: only k_bank_wide does that
-        if (!wide_ok || out_map || (epi != EPI_GAUGED && epi != EPI_GAUGED_EDGE && epi != EPI_PLAIN_ADD) ||
+        if (!wide_ok || out_map ||
             ((uintptr_t)quant->X & 15) || (quant->ldx & 1))
             return (int)cudaErrorInvalidValue;
         a.q = *quant;
@@ -1218,15 +1219,9 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         }
         dim3 grid(t.nout / 64, wz, wrh);
         const size_t sm = wide_smem_bytes(a.kps);
-        if (epi == EPI_GAUGED)
-            err = launch_k(k_bank_wide<EPI_GAUGED, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
-                           r.maps[mi].l32, a, true);
-        else if (epi == EPI_GAUGED_EDGE)
-            err = launch_k(k_bank_wide<EPI_GAUGED_EDGE, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
-                           r.maps[mi].l32, a, true);
-        else
-            err = launch_k(k_bank_wide<EPI_PLAIN_ADD, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t, r.maps[mi].h32,
-                           r.maps[mi].l32, a, true);
+        B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t,
+                                          r.maps[mi].h32, r.maps[mi].l32, a, true);
+                      break)
     } else if (tc_wide && wide_ok && wz == 1) {
         // one CTA per 64 output columns over the whole K range (no split, no cluster)
         a.ksplit = 1;
@@ -1262,7 +1257,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.stages = MAX_STAGES;
         a.trace = trace;
         if (race) {
-            if (epi != EPI_GAUGED || race->ld < mtiles * 4) return (int)cudaErrorInvalidValue;
+            if ((epi != EPI_GAUGED && epi != EPI_PLAIN_OUT) || race->ld < mtiles * 4) return (int)cudaErrorInvalidValue;
             a.race = *race;
         }
         size_t smem = (size_t)MAX_STAGES * STAGE + 1024;
