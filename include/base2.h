@@ -64,6 +64,18 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out);
 int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t* e, const int64_t* b,
                 int32_t nin, int32_t nout);
 
+/* A bank's tensor-core layout computed ahead of time (streaming_machine_b200/layout.py writes it to disk beside the
+ * reference's device files, base2_gpu.py:9-17): wh = w >> 8 and wl = (w & 255) - 128 as int8 [nout_pad][nin]
+ * (K-major, nout_pad = nout rounded up to 128, padded outputs w = 0), colcorr [nout_pad] = 128 sum_i w[i][j] - 16384 nin,
+ * colcorr_kb [nin / 128][nout_pad] the same per 128-input block (0 on padded outputs). Given after that bank's
+ * b2_set_bank and before b2_finalize, finalize uploads it instead of building it on the device. No reference
+ * counterpart: the reference's device layout is the [nin][nout] int16 bank itself. */
+int b2_set_bank_layout(b2_handle* h, const char* name, const int8_t* wh, const int8_t* wl, const int64_t* colcorr,
+                       const int64_t* colcorr_kb);
+
+/* Copy a finalized bank's tensor-core layout (as above) to host buffers: to check or save a layout file. */
+int b2_get_bank_layout(b2_handle* h, const char* name, int8_t* wh, int8_t* wl, int64_t* colcorr, int64_t* colcorr_kb);
+
 /* A table or embedding by its npz key (base2_convert.py:46-59): "wte" [vocab][d], "wpe" [n_ctx][d], "phi" [65536],
  * "arrival" [n], "log2" [65536], "exp2" [65536]. Pythia (pythia_convert.py's keys, `plates=finished`): "embed.w"
  * [vocab][d] and "embed.e" [vocab] (each word's row and its power of two), "cos"/"sin" [n_ctx][rot/2] at 2^-30, and

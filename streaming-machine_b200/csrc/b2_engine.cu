@@ -740,6 +740,32 @@ int b2_set_bank(b2_handle* h, const char* name, const int16_t* w, const int64_t*
     return B2_OK;
 }
 
+int b2_set_bank_layout(b2_handle* h, const char* name, const int8_t* wh, const int8_t* wl, const int64_t* colcorr,
+                       const int64_t* colcorr_kb) {
+    if (!h || !name || !wh || !wl || !colcorr || !colcorr_kb) return fail(h, B2_ERR_ARG, "b2_set_bank_layout: null argument");
+    CK(cudaSetDevice(h->device));
+    const int bi = bank_index(h, name);
+    if (bi < 0) return fail(h, B2_ERR_ARG, "b2_set_bank_layout: unknown bank '%s'", name);
+    DevBank& bk = h->banks[bi];
+    if (!bk.w) return fail(h, B2_ERR_STATE, "b2_set_bank_layout %s: b2_set_bank first", name);
+    if (h->flags) return fail(h, B2_ERR_STATE, "b2_set_bank_layout: a handle with float stages has no tensor-core layout");
+    const int rc = tc_bank_upload(bk.tc, bk.nin, bk.nout, wh, wl, colcorr, colcorr_kb);
+    if (rc) return fail(h, B2_ERR_CUDA, "b2_set_bank_layout %s: %s", name, cudaGetErrorString((cudaError_t)rc));
+    h->finalized = false;
+    return B2_OK;
+}
+
+int b2_get_bank_layout(b2_handle* h, const char* name, int8_t* wh, int8_t* wl, int64_t* colcorr, int64_t* colcorr_kb) {
+    if (!h || !name || !wh || !wl || !colcorr || !colcorr_kb) return fail(h, B2_ERR_ARG, "b2_get_bank_layout: null argument");
+    CK(cudaSetDevice(h->device));
+    const int bi = bank_index(h, name);
+    if (bi < 0) return fail(h, B2_ERR_ARG, "b2_get_bank_layout: unknown bank '%s'", name);
+    if (!h->finalized || !h->banks[bi].tc.ready) return fail(h, B2_ERR_STATE, "b2_get_bank_layout %s: no tensor-core layout", name);
+    const int rc = tc_bank_download(h->banks[bi].tc, wh, wl, colcorr, colcorr_kb);
+    if (rc) return fail(h, B2_ERR_CUDA, "b2_get_bank_layout %s: %s", name, cudaGetErrorString((cudaError_t)rc));
+    return B2_OK;
+}
+
 int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n) {
     if (!h || !name || !data || n <= 0) return fail(h, B2_ERR_ARG, "b2_set_array: bad argument");
     CK(cudaSetDevice(h->device));

@@ -1056,22 +1056,57 @@ int tc_init() {
     return 0;
 }
 
-int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
+static int tc_bank_alloc(TcBank& t, int nin, int nout) {
     tc_bank_free(t);
     if (nin % 128) return (int)cudaErrorInvalidValue;
     t.nin = nin;
     t.nout = nout;
     t.nout_pad = (nout + 127) / 128 * 128;
-    t.w16 = w;
     cudaError_t e;
     if ((e = cudaMalloc(&t.wh, (size_t)t.nout_pad * nin)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&t.wl, (size_t)t.nout_pad * nin)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&t.colcorr, sizeof(int64_t) * t.nout_pad)) != cudaSuccess) return (int)e;
     if ((e = cudaMalloc(&t.colcorr_kb, sizeof(int64_t) * t.nout_pad * (nin / 128))) != cudaSuccess) return (int)e;
-    k_weight_planes<<<dim3(t.nout_pad / 32, (nin + 31) / 32), dim3(32, 8)>>>(w, nin, nout, t.wh, t.wl);
-    k_colcorr<<<(t.nout_pad + 255) / 256, 256>>>(w, nin, nout, t.nout_pad, t.colcorr);
-    k_colcorr_kb<<<dim3((t.nout_pad + 255) / 256, nin / 128), 256>>>(w, nin, nout, t.nout_pad, t.colcorr_kb);
-    if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    return 0;
+}
+
+int tc_bank_upload(TcBank& t, int nin, int nout, const int8_t* wh, const int8_t* wl, const int64_t* cc, const int64_t* cckb) {
+    int rc = tc_bank_alloc(t, nin, nout);
+    if (rc) return rc;
+    const size_t np = (size_t)t.nout_pad;
+    cudaError_t e;
+    if ((e = cudaMemcpy(t.wh, wh, np * nin, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(t.wl, wl, np * nin, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(t.colcorr, cc, sizeof(int64_t) * np, cudaMemcpyHostToDevice)) != cudaSuccess ||
+        (e = cudaMemcpy(t.colcorr_kb, cckb, sizeof(int64_t) * np * (nin / 128), cudaMemcpyHostToDevice)) != cudaSuccess)
+        return (int)e;
+    t.prebuilt = 1;
+    return 0;
+}
+
+int tc_bank_download(const TcBank& t, int8_t* wh, int8_t* wl, int64_t* cc, int64_t* cckb) {
+    if (!t.ready) return (int)cudaErrorInvalidValue;
+    const size_t np = (size_t)t.nout_pad;
+    cudaError_t e;
+    if ((e = cudaMemcpy(wh, t.wh, np * t.nin, cudaMemcpyDeviceToHost)) != cudaSuccess ||
+        (e = cudaMemcpy(wl, t.wl, np * t.nin, cudaMemcpyDeviceToHost)) != cudaSuccess ||
+        (e = cudaMemcpy(cc, t.colcorr, sizeof(int64_t) * np, cudaMemcpyDeviceToHost)) != cudaSuccess ||
+        (e = cudaMemcpy(cckb, t.colcorr_kb, sizeof(int64_t) * np * (t.nin / 128), cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return (int)e;
+    return 0;
+}
+
+int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
+    cudaError_t e;
+    if (!(t.prebuilt && t.nin == nin && t.nout == nout)) {   // no uploaded layout: build it from w on the device
+        int rc = tc_bank_alloc(t, nin, nout);
+        if (rc) return rc;
+        k_weight_planes<<<dim3(t.nout_pad / 32, (nin + 31) / 32), dim3(32, 8)>>>(w, nin, nout, t.wh, t.wl);
+        k_colcorr<<<(t.nout_pad + 255) / 256, 256>>>(w, nin, nout, t.nout_pad, t.colcorr);
+        k_colcorr_kb<<<dim3((t.nout_pad + 255) / 256, nin / 128), 256>>>(w, nin, nout, t.nout_pad, t.colcorr_kb);
+        if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
+    }
+    t.w16 = w;
     int rc = make_map(t.map_wh, t.wh, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wl, t.wl, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wh64, t.wh, nin, t.nout_pad, nin, 64);
@@ -1089,6 +1124,7 @@ void tc_bank_free(TcBank& t) {
     t.wh = t.wl = nullptr;
     t.colcorr = t.colcorr_kb = nullptr;
     t.ready = 0;
+    t.prebuilt = 0;
 }
 
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err) {

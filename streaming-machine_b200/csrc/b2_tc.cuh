@@ -20,6 +20,7 @@ struct TcMap { alignas(64) unsigned char bytes[128]; };
 // A bank in the tensor-core layout: the two weight planes, K-major ([out][in]), padded to 128 outputs.
 struct TcBank {
     int ready = 0;
+    int prebuilt = 0;            // the planes and corrections were uploaded (tc_bank_upload), not built from w
     int nin = 0, nout = 0, nout_pad = 0;
     int8_t* wh = nullptr;        // [nout_pad][nin]
     int8_t* wl = nullptr;        // [nout_pad][nin]
@@ -85,6 +86,10 @@ struct TcRace {
 int tc_min_rows_default();
 int tc_init();
 int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout);
+// a layout computed ahead of time (host arrays: wh, wl [nout_pad][nin], cc [nout_pad], cckb [nin/128][nout_pad]); the
+// next tc_bank_build of the same shape keeps it instead of building one
+int tc_bank_upload(TcBank& t, int nin, int nout, const int8_t* wh, const int8_t* wl, const int64_t* cc, const int64_t* cckb);
+int tc_bank_download(const TcBank& t, int8_t* wh, int8_t* wl, int64_t* cc, int64_t* cckb);
 void tc_bank_free(TcBank& t);
 int tc_rows_alloc(TcRows& r, int rows_cap, int kmax, uint32_t* err);
 void tc_rows_free(TcRows& r);

@@ -26,8 +26,8 @@ STATUS = {0: "OK", 1: "ERR_ARG", 2: "ERR_CUDA", 3: "ERR_NOMEM", 4: "ERR_CTX", 5:
 # every symbol include/base2.h declares
 EXPORTS = ("b2_create", "b2_set_bank", "b2_set_array", "b2_set_scalar", "b2_finalize", "b2_alloc_streams",
            "b2_prefill", "b2_step", "b2_generate", "b2_step_host", "b2_bank", "b2_gauge", "b2_bank_noalloc",
-           "b2_rewind", "b2_profile", "b2_profile_read", "b2_sync", "b2_check_wait", "b2_last_error", "b2_destroy",
-           "b2_abi_version")
+           "b2_rewind", "b2_profile", "b2_profile_read", "b2_sync", "b2_check_wait", "b2_set_bank_layout",
+           "b2_get_bank_layout", "b2_last_error", "b2_destroy", "b2_abi_version")
 PROF_CLASSES = ("bank", "attend", "quant", "heads", "race", "other")
 
 
@@ -68,6 +68,8 @@ def lib():
         L.b2_profile_read.argtypes = [vp, vp, vp, vp]
         L.b2_sync.argtypes = [vp]
         L.b2_check_wait.argtypes = [vp, vp]
+        L.b2_set_bank_layout.argtypes = [vp, cp, vp, vp, vp, vp]
+        L.b2_get_bank_layout.argtypes = [vp, cp, vp, vp, vp, vp]
         L.b2_last_error.argtypes = [vp]
         L.b2_last_error.restype = cp
         L.b2_destroy.argtypes = [vp]
@@ -95,9 +97,10 @@ class Engine:
     Pythia's "embed.w") on one GPU, with `n_streams` independent streams of up to `max_ctx` positions."""
 
     def __init__(self, M: dict, device: int = 0, n_streams: int = 1, max_ctx: int = 1024,
-                 gauge: str = "int", edge: str = "int", arrival: str = "int", turn: str = "int"):
+                 gauge: str = "int", edge: str = "int", arrival: str = "int", turn: str = "int", layout: dict | None = None):
         """gauge=/edge=/arrival= "float" (and Pythia's turn=) put that stage back to float64, as the reference's
-        switches do (base2.py:10-11, pythia_base2.py:20)."""
+        switches do (base2.py:10-11, pythia_base2.py:20). layout: the banks' tensor-core layouts computed ahead of time
+        ({bank: {wh, wl, cc, cckb}}, streaming_machine_b200.layout.read_tc_layout), uploaded instead of built."""
         torch = _torch()
         self.torch = torch
         self.device = torch.device("cuda", device)
@@ -127,6 +130,11 @@ class Engine:
             b = np.ascontiguousarray(M[name + ".b"], dtype=np.int64) if name + ".b" in M else None   # Pythia's head
             self._call("b2_set_bank", h, name.encode(), w.ctypes.data, e.ctypes.data,
                        b.ctypes.data if b is not None else None, w.shape[0], w.shape[1])
+            if layout is not None:
+                t = layout[name]
+                arrs = [np.ascontiguousarray(t[k], dtype=dt) for k, dt in
+                        (("wh", np.int8), ("wl", np.int8), ("cc", np.int64), ("cckb", np.int64))]
+                self._call("b2_set_bank_layout", h, name.encode(), *[a.ctypes.data for a in arrs])
         if self.pythia:
             norms = [f"ln{i}.{l}" for l in range(n_layer) for i in (1, 2)] + ["lnf"]
             arrays = ["embed.w", "embed.e", "cos", "sin", "phi", "arrival", "log2", "exp2"] + \
@@ -285,6 +293,17 @@ class Engine:
 
     def sync(self):
         self._call("b2_sync", self.h)
+
+    def bank_layout(self, name: str) -> dict:
+        """The tensor-core layout the device holds for a bank (as streaming_machine_b200.layout.tc_layout gives it)."""
+        nin, nout = (self.cfg.d_ff, self.cfg.d_model) if name.startswith("mproj") else (self.cfg.d_model, None)
+        nout = nout or ({"qkv": 3 * self.cfg.d_model, "proj": self.cfg.d_model, "fc": self.cfg.d_ff}.get(
+            name.split(".")[0]) if name != "head" else self.V)
+        pad = (nout + 127) // 128 * 128
+        out = dict(wh=np.empty((pad, nin), np.int8), wl=np.empty((pad, nin), np.int8), cc=np.empty(pad, np.int64),
+                   cckb=np.empty((nin // 128, pad), np.int64))
+        self._call("b2_get_bank_layout", self.h, name.encode(), *[out[k].ctypes.data for k in ("wh", "wl", "cc", "cckb")])
+        return out
 
     def set_wait_limit(self, ns: int):
         """How long a device-side wait may take before the kernel gives up and the call reports B2_ERR_DEVICE
