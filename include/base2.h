@@ -85,7 +85,11 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
 /* A scalar by its npz key: "log2_768", "eps40" (base2_convert.py:60-61); Pythia: "eps40", "half_log2_hs", "rot"
  * (16) and each norm's gain exponent "ln1.<l>.ge", "ln2.<l>.ge", "lnf.ge". One engine setting besides: "wait_ns",
  * how long a device-side wait (a TMA or bulk-copy completion, a counter other CTAs raise) may take before the
- * kernel gives up, flags the call and returns (default 0 = 0.5 s); it may be set at any time. */
+ * kernel gives up, flags the call and returns (default 0 = 0.5 s); it may be set at any time. And "top_read" (the
+ * reference's top=plain / top=fr switch, base2_stream_fr2.swift:23-38): 0 (default) scores every word then races;
+ * 1 races decode steps of up to 4 streams that store no scores by the exact collapsing read (every word's coarse score
+ * from the high byte plane, bounds from the input's positive and negative sums, only the words that can still win read
+ * their low bytes): the same words. */
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v);
 
 /* All arrays given: build the device layouts. */

@@ -87,6 +87,10 @@ struct b2_handle {
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int early_keys = 1;          // decode arrival: earlier positions' keys copied before the dependency wait (B2_EARLY_KEYS=0)
     int att_split = 1;           // few (row, head) units with long contexts: keys split over a cluster (B2_ATT_SPLIT=0)
+    // the collapsing top read (b2_set_scalar "top_read" 1): decode steps of <= TOPFR_ROWS streams that store no scores
+    int top_fr = 0;
+    int64_t *fr_C = nullptr, *fr_HIS = nullptr, *fr_p5v = nullptr, *fr_sv = nullptr;
+    int32_t *fr_p5i = nullptr, *fr_list = nullptr, *fr_cnt = nullptr, *fr_si = nullptr;
     int sms = 148;               // the device's SM count
     int fuse_heads = 1;          // GPT-2 decode: heads16 in the qkv bank's epilogue (B2_FUSE_HEADS=0: its own kernel)
     uint64_t* split_trace = nullptr;  // B2_SPLIT_TRACE=<file>: the split-K bank kernels' stamps of the last step
@@ -522,6 +526,50 @@ TcQuant wq_args(b2_handle* h, int site, const int64_t* X, int ldx, const uint64_
     return q;
 }
 
+// the collapsing top read over the head's quantised rows (k_quant done): coarse sums and bounds of every word, T5 and
+// the words still in, their exact scores, the race among them; the words by slot into race_out
+constexpr int FR_PARTS = 296, FR_FIN = 148;
+bool top_fr_ok(const b2_handle* h, int n) {
+    const DevBank& hb = h->banks[4 * h->cfg.n_layer];
+    return h->top_fr && !h->want_logits && n <= TOPFR_ROWS && hb.tc.ready && hb.nin == TOPFR_NIN && h->fr_C;
+}
+int run_top_fr(b2_handle* h, int n, cudaStream_t st) {
+    const DevBank& hb = h->banks[4 * h->cfg.n_layer];
+    TopFrArgs a{};
+    a.wh = hb.tc.wh;
+    a.wl = hb.tc.wl;
+    a.x16 = h->x16;
+    a.ex = h->ex;
+    a.LS = h->LS;
+    a.e = hb.e;
+    a.b = hb.b;
+    a.EXP2 = h->EXP2;
+    a.nout = hb.nout;
+    a.rows = n;
+    a.C = h->fr_C;
+    a.HIS = h->fr_HIS;
+    a.p5v = h->fr_p5v;
+    a.p5i = h->fr_p5i;
+    a.nparts = FR_PARTS;
+    a.list = h->fr_list;
+    a.cnt = h->fr_cnt;
+    a.sv = h->fr_sv;
+    a.si = h->fr_si;
+    a.nfin = FR_FIN;
+    a.stamp = stamp_slot(h, B2_PROF_BANK);
+    const bool py = h->cfg.kind == B2_PYTHIA;
+    int rc = py ? launch(h, B2_PROF_BANK, "top_coarse", k_top_coarse<EPI_PLAIN_OUT>, FR_PARTS, 256, 0, st, a)
+                : launch(h, B2_PROF_BANK, "top_coarse", k_top_coarse<EPI_GAUGED>, FR_PARTS, 256, 0, st, a);
+    if (rc) return rc;
+    a.stamp = nullptr;
+    if ((rc = launch(h, B2_PROF_RACE, "top_select", k_top_select, n, 1024, 0, st, a))) return rc;
+    rc = py ? launch(h, B2_PROF_RACE, "top_finish", k_top_finish<EPI_PLAIN_OUT>, dim3(FR_FIN, n), 256, 0, st, a)
+            : launch(h, B2_PROF_RACE, "top_finish", k_top_finish<EPI_GAUGED>, dim3(FR_FIN, n), 256, 0, st, a);
+    if (rc) return rc;
+    return launch(h, B2_PROF_RACE, "race", k_race_parts, n, 256, 0, st, (const int64_t*)h->fr_sv, (const int32_t*)h->fr_si,
+                  FR_FIN, FR_FIN, h->race_out);
+}
+
 int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, F = c.d_ff;
@@ -550,6 +598,7 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, next))) return rc;
     }
     if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
+    if (top_fr_ok(h, n)) return run_top_fr(h, n, st);
     // the race inside the head's epilogue (per 32-column group), the logits stored only when the caller wants them
     const TcRace race{h->race_v, h->race_i, h->race_ld};
     if ((rc = run_bank(h, 4 * L, EPI_GAUGED, n, h->want_logits ? h->logits : nullptr, c.vocab, nullptr, st, nullptr,
@@ -596,6 +645,7 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
     }
     if ((rc = run_gauge(h, h->R, nullptr, n, 2 * L, h->ATT, st))) return rc;
     if ((rc = run_quant(h, h->ATT, d, nullptr, n, 0, st))) return rc;
+    if (top_fr_ok(h, n)) return run_top_fr(h, n, st);
     const TcRace race{h->race_v, h->race_i, h->race_ld};
     if ((rc = run_bank(h, 4 * L, EPI_PLAIN_OUT, n, h->want_logits ? h->logits : nullptr, c.vocab, nullptr, st, nullptr,
                        nullptr, nullptr, nullptr, &race)))
@@ -811,6 +861,12 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
 
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v) {
     if (!h || !name) return B2_ERR_ARG;
+    if (!strcmp(name, "top_read")) {   // 0: every word's exact score, then the race; 1: the collapsing read
+        if (v != 0 && v != 1) return fail(h, B2_ERR_ARG, "top_read = %lld (0 or 1)", (long long)v);
+        h->top_fr = (int)v;
+        drop_graph(h);
+        return B2_OK;
+    }
     if (!strcmp(name, "wait_ns")) {   // the bounded device waits' limit (not a model scalar: finalize state unchanged)
         if (v < 0) return fail(h, B2_ERR_ARG, "wait_ns = %lld is negative", (long long)v);
         CK(cudaSetDevice(h->device));
@@ -945,7 +1001,8 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     CK(cudaSetDevice(h->device));
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
-    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->race_v,
+    void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->fr_C, h->fr_HIS,
+                   h->fr_p5v, h->fr_p5i, h->fr_list, h->fr_cnt, h->fr_sv, h->fr_si, h->race_v,
                    h->race_i, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
@@ -977,6 +1034,15 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     h->race_ld = 4 * ((c.vocab + 127) / 128);
     if ((rc = dalloc(h, &h->race_v, (size_t)FUSED_ROWS * h->race_ld))) return rc;
     if ((rc = dalloc(h, &h->race_i, (size_t)FUSED_ROWS * h->race_ld))) return rc;
+    {
+        const size_t V = (size_t)c.vocab;
+        if ((rc = dalloc(h, &h->fr_C, TOPFR_ROWS * V)) || (rc = dalloc(h, &h->fr_HIS, TOPFR_ROWS * V)) ||
+            (rc = dalloc(h, &h->fr_p5v, (size_t)TOPFR_ROWS * FR_PARTS * 5)) ||
+            (rc = dalloc(h, &h->fr_p5i, (size_t)TOPFR_ROWS * FR_PARTS * 5)) || (rc = dalloc(h, &h->fr_list, TOPFR_ROWS * V)) ||
+            (rc = dalloc(h, &h->fr_cnt, TOPFR_ROWS)) || (rc = dalloc(h, &h->fr_sv, (size_t)TOPFR_ROWS * FR_FIN)) ||
+            (rc = dalloc(h, &h->fr_si, (size_t)TOPFR_ROWS * FR_FIN)))
+            return rc;
+    }
     CK(cudaMemset(h->wq_acc, 0, sizeof(int64_t) * 2 * 4 * L * FUSED_ROWS));
     CK(cudaMemset(h->wq_nsat, 0, sizeof(int32_t) * 4 * L * FUSED_ROWS));
     CK(cudaMemset(h->wq_ctr, 0, sizeof(unsigned long long) * 4 * L * 2));

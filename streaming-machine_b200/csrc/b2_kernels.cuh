@@ -1255,3 +1255,245 @@ __global__ void k_prefill_rows(int r0, int rows, const int32_t* __restrict__ row
 }
 
 }  // namespace b2
+
+namespace b2 {
+
+// ---------------------------------------------------------------------------------------------------------------------
+// The exact collapsing top read (the reference's top=fr, base2_stream_fr2.swift:23-38, kernels :194-406, host
+// :832-898), for decode steps of a few streams whose scores are not stored. A head weight is w = 256 wh + lo with
+// wh = w >> 8 (the wh plane) and lo = w & 255 = wl + 128 (the wl plane), so a word's pile is 256 C + L with
+// C = sum wh x over the whole plane and L = sum lo x in [255 SN, 255 SP] (SN, SP: the sums of the input's negative
+// and positive values). The head's epilogue is non-decreasing in the pile (no wrap: |pile| < 2^42), so every word has
+// a low and a high score; T5 is the 5th-best low (larger, then lower slot), and a word whose high is below T5 is below
+// five other words' exact scores: only the words still in read their wl rows and get the exact score, and the race
+// runs among them (largest, ties to the lowest slot: base2.py:34-40). Bit-exact with the plain race.
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int TOPFR_ROWS = 4;    // streams per decode step the collapsing read takes
+constexpr int TOPFR_NIN = 768;   // the head's inputs (a lane holds 24 of them)
+
+struct TopFrArgs {
+    const int8_t* wh;            // [nout_pad][nin] K-major (word by word)
+    const int8_t* wl;
+    const int32_t* x16;          // [rows][nin] the head's input, to16'd (k_quant)
+    const int32_t* ex;           // [rows]
+    const int64_t* LS;           // [rows] (gauged head)
+    const int32_t* e;            // [nout]
+    const int64_t* b;            // [nout]
+    const int32_t* EXP2;
+    int nout, rows;
+    int64_t* C;                  // [TOPFR_ROWS][nout] every word's coarse sum (sum wh x)
+    int64_t* HIS;                // [TOPFR_ROWS][nout] its high score
+    int64_t* p5v;                // [TOPFR_ROWS][nparts][5] each coarse CTA's five best lows
+    int32_t* p5i;
+    int nparts;
+    int32_t* list;               // [TOPFR_ROWS][nout] the words still in
+    int32_t* cnt;                // [TOPFR_ROWS]
+    int64_t* sv;                 // [TOPFR_ROWS][nfin] each finishing CTA's best (score, word)
+    int32_t* si;
+    int nfin;
+    uint64_t* stamp;             // b2_profile mode 2 (the coarse read)
+};
+
+// (larger score, then lower slot) first: the race's own order
+B2_DEV bool fr_better(int64_t a, int ia, int64_t b, int ib) { return a > b || (a == b && ia < ib); }
+B2_DEV void fr_put5(int64_t* v, int* ix, int64_t u, int iu) {
+    if (!fr_better(u, iu, v[4], ix[4])) return;
+    v[4] = u;
+    ix[4] = iu;
+#pragma unroll
+    for (int k = 4; k > 0; k--)
+        if (fr_better(v[k], ix[k], v[k - 1], ix[k - 1])) {
+            const int64_t tv = v[k]; v[k] = v[k - 1]; v[k - 1] = tv;
+            const int ti = ix[k]; ix[k] = ix[k - 1]; ix[k - 1] = ti;
+        }
+}
+template <int EPI>
+B2_DEV int64_t fr_score(int64_t pile, int j, int r, const TopFrArgs& a) {
+    const int64_t ex = a.ex[r];
+    const int64_t LS = EPI == EPI_GAUGED ? a.LS[r] : 0;
+    const int64_t e2 = EPI == EPI_GAUGED ? (int64_t)__ldg(a.EXP2 + (wsub(0, LS) & 0xFFFF)) : 0;
+    return epi_value<EPI>(pile, (int64_t)a.e[j], a.b[j], ex, LS, e2, nullptr);
+}
+// this lane's 24 inputs of row r (inputs 16 lane .. + 16 and 512 + 8 lane .. + 8) and the row's S1, SP, SN
+B2_DEV void fr_row(const TopFrArgs& a, int r, int lane, int (&x)[24], int64_t& S1, int64_t& SP, int64_t& SN) {
+    const int32_t* xr = a.x16 + (size_t)r * TOPFR_NIN;
+    const int4* p = reinterpret_cast<const int4*>(xr + 16 * lane);
+    const int4* q = reinterpret_cast<const int4*>(xr + 512 + 8 * lane);
+    int4 t[6] = {p[0], p[1], p[2], p[3], q[0], q[1]};
+#pragma unroll
+    for (int u = 0; u < 6; u++) { x[4 * u] = t[u].x; x[4 * u + 1] = t[u].y; x[4 * u + 2] = t[u].z; x[4 * u + 3] = t[u].w; }
+    int64_t s1 = 0, sp = 0, sn = 0;
+#pragma unroll
+    for (int u = 0; u < 24; u++) { s1 += x[u]; if (x[u] > 0) sp += x[u]; else sn += x[u]; }
+    S1 = warp_sum64(s1);
+    SP = warp_sum64(sp);
+    SN = warp_sum64(sn);
+}
+// sum over the word's 768 bytes of a plane times the input: lane takes bytes 16 lane .. + 16 and 512 + 8 lane .. + 8
+B2_DEV int64_t fr_dot(const int8_t* row, const int (&x)[24], int lane) {
+    const int4 u = *reinterpret_cast<const int4*>(row + 16 * lane);
+    const int2 v = *reinterpret_cast<const int2*>(row + 512 + 8 * lane);
+    const uint32_t wd[6] = {(uint32_t)u.x, (uint32_t)u.y, (uint32_t)u.z, (uint32_t)u.w, (uint32_t)v.x, (uint32_t)v.y};
+    int s = 0;                                   // |byte x| <= 2^22, 24 of them < 2^27
+#pragma unroll
+    for (int k = 0; k < 6; k++)
+#pragma unroll
+        for (int t = 0; t < 4; t++) s += (int)(int8_t)(wd[k] >> (8 * t)) * x[4 * k + t];
+    return warp_sum64((int64_t)s);
+}
+
+// (a)-(c): every word's coarse sum and its low and high score; each CTA's five best lows per row. A warp per word.
+template <int EPI>
+__global__ void __launch_bounds__(256) k_top_coarse(TopFrArgs a) {
+    griddep_wait();
+    stamp_begin(a.stamp);
+    griddep_launch();
+    __shared__ int64_t s5v[TOPFR_ROWS][8][5];
+    __shared__ int s5i[TOPFR_ROWS][8][5];
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int64_t bv[TOPFR_ROWS][5];
+    int bi[TOPFR_ROWS][5];
+#pragma unroll
+    for (int r = 0; r < TOPFR_ROWS; r++)
+#pragma unroll
+        for (int k = 0; k < 5; k++) { bv[r][k] = INT64_MIN; bi[r][k] = 0x7fffffff; }
+    const int gw = blockIdx.x * 8 + wid, nw = gridDim.x * 8;
+#pragma unroll
+    for (int r = 0; r < TOPFR_ROWS; r++) {
+        if (r >= a.rows) break;
+        int x[24];
+        int64_t S1, SP, SN;
+        fr_row(a, r, lane, x, S1, SP, SN);
+        for (int j = gw; j < a.nout; j += nw) {
+            const int64_t c = fr_dot(a.wh + (size_t)j * TOPFR_NIN, x, lane);
+            if (lane == 0) {
+                const int64_t lo = fr_score<EPI>(256 * c + 255 * SN, j, r, a);
+                const int64_t hi = fr_score<EPI>(256 * c + 255 * SP, j, r, a);
+                a.C[(size_t)r * a.nout + j] = c;
+                a.HIS[(size_t)r * a.nout + j] = hi;
+                fr_put5(bv[r], bi[r], lo, j);
+            }
+        }
+        if (lane == 0)
+#pragma unroll
+            for (int k = 0; k < 5; k++) { s5v[r][wid][k] = bv[r][k]; s5i[r][wid][k] = bi[r][k]; }
+    }
+    __syncthreads();
+    if (threadIdx.x < TOPFR_ROWS && (int)threadIdx.x < a.rows) {
+        const int r = threadIdx.x;
+        int64_t v[5];
+        int ix[5];
+#pragma unroll
+        for (int k = 0; k < 5; k++) { v[k] = INT64_MIN; ix[k] = 0x7fffffff; }
+        for (int w = 0; w < 8; w++)
+#pragma unroll
+            for (int k = 0; k < 5; k++) fr_put5(v, ix, s5v[r][w][k], s5i[r][w][k]);
+        for (int k = 0; k < 5; k++) {
+            a.p5v[((size_t)r * a.nparts + blockIdx.x) * 5 + k] = v[k];
+            a.p5i[((size_t)r * a.nparts + blockIdx.x) * 5 + k] = ix[k];
+        }
+    }
+}
+
+// the five best over a warp's lanes, each lane holding its own five best in order: five rounds of the warp's best head,
+// popped from the lane that holds it
+B2_DEV void fr_merge5(int64_t* v, int* ix) {
+    int64_t ov[5];
+    int oi[5];
+#pragma unroll
+    for (int k = 0; k < 5; k++) {
+        int64_t bv = v[0];
+        int bi = ix[0];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const int64_t cv = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int ci = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (fr_better(cv, ci, bv, bi)) { bv = cv; bi = ci; }
+        }
+        if (v[0] == bv && ix[0] == bi) {
+#pragma unroll
+            for (int q = 0; q < 4; q++) { v[q] = v[q + 1]; ix[q] = ix[q + 1]; }
+            v[4] = INT64_MIN;
+            ix[4] = 0x7fffffff;
+        }
+        ov[k] = bv;
+        oi[k] = bi;
+    }
+#pragma unroll
+    for (int k = 0; k < 5; k++) { v[k] = ov[k]; ix[k] = oi[k]; }
+}
+
+// T5 (the 5th-best low of the row) and the words still in (high >= T5): one CTA per row
+__global__ void __launch_bounds__(1024) k_top_select(TopFrArgs a) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ int64_t s5v[32][5];
+    __shared__ int s5i[32][5];
+    __shared__ int64_t s_t5;
+    __shared__ int s_cnt;
+    const int r = blockIdx.x, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int64_t v[5];
+    int ix[5];
+#pragma unroll
+    for (int k = 0; k < 5; k++) { v[k] = INT64_MIN; ix[k] = 0x7fffffff; }
+    for (int t = threadIdx.x; t < a.nparts; t += blockDim.x)
+#pragma unroll
+        for (int k = 0; k < 5; k++) fr_put5(v, ix, a.p5v[((size_t)r * a.nparts + t) * 5 + k], a.p5i[((size_t)r * a.nparts + t) * 5 + k]);
+    fr_merge5(v, ix);
+    if (lane == 0)
+#pragma unroll
+        for (int k = 0; k < 5; k++) { s5v[wid][k] = v[k]; s5i[wid][k] = ix[k]; }
+    if (threadIdx.x == 0) s_cnt = 0;
+    __syncthreads();
+    if (wid == 0) {
+#pragma unroll
+        for (int k = 0; k < 5; k++) { v[k] = s5v[lane][k]; ix[k] = s5i[lane][k]; }
+        fr_merge5(v, ix);
+        if (lane == 0) s_t5 = v[4];
+    }
+    __syncthreads();
+    const int64_t t5 = s_t5;
+    for (int j0 = 0; j0 < a.nout; j0 += blockDim.x) {
+        const int j = j0 + threadIdx.x;
+        const bool keep = j < a.nout && a.HIS[(size_t)r * a.nout + j] >= t5;
+        const uint32_t m = __ballot_sync(0xffffffffu, keep);
+        int base = 0;
+        if (lane == 0 && m) base = atomicAdd(&s_cnt, __popc(m));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (keep) a.list[(size_t)r * a.nout + base + __popc(m & ((1u << lane) - 1))] = j;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) a.cnt[r] = s_cnt;
+}
+
+// (d): the words still in, exactly: pile = 256 C + sum wl x + 128 S1 (lo = wl + 128), the head's own score, and each
+// CTA's best (score, word) per row (k_race_parts then picks the row's word). A warp per word still in.
+template <int EPI>
+__global__ void __launch_bounds__(256) k_top_finish(TopFrArgs a) {
+    griddep_wait();
+    griddep_launch();
+    __shared__ int64_t sv[8];
+    __shared__ int si[8];
+    const int r = blockIdx.y, lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    int x[24];
+    int64_t S1, SP, SN;
+    fr_row(a, r, lane, x, S1, SP, SN);
+    const int n = a.cnt[r];
+    int64_t best = INT64_MIN;
+    int bw = 0x7fffffff;
+    for (int k = blockIdx.x * 8 + wid; k < n; k += gridDim.x * 8) {
+        const int j = a.list[(size_t)r * a.nout + k];
+        const int64_t l = fr_dot(a.wl + (size_t)j * TOPFR_NIN, x, lane);
+        const int64_t s = fr_score<EPI>(wadd(wadd(wmul(256, a.C[(size_t)r * a.nout + j]), l), wmul(128, S1)), j, r, a);
+        if (fr_better(s, j, best, bw)) { best = s; bw = j; }
+    }
+    if (lane == 0) { sv[wid] = best; si[wid] = bw; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < 8; w++) if (fr_better(sv[w], si[w], best, bw)) { best = sv[w]; bw = si[w]; }
+        a.sv[(size_t)r * a.nfin + blockIdx.x] = best;
+        a.si[(size_t)r * a.nfin + blockIdx.x] = bw;
+    }
+}
+
+}  // namespace b2

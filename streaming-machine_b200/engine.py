@@ -305,6 +305,11 @@ class Engine:
         self._call("b2_get_bank_layout", self.h, name.encode(), *[out[k].ctypes.data for k in ("wh", "wl", "cc", "cckb")])
         return out
 
+    def set_top_read(self, collapsing: bool):
+        """The reference's top=fr (True) / top=plain (False) switch: decode steps of up to 4 streams that store no
+        scores pick their word by the exact collapsing read."""
+        self._call("b2_set_scalar", self.h, b"top_read", int(bool(collapsing)))
+
     def set_wait_limit(self, ns: int):
         """How long a device-side wait may take before the kernel gives up and the call reports B2_ERR_DEVICE
         (0 = the default, 0.5 s)."""
