@@ -315,8 +315,8 @@ def run_decode(args, name):
         tok = run((p - Cur.pos) % cycle, host, tok)
         return tok
 
-    if args.quick:                           # profiling aid: W + K steps, one short JSON line, nothing else
-        position_at(start)
+    if args.quick:                           # profiling aid: W + K steps from the job's start, one short JSON line
+        position_at(W % cycle)
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         run(K)

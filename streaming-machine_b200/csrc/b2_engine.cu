@@ -73,6 +73,7 @@ struct b2_handle {
     int max_rows = 0;
     int32_t *row_slot = nullptr, *row_pos = nullptr, *row_tok = nullptr;
     int64_t *R = nullptr, *QKV = nullptr, *ATT = nullptr, *HID = nullptr;
+    int64_t* G2 = nullptr;       // Pythia decode: the second norm's rows ([FUSED_ROWS][d])
     int32_t *x16 = nullptr, *ex = nullptr, *q16 = nullptr, *qexp = nullptr;
     int64_t* LS = nullptr;
     TcRows tcr{};
@@ -422,14 +423,19 @@ int run_attend(b2_handle* h, int rows, int l, uint64_t* or_out, cudaStream_t st,
 
 // Pythia's layer norm (pythia_base2.py:100-110) of rows of X (gathered by src_rows when given) into out [rows][d]
 int run_gauge(b2_handle* h, const int64_t* X, const int32_t* src_rows, int rows, int ni, int64_t* out, cudaStream_t st,
-              uint64_t* or_out = nullptr) {
+              uint64_t* or_out = nullptr, int ni2 = -1, int64_t* out2 = nullptr, uint64_t* or_out2 = nullptr) {
     const b2_handle::Norm& nm = h->norms[ni];
     if (h->flags & B2_GAUGE_FLOAT)
         return launch(h, B2_PROF_QUANT, "gauge_ln_float", k_gauge_ln_float<256>, rows, 256, 0, st, X, h->cfg.d_model,
                       src_rows, rows, (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out);
-    return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, rows, 256, 0, st, X, h->cfg.d_model, src_rows, rows,
-                  (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2, (const int32_t*)h->EXP2,
-                  h->eps40, h->d_err, stamp_slot(h, B2_PROF_QUANT), or_out);
+    GaugeTwo two{};
+    if (ni2 >= 0) {
+        const b2_handle::Norm& n2 = h->norms[ni2];
+        two = GaugeTwo{n2.g, n2.ge, n2.b, out2, or_out2};
+    }
+    return launch(h, B2_PROF_QUANT, "gauge_ln", k_gauge_ln<256>, dim3(rows, ni2 >= 0 ? 2 : 1), 256, 0, st, X, h->cfg.d_model,
+                  src_rows, rows, (const int64_t*)nm.g, nm.ge, (const int64_t*)nm.b, out, (const int32_t*)h->LOG2,
+                  (const int32_t*)h->EXP2, h->eps40, h->d_err, stamp_slot(h, B2_PROF_QUANT), or_out, two);
 }
 
 // Pythia's layers + head (pythia_base2.py:161-169): the parallel residual R <- R + A(g1 R) + M(g2 R). Both norms read R
@@ -608,10 +614,10 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
                   (const int32_t*)h->race_i, h->race_ld, h->race_ld, h->race_out);
 }
 
-// Pythia-160M (pythia_base2.py:161-169) the same way: both norms publish their rows' ORs, the four banks quantise
-// their rows in the kernel, so a layer is 8 launches (norm, qkv, turn + key/value append, arrival, norm, fc + bend,
-// mproj, proj) instead of 12. The second norm's output goes to the QKV buffer (free once the turn has read it): fc
-// writes its 3,072 columns into HID while other CTAs may still be quantising their rows of its input.
+// Pythia-160M (pythia_base2.py:161-169) the same way: the norms publish their rows' ORs, the four banks quantise
+// their rows in the kernel, so a layer is 7 launches (both norms, qkv, turn + key/value append, arrival, fc + bend,
+// mproj, proj) instead of 12. The second norm's output has its own buffer (G2): fc writes its 3,072 columns into HID
+// while other CTAs may still be quantising their rows of its input.
 int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, H = c.n_head, F = c.d_ff;
@@ -622,8 +628,9 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
     if (rc) return rc;
     for (int l = 0; l < L; l++) {
         uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
-        // attention branch: g1 R -> qkv -> turn and key/value append -> arrival
-        if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l, h->ATT, st, o0))) return rc;
+        // both norms of R (one launch): g1 R -> ATT (qkv's input), g2 R -> G2 (fc's input)
+        if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l, h->ATT, st, o0, 2 * l + 1, h->G2, o0 + 2 * FUSED_ROWS))) return rc;
+        // attention branch: qkv -> turn and key/value append -> arrival
         TcQuant q = wq_args(h, 4 * l, h->ATT, d, o0);
         if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, n, h->QKV, 3 * d, nullptr, st, nullptr, nullptr, &q))) return rc;
         if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(n, 3 * H), 32, 0, st,
@@ -632,9 +639,8 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
                          (const double*)nullptr, (const double*)nullptr, (int64_t*)nullptr, stamp_slot(h, B2_PROF_HEADS))))
             return rc;
         if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st, 0, true))) return rc;
-        // MLP branch from the same R: g2 R -> fc + bend -> mproj; then both branches into R (mproj, proj)
-        if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l + 1, h->QKV, st, o0 + 2 * FUSED_ROWS))) return rc;
-        q = wq_args(h, 4 * l + 2, h->QKV, d, o0 + 2 * FUSED_ROWS);
+        // MLP branch from the same R: fc + bend -> mproj; then both branches into R (mproj, proj)
+        q = wq_args(h, 4 * l + 2, h->G2, d, o0 + 2 * FUSED_ROWS);
         if ((rc = run_bank(h, 4 * l + 2, EPI_PLAIN_EDGE, n, h->HID, F, nullptr, st, nullptr, nullptr, &q,
                            o0 + 3 * FUSED_ROWS)))
             return rc;
@@ -1002,7 +1008,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     const b2_config& c = h->cfg;
     // drop old stream/row buffers
     void* old[] = {h->pf_blocks, h->sigf, h->qraw, h->kv.kraw, h->row_or, h->wq_acc, h->wq_nsat, h->wq_ctr, h->fr_C, h->fr_HIS,
-                   h->fr_p5v, h->fr_p5i, h->fr_list, h->fr_cnt, h->fr_sv, h->fr_si, h->race_v,
+                   h->fr_p5v, h->fr_p5i, h->fr_list, h->fr_cnt, h->fr_sv, h->fr_si, h->G2, h->race_v,
                    h->race_i, h->kv.k, h->kv.kmask, h->kv.kexp, h->kv.v, h->slot_len, h->slot_tok, h->row_slot, h->row_pos,
                    h->row_tok, h->R, h->QKV, h->ATT, h->HID, h->x16, h->ex, h->q16, h->qexp, h->LS, h->head_rows,
                    h->race_out, h->logits};
@@ -1034,6 +1040,7 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     h->race_ld = 4 * ((c.vocab + 127) / 128);
     if ((rc = dalloc(h, &h->race_v, (size_t)FUSED_ROWS * h->race_ld))) return rc;
     if ((rc = dalloc(h, &h->race_i, (size_t)FUSED_ROWS * h->race_ld))) return rc;
+    if ((rc = dalloc(h, &h->G2, (size_t)FUSED_ROWS * d))) return rc;
     {
         const size_t V = (size_t)c.vocab;
         if ((rc = dalloc(h, &h->fr_C, TOPFR_ROWS * V)) || (rc = dalloc(h, &h->fr_HIS, TOPFR_ROWS * V)) ||

@@ -112,15 +112,26 @@ __global__ void __launch_bounds__(NT) k_quant(const int64_t* __restrict__ X, int
 // out = power(c * g, (ge + 16) * 65536 - LS) + b with c = d * x16 - S1 (power exactly, as the reference's big ints).
 // One CTA per row; src_rows (optional) gathers rows. Output int64 [rows][d] (the plain bank after it to16s it).
 // ---------------------------------------------------------------------------------------------------------------------
+// a second norm of the same rows in the same launch (blockIdx.y = 1): Pythia's two norms of a layer both read R
+// before either branch adds into it (pythia_base2.py:163-167)
+struct GaugeTwo {
+    const int64_t* g = nullptr;
+    int64_t ge = 0;
+    const int64_t* b = nullptr;
+    int64_t* out = nullptr;
+    uint64_t* or_out = nullptr;
+};
 template <int NT>
 __global__ void __launch_bounds__(NT) k_gauge_ln(const int64_t* __restrict__ R, int d, const int32_t* __restrict__ src_rows,
                                                  int rows, const int64_t* __restrict__ g, int64_t ge,
                                                  const int64_t* __restrict__ b, int64_t* __restrict__ out,
                                                  const int32_t* __restrict__ LOG2, const int32_t* __restrict__ EXP2,
-                                                 int64_t eps40, uint32_t* err, uint64_t* stamp, uint64_t* or_out) {
+                                                 int64_t eps40, uint32_t* err, uint64_t* stamp, uint64_t* or_out,
+                                                 GaugeTwo two) {
     griddep_wait();
     stamp_begin(stamp);
     griddep_launch();
+    if (blockIdx.y == 1) { g = two.g; ge = two.ge; b = two.b; out = two.out; or_out = two.or_out; }
     __shared__ uint64_t s_or[NT / 32];
     __shared__ int64_t s_1[NT / 32], s_2[NT / 32];
     __shared__ int64_t s_F, s_S1;
