@@ -1233,7 +1233,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
     const bool wide_ok = wide_fits(t, rows, &wz);
     const int wrh = (rows + WIDE_ROWS - 1) / WIDE_ROWS;
     if (quant) {                      // the rows quantised in the kernel: only k_bank_wide does that
-        if (!wide_ok || out_map ||
+        if (!wide_ok || out_map || race ||
             ((uintptr_t)quant->X & 15) || (quant->ldx & 1))
             return (int)cudaErrorInvalidValue;
         a.q = *quant;
@@ -1258,7 +1258,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E, true>, grid, dim3(WIDE_THREADS), sm, wz, st, pdl, t,
                                           r.maps[mi].h32, r.maps[mi].l32, a, true);
                       break)
-    } else if (tc_wide && wide_ok && wz == 1) {
+    } else if (tc_wide && wide_ok && wz == 1 && !race) {   // the race runs in k_bank_tiles' epilogue only
         // one CTA per 64 output columns over the whole K range (no split, no cluster)
         a.ksplit = 1;
         a.kps = kb;
@@ -1272,7 +1272,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         B2_EPI_SWITCH(epi, err = launch_k(k_bank_wide<E, false>, grid, dim3(WIDE_THREADS), wide_smem_bytes(kb), 1, st, pdl, t,
                                           r.maps[mi].h32, r.maps[mi].l32, a, true);
                       break)
-    } else if (ksplit > 1) {
+    } else if (ksplit > 1 && !race) {
         a.ksplit = ksplit;
         a.kps = kb / ksplit;
         a.trace = trace;

@@ -8,7 +8,9 @@
 * a bounded device wait that runs out (b2_check_wait with a short "wait_ns"): B2_ERR_DEVICE, and the handle still
   works afterwards;
 * decode steps whose stream count moves across the 32-row halves on one handle (33, then 20, then 33 streams): the
-  quantising bank kernels' CTA split and arrival counters stay consistent.
+  quantising bank kernels' CTA split and arrival counters stay consistent;
+* decode-step bank inputs with +32768 entries (base2.py:24-27 rounds a row's largest value up to 2^15; the byte
+  planes carry it as 32512 and the pile adds 256 w back), met by the in-kernel quantisation's +32768 lists.
 """
 import numpy as np
 import pytest
@@ -125,3 +127,38 @@ def test_stream_count_across_row_halves(gpu_engine, orc):
                 got[s].append(int(o[s]))
     assert np.array_equal(np.asarray(got[:20]), orc.generate(ids[:20], 8))
     assert np.array_equal(np.asarray(got[20:]), orc.generate(ids[20:], 6))
+
+
+def test_plus_32768_inputs_in_decode_banks(M):
+    """Residual columns held at 2^20 - 1 through every layer (their embedding columns set, wpe's zeroed, and the proj
+    and mproj output columns zeroed), so that to16 rounds them to +32768 in every qkv and fc input row (the row's
+    largest value: every other |value| stays below 2^20). The columns fall in different CTAs' shares of the row and on
+    both sides of the qkv bank's K split; 40 streams fill one row half and part of the next."""
+    from oracle.oracle import Oracle
+    from streaming_machine_b200 import engine
+    cols = [5, 200, 383, 384, 700]
+    M2 = dict(M)
+    wte, wpe = M["wte"].copy(), M["wpe"].copy()
+    wte[:, cols] = (1 << 20) - 1
+    wpe[:, cols] = 0
+    M2["wte"], M2["wpe"] = wte, wpe
+    for l in range(12):
+        for b in ("proj", "mproj"):
+            w, bb = M[f"{b}.{l}.w"].copy(), M[f"{b}.{l}.b"].copy()
+            w[:, cols] = 0
+            bb[cols] = 0
+            M2[f"{b}.{l}.w"], M2[f"{b}.{l}.b"] = w, bb
+    ids = np.random.default_rng(25).integers(0, V, (40, 8))
+    # every embedded row (any word, any position) has these columns as its largest values: layer 0's qkv inputs
+    # reach +32768 there in every decode step
+    assert np.abs(np.delete(wte, cols, 1)).max() + np.abs(np.delete(wpe, cols, 1)).max() < (1 << 20) - 1
+    e = engine.Engine(M2, n_streams=40, max_ctx=32)
+    try:
+        tok, lg = _words_and_scores(e, ids, 4)
+        tok_graph = e.generate(ids, 4)
+    finally:
+        e.close()
+    want_tok, want_lg = Oracle(M2).generate(ids, 4, logits=True)
+    assert np.array_equal(lg, want_lg)
+    assert np.array_equal(tok, want_tok)
+    assert np.array_equal(tok_graph, want_tok)
