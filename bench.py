@@ -48,6 +48,11 @@ UNIT = "tokens/s"
 KV_BYTES_PER_KEY = 55_872              # per stream per attended key: 12 x (K 768x2 + V 768x4 + 12 exponents x 4)
 WEIGHT_BYTES = {"gpt2": 247_064_064, "pythia": 247_136_256}   # 48 banks + head, int16, read once per step
 BANK_LAUNCHES = 49                     # 48 layer banks + the head per decode step
+# DRAM bytes per bank launch of a decode step, (12 x (qkv + proj + fc + mproj) + head) / 49, from ncu captures of
+# single launches (dram__bytes_read.sum + dram__bytes_write.sum; commands and per-bank figures in the decode-bank
+# summary under profiles/). Not measured in this run; None where no capture was made (C5's 512-row path).
+BANK_TRAFFIC = {"c1": 5_302_930, "c2": 6_094_770, "c3": 5_472_705}
+BANK_TRAFFIC_SOURCE = "ncu: dram__bytes_read.sum + dram__bytes_write.sum of single bank launches (profiles/)"
 VOCAB = {"gpt2": 50257, "pythia": 50304}
 
 DECODE = {
@@ -384,7 +389,9 @@ def run_decode(args, name):
     att_gbs = kv_bytes / (att_ms / 1000.0) / 1e9 if att_ms > 0 else None
     step_bytes = (wbytes * K + kv_bytes) / K
     roofline = {"bound": "hbm", "achieved": round(bank_gbs, 1) if bank_gbs else None, "peak": peak, "unit": "GB/s",
-                "frac": round(bank_gbs / peak, 4) if bank_gbs else None, "traffic": None,
+                "frac": round(bank_gbs / peak, 4) if bank_gbs else None,
+                "traffic": BANK_TRAFFIC.get(name) if world == 1 or cfg["scaling"] == "weak" else None,
+                "traffic_source": BANK_TRAFFIC_SOURCE if name in BANK_TRAFFIC else None,
                 "kernel": "bank product (48 layer banks + the head per step)",
                 "algorithmic_bytes_per_launch": round(wbytes / BANK_LAUNCHES),
                 "avg_launch_us": round(1000 * bank_ms / max(bank_n, 1), 3),
