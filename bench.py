@@ -247,8 +247,11 @@ def run_decode(args, name):
 
     cfg = DECODE[name]
     rank, world, local_rank = env_rank()
+    alone = bool(args.rank_of) and world == 1
+    if alone:                                # one rank of an N-GPU strong-scaling run, alone on this GPU
+        world, rank = (int(x) for x in args.rank_of.split(":"))
     torch.cuda.set_device(local_rank)
-    dist = _dist(local_rank, world)
+    dist = None if alone else _dist(local_rank, world)
 
     def barrier():
         if dist:
@@ -425,8 +428,13 @@ def run_decode(args, name):
     if rank == 0 and world == 1 and not args.no_cpu:
         cv, cores, sample, _ = cpu_sample(name, 2, 0, budget_s=30.0)
         line["cpu_baseline"] = {"value": round(cv, 4), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample}
+    if alone:
+        line["n_gpus"] = 1
+        line["rank_of"] = {"world": world, "rank": rank,
+                           "note": "this rank's shard alone on one GPU; value = all streams x K / this rank's time, the "
+                                   "N-GPU aggregate if every rank took as long"}
     eng.close()
-    if rank == 0:
+    if rank == 0 or alone:
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
@@ -544,7 +552,12 @@ def main():
                     help="c2 (default): the metric's batch-64 decode; c1/c3/c5 the other decode configs; c4 the "
                          "prompt pass")
     ap.add_argument("--quick", action="store_true", help="profiling aid: --warmup and --steps decode steps only")
+    ap.add_argument("--rank-of", default="", metavar="N:R",
+                    help="profiling aid (c5): rank R's shard of an N-GPU run, timed alone on this GPU with the same "
+                         "procedure (the ranks share nothing inside the timed region); its line is that rank's")
     args = ap.parse_args()
+    if args.rank_of and (args.config != "c5" or len(args.rank_of.split(":")) != 2):
+        ap.error("--rank-of N:R applies to the strong-scaling config c5")
     if args.warmup < 3 and not args.quick and args.impl == "ours":
         ap.error("--warmup must be at least 3")
     if args.impl == "reference":
