@@ -622,18 +622,29 @@ __global__ void __launch_bounds__(NW * 32) k_attend_bulk(AttnArgs a) {
         griddep_launch();
     }
     ASTAMP(1)
+    const int pl = p - k0;                   // the row's own key, local index (this CTA's when 0 <= pl < nl)
+    const bool own = a.early && wid == 0 && pl >= 0 && pl < nl;
+    uint32_t okw = 0;
+    unsigned long long okm = 0;
+    int32_t oke = 0;
+    if (own) {                               // read now, with q; stored after the bulk copy that may cover its slot
+        const size_t e = base + pl;
+        okw = __ldcg(reinterpret_cast<const unsigned int*>(a.kv.k + e * 64) + lane);
+        if (lane == 0) {
+            okm = __ldcg((const unsigned long long*)a.kv.kmask + e);
+            oke = __ldcg(a.kv.kexp + e);
+        }
+    }
     if (tid < 64) qs[tid] = a.q16[(size_t)r * d + h * 64 + tid];
     const int64_t eq = a.qexp[r * H + h];
     // a wait that gives up flags the call (DERR_TIMEOUT); a cluster's CTAs still meet at every barrier
     const bool copied = mbar_wait(&bar, 0, a.err);
     if (CS == 1 && !copied) return;
-    const int pl = p - k0;                   // the row's own key, local index (this CTA's when 0 <= pl < nl)
-    if (a.early && wid == 0 && pl >= 0 && pl < nl) {   // after the bulk copy (which may have covered its slot)
-        const size_t e = base + pl;
-        reinterpret_cast<uint32_t*>(Ks + (size_t)pl * 64)[lane] = __ldcg(reinterpret_cast<const unsigned int*>(a.kv.k + e * 64) + lane);
+    if (own) {
+        reinterpret_cast<uint32_t*>(Ks + (size_t)pl * 64)[lane] = okw;
         if (lane == 0) {
-            KMs[pl] = __ldcg((const unsigned long long*)a.kv.kmask + e);
-            KEs[pl] = __ldcg(a.kv.kexp + e);
+            KMs[pl] = okm;
+            KEs[pl] = oke;
         }
     }
     __syncthreads();
