@@ -868,6 +868,190 @@ __global__ void __launch_bounds__(TILE_THREADS, 1)
     tstamp(a, 7);
 }
 
+// ---------------------------------------------------------------------------------------------------------------------
+// Decode banks at <= 2 rows (batch-1 streams): a coalesced int16 GEMV on the CUDA cores over the reference-layout
+// weights [nin][nout], the rows quantised in every CTA (a row of 768 inputs is 6 KB: converting it in each CTA costs
+// less than any hand-off between CTAs, and nothing waits on another CTA). CTA (mt, kz) owns output columns
+// 64 mt .. + 64 and inputs 768 kz .. + 768; a bank with more inputs is split over a (1, nin / 768, 1) cluster whose
+// partial piles are summed over DSMEM by rank 0. 512 threads: thread t takes columns 8 (t % 8) .. + 8 and inputs
+// 12 (t / 8) .. + 12 of the range; its 12 x 8 weights (one 16-byte load per input, eight threads reading one
+// 128-byte row segment) are read BEFORE the dependency wait and held in registers. After the wait: the rows' x16 into
+// shared memory (to16 by the OR the producer published; x16 = +32768 is an ordinary int32 here, no correction), S1 and
+// S2 (gauged banks, whose 768 inputs are one CTA's), the exact products summed in int64 (|x16 w| <= 2^30), a shuffle
+// and shared-memory reduction over the 64 input slices, then the bank's epilogue with warp r on row r, lane l on
+// columns 2l, 2l + 1 (the qkv bank's 64 columns are one head part: heads16's OR is one warp's).
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int GEMV_THREADS = 512;
+constexpr int GEMV_KR = 768;          // inputs per CTA
+constexpr int GEMV_MAX_ROWS = 2;
+
+template <int EPI, int R>
+__global__ void __launch_bounds__(GEMV_THREADS, 1) k_bank_gemv(const TcArgs a) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    __shared__ int32_t xs[R][GEMV_KR];                // the rows' x16 over this CTA's inputs
+    __shared__ int64_t red[GEMV_THREADS / 32][64][R]; // per-warp partial piles
+    __shared__ int64_t s_pile[R][64];                 // this CTA's piles (read by rank 0 of a K split over DSMEM)
+    __shared__ int64_t s_1[GEMV_THREADS / 32][R], s_2[GEMV_THREADS / 32][R];
+    __shared__ int32_t s_sh[R];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, kz = blockIdx.y, nz = gridDim.y;
+    const int cg = tid & 7, ks = tid >> 3;
+    const int k0 = kz * GEMV_KR + ks * 12;            // this thread's first input
+    const int c0 = mt * 64 + cg * 8;                  // its first column
+    const bool cvalid = c0 < a.nout;                  // nout % 8 == 0: a column group is all in or all out
+    // the weights, independent of earlier kernels
+    int4 w[12];
+#pragma unroll
+    for (int u = 0; u < 12; u++)
+        w[u] = cvalid ? __ldg(reinterpret_cast<const int4*>(a.w16 + (size_t)(k0 + u) * a.nout + c0)) : make_int4(0, 0, 0, 0);
+    const int j0 = mt * 64 + 2 * lane, j1 = j0 + 1;  // the epilogue's columns (warp r < R: row r)
+    const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
+    const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
+    const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
+    const bool heads = EPI == EPI_GAUGED && a.heads;
+    griddep_wait();
+    stamp_begin(a.stamp);
+    griddep_launch();
+
+    // ---- the rows' x16 over this CTA's inputs; S1, S2 over the row (gauged banks: the CTA holds the whole row) ----
+    if (tid < R) s_sh[tid] = tid < a.rows ? to16_shift(a.q.xor_in[tid]) : 0;
+    __syncthreads();
+    int64_t p1[R], p2[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        p1[r] = 0;
+        p2[r] = 0;
+        const int sh = s_sh[r];
+        for (int i = tid; i < GEMV_KR; i += GEMV_THREADS) {
+            int32_t x = 0;
+            if (r < a.rows) {
+                const int64_t v = a.q.X[(size_t)r * a.q.ldx + kz * GEMV_KR + i];
+                x = (int32_t)(sh ? (int64_t)((uint64_t)v + (1ull << (sh - 1))) >> sh : v);
+            }
+            xs[r][i] = x;
+            p1[r] += x;
+            p2[r] += (int64_t)x * x;
+        }
+        if (GAUGED) {
+            p1[r] = warp_sum64(p1[r]);
+            p2[r] = warp_sum64(p2[r]);
+            if (lane == 0) {
+                s_1[warp][r] = p1[r];
+                s_2[warp][r] = p2[r];
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- the products: 12 inputs x 8 columns x R rows per thread ----
+    int64_t acc[R][8];
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int c = 0; c < 8; c++) acc[r][c] = 0;
+#pragma unroll
+    for (int u = 0; u < 12; u++) {
+        const int32_t wv[8] = {(int16_t)(w[u].x & 0xFFFF), (int16_t)((uint32_t)w[u].x >> 16),
+                               (int16_t)(w[u].y & 0xFFFF), (int16_t)((uint32_t)w[u].y >> 16),
+                               (int16_t)(w[u].z & 0xFFFF), (int16_t)((uint32_t)w[u].z >> 16),
+                               (int16_t)(w[u].w & 0xFFFF), (int16_t)((uint32_t)w[u].w >> 16)};
+#pragma unroll
+        for (int r = 0; r < R; r++) {
+            const int32_t x = xs[r][ks * 12 + u];
+#pragma unroll
+            for (int c = 0; c < 8; c++) acc[r][c] += (int64_t)x * wv[c];
+        }
+    }
+    // over the warp's four input slices (lanes cg, cg + 8, cg + 16, cg + 24), then over the 16 warps
+#pragma unroll
+    for (int r = 0; r < R; r++)
+#pragma unroll
+        for (int c = 0; c < 8; c++) {
+            acc[r][c] += __shfl_xor_sync(0xffffffffu, acc[r][c], 8);
+            acc[r][c] += __shfl_xor_sync(0xffffffffu, acc[r][c], 16);
+        }
+    if (lane < 8) {
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) red[warp][lane * 8 + c][r] = acc[r][c];
+    }
+    __syncthreads();
+    if (tid < 64 * R) {
+        const int col = tid & 63, r = tid >> 6;
+        int64_t s = 0;
+#pragma unroll
+        for (int q = 0; q < GEMV_THREADS / 32; q++) s += red[q][col][r];
+        s_pile[r][col] = s;
+    }
+    __syncthreads();
+    if (nz > 1) cluster_sync();       // every CTA's piles are in place
+    if (kz == 0 && warp < R && warp < a.rows) {
+        const int r = warp;
+        int64_t P0 = s_pile[r][2 * lane], P1 = s_pile[r][2 * lane + 1];
+        for (int p = 1; p < nz; p++) {
+            P0 += ld_dsmem(mapa(saddr(&s_pile[r][2 * lane]), (uint32_t)p));
+            P1 += ld_dsmem(mapa(saddr(&s_pile[r][2 * lane + 1]), (uint32_t)p));
+        }
+        const int64_t ex = -16 + s_sh[r];
+        int64_t LS = 0, e2 = 0;
+        if (GAUGED) {
+            int64_t S1 = 0, S2 = 0;
+#pragma unroll
+            for (int q = 0; q < GEMV_THREADS / 32; q++) {
+                S1 = wadd(S1, s_1[q][r]);
+                S2 = wadd(S2, s_2[q][r]);
+            }
+            LS = gauge_LS(S1, S2, (int)ex, a.q.LOG2, a.q.log768, a.q.eps40);
+            e2 = __ldg(a.epi.EXP2 + (wsub(0, LS) & 0xFFFF));
+        }
+        const int64_t v0 = cv0 ? epi_value<EPI>(P0, e0, b0, ex, LS, e2, a.epi.PHI) : 0;
+        const int64_t v1 = cv1 ? epi_value<EPI>(P1, e1, b1, ex, LS, e2, a.epi.PHI) : 0;
+        if (!heads) {
+            int64_t* o = a.epi.out + (size_t)r * a.epi.ldo + j0;
+            const int64_t w0 = EPI == EPI_PLAIN_ADD && cv0 ? wadd(o[0], v0) : v0;
+            const int64_t w1 = EPI == EPI_PLAIN_ADD && cv1 ? wadd(o[1], v1) : v1;
+            if (cv0) o[0] = w0;
+            if (cv1) o[1] = w1;
+            if (a.or_out) {                          // the next bank's row OR over these 64 columns
+                const uint64_t wor = warp_or64((cv0 ? mag(w0) : 0) | (cv1 ? mag(w1) : 0));
+                if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)wor);
+            }
+        } else {
+            // heads16 (base2_stream.swift:112-119; base2.py:93): the tile is head part mt, the row's OR this warp's
+            const int H = a.hd.kv.H, dm = H * 64, kind = mt / H, hh = mt % H, dd = 2 * lane;
+            const uint64_t por = warp_or64(mag(v0) | mag(v1));
+            const int sh = to16_shift(por);
+            const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
+            if (kind == 0) {
+                *reinterpret_cast<int2*>(a.hd.q16 + (size_t)r * dm + hh * 64 + dd) = make_int2(x0, x1);
+                if (lane == 0) a.hd.qexp[r * H + hh] = -16 + sh;
+            } else {
+                const int pos = a.hd.row_pos[r];
+                const bool pv = pos >= 0 && pos < a.hd.kv.lim;
+                if (!pv && lane == 0) set_err(a.err, DERR_POS);
+                const size_t idx = pv ? kv_index(a.hd.row_slot[r], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
+                if (kind == 1) {
+                    // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
+                    const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
+                    const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
+                    if (pv) {
+                        *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+                        if (lane == 0) {
+                            a.hd.kv.kmask[idx] = interleave32(be, bo);
+                            a.hd.kv.kexp[idx] = -16 + sh;
+                        }
+                    }
+                } else if (pv) {
+                    if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
+                    *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
+                }
+            }
+        }
+    }
+    if (nz > 1) cluster_sync();       // no CTA leaves while rank 0 may still read its piles
+}
+
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
 __global__ void k_weight_planes(const int16_t* __restrict__ w, int nin, int nout, int8_t* __restrict__ wh,
                                 int8_t* __restrict__ wl) {
@@ -962,6 +1146,33 @@ cudaError_t launch_k(K kernel, dim3 grid, dim3 block, size_t smem, int cluster_y
                               *reinterpret_cast<const CUtensorMap*>(xh.bytes), *reinterpret_cast<const CUtensorMap*>(xl.bytes), a);
 }
 
+// a kernel that takes only TcArgs (k_bank_gemv), as a cluster (1, cluster_y, 1) when cluster_y > 1
+template <class K>
+cudaError_t launch_args(K kernel, dim3 grid, dim3 block, int cluster_y, cudaStream_t st, bool pdl, const TcArgs& a) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (cluster_y > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = 1;
+        at[na].val.clusterDim.y = cluster_y;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, kernel, a);
+}
+
 #define B2_EPI_SWITCH(EPIV, CALL)                                      \
     switch (EPIV) {                                                    \
         case EPI_GAUGED: { constexpr int E = EPI_GAUGED; CALL; }           \
@@ -997,11 +1208,14 @@ static const WideCaps& wide_caps() {
 // the in-kernel-quantising decode banks split a 768-input bank over this many CTAs when the launch still fits
 // (2: half the K blocks, MMAs, quantisation and finish per CTA, one DSMEM pair sum; 1: B2_WIDE_KZ=1)
 static int tc_wide_kz = 2;
+// decode banks at <= 2 rows run the CUDA-core GEMV (k_bank_gemv) instead of k_bank_wide (B2_GEMV=0: k_bank_wide)
+static int tc_gemv = 1;
 
 // shared-memory and cluster opt-ins for every instantiation, once, before any launch (never inside a capture)
 int tc_init() {
     if (const char* v = getenv("B2_WIDE")) tc_wide = atoi(v);
     if (const char* v = getenv("B2_WIDE_KZ")) tc_wide_kz = atoi(v);
+    if (const char* v = getenv("B2_GEMV")) tc_gemv = atoi(v);
     void* split[] = {(void*)k_bank_split<EPI_GAUGED>, (void*)k_bank_split<EPI_GAUGED_EDGE>,
                      (void*)k_bank_split<EPI_PLAIN_ADD>, (void*)k_bank_split<EPI_PLAIN_OUT>,
                      (void*)k_bank_split<EPI_PLAIN_EDGE>};
@@ -1183,6 +1397,15 @@ static int wide_quant_split(const TcBank& t) {
     return wz;
 }
 
+// k_bank_gemv takes this quantised decode bank at `rows` rows: whole 768-input ranges (a cluster of at most 4 along K),
+// 16-byte weight rows (nout % 8 == 0), and a gauged bank's row in one CTA
+static bool gemv_fits(const TcBank& t, int epi, int rows) {
+    const int nz = t.nin / GEMV_KR;
+    const bool gauged = epi == EPI_GAUGED || epi == EPI_GAUGED_EDGE;
+    return tc_gemv && t.w16 && rows >= 1 && rows <= GEMV_MAX_ROWS && t.nin % GEMV_KR == 0 && (nz == 1 || nz == 2 || nz == 4) &&
+           t.nout % 8 == 0 && !(gauged && nz != 1) && wide_caps().ctas[nz] >= nz;
+}
+
 int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, const int64_t* LS, const int32_t* e,
             const int64_t* b, int64_t* out, int ldo, const int32_t* out_map, const int32_t* EXP2, const int32_t* PHI,
             cudaStream_t st, bool pdl, const TcHeads* heads, bool* heads_done, uint64_t* trace, const TcQuant* quant,
@@ -1237,6 +1460,21 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             ((uintptr_t)quant->X & 15) || (quant->ldx & 1))
             return (int)cudaErrorInvalidValue;
         a.q = *quant;
+        if (gemv_fits(t, epi, rows)) {            // batch-1 decode: the CUDA-core GEMV, no hand-off between CTAs
+            if (heads && epi == EPI_GAUGED) {
+                a.heads = 1;
+                a.hd = *heads;
+                if (heads_done) *heads_done = true;
+            }
+            const int nz = t.nin / GEMV_KR;
+            dim3 grid((t.nout + 63) / 64, nz, 1);
+            if (rows == 1) {
+                B2_EPI_SWITCH(epi, err = launch_args(k_bank_gemv<E, 1>, grid, dim3(GEMV_THREADS), nz, st, pdl, a); break)
+            } else {
+                B2_EPI_SWITCH(epi, err = launch_args(k_bank_gemv<E, 2>, grid, dim3(GEMV_THREADS), nz, st, pdl, a); break)
+            }
+            return (int)err;
+        }
         a.q.xh = r.xh;
         a.q.xl = r.xl;
         a.q.sat = r.sat;

@@ -129,11 +129,13 @@ def test_stream_count_across_row_halves(gpu_engine, orc):
     assert np.array_equal(np.asarray(got[20:]), orc.generate(ids[20:], 6))
 
 
-def test_plus_32768_inputs_in_decode_banks(M):
+@pytest.mark.parametrize("n_streams", [40, 2])
+def test_plus_32768_inputs_in_decode_banks(M, n_streams):
     """Residual columns held at 2^20 - 1 through every layer (their embedding columns set, wpe's zeroed, and the proj
     and mproj output columns zeroed), so that to16 rounds them to +32768 in every qkv and fc input row (the row's
     largest value: every other |value| stays below 2^20). The columns fall in different CTAs' shares of the row and on
-    both sides of the qkv bank's K split; 40 streams fill one row half and part of the next."""
+    both sides of the qkv bank's K split; 40 streams fill one row half and part of the next, 2 streams run the
+    CUDA-core GEMV banks."""
     from oracle.oracle import Oracle
     from streaming_machine_b200 import engine
     cols = [5, 200, 383, 384, 700]
@@ -148,11 +150,11 @@ def test_plus_32768_inputs_in_decode_banks(M):
             w[:, cols] = 0
             bb[cols] = 0
             M2[f"{b}.{l}.w"], M2[f"{b}.{l}.b"] = w, bb
-    ids = np.random.default_rng(25).integers(0, V, (40, 8))
+    ids = np.random.default_rng(25).integers(0, V, (n_streams, 8))
     # every embedded row (any word, any position) has these columns as its largest values: layer 0's qkv inputs
     # reach +32768 there in every decode step
     assert np.abs(np.delete(wte, cols, 1)).max() + np.abs(np.delete(wpe, cols, 1)).max() < (1 << 20) - 1
-    e = engine.Engine(M2, n_streams=40, max_ctx=32)
+    e = engine.Engine(M2, n_streams=n_streams, max_ctx=32)
     try:
         tok, lg = _words_and_scores(e, ids, 4)
         tok_graph = e.generate(ids, 4)

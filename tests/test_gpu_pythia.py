@@ -51,7 +51,7 @@ def test_pythia_c5_golden_streams(pythia_engine, pgold):
         assert [sha(r) for r in lgs] == want["greedy_logits_sha"]
 
 
-@pytest.mark.parametrize("n_streams,prompt,words", [(8, 16, 6), (64, 64, 3)])
+@pytest.mark.parametrize("n_streams,prompt,words", [(1, 16, 6), (2, 16, 6), (8, 16, 6), (64, 64, 3)])
 def test_pythia_batch_vs_oracle(pythia_engine, porc, n_streams, prompt, words):
     """Many streams at once (64 x 64 prompt rows take the tensor-core banks): every word and every score row equal
     the oracle's."""
