@@ -141,7 +141,7 @@ namespace {
 constexpr int FUSED_ROWS = 64;
 constexpr size_t ATT_BULK_MAX = 200 * 1024;   // shared memory the bulk-copy arrival may take
 constexpr int ATT_NW = 8;                      // warps per (row, head) CTA of the bulk-copy arrival
-constexpr int ATT_CS = 4;                      // CTAs per (row, head) cluster when the arrival splits the keys
+constexpr int ATT_CS = 8;                      // CTAs per (row, head) cluster when the arrival splits the keys
 constexpr size_t PF_SMEM_MAX = 200 * 1024;    // and the prompt pass's query-block arrival
 constexpr int SPLIT_TRACE_LAUNCHES = 64, SPLIT_TRACE_SLOT = 160 * 8;   // B2_SPLIT_TRACE: launches x (CTAs x stamps)
 
