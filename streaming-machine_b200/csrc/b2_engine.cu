@@ -615,8 +615,8 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
 }
 
 // Pythia-160M (pythia_base2.py:161-169) the same way: the norms publish their rows' ORs, the four banks quantise
-// their rows in the kernel, so a layer is 7 launches (both norms, qkv, turn + key/value append, arrival, fc + bend,
-// mproj, proj) instead of 12. The second norm's output has its own buffer (G2): fc writes its 3,072 columns into HID
+// their rows in the kernel and qkv's epilogue does the turn and the key/value append, so a layer is 6 launches (both
+// norms, qkv + turn + key/value append, arrival, fc + bend, mproj, proj) instead of 12. The second norm's output has its own buffer (G2): fc writes its 3,072 columns into HID
 // while other CTAs may still be quantising their rows of its input.
 int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
     const b2_config& c = h->cfg;
@@ -630,10 +630,19 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
         uint64_t* o0 = OR + (size_t)(4 * l) * FUSED_ROWS;
         // both norms of R (one launch): g1 R -> ATT (qkv's input), g2 R -> G2 (fc's input)
         if ((rc = run_gauge(h, h->R, nullptr, n, 2 * l, h->ATT, st, o0, 2 * l + 1, h->G2, o0 + 2 * FUSED_ROWS))) return rc;
-        // attention branch: qkv -> turn and key/value append -> arrival
+        // attention branch: qkv with the turn and the key/value append in its epilogue (or a heads kernel after it)
+        // -> arrival
         TcQuant q = wq_args(h, 4 * l, h->ATT, d, o0);
-        if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, n, h->QKV, 3 * d, nullptr, st, nullptr, nullptr, &q))) return rc;
-        if ((rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(n, 3 * H), 32, 0, st,
+        TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
+        hd.pythia = 1;
+        hd.COS = h->COS;
+        hd.SIN = h->SIN;
+        bool heads_done = false;
+        if ((rc = run_bank(h, 4 * l + 0, EPI_PLAIN_OUT, n, h->QKV, 3 * d, nullptr, st, h->fuse_heads ? &hd : nullptr,
+                           &heads_done, &q)))
+            return rc;
+        if (!heads_done &&
+            (rc = launch(h, B2_PROF_HEADS, "heads_pythia", k_heads_pythia, dim3(n, 3 * H), 32, 0, st,
                          (const int64_t*)h->QKV, n, (const int32_t*)h->row_slot, (const int32_t*)h->row_pos, l, h->kv,
                          (int)h->rot, (const int32_t*)h->COS, (const int32_t*)h->SIN, h->q16, h->qexp, h->d_err,
                          (const double*)nullptr, (const double*)nullptr, (int64_t*)nullptr, stamp_slot(h, B2_PROF_HEADS))))

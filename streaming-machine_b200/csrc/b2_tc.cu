@@ -141,6 +141,64 @@ B2_DEV void finish(const TcArgs& a, const RowData& r, int n, int j, int64_t pile
     *o = EPI == EPI_PLAIN_ADD ? wadd(*o, v) : v;
 }
 
+// the qkv bank's epilogue when its 64-column tile is one head part (heads16: base2_stream.swift:112-119, base2.py:93;
+// Pythia's turn first: pythia_base2.py:116-134, the arithmetic of k_heads_pythia): one row held by one warp, lane l
+// with columns 2l, 2l + 1 (values v0, v1). GPT-2's parts are q of every head, then k, then v (part = kind H + head);
+// Pythia's are q, k, v per head (part = 3 head + kind). Pythia's q and k are turned (dims t and t + 8 of the first 16
+// pair up: lanes l and l ^ 4 for l < 8; an input past 2^31 is where the reference asserts); then q and k are to16'd
+// over the part (the row's OR is this warp's): q to q16, k to the key store with its +32768 bits and exponent; v goes
+// to the value store as it is (int32, or DERR_VOVF).
+B2_DEV void heads_row(const TcArgs& a, int mt, int n, int slot, int pos, bool rv, int64_t v0, int64_t v1) {
+    const int lane = threadIdx.x & 31, H = a.hd.kv.H, dm = H * 64, dd = 2 * lane;
+    const bool py = a.hd.pythia != 0;
+    const int kind = py ? mt % 3 : mt / H, hh = py ? mt / 3 : mt % H;
+    const bool pv = rv && pos >= 0 && pos < a.hd.kv.lim;
+    if (rv && !pv && lane == 0 && (py || kind > 0)) set_err(a.err, DERR_POS);
+    if (py && kind < 2) {
+        const bool big = pv && lane < 8 && (mag(v0) >= (1ull << 31) || mag(v1) >= (1ull << 31));
+        if (__any_sync(0xffffffffu, big) && lane == 0) set_err(a.err, DERR_RANGE);
+        const int64_t p0 = __shfl_xor_sync(0xffffffffu, v0, 4), p1 = __shfl_xor_sync(0xffffffffu, v1, 4);
+        if (pv && lane < 8) {
+            const int t0 = (2 * lane) & 7;              // dims 2l, 2l + 1 modulo the pair distance 8
+            const size_t cb = (size_t)pos * 8 + t0;
+            const int64_t c0 = a.hd.COS[cb], s0 = a.hd.SIN[cb], c1 = a.hd.COS[cb + 1], s1 = a.hd.SIN[cb + 1];
+            if (lane < 4) {                             // a (this lane), b (the partner): a c - b s
+                v0 = rshift(wsub(wmul(v0, c0), wmul(p0, s0)), 30);
+                v1 = rshift(wsub(wmul(v1, c1), wmul(p1, s1)), 30);
+            } else {                                    // b (this lane), a (the partner): b c + a s
+                v0 = rshift(wadd(wmul(v0, c0), wmul(p0, s0)), 30);
+                v1 = rshift(wadd(wmul(v1, c1), wmul(p1, s1)), 30);
+            }
+        }
+    }
+    const uint64_t por = warp_or64(rv ? (mag(v0) | mag(v1)) : 0);
+    const int sh = to16_shift(por);
+    const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
+    if (kind == 0) {
+        if (rv && (!py || pv)) {
+            *reinterpret_cast<int2*>(a.hd.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
+            if (lane == 0) a.hd.qexp[n * H + hh] = -16 + sh;
+        }
+        return;
+    }
+    const size_t idx = pv ? kv_index(slot, a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
+    if (kind == 1) {
+        // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
+        const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
+        const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
+        if (pv) {
+            *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
+            if (lane == 0) {
+                a.hd.kv.kmask[idx] = interleave32(be, bo);
+                a.hd.kv.kexp[idx] = -16 + sh;
+            }
+        }
+    } else if (pv) {
+        if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
+        *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
+    }
+}
+
 // ---------------------------------------------------------------------------------------------------------------------
 // Decode banks (rows <= 64, few output tiles): split-K over a thread-block cluster (1, ksplit, 1). Each CTA holds one
 // or two K blocks (all loaded at once; the weights before the dependency wait), keeps its partial int64 tile in its
@@ -401,7 +459,7 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
     const int64_t colc0 = cv0 ? a.colcorr[j0] : 0, colc1 = cv1 ? a.colcorr[j1] : 0;
     const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
     const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
-    const bool heads = EPI == EPI_GAUGED && a.heads;
+    const bool heads = (EPI == EPI_GAUGED || EPI == EPI_PLAIN_OUT) && a.heads;
     griddep_wait();
     stamp_begin(a.stamp);
     griddep_launch();
@@ -665,42 +723,12 @@ __global__ void __launch_bounds__(WIDE_THREADS, 1)
             }
         }
     } else {
-        // heads16 (base2_stream.swift:112-119; base2.py:93): the tile is head part mt, a row's OR is this warp's
-        const int H = a.hd.kv.H, dm = H * 64, kind = mt / H, hh = mt % H, dd = 2 * lane;
 #pragma unroll
         for (int it = 0; it < RPW; it++) {
             if (it >= nrpw) break;
             const int nl = nz == 1 ? warp + 16 * it : 16 * kz + warp, n = r0 + nl;
             const bool rv = n < a.rows && go;
-            const uint64_t por = warp_or64(rv ? (mag(v0[it]) | mag(v1[it])) : 0);
-            const int sh = to16_shift(por);
-            const int32_t x0 = (int32_t)rshift(v0[it], sh), x1 = (int32_t)rshift(v1[it], sh);
-            if (kind == 0) {
-                if (rv) {
-                    *reinterpret_cast<int2*>(a.hd.q16 + (size_t)n * dm + hh * 64 + dd) = make_int2(x0, x1);
-                    if (lane == 0) a.hd.qexp[n * H + hh] = -16 + sh;
-                }
-            } else {
-                const int pos = rv ? s_pos[nl] : 0;
-                const bool pv = rv && pos >= 0 && pos < a.hd.kv.lim;
-                if (rv && !pv && lane == 0) set_err(a.err, DERR_POS);
-                const size_t idx = pv ? kv_index(s_slot[nl], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
-                if (kind == 1) {
-                    // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
-                    const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
-                    const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
-                    if (pv) {
-                        *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
-                        if (lane == 0) {
-                            a.hd.kv.kmask[idx] = interleave32(be, bo);
-                            a.hd.kv.kexp[idx] = -16 + sh;
-                        }
-                    }
-                } else if (pv) {
-                    if (v0[it] != (int64_t)(int32_t)v0[it] || v1[it] != (int64_t)(int32_t)v1[it]) set_err(a.err, DERR_VOVF);
-                    *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0[it], (int32_t)v1[it]);
-                }
-            }
+            heads_row(a, mt, n, rv ? s_slot[nl] : 0, rv ? s_pos[nl] : 0, rv, v0[it], v1[it]);
         }
     }
     tstamp(a, 5);
@@ -908,7 +936,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_bank_gemv(const TcArgs a) {
     const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
     const int64_t e0 = cv0 ? (int64_t)a.epi.e[j0] : 0, b0 = cv0 ? a.epi.b[j0] : 0;
     const int64_t e1 = cv1 ? (int64_t)a.epi.e[j1] : 0, b1 = cv1 ? a.epi.b[j1] : 0;
-    const bool heads = EPI == EPI_GAUGED && a.heads;
+    const bool heads = (EPI == EPI_GAUGED || EPI == EPI_PLAIN_OUT) && a.heads;
     griddep_wait();
     stamp_begin(a.stamp);
     griddep_launch();
@@ -1018,35 +1046,7 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_bank_gemv(const TcArgs a) {
                 if (lane == 0) atomicOr((unsigned long long*)&a.or_out[r], (unsigned long long)wor);
             }
         } else {
-            // heads16 (base2_stream.swift:112-119; base2.py:93): the tile is head part mt, the row's OR this warp's
-            const int H = a.hd.kv.H, dm = H * 64, kind = mt / H, hh = mt % H, dd = 2 * lane;
-            const uint64_t por = warp_or64(mag(v0) | mag(v1));
-            const int sh = to16_shift(por);
-            const int32_t x0 = (int32_t)rshift(v0, sh), x1 = (int32_t)rshift(v1, sh);
-            if (kind == 0) {
-                *reinterpret_cast<int2*>(a.hd.q16 + (size_t)r * dm + hh * 64 + dd) = make_int2(x0, x1);
-                if (lane == 0) a.hd.qexp[r * H + hh] = -16 + sh;
-            } else {
-                const int pos = a.hd.row_pos[r];
-                const bool pv = pos >= 0 && pos < a.hd.kv.lim;
-                if (!pv && lane == 0) set_err(a.err, DERR_POS);
-                const size_t idx = pv ? kv_index(a.hd.row_slot[r], a.hd.layer, hh, pos, a.hd.kv.L, H, a.hd.kv.ctx) : 0;
-                if (kind == 1) {
-                    // +32768 is not an int16: a bit per entry, lane l's two columns are bits 2l, 2l + 1
-                    const uint32_t be = __ballot_sync(0xffffffffu, pv && x0 == 32768);
-                    const uint32_t bo = __ballot_sync(0xffffffffu, pv && x1 == 32768);
-                    if (pv) {
-                        *reinterpret_cast<uint32_t*>(a.hd.kv.k + idx * 64 + dd) = ((uint32_t)x0 & 0xFFFFu) | ((uint32_t)x1 << 16);
-                        if (lane == 0) {
-                            a.hd.kv.kmask[idx] = interleave32(be, bo);
-                            a.hd.kv.kexp[idx] = -16 + sh;
-                        }
-                    }
-                } else if (pv) {
-                    if (v0 != (int64_t)(int32_t)v0 || v1 != (int64_t)(int32_t)v1) set_err(a.err, DERR_VOVF);
-                    *reinterpret_cast<int2*>(a.hd.kv.v + idx * 64 + dd) = make_int2((int32_t)v0, (int32_t)v1);
-                }
-            }
+            heads_row(a, mt, r, a.hd.row_slot[r], a.hd.row_pos[r], true, v0, v1);
         }
     }
     if (nz > 1) cluster_sync();       // no CTA leaves while rank 0 may still read its piles
@@ -1397,6 +1397,11 @@ static int wide_quant_split(const TcBank& t) {
     return wz;
 }
 
+// the qkv bank's epilogue does the q/k/v split (heads_row) for GPT-2's gauged qkv and Pythia's plain one
+static bool heads_fit(const TcHeads& h, int epi) {
+    return h.pythia ? (epi == EPI_PLAIN_OUT && h.COS && h.SIN) : epi == EPI_GAUGED;
+}
+
 // k_bank_gemv takes this quantised decode bank at `rows` rows: whole 768-input ranges (a cluster of at most 4 along K),
 // 16-byte weight rows (nout % 8 == 0), and a gauged bank's row in one CTA
 static bool gemv_fits(const TcBank& t, int epi, int rows) {
@@ -1461,7 +1466,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             return (int)cudaErrorInvalidValue;
         a.q = *quant;
         if (gemv_fits(t, epi, rows)) {            // batch-1 decode: the CUDA-core GEMV, no hand-off between CTAs
-            if (heads && epi == EPI_GAUGED) {
+            if (heads && heads_fit(*heads, epi)) {
                 a.heads = 1;
                 a.hd = *heads;
                 if (heads_done) *heads_done = true;
@@ -1486,7 +1491,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.ksplit = wz;
         a.kps = kb / wz;
         a.trace = trace;
-        if (heads && epi == EPI_GAUGED) {
+        if (heads && heads_fit(*heads, epi)) {
             a.heads = 1;
             a.hd = *heads;
             if (heads_done) *heads_done = true;
@@ -1501,7 +1506,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.ksplit = 1;
         a.kps = kb;
         a.trace = trace;
-        if (heads && epi == EPI_GAUGED && !out_map) {
+        if (heads && epi == EPI_GAUGED && !heads->pythia && !out_map) {
             a.heads = 1;
             a.hd = *heads;
             if (heads_done) *heads_done = true;
@@ -1514,7 +1519,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.ksplit = ksplit;
         a.kps = kb / ksplit;
         a.trace = trace;
-        if (heads && epi == EPI_GAUGED && !out_map) {
+        if (heads && epi == EPI_GAUGED && !heads->pythia && !out_map) {
             a.heads = 1;
             a.hd = *heads;
             if (heads_done) *heads_done = true;

@@ -54,6 +54,9 @@ struct TcHeads {
     const int32_t* row_slot;
     const int32_t* row_pos;
     int layer;
+    int pythia = 0;                  // Pythia's parts (q, k, v per head) and its turn of q and k (16 dims)
+    const int32_t* COS = nullptr;    // [n_ctx][8] at 2^-30 (Pythia)
+    const int32_t* SIN = nullptr;
 };
 
 // a decode bank's rows quantised inside k_bank_wide instead of by a quant kernel before it: the rows' int64 values
