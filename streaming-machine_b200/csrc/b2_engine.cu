@@ -88,6 +88,10 @@ struct b2_handle {
     int att_bulk = 1;            // the arrival by bulk copies into shared memory (B2_ATT_BULK=0: per-warp loads)
     int early_keys = 1;          // decode arrival: earlier positions' keys copied before the dependency wait (B2_EARLY_KEYS=0)
     int att_split = 1;           // few (row, head) units with long contexts: keys split over a cluster (B2_ATT_SPLIT=0)
+    int qkv_unsplit = 0;         // decode qkv banks on one CTA per tile (set per stream allocation, B2_QKV_PAIR=1: never):
+                                 // with many rows the arrival that follows runs one CTA per (row, head) and starts on
+                                 // the SMs a CTA-pair qkv would hold
+    int qkv_pair = 0;            // B2_QKV_PAIR=1
     // the collapsing top read (b2_set_scalar "top_read" 1): decode steps of <= TOPFR_ROWS streams that store no scores
     int top_fr = 0;
     int64_t *fr_C = nullptr, *fr_HIS = nullptr, *fr_p5v = nullptr, *fr_sv = nullptr;
@@ -589,6 +593,7 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         const TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
         bool heads_done = false;
         TcQuant q = wq_args(h, 4 * l, h->R, d, o0);
+        q.unsplit = h->qkv_unsplit;
         if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &q))) return rc;
         if (!heads_done) return fail(h, B2_ERR_STATE, "qkv bank %d: heads16 not done in its epilogue", l);
         if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st, 0, true))) return rc;
@@ -633,6 +638,7 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
         // attention branch: qkv with the turn and the key/value append in its epilogue (or a heads kernel after it)
         // -> arrival
         TcQuant q = wq_args(h, 4 * l, h->ATT, d, o0);
+        q.unsplit = h->qkv_unsplit;
         TcHeads hd{h->q16, h->qexp, h->kv, h->row_slot, h->row_pos, l};
         hd.pythia = 1;
         hd.COS = h->COS;
@@ -748,6 +754,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_ATT_BULK")) h->att_bulk = atoi(v);
     if (const char* v = getenv("B2_EARLY_KEYS")) h->early_keys = atoi(v);
     if (const char* v = getenv("B2_ATT_SPLIT")) h->att_split = atoi(v);
+    if (const char* v = getenv("B2_QKV_PAIR")) h->qkv_pair = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;
@@ -1092,6 +1099,9 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     h->n_slots = n_streams;
     h->max_ctx = max_ctx;
     h->primed = false;
+    // the decode arrival at the full stream count runs one CTA per (row, head) unless few rows with long contexts
+    // split it over clusters (run_attend's rule); then qkv goes unsplit, so that arrival's CTAs find SMs while it runs
+    h->qkv_unsplit = !h->qkv_pair && !(n_streams * h->cfg.n_head < 2 * h->sms && max_ctx >= 256);
     return B2_OK;
 }
 

@@ -1484,7 +1484,7 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
         a.q.xl = r.xl;
         a.q.sat = r.sat;
         a.q.kmax = r.kmax;
-        const int qz = wide_quant_split(t);
+        const int qz = quant->unsplit ? 1 : wide_quant_split(t);
         if (qz > 2 && (heads || epi != EPI_PLAIN_ADD)) return (int)cudaErrorInvalidValue;
         if ((t.nout / 64) * qz * wrh > wide_caps().ctas[qz]) return (int)cudaErrorInvalidValue;
         wz = qz;

@@ -72,6 +72,8 @@ struct TcQuant {
     unsigned long long* ctr = nullptr;   // [2]
     const int32_t* LOG2 = nullptr;
     int64_t log768 = 0, eps40 = 0;
+    int unsplit = 0;                     // 1: one CTA per tile even where the bank would take a CTA pair (a choice made
+                                         // per handle, never per launch: the arrival counter needs it fixed per site)
     int8_t* xh = nullptr;
     int8_t* xl = nullptr;
     int16_t* sat = nullptr;
