@@ -89,7 +89,11 @@ int b2_set_array(b2_handle* h, const char* name, const int64_t* data, int64_t n)
  * reference's top=plain / top=fr switch, base2_stream_fr2.swift:23-38): 0 (default) scores every word then races;
  * 1 races decode steps of up to 4 streams that store no scores by the exact collapsing read (every word's coarse score
  * from the high byte plane, bounds from the input's positive and negative sums, only the words that can still win read
- * their low bytes): the same words. */
+ * their low bytes): the same words. "entry_tables" (GPT-2; the reference's stored layer-0 entry, base2_entry.py,
+ * base2_layer0.py, base2_stream_fr2.swift:407-428): 1 makes every decode step take layer 0's qkv piles from two stored
+ * rows, wte . W and wpe . W of the qkv.0 bank (built as exact int64 piles at the next b2_alloc_streams, 0.95 GB for
+ * GPT-2 124M), instead of the bank product: the same bits, refused (B2_ERR_ARG) when an embedded value can reach 2^15,
+ * where to16 would round the row; 0 (default) drops them. */
 int b2_set_scalar(b2_handle* h, const char* name, int64_t v);
 
 /* All arrays given: build the device layouts. */

@@ -94,6 +94,9 @@ struct b2_handle {
     int qkv_pair = 0;            // B2_QKV_PAIR=1
     // the collapsing top read (b2_set_scalar "top_read" 1): decode steps of <= TOPFR_ROWS streams that store no scores
     int top_fr = 0;
+    int entry = 0;                  // "entry_tables" 1: layer 0's qkv bank of a decode step from stored rows
+    int64_t* entry_w = nullptr;     // [vocab][3d] = wte . W(qkv.0), built at the first b2_alloc_streams after finalize
+    int64_t* entry_p = nullptr;     // [n_ctx][3d] = wpe . W(qkv.0)
     int64_t *fr_C = nullptr, *fr_HIS = nullptr, *fr_p5v = nullptr, *fr_sv = nullptr;
     int32_t *fr_p5i = nullptr, *fr_list = nullptr, *fr_cnt = nullptr, *fr_si = nullptr;
     int sms = 148;               // the device's SM count
@@ -594,7 +597,17 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         bool heads_done = false;
         TcQuant q = wq_args(h, 4 * l, h->R, d, o0);
         q.unsplit = h->qkv_unsplit;
-        if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &q))) return rc;
+        if (l == 0 && h->entry_w) {   // layer 0's qkv from the stored rows (same bits: the pile is Tw[word] + Tp[pos])
+            const DevBank& b0 = h->banks[0];
+            prof_begin(h, B2_PROF_BANK, st);
+            rc = tc_entry_qkv(b0.tc, h->entry_w, h->entry_p, h->row_tok, h->wte, h->wpe, c.vocab, c.n_ctx, n, b0.e, b0.b,
+                              h->EXP2, q, hd, h->d_err, st, h->pdl && h->prof.timing != 1, stamp_slot(h, B2_PROF_BANK));
+            prof_end(h, B2_PROF_BANK, st);
+            if (rc) return fail(h, B2_ERR_CUDA, "entry qkv: %s", cudaGetErrorString((cudaError_t)rc));
+            heads_done = true;
+        } else if ((rc = run_bank(h, 4 * l, EPI_GAUGED, n, h->QKV, 3 * d, nullptr, st, &hd, &heads_done, &q))) {
+            return rc;
+        }
         if (!heads_done) return fail(h, B2_ERR_STATE, "qkv bank %d: heads16 not done in its epilogue", l);
         if ((rc = run_attend(h, n, l, o0 + FUSED_ROWS, st, 0, true))) return rc;
         q = wq_args(h, 4 * l + 1, h->ATT, d, o0 + FUSED_ROWS);
@@ -889,6 +902,18 @@ int b2_set_scalar(b2_handle* h, const char* name, int64_t v) {
         drop_graph(h);
         return B2_OK;
     }
+    if (!strcmp(name, "entry_tables")) {   // GPT-2: layer 0's qkv piles of a decode step from stored rows (0 or 1)
+        if ((v != 0 && v != 1) || (v && h->cfg.kind != B2_GPT2))
+            return fail(h, B2_ERR_ARG, "entry_tables = %lld (0 or 1, GPT-2 only)", (long long)v);
+        h->entry = (int)v;
+        if (!v) {
+            dfree(h, h->entry_w);
+            dfree(h, h->entry_p);
+            h->entry_w = h->entry_p = nullptr;
+        }
+        drop_graph(h);
+        return B2_OK;
+    }
     if (!strcmp(name, "wait_ns")) {   // the bounded device waits' limit (not a model scalar: finalize state unchanged)
         if (v < 0) return fail(h, B2_ERR_ARG, "wait_ns = %lld is negative", (long long)v);
         CK(cudaSetDevice(h->device));
@@ -961,6 +986,9 @@ int finalize_pythia(b2_handle* h) {
 int b2_finalize(b2_handle* h) {
     if (!h) return B2_ERR_ARG;
     CK(cudaSetDevice(h->device));
+    dfree(h, h->entry_w);             // stored rows of the old weights
+    dfree(h, h->entry_p);
+    h->entry_w = h->entry_p = nullptr;
     for (size_t i = 0; i < h->banks.size(); i++)
         if (!h->banks[i].w) return fail(h, B2_ERR_STATE, "bank %zu not set", i);
     if (h->cfg.kind == B2_PYTHIA) {
@@ -1013,6 +1041,55 @@ int b2_finalize(b2_handle* h) {
     if (env && tc_ok) h->tc_min_rows = atoi(env);
     h->finalized = true;
     return B2_OK;
+}
+
+// the stored rows of layer 0's qkv bank (the reference's stored layer-0 entry, base2_entry.py / base2_layer0.py):
+// Tw = wte . W and Tp = wpe . W as exact int64 piles, by the bank kernels themselves (plain epilogue with zero
+// exponents and biases: an input row below 2^15 has shift 0, so the stored value is the pile). Valid only when every
+// embedded value is below 2^15 (max|wte| + max|wpe| < 2^15); otherwise refused.
+int build_entry(b2_handle* h) {
+    const b2_config& c = h->cfg;
+    const int d = c.d_model, n3 = 3 * d;
+    const DevBank& bk = h->banks[0];
+    if (c.kind != B2_GPT2 || !bk.tc.ready || bk.nin != d || bk.nout != n3)
+        return fail(h, B2_ERR_STATE, "entry tables: the tensor-core qkv.0 bank is needed");
+    unsigned long long* mx = nullptr;
+    int rc = dalloc(h, &mx, 2);
+    if (rc) return rc;
+    CK(cudaMemset(mx, 0, 2 * sizeof(unsigned long long)));
+    if ((rc = tc_absmax(h->wte, (size_t)c.vocab * d, mx, 0)) || (rc = tc_absmax(h->wpe, (size_t)c.n_ctx * d, mx + 1, 0))) {
+        dfree(h, mx);
+        return fail(h, B2_ERR_CUDA, "entry tables: %s", cudaGetErrorString((cudaError_t)rc));
+    }
+    unsigned long long m[2] = {0, 0};
+    CK(cudaMemcpy(m, mx, sizeof m, cudaMemcpyDeviceToHost));
+    dfree(h, mx);
+    if (m[0] + m[1] >= 32768)
+        return fail(h, B2_ERR_ARG, "entry tables: embedded values reach 2^15 (max |wte| %llu + max |wpe| %llu)", m[0], m[1]);
+    int32_t* e0 = nullptr;
+    int64_t* b0 = nullptr;
+    if ((rc = dalloc(h, &h->entry_w, (size_t)c.vocab * n3)) || (rc = dalloc(h, &h->entry_p, (size_t)c.n_ctx * n3)) ||
+        (rc = dalloc(h, &e0, n3)) || (rc = dalloc(h, &b0, n3)))
+        return rc;
+    CK(cudaMemset(e0, 0, sizeof(int32_t) * n3));
+    CK(cudaMemset(b0, 0, sizeof(int64_t) * n3));
+    const int64_t* src[2] = {h->wte, h->wpe};
+    int64_t* dst[2] = {h->entry_w, h->entry_p};
+    const int nrows[2] = {c.vocab, c.n_ctx};
+    for (int k = 0; k < 2 && !rc; k++)
+        for (int r0 = 0; r0 < nrows[k] && !rc; r0 += h->max_rows) {
+            const int rows = std::min(h->max_rows, nrows[k] - r0);
+            if ((rc = run_quant(h, src[k] + (size_t)r0 * d, d, nullptr, rows, 0, 0))) break;
+            rc = tc_bank(bk.tc, h->tcr, EPI_PLAIN_OUT, rows, h->ex, h->LS, e0, b0, dst[k] + (size_t)r0 * n3, n3, nullptr,
+                         h->EXP2, h->PHI, 0, false);
+            if (rc) rc = fail(h, B2_ERR_CUDA, "entry tables: %s", cudaGetErrorString((cudaError_t)rc));
+        }
+    cudaError_t e = cudaDeviceSynchronize();
+    dfree(h, e0);
+    dfree(h, b0);
+    if (rc) return rc;
+    if (e != cudaSuccess) return fail(h, B2_ERR_CUDA, "entry tables: %s", cudaGetErrorString(e));
+    return read_device_error(h);
 }
 
 int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
@@ -1102,6 +1179,8 @@ int b2_alloc_streams(b2_handle* h, int32_t n_streams, int32_t max_ctx) {
     // the decode arrival at the full stream count runs one CTA per (row, head) unless few rows with long contexts
     // split it over clusters (run_attend's rule); then qkv goes unsplit, so that arrival's CTAs find SMs while it runs
     h->qkv_unsplit = !h->qkv_pair && !(n_streams * h->cfg.n_head < 2 * h->sms && max_ctx >= 256);
+    if (h->entry && !h->entry_w && h->use_tc && h->tc_min_rows < (1 << 30))
+        return build_entry(h);
     return B2_OK;
 }
 

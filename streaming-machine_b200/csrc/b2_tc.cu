@@ -1052,6 +1052,76 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1) k_bank_gemv(const TcArgs a) {
     if (nz > 1) cluster_sync();       // no CTA leaves while rank 0 may still read its piles
 }
 
+// ---------------------------------------------------------------------------------------------------------------------
+// Layer 0's qkv bank of a decode step from stored rows (the reference's stored layer-0 entry: base2_entry.py,
+// base2_layer0.py; Metal carry0 / entry_gate1 / entry_add1, base2_stream_fr2.swift:407-428). A decode row is
+// x = wte[word] + wpe[position]; when every embedded value is below 2^15 in magnitude (checked when the tables are
+// built) to16 keeps x as it is (shift 0), so the pile is exactly Tw[word] + Tp[position], Tw = wte . W and Tp = wpe . W
+// computed once (the product is linear; the reference's carry, the rounding of a sum against the sum of roundings, is
+// zero at shift 0). The row's S1 and S2 for the gauge come from x itself. One CTA of 16 warps per row: the block sums,
+// then warp w takes head parts w, w + 16, w + 32 (64 columns each, lane l columns 2l, 2l + 1) through the gauged
+// epilogue and heads_row.
+// ---------------------------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(512) k_entry_qkv(const TcArgs a, const int64_t* __restrict__ Tw,
+                                                    const int64_t* __restrict__ Tp, const int32_t* __restrict__ row_tok,
+                                                    const int64_t* __restrict__ wte, const int64_t* __restrict__ wpe,
+                                                    int vocab, int nctx) {
+    griddep_wait();
+    stamp_begin(a.stamp);
+    griddep_launch();
+    __shared__ int64_t s_1[16], s_2[16];
+    const int r = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tok = row_tok[r], pos = a.hd.row_pos[r], slot = a.hd.row_slot[r];
+    const bool ok = tok >= 0 && tok < vocab && pos >= 0 && pos < nctx;   // otherwise flagged by the embedding kernel
+    const int d = a.nin, nout = a.nout;
+    int64_t p1 = 0, p2 = 0;
+    if (ok)
+        for (int i = tid; i < d; i += 512) {
+            const int64_t x = wte[(size_t)tok * d + i] + wpe[(size_t)pos * d + i];
+            p1 += x;
+            p2 += x * x;
+        }
+    p1 = warp_sum64(p1);
+    p2 = warp_sum64(p2);
+    if (lane == 0) {
+        s_1[warp] = p1;
+        s_2[warp] = p2;
+    }
+    __syncthreads();
+    int64_t S1 = 0, S2 = 0;
+#pragma unroll
+    for (int q = 0; q < 16; q++) {
+        S1 = wadd(S1, s_1[q]);
+        S2 = wadd(S2, s_2[q]);
+    }
+    const int64_t ex = -16;                           // shift 0
+    const int64_t LS = gauge_LS(S1, S2, (int)ex, a.q.LOG2, a.q.log768, a.q.eps40);
+    const int64_t e2 = __ldg(a.epi.EXP2 + (wsub(0, LS) & 0xFFFF));
+    for (int part = warp; part * 64 < nout; part += 16) {
+        const int j0 = part * 64 + 2 * lane;
+        const bool c0 = j0 < nout, c1 = j0 + 1 < nout;
+        int64_t v0 = 0, v1 = 0;
+        if (ok && c0) {
+            const int64_t P0 = Tw[(size_t)tok * nout + j0] + Tp[(size_t)pos * nout + j0];
+            v0 = epi_value<EPI_GAUGED>(P0, (int64_t)a.epi.e[j0], a.epi.b[j0], ex, LS, e2, a.epi.PHI);
+        }
+        if (ok && c1) {
+            const int64_t P1 = Tw[(size_t)tok * nout + j0 + 1] + Tp[(size_t)pos * nout + j0 + 1];
+            v1 = epi_value<EPI_GAUGED>(P1, (int64_t)a.epi.e[j0 + 1], a.epi.b[j0 + 1], ex, LS, e2, a.epi.PHI);
+        }
+        heads_row(a, part, r, slot, pos, ok, v0, v1);
+    }
+}
+
+// the largest |x| over n int64 values (atomicMax into *out, which starts at 0)
+__global__ void k_absmax(const int64_t* __restrict__ x, size_t n, unsigned long long* out) {
+    uint64_t m = 0;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+        m = max(m, mag(x[i]));
+    m = warp_max_u64(m);
+    if ((threadIdx.x & 31) == 0) atomicMax(out, (unsigned long long)m);
+}
+
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
 __global__ void k_weight_planes(const int16_t* __restrict__ w, int nin, int nout, int8_t* __restrict__ wh,
                                 int8_t* __restrict__ wl) {
@@ -1547,6 +1617,37 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
                       break)
     }
     return (int)err;
+}
+
+int tc_entry_qkv(const TcBank& t, const int64_t* Tw, const int64_t* Tp, const int32_t* row_tok, const int64_t* wte,
+                 const int64_t* wpe, int vocab, int nctx, int rows, const int32_t* e, const int64_t* b, const int32_t* EXP2,
+                 const TcQuant& q, const TcHeads& hd, uint32_t* err, cudaStream_t st, bool pdl, uint64_t* stamp) {
+    if (rows < 1 || hd.pythia || t.nout % 64) return (int)cudaErrorInvalidValue;
+    TcArgs a{};
+    a.nin = t.nin;
+    a.nout = t.nout;
+    a.rows = rows;
+    a.err = err;
+    a.q = q;
+    a.epi = EpiArgs{nullptr, nullptr, e, b, nullptr, 0, nullptr, EXP2, nullptr};
+    a.heads = 1;
+    a.hd = hd;
+    a.stamp = stamp;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(rows);
+    cfg.blockDim = dim3(512);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return (int)cudaLaunchKernelEx(&cfg, k_entry_qkv, a, Tw, Tp, row_tok, wte, wpe, vocab, nctx);
+}
+
+int tc_absmax(const int64_t* x, size_t n, unsigned long long* out, cudaStream_t st) {
+    k_absmax<<<296, 256, 0, st>>>(x, n, out);
+    return (int)cudaGetLastError();
 }
 
 }  // namespace b2

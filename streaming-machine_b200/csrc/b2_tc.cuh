@@ -107,4 +107,12 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
             const TcRace* race = nullptr, uint64_t* stamp = nullptr);
 
+// layer 0's qkv bank of a decode step from the stored rows Tw [vocab][nout] = wte . W and Tp [n_ctx][nout] = wpe . W
+// (valid when every embedded value is below 2^15; the gauged epilogue and heads16 as the bank does them)
+int tc_entry_qkv(const TcBank& t, const int64_t* Tw, const int64_t* Tp, const int32_t* row_tok, const int64_t* wte,
+                 const int64_t* wpe, int vocab, int nctx, int rows, const int32_t* e, const int64_t* b, const int32_t* EXP2,
+                 const TcQuant& q, const TcHeads& hd, uint32_t* err, cudaStream_t st, bool pdl, uint64_t* stamp);
+// the largest |x| of n int64 values into *out (device; *out must start at 0)
+int tc_absmax(const int64_t* x, size_t n, unsigned long long* out, cudaStream_t st);
+
 }  // namespace b2

@@ -310,6 +310,11 @@ class Engine:
         scores pick their word by the exact collapsing read."""
         self._call("b2_set_scalar", self.h, b"top_read", int(bool(collapsing)))
 
+    def set_entry_tables(self, on: bool):
+        """GPT-2: layer 0's qkv bank of every decode step from stored rows (wte . W and wpe . W, the reference's stored
+        layer-0 entry), built at the next alloc_streams; refused when an embedded value can reach 2^15."""
+        self._call("b2_set_scalar", self.h, b"entry_tables", int(bool(on)))
+
     def set_wait_limit(self, ns: int):
         """How long a device-side wait may take before the kernel gives up and the call reports B2_ERR_DEVICE
         (0 = the default, 0.5 s)."""

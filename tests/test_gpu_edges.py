@@ -164,3 +164,26 @@ def test_plus_32768_inputs_in_decode_banks(M, n_streams):
     assert np.array_equal(lg, want_lg)
     assert np.array_equal(tok, want_tok)
     assert np.array_equal(tok_graph, want_tok)
+
+
+def test_stored_layer0_entry_rows(M, orc):
+    """Layer 0's qkv bank of a decode step from stored rows (entry_tables: Tw = wte . W, Tp = wpe . W, the reference's
+    stored layer-0 entry): every word and score row equal to the oracle's at 1 stream (the CUDA-core banks) and 40
+    streams (the tensor-core banks), and C2's 64 streams over 24 words."""
+    from streaming_machine_b200 import engine
+    e = engine.Engine(M, n_streams=1, max_ctx=160)
+    try:
+        e.set_entry_tables(True)
+        for n in (1, 40):
+            e.alloc_streams(n, 64)
+            ids = np.random.default_rng(26 + n).integers(0, V, (n, 16))
+            tok, lg = _words_and_scores(e, ids, 4)
+            want_tok, want_lg = orc.generate(ids, 4, logits=True)
+            assert np.array_equal(lg, want_lg)
+            assert np.array_equal(tok, want_tok)
+        e.alloc_streams(64, 160)
+        ids = np.random.default_rng(1).integers(0, V, (64, 32))
+        got = e.generate(ids, 24)
+        assert np.array_equal(got, orc.generate(ids, 24))
+    finally:
+        e.close()
