@@ -92,6 +92,7 @@ struct b2_handle {
                                  // with many rows the arrival that follows runs one CTA per (row, head) and starts on
                                  // the SMs a CTA-pair qkv would hold
     int qkv_pair = 0;            // B2_QKV_PAIR=1
+    int gemv_head = 1;           // decode heads at <= 2 rows on the CUDA-core GEMV head (B2_GEMV_HEAD=0: the tile head)
     // the collapsing top read (b2_set_scalar "top_read" 1): decode steps of <= TOPFR_ROWS streams that store no scores
     int top_fr = 0;
     int entry = 0;                  // "entry_tables" 1: layer 0's qkv bank of a decode step from stored rows
@@ -583,6 +584,24 @@ int run_top_fr(b2_handle* h, int n, cudaStream_t st) {
                   FR_FIN, FR_FIN, h->race_out);
 }
 
+// the head of a decode step of one or two rows on the CUDA-core GEMV head (its rows quantised in the kernel, the race
+// in its epilogue), then the words from the 32-column winners; false when that head does not apply
+bool gemv_head_ok(const b2_handle* h, int n) {
+    return h->gemv_head && n <= 2 && h->banks[4 * h->cfg.n_layer].tc.map_w16_ok && !top_fr_ok(h, n);
+}
+int run_gemv_head(b2_handle* h, int epi, const int64_t* X, int n, cudaStream_t st) {
+    const DevBank& hb = h->banks[4 * h->cfg.n_layer];
+    const TcRace race{h->race_v, h->race_i, h->race_ld};
+    prof_begin(h, B2_PROF_BANK, st);
+    const int rc = tc_head_gemv(hb.tc, epi, X, h->cfg.d_model, n, hb.e, hb.b, h->EXP2, h->LOG2, h->log768, h->eps40, race,
+                                h->want_logits ? h->logits : nullptr, h->cfg.vocab, h->d_err, h->sms, st,
+                                h->pdl && h->prof.timing != 1, stamp_slot(h, B2_PROF_BANK));
+    prof_end(h, B2_PROF_BANK, st);
+    if (rc) return fail(h, B2_ERR_CUDA, "GEMV head: %s", cudaGetErrorString((cudaError_t)rc));
+    return launch(h, B2_PROF_RACE, "race", k_race_parts, n, 256, 0, st, (const int64_t*)h->race_v,
+                  (const int32_t*)h->race_i, h->race_ld, h->race_ld, h->race_out);
+}
+
 int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
     const b2_config& c = h->cfg;
     const int d = c.d_model, L = c.n_layer, F = c.d_ff;
@@ -621,6 +640,7 @@ int run_decode_wq(b2_handle* h, int n, cudaStream_t st) {
         q = wq_args(h, 4 * l + 3, h->HID, F, o0 + 3 * FUSED_ROWS);
         if ((rc = run_bank(h, 4 * l + 3, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q, next))) return rc;
     }
+    if (gemv_head_ok(h, n)) return run_gemv_head(h, EPI_GAUGED, h->R, n, st);
     if ((rc = run_quant(h, h->R, d, nullptr, n, 1, st))) return rc;
     if (top_fr_ok(h, n)) return run_top_fr(h, n, st);
     // the race inside the head's epilogue (per 32-column group), the logits stored only when the caller wants them
@@ -678,6 +698,7 @@ int run_decode_wq_pythia(b2_handle* h, int n, cudaStream_t st) {
         if ((rc = run_bank(h, 4 * l + 1, EPI_PLAIN_ADD, n, h->R, d, nullptr, st, nullptr, nullptr, &q))) return rc;
     }
     if ((rc = run_gauge(h, h->R, nullptr, n, 2 * L, h->ATT, st))) return rc;
+    if (gemv_head_ok(h, n)) return run_gemv_head(h, EPI_PLAIN_OUT, h->ATT, n, st);
     if ((rc = run_quant(h, h->ATT, d, nullptr, n, 0, st))) return rc;
     if (top_fr_ok(h, n)) return run_top_fr(h, n, st);
     const TcRace race{h->race_v, h->race_i, h->race_ld};
@@ -768,6 +789,7 @@ int b2_create(const b2_config* cfg, int device, int flags, b2_handle** out) {
     if (const char* v = getenv("B2_EARLY_KEYS")) h->early_keys = atoi(v);
     if (const char* v = getenv("B2_ATT_SPLIT")) h->att_split = atoi(v);
     if (const char* v = getenv("B2_QKV_PAIR")) h->qkv_pair = atoi(v);
+    if (const char* v = getenv("B2_GEMV_HEAD")) h->gemv_head = atoi(v);
     if (const char* v = getenv("B2_FUSE_HEADS")) h->fuse_heads = atoi(v);
     if (const char* v = getenv("B2_WQ")) h->wq = atoi(v);
     if (const char* v = getenv("B2_SPLIT_TRACE")) h->split_trace_path = v;

@@ -1122,6 +1122,199 @@ __global__ void k_absmax(const int64_t* __restrict__ x, size_t n, unsigned long 
     if ((threadIdx.x & 31) == 0) atomicMax(out, (unsigned long long)m);
 }
 
+// ---------------------------------------------------------------------------------------------------------------------
+// The head of a decode step of <= 2 rows as a CUDA-core GEMV over the reference-layout weights [768][wld] int16:
+// persistent CTAs (one an SM) walk 64-column tiles, each tile brought into shared memory by three TMA boxes
+// (64 columns x 256 rows) through a two-stage ring, the first two before the dependency wait. The CTA reads its rows
+// whole (768 values) and quantises them itself (OR, to16, S1 and S2 for the gauge); per tile thread t multiplies
+// columns 8 (t % 8) .. + 8 over inputs 12 (t / 8) .. + 12 (exact int64 piles), the 64 input slices are summed by
+// shuffles and shared memory, and warp r forms row r's values and races each 32-column group (ties to the lowest
+// column, base2.py:114) into the race buffer k_race_parts reads. Every wait on the ring is bounded and agreed on by
+// the whole CTA (a timeout ends the CTA's loop, flagged, after the copies in flight have landed or a bound passed).
+// ---------------------------------------------------------------------------------------------------------------------
+constexpr int HG_BOX_ROWS = 256;
+constexpr int HG_TILE = GEMV_KR * 64;             // int16 of one tile
+constexpr int HG_TILE_BYTES = HG_TILE * 2;        // 98,304
+constexpr size_t HG_SMEM = 2 * (size_t)HG_TILE_BYTES + 128;
+
+template <int EPI, int R>
+__global__ void __launch_bounds__(GEMV_THREADS, 1)
+    k_head_gemv(const __grid_constant__ CUtensorMap mw, const TcArgs a, const TcRace race) {
+    constexpr bool GAUGED = EPI == EPI_GAUGED || EPI == EPI_GAUGED_EDGE;
+    extern __shared__ uint8_t smem_raw[];
+    int16_t* W = reinterpret_cast<int16_t*>(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);   // [2][768][64]
+    __shared__ uint64_t full[2];
+    __shared__ int32_t xs[R][GEMV_KR];
+    __shared__ int64_t red[GEMV_THREADS / 32][64][R];
+    __shared__ int64_t s_pile[R][64];
+    __shared__ uint64_t s_or[GEMV_THREADS / 32][R];
+    __shared__ int64_t s_1[GEMV_THREADS / 32][R], s_2[GEMV_THREADS / 32][R];
+    __shared__ int s_dead;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, cg = tid & 7, ks = tid >> 3;
+    const int ntiles = (a.nout + 63) / 64, G = gridDim.x;
+    const int my = (int)blockIdx.x < ntiles ? (ntiles - (int)blockIdx.x + G - 1) / G : 0;
+    if (tid == 0) {
+        mbar_init(&full[0], 1);
+        mbar_init(&full[1], 1);
+        s_dead = (*(volatile uint32_t*)a.err & DERR_TIMEOUT) != 0;
+        fence_mbar_init();
+    }
+    __syncthreads();
+    const int nissue = s_dead ? 0 : my;
+    if (tid == 0) {                   // the first two tiles' weights: independent of earlier kernels
+        const uint64_t pol = l2_evict_first();
+        for (int s = 0; s < 2 && s < nissue; s++) {
+            const int tile = blockIdx.x + s * G;
+            mbar_expect_tx(&full[s], HG_TILE_BYTES);
+            for (int bx = 0; bx < GEMV_KR / HG_BOX_ROWS; bx++)
+                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], tile * 64, bx * HG_BOX_ROWS, pol);
+        }
+    }
+    griddep_wait();
+    stamp_begin(a.stamp);
+    griddep_launch();
+
+    // ---- the rows: OR, to16 shift, x16, S1, S2 ----
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        uint64_t o = 0;
+        if (r < a.rows)
+            for (int i = tid; i < GEMV_KR; i += GEMV_THREADS) o |= mag(a.q.X[(size_t)r * a.q.ldx + i]);
+        o = warp_or64(o);
+        if (lane == 0) s_or[warp][r] = o;
+    }
+    __syncthreads();
+    int sh[R];
+#pragma unroll
+    for (int r = 0; r < R; r++) {
+        uint64_t all = 0;
+#pragma unroll
+        for (int q = 0; q < GEMV_THREADS / 32; q++) all |= s_or[q][r];
+        sh[r] = to16_shift(all);
+        int64_t p1 = 0, p2 = 0;
+        for (int i = tid; i < GEMV_KR; i += GEMV_THREADS) {
+            int32_t x = 0;
+            if (r < a.rows) x = (int32_t)rshift(a.q.X[(size_t)r * a.q.ldx + i], sh[r]);
+            xs[r][i] = x;
+            p1 += x;
+            p2 += (int64_t)x * x;
+        }
+        if (GAUGED) {
+            p1 = warp_sum64(p1);
+            p2 = warp_sum64(p2);
+            if (lane == 0) {
+                s_1[warp][r] = p1;
+                s_2[warp][r] = p2;
+            }
+        }
+    }
+    __syncthreads();
+    // the epilogue's row constants (warp r < R forms row r)
+    const int er = warp < R ? warp : 0;
+    const int64_t ex = -16 + sh[er];
+    int64_t LS = 0, e2 = 0;
+    if (GAUGED && warp < R && warp < a.rows) {
+        int64_t S1 = 0, S2 = 0;
+#pragma unroll
+        for (int q = 0; q < GEMV_THREADS / 32; q++) {
+            S1 = wadd(S1, s_1[q][er]);
+            S2 = wadd(S2, s_2[q][er]);
+        }
+        LS = gauge_LS(S1, S2, (int)ex, a.q.LOG2, a.q.log768, a.q.eps40);
+        e2 = __ldg(a.epi.EXP2 + (wsub(0, LS) & 0xFFFF));
+    }
+
+    int it = 0;
+    for (; it < nissue; it++) {
+        const int s = it & 1, tile = blockIdx.x + it * G;
+        const bool got = mbar_wait(&full[s], (it >> 1) & 1, a.err);
+        if (__syncthreads_or(!got)) break;       // a wait that gave up ends every thread's loop (flagged)
+        const int16_t* Ws = W + (size_t)s * HG_TILE;
+        int64_t acc[R][8];
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) acc[r][c] = 0;
+#pragma unroll
+        for (int u = 0; u < 12; u++) {
+            const int4 w = *reinterpret_cast<const int4*>(Ws + (ks * 12 + u) * 64 + cg * 8);
+            const int32_t wv[8] = {(int16_t)(w.x & 0xFFFF), (int16_t)((uint32_t)w.x >> 16),
+                                   (int16_t)(w.y & 0xFFFF), (int16_t)((uint32_t)w.y >> 16),
+                                   (int16_t)(w.z & 0xFFFF), (int16_t)((uint32_t)w.z >> 16),
+                                   (int16_t)(w.w & 0xFFFF), (int16_t)((uint32_t)w.w >> 16)};
+#pragma unroll
+            for (int r = 0; r < R; r++) {
+                const int32_t x = xs[r][ks * 12 + u];
+#pragma unroll
+                for (int c = 0; c < 8; c++) acc[r][c] += (int64_t)x * wv[c];
+            }
+        }
+        // over the warp's four input slices (lanes cg, cg + 8, cg + 16, cg + 24), then over the 16 warps
+#pragma unroll
+        for (int r = 0; r < R; r++)
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                acc[r][c] += __shfl_xor_sync(0xffffffffu, acc[r][c], 8);
+                acc[r][c] += __shfl_xor_sync(0xffffffffu, acc[r][c], 16);
+            }
+        if (lane < 8) {
+#pragma unroll
+            for (int r = 0; r < R; r++)
+#pragma unroll
+                for (int c = 0; c < 8; c++) red[warp][lane * 8 + c][r] = acc[r][c];
+        }
+        __syncthreads();                         // the partial piles are in; every thread is done with stage s
+        if (tid == 0 && it + 2 < nissue) {       // refill stage s with the tile after next
+            const int nt = blockIdx.x + (it + 2) * G;
+            mbar_expect_tx(&full[s], HG_TILE_BYTES);
+            for (int bx = 0; bx < GEMV_KR / HG_BOX_ROWS; bx++)
+                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], nt * 64, bx * HG_BOX_ROWS,
+                                 l2_evict_first());
+        }
+        if (tid < 64 * R) {
+            const int col = tid & 63, r = tid >> 6;
+            int64_t v = 0;
+#pragma unroll
+            for (int q = 0; q < GEMV_THREADS / 32; q++) v += red[q][col][r];
+            s_pile[r][col] = v;
+        }
+        __syncthreads();
+        if (warp < R && warp < a.rows) {
+            const int r = warp, j0 = tile * 64 + 2 * lane, j1 = j0 + 1;
+            const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
+            const int64_t v0 = cv0 ? epi_value<EPI>(s_pile[r][2 * lane], (int64_t)a.epi.e[j0], a.epi.b[j0], ex, LS, e2,
+                                                    a.epi.PHI) : 0;
+            const int64_t v1 = cv1 ? epi_value<EPI>(s_pile[r][2 * lane + 1], (int64_t)a.epi.e[j1], a.epi.b[j1], ex, LS,
+                                                    e2, a.epi.PHI) : 0;
+            if (a.epi.out) {
+                int64_t* op = a.epi.out + (size_t)r * a.epi.ldo + j0;
+                if (cv0) op[0] = v0;
+                if (cv1) op[1] = v1;
+            }
+            int64_t bv = cv0 ? v0 : INT64_MIN;
+            int bi = cv0 ? j0 : 0x7fffffff;
+            if (cv1) race_merge(bv, bi, v1, j1);
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) {
+                const int64_t ov = __shfl_xor_sync(0xffffffffu, bv, off);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                race_merge(bv, bi, ov, oi);
+            }
+            if ((lane & 15) == 0) {              // lanes 0-15: the tile's columns 0-31, lanes 16-31: 32-63
+                const size_t q = (size_t)r * race.ld + tile * 2 + (lane >> 4);
+                race.v[q] = bv;
+                race.i[q] = bi;
+            }
+        }
+    }
+    if (it < nissue && tid == 0) {     // gave up: let the copies still in flight land (bounded) before the CTA leaves
+        const uint64_t t0 = gtime(), lim = wait_limit(a.err);
+        for (int j = it; j < nissue && j < it + 2; j++)
+            while (!mbar_try_wait(&full[j & 1], (j >> 1) & 1) && gtime() - t0 <= lim) {
+            }
+    }
+}
+
 // ---- weight planes: [nin][nout] int16 -> [nout_pad][nin] wh, wl (transposed through shared memory) ----
 __global__ void k_weight_planes(const int16_t* __restrict__ w, int nin, int nout, int8_t* __restrict__ wh,
                                 int8_t* __restrict__ wl) {
@@ -1183,6 +1376,21 @@ int make_map(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld, 
     cuuint32_t es[2] = {1, 1};
     CUresult r = fn(reinterpret_cast<CUtensorMap*>(m.bytes), CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, es,
                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
+}
+
+// 2-D int16 tensor [outer][inner] (row stride ld elements, a multiple of 8; mapped as uint16, a copy of the bits), box
+// 64 x 256, no swizzle (k_head_gemv)
+int make_map16(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld) {
+    auto fn = encode_fn();
+    if (!fn) return (int)cudaErrorNotSupported;
+    cuuint64_t dims[2] = {inner, outer};
+    cuuint64_t strides[1] = {ld * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)HG_BOX_ROWS};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(reinterpret_cast<CUtensorMap*>(m.bytes), CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, base, dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? 0 : (int)cudaErrorInvalidValue;
 }
@@ -1309,6 +1517,12 @@ int tc_init() {
         cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, wide_smem_bytes(WIDE_MAX_KB));
         if (e != cudaSuccess) return (int)e;
     }
+    void* heads[] = {(void*)k_head_gemv<EPI_GAUGED, 1>, (void*)k_head_gemv<EPI_GAUGED, 2>,
+                     (void*)k_head_gemv<EPI_PLAIN_OUT, 1>, (void*)k_head_gemv<EPI_PLAIN_OUT, 2>};
+    for (void* f : heads) {
+        cudaError_t e = cudaFuncSetAttribute(f, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)HG_SMEM);
+        if (e != cudaSuccess) return (int)e;
+    }
     // this device's co-residency for k_bank_wide launches (cluster sizes 1, 2, 4)
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -1391,6 +1605,23 @@ int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
         if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
     }
     t.w16 = w;
+    if (t.wpad) cudaFree(t.wpad);
+    t.wpad = nullptr;
+    t.wld = nout;
+    t.map_w16_ok = 0;
+    if (nout > 4096 && nin == GEMV_KR) {      // a head: the GEMV head reads its rows through TMA (16-byte rows)
+        const int16_t* src = w;
+        if (nout % 8) {
+            t.wld = (nout + 7) / 8 * 8;
+            if ((e = cudaMalloc(&t.wpad, sizeof(int16_t) * (size_t)nin * t.wld)) != cudaSuccess) return (int)e;
+            if ((e = cudaMemset(t.wpad, 0, sizeof(int16_t) * (size_t)nin * t.wld)) != cudaSuccess) return (int)e;
+            if ((e = cudaMemcpy2D(t.wpad, sizeof(int16_t) * t.wld, w, sizeof(int16_t) * nout, sizeof(int16_t) * nout, nin,
+                                  cudaMemcpyDeviceToDevice)) != cudaSuccess)
+                return (int)e;
+            src = t.wpad;
+        }
+        if (make_map16(t.map_w16, (void*)src, (uint64_t)t.wld, (uint64_t)nin, (uint64_t)t.wld) == 0) t.map_w16_ok = 1;
+    }
     int rc = make_map(t.map_wh, t.wh, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wl, t.wl, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wh64, t.wh, nin, t.nout_pad, nin, 64);
@@ -1405,6 +1636,9 @@ void tc_bank_free(TcBank& t) {
     if (t.wl) cudaFree(t.wl);
     if (t.colcorr) cudaFree(t.colcorr);
     if (t.colcorr_kb) cudaFree(t.colcorr_kb);
+    if (t.wpad) cudaFree(t.wpad);
+    t.wpad = nullptr;
+    t.map_w16_ok = 0;
     t.wh = t.wl = nullptr;
     t.colcorr = t.colcorr_kb = nullptr;
     t.ready = 0;
@@ -1617,6 +1851,46 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
                       break)
     }
     return (int)err;
+}
+
+int tc_head_gemv(const TcBank& t, int epi, const int64_t* X, int ldx, int rows, const int32_t* e, const int64_t* b,
+                 const int32_t* EXP2, const int32_t* LOG2, int64_t log768, int64_t eps40, const TcRace& race,
+                 int64_t* out, int ldo, uint32_t* err, int grid, cudaStream_t st, bool pdl, uint64_t* stamp) {
+    if (!t.map_w16_ok || t.nin != GEMV_KR || rows < 1 || rows > GEMV_MAX_ROWS || (epi != EPI_GAUGED && epi != EPI_PLAIN_OUT) ||
+        !race.v || race.ld < 2 * ((t.nout + 63) / 64) || grid < 1)
+        return (int)cudaErrorInvalidValue;
+    TcArgs a{};
+    a.nin = t.nin;
+    a.nout = t.nout;
+    a.rows = rows;
+    a.err = err;
+    a.q.X = X;
+    a.q.ldx = ldx;
+    a.q.LOG2 = LOG2;
+    a.q.log768 = log768;
+    a.q.eps40 = eps40;
+    a.epi = EpiArgs{nullptr, nullptr, e, b, out, ldo, nullptr, EXP2, nullptr};
+    a.stamp = stamp;
+    const int ntiles = (t.nout + 63) / 64;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(grid < ntiles ? grid : ntiles);
+    cfg.blockDim = dim3(GEMV_THREADS);
+    cfg.dynamicSmemBytes = HG_SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    const CUtensorMap& m = *reinterpret_cast<const CUtensorMap*>(t.map_w16.bytes);
+    cudaError_t r;
+    if (epi == EPI_GAUGED)
+        r = rows == 1 ? cudaLaunchKernelEx(&cfg, k_head_gemv<EPI_GAUGED, 1>, m, a, race)
+                      : cudaLaunchKernelEx(&cfg, k_head_gemv<EPI_GAUGED, 2>, m, a, race);
+    else
+        r = rows == 1 ? cudaLaunchKernelEx(&cfg, k_head_gemv<EPI_PLAIN_OUT, 1>, m, a, race)
+                      : cudaLaunchKernelEx(&cfg, k_head_gemv<EPI_PLAIN_OUT, 2>, m, a, race);
+    return (int)r;
 }
 
 int tc_entry_qkv(const TcBank& t, const int64_t* Tw, const int64_t* Tp, const int32_t* row_tok, const int64_t* wte,

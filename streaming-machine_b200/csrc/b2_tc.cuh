@@ -29,6 +29,10 @@ struct TcBank {
     const int16_t* w16 = nullptr;  // the reference-layout bank [nin][nout] (for the +32768 correction)
     TcMap map_wh, map_wl;        // box: 128 bytes of K x 128 outputs
     TcMap map_wh64, map_wl64;    // box: 128 bytes of K x 64 outputs (k_bank_wide)
+    int16_t* wpad = nullptr;     // heads (nout > 4096) whose rows are not 16-byte pieces: the rows padded with zeros
+    int wld = 0;                 // the row stride the GEMV head reads (nout, or nout rounded up to 8)
+    TcMap map_w16;               // heads: int16 [nin][wld], box 64 columns x 256 rows (k_head_gemv)
+    int map_w16_ok = 0;
 };
 
 // Row-side buffers: the activations' planes and their corrections.
@@ -106,6 +110,13 @@ int tc_bank(const TcBank& t, TcRows& r, int epi, int rows, const int32_t* ex, co
             cudaStream_t st, bool pdl, const TcHeads* heads = nullptr, bool* heads_done = nullptr,
             uint64_t* trace = nullptr, const TcQuant* quant = nullptr, uint64_t* or_out = nullptr,
             const TcRace* race = nullptr, uint64_t* stamp = nullptr);
+
+// the head of a decode step of <= 2 rows as a CUDA-core GEMV (k_head_gemv): X [rows][ldx] int64 quantised in the kernel
+// (its OR, to16, and for EPI_GAUGED the gauge), the race in its epilogue into race (and the scores into out when out is
+// given); the bank must have map_w16_ok (a head built with more than 4,096 outputs)
+int tc_head_gemv(const TcBank& t, int epi, const int64_t* X, int ldx, int rows, const int32_t* e, const int64_t* b,
+                 const int32_t* EXP2, const int32_t* LOG2, int64_t log768, int64_t eps40, const TcRace& race,
+                 int64_t* out, int ldo, uint32_t* err, int grid, cudaStream_t st, bool pdl, uint64_t* stamp);
 
 // layer 0's qkv bank of a decode step from the stored rows Tw [vocab][nout] = wte . W and Tp [n_ctx][nout] = wpe . W
 // (valid when every embedded value is below 2^15; the gauged epilogue and heads16 as the bank does them)

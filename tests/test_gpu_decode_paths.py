@@ -1,5 +1,5 @@
 """The decode step's alternative paths against each other and the oracle: rows quantised inside the bank kernels (the
-default, producers publishing each row's OR; at <= 2 streams the CUDA-core GEMV banks) and a quantisation kernel before
+default, producers publishing each row's OR; at <= 2 streams the CUDA-core GEMV banks and GEMV head) and a quantisation kernel before
 every bank (B2_WQ=0); stream counts that fill one or two 32-row halves partly; words with and without the logits
 stored (the head's folded race)."""
 import os
@@ -41,7 +41,7 @@ def _run(e, ids, words):
 
 @pytest.mark.parametrize("n", [1, 2, 3, 31, 33])
 def test_default_decode_vs_oracle(gpu_engine, orc, n):
-    """Every logit of 4 words: one and two streams (the CUDA-core GEMV banks), three, just under / over one 32-row half
+    """Every logit of 4 words: one and two streams (the CUDA-core GEMV banks and head), three, just under / over one 32-row half
     (64 streams: test_gpu_parity)."""
     e = with_streams(gpu_engine, 64, 160)
     ids = np.random.default_rng(100 + n).integers(0, V, (n, 32))
