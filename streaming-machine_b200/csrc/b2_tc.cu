@@ -1123,9 +1123,11 @@ __global__ void k_absmax(const int64_t* __restrict__ x, size_t n, unsigned long 
 }
 
 // ---------------------------------------------------------------------------------------------------------------------
-// The head of a decode step of <= 2 rows as a CUDA-core GEMV over the reference-layout weights [768][wld] int16:
-// persistent CTAs (one an SM) walk 64-column tiles, each tile brought into shared memory by three TMA boxes
-// (64 columns x 256 rows) through a two-stage ring, the first two before the dependency wait. The CTA reads its rows
+// The head of a decode step of <= 2 rows as a CUDA-core GEMV over the weights stored as 64-column tiles
+// ([tile][768][64] int16, each tile one contiguous 96 KB block, so the reads stream through DRAM in order):
+// persistent CTAs (one an SM) walk the tiles, each brought into shared memory by three TMA boxes (64 columns x 256
+// rows) through a two-stage ring, the first two, and the columns' exponents and biases, before the dependency wait.
+// The CTA reads its rows
 // whole (768 values) and quantises them itself (OR, to16, S1 and S2 for the gauge); per tile thread t multiplies
 // columns 8 (t % 8) .. + 8 over inputs 12 (t / 8) .. + 12 (exact int64 piles), the 64 input slices are summed by
 // shuffles and shared memory, and warp r forms row r's values and races each 32-column group (ties to the lowest
@@ -1136,6 +1138,7 @@ constexpr int HG_BOX_ROWS = 256;
 constexpr int HG_TILE = GEMV_KR * 64;             // int16 of one tile
 constexpr int HG_TILE_BYTES = HG_TILE * 2;        // 98,304
 constexpr size_t HG_SMEM = 2 * (size_t)HG_TILE_BYTES + 128;
+constexpr int HG_PRE = 8;                         // tiles per CTA whose exponents and biases are staged in shared memory
 
 template <int EPI, int R>
 __global__ void __launch_bounds__(GEMV_THREADS, 1)
@@ -1149,6 +1152,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
     __shared__ int64_t s_pile[R][64];
     __shared__ uint64_t s_or[GEMV_THREADS / 32][R];
     __shared__ int64_t s_1[GEMV_THREADS / 32][R], s_2[GEMV_THREADS / 32][R];
+    __shared__ int32_t s_e[HG_PRE][64];
+    __shared__ int64_t s_b[HG_PRE][64];
     __shared__ int s_dead;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, cg = tid & 7, ks = tid >> 3;
     const int ntiles = (a.nout + 63) / 64, G = gridDim.x;
@@ -1167,8 +1172,15 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
             const int tile = blockIdx.x + s * G;
             mbar_expect_tx(&full[s], HG_TILE_BYTES);
             for (int bx = 0; bx < GEMV_KR / HG_BOX_ROWS; bx++)
-                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], tile * 64, bx * HG_BOX_ROWS, pol);
+                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], 0,
+                                 tile * GEMV_KR + bx * HG_BOX_ROWS, pol);
         }
+    }
+    for (int q = tid; q < HG_PRE * 64; q += GEMV_THREADS) {     // the columns' exponents and biases (read-only inputs)
+        const int t = q >> 6, j = (blockIdx.x + t * G) * 64 + (q & 63);
+        const bool v = t < my && j < a.nout;
+        s_e[t][q & 63] = v ? __ldg(a.epi.e + j) : 0;
+        s_b[t][q & 63] = v ? __ldg(a.epi.b + j) : 0;
     }
     griddep_wait();
     stamp_begin(a.stamp);
@@ -1268,8 +1280,8 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
             const int nt = blockIdx.x + (it + 2) * G;
             mbar_expect_tx(&full[s], HG_TILE_BYTES);
             for (int bx = 0; bx < GEMV_KR / HG_BOX_ROWS; bx++)
-                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], nt * 64, bx * HG_BOX_ROWS,
-                                 l2_evict_first());
+                tma_load_2d_hint(W + (size_t)s * HG_TILE + bx * HG_BOX_ROWS * 64, &mw, &full[s], 0,
+                                 nt * GEMV_KR + bx * HG_BOX_ROWS, l2_evict_first());
         }
         if (tid < 64 * R) {
             const int col = tid & 63, r = tid >> 6;
@@ -1282,10 +1294,13 @@ __global__ void __launch_bounds__(GEMV_THREADS, 1)
         if (warp < R && warp < a.rows) {
             const int r = warp, j0 = tile * 64 + 2 * lane, j1 = j0 + 1;
             const bool cv0 = j0 < a.nout, cv1 = j1 < a.nout;
-            const int64_t v0 = cv0 ? epi_value<EPI>(s_pile[r][2 * lane], (int64_t)a.epi.e[j0], a.epi.b[j0], ex, LS, e2,
-                                                    a.epi.PHI) : 0;
-            const int64_t v1 = cv1 ? epi_value<EPI>(s_pile[r][2 * lane + 1], (int64_t)a.epi.e[j1], a.epi.b[j1], ex, LS,
-                                                    e2, a.epi.PHI) : 0;
+            const bool pre = it < HG_PRE;
+            const int64_t e0 = !cv0 ? 0 : pre ? (int64_t)s_e[it][2 * lane] : (int64_t)a.epi.e[j0];
+            const int64_t e1 = !cv1 ? 0 : pre ? (int64_t)s_e[it][2 * lane + 1] : (int64_t)a.epi.e[j1];
+            const int64_t b0 = !cv0 ? 0 : pre ? s_b[it][2 * lane] : a.epi.b[j0];
+            const int64_t b1 = !cv1 ? 0 : pre ? s_b[it][2 * lane + 1] : a.epi.b[j1];
+            const int64_t v0 = cv0 ? epi_value<EPI>(s_pile[r][2 * lane], e0, b0, ex, LS, e2, a.epi.PHI) : 0;
+            const int64_t v1 = cv1 ? epi_value<EPI>(s_pile[r][2 * lane + 1], e1, b1, ex, LS, e2, a.epi.PHI) : 0;
             if (a.epi.out) {
                 int64_t* op = a.epi.out + (size_t)r * a.epi.ldo + j0;
                 if (cv0) op[0] = v0;
@@ -1381,7 +1396,7 @@ int make_map(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld, 
 }
 
 // 2-D int16 tensor [outer][inner] (row stride ld elements, a multiple of 8; mapped as uint16, a copy of the bits), box
-// 64 x 256, no swizzle (k_head_gemv)
+// 64 x 256, no swizzle (k_head_gemv's tiles: inner 64, outer tiles x 768)
 int make_map16(TcMap& m, void* base, uint64_t inner, uint64_t outer, uint64_t ld) {
     auto fn = encode_fn();
     if (!fn) return (int)cudaErrorNotSupported;
@@ -1605,22 +1620,21 @@ int tc_bank_build(TcBank& t, const int16_t* w, int nin, int nout) {
         if ((e = cudaGetLastError()) != cudaSuccess) return (int)e;
     }
     t.w16 = w;
-    if (t.wpad) cudaFree(t.wpad);
-    t.wpad = nullptr;
-    t.wld = nout;
+    if (t.wt) cudaFree(t.wt);
+    t.wt = nullptr;
     t.map_w16_ok = 0;
-    if (nout > 4096 && nin == GEMV_KR) {      // a head: the GEMV head reads its rows through TMA (16-byte rows)
-        const int16_t* src = w;
-        if (nout % 8) {
-            t.wld = (nout + 7) / 8 * 8;
-            if ((e = cudaMalloc(&t.wpad, sizeof(int16_t) * (size_t)nin * t.wld)) != cudaSuccess) return (int)e;
-            if ((e = cudaMemset(t.wpad, 0, sizeof(int16_t) * (size_t)nin * t.wld)) != cudaSuccess) return (int)e;
-            if ((e = cudaMemcpy2D(t.wpad, sizeof(int16_t) * t.wld, w, sizeof(int16_t) * nout, sizeof(int16_t) * nout, nin,
-                                  cudaMemcpyDeviceToDevice)) != cudaSuccess)
+    if (nout > 4096 && nin == GEMV_KR) {      // a head: the GEMV head's copy, 64-column tiles each one contiguous block
+        const int nt = (nout + 63) / 64;
+        const size_t tile = (size_t)nin * 64;
+        if ((e = cudaMalloc(&t.wt, sizeof(int16_t) * tile * nt)) != cudaSuccess) return (int)e;
+        if ((e = cudaMemset(t.wt, 0, sizeof(int16_t) * tile * nt)) != cudaSuccess) return (int)e;
+        for (int q = 0; q < nt; q++) {
+            const int wc = nout - q * 64 < 64 ? nout - q * 64 : 64;
+            if ((e = cudaMemcpy2D(t.wt + q * tile, sizeof(int16_t) * 64, w + (size_t)q * 64, sizeof(int16_t) * nout,
+                                  sizeof(int16_t) * wc, nin, cudaMemcpyDeviceToDevice)) != cudaSuccess)
                 return (int)e;
-            src = t.wpad;
         }
-        if (make_map16(t.map_w16, (void*)src, (uint64_t)t.wld, (uint64_t)nin, (uint64_t)t.wld) == 0) t.map_w16_ok = 1;
+        if (make_map16(t.map_w16, t.wt, 64, (uint64_t)nt * nin, 64) == 0) t.map_w16_ok = 1;
     }
     int rc = make_map(t.map_wh, t.wh, nin, t.nout_pad, nin, 128);
     if (!rc) rc = make_map(t.map_wl, t.wl, nin, t.nout_pad, nin, 128);
@@ -1636,8 +1650,8 @@ void tc_bank_free(TcBank& t) {
     if (t.wl) cudaFree(t.wl);
     if (t.colcorr) cudaFree(t.colcorr);
     if (t.colcorr_kb) cudaFree(t.colcorr_kb);
-    if (t.wpad) cudaFree(t.wpad);
-    t.wpad = nullptr;
+    if (t.wt) cudaFree(t.wt);
+    t.wt = nullptr;
     t.map_w16_ok = 0;
     t.wh = t.wl = nullptr;
     t.colcorr = t.colcorr_kb = nullptr;

@@ -29,9 +29,9 @@ struct TcBank {
     const int16_t* w16 = nullptr;  // the reference-layout bank [nin][nout] (for the +32768 correction)
     TcMap map_wh, map_wl;        // box: 128 bytes of K x 128 outputs
     TcMap map_wh64, map_wl64;    // box: 128 bytes of K x 64 outputs (k_bank_wide)
-    int16_t* wpad = nullptr;     // heads (nout > 4096) whose rows are not 16-byte pieces: the rows padded with zeros
-    int wld = 0;                 // the row stride the GEMV head reads (nout, or nout rounded up to 8)
-    TcMap map_w16;               // heads: int16 [nin][wld], box 64 columns x 256 rows (k_head_gemv)
+    int16_t* wt = nullptr;       // heads (nout > 4096): the weights as 64-column tiles, [tile][nin][64] int16 (zeros past
+                                 // nout), so that the GEMV head reads each tile as one contiguous 96 KB block
+    TcMap map_w16;               // over wt as [tiles * nin][64], box 64 columns x 256 rows (k_head_gemv)
     int map_w16_ok = 0;
 };
 
