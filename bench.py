@@ -51,7 +51,7 @@ BANK_LAUNCHES = 49                     # 48 layer banks + the head per decode st
 # DRAM bytes per bank launch of a decode step, (12 x (qkv + proj + fc + mproj) + head) / 49, from ncu captures of
 # single launches (dram__bytes_read.sum + dram__bytes_write.sum; commands and per-bank figures in the decode-bank
 # summary under profiles/). Not measured in this run; None where no capture was made (C5's 512-row path).
-BANK_TRAFFIC = {"c1": 5_160_866, "c2": 6_096_274, "c3": 5_472_705}
+BANK_TRAFFIC = {"c1": 5_175_824, "c2": 6_096_274, "c3": 5_472_705}
 BANK_TRAFFIC_SOURCE = "ncu: dram__bytes_read.sum + dram__bytes_write.sum of single bank launches (profiles/)"
 VOCAB = {"gpt2": 50257, "pythia": 50304}
 
